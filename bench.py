@@ -1,0 +1,406 @@
+"""Benchmark of the int4 KV-cache decode-attention path (task config 1 @ 32K).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--context 32768] [--window 0]
+
+One step = one decode step of one attention layer: quantize-on-append of the
+new token's K/V into the preallocated int4 cache, then fused decode attention
+over the whole context (H=32, Hkv=16, D=128, batch 1, fp16 Q/out, fp16
+scales/biases). Steps rotate over 8 independent layer caches (8 x 75.5 MB,
+larger than the 126 MB L2), so every step streams its cache from HBM. The
+appended slot is rewritten on each rotation, so every step attends over
+exactly `--context` tokens.
+
+The metric is decode-attention tokens/s (steps/s x batch), whole job: with
+N GPUs (torchrun, one process per GPU) every rank serves its own layer caches
+(weak scaling: independent KV heads / sequences per GPU, no data-path
+collective); value = total steps / max-over-ranks time.
+
+`--impl reference` times the reference's algorithm on the host CPU instead
+(the CPU oracle in oracle/: quantize the new token, concatenate it onto the
+packed cache as engine/gemma4_multilayer.cpp:228-236 does, dequantize to fp32
+and run SDPA, engine/gemma4_multilayer.cpp:307-308,349), OpenMP over all host
+threads; MLX itself is not installable here.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, HKV, D = 32, 16, 128
+LAYERS = 8
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--context", type=int, default=32768)
+    ap.add_argument("--window", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def bytes_per_step(n_ctx: int, window: int) -> dict:
+    vis = min(n_ctx, window) if window > 0 else n_ctx
+    per_tok = 2 * (D // 2 + 2 * (D // 64) * 2) * HKV  # K+V codes, fp16 scale+bias, all KV heads
+    attn = per_tok * vis + H * D * 2 * 2             # cache + Q + O (fp16)
+    append = 2 * HKV * D * 2 + per_tok               # read new K/V fp16, write one token
+    return {"attn": attn, "append": append, "step": attn + append, "per_token": per_tok}
+
+
+# ------------------------------------------------------------------ clocks --
+
+class Clocks:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]), power=float(parts[3]),
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], pcap=parts[8]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        load = [r for r in rows if r["power"] > 250.0] or rows
+        reasons = set()
+        for r in load:
+            for key, name in (("hw", "hw_slowdown"), ("hwt", "hw_thermal_slowdown"),
+                              ("swt", "sw_thermal_slowdown"), ("pcap", "sw_power_cap")):
+                if r[key].lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r["sm"] for r in load),
+                "sm_max_mhz": max(r["smax"] for r in rows), "reasons": sorted(reasons),
+                "samples": len(rows), "samples_under_load": len(load)}
+
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def ncu_traffic(n_ctx: int, window: int):
+    """Per-launch DRAM bytes of the decode kernel from the committed ncu summary,
+    scaled to this context when it was captured at another size."""
+    path = os.path.join(ROOT, "profiles", "sdpa_decode_int4_cfg1_global.md")
+    if not os.path.exists(path) or window > 0:
+        return None
+    txt = open(path).read()
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)\s*@\s*context\s*(\d+)", txt)
+    if not m:
+        return None
+    return float(m.group(1)) * n_ctx / float(m.group(2))
+
+
+# -------------------------------------------------------------- ours (GPU) --
+
+def run_ours(args, rank: int, world: int, local_rank: int):
+    import torch
+    import torch.distributed as dist
+    import gemma4metal_b200.turboquant as tq
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    n_ctx, window = args.context, args.window
+    cap = (n_ctx + 3) // 4 * 4
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+
+    def rms_norm(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True)) * w
+
+    wq = 1 + 0.1 * torch.randn(D, device=dev, generator=gen)
+    wk = 1 + 0.1 * torch.randn(D, device=dev, generator=gen)
+    layers = []
+    for _ in range(LAYERS):
+        cache = tq.KVCache(1, HKV, D, cap, device=dev)
+        k = rms_norm(torch.randn(1, HKV, n_ctx - 1, D, device=dev, generator=gen), wk).half()
+        v = torch.randn(1, HKV, n_ctx - 1, D, device=dev, generator=gen).half()
+        cache.append(k, v, pos=0)
+        del k, v
+        q = rms_norm(torch.randn(1, H, D, device=dev, generator=gen), wq).half()
+        kn = rms_norm(torch.randn(1, HKV, 1, D, device=dev, generator=gen), wk).half()
+        vn = torch.randn(1, HKV, 1, D, device=dev, generator=gen).half()
+        out = torch.empty(1, H, D, dtype=torch.float16, device=dev)
+        layers.append(dict(cache=cache, q=q, kn=kn, vn=vn, out=out))
+    nbytes = tq.sdpa_int4_workspace_size(1, H, HKV, D, n_ctx, window)
+    wss = [tq.workspace(dev, nbytes) if i == 0 else None for i in range(1)]
+    ws = wss[0]
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(Lr, s, with_append=True):
+        c = Lr["cache"]
+        if with_append:
+            tq.quantize_append(Lr["kn"], Lr["vn"], *c.tensors(), pos=n_ctx - 1, s=s)
+        tq.sdpa_int4(Lr["q"], *c.tensors(), H // HKV, 1.0, window, s=s, n_tokens=n_ctx,
+                     out=Lr["out"], ws=ws)
+
+    # eager warm-up (plans, occupancy, attributes) then one graph per layer
+    with torch.cuda.stream(stream):
+        for Lr in layers:
+            step(Lr, stream)
+    torch.cuda.synchronize()
+    graphs, kgraphs = [], []
+    for Lr in layers:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                step(Lr, stream)
+        graphs.append(g)
+        g2 = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g2, stream=stream):
+                step(Lr, stream, with_append=False)
+        kgraphs.append(g2)
+    torch.cuda.synchronize()
+
+    clocks = Clocks(local_rank)
+    clocks.start()
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            graphs[i % LAYERS].replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for i in range(args.steps):
+            graphs[i % LAYERS].replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_ms = e0.elapsed_time(e1)
+
+    # decode kernel alone (same rotation), for the roofline
+    reps = max(LAYERS * 50, 2000)
+    k0 = torch.cuda.Event(enable_timing=True)
+    k1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        for i in range(LAYERS * 4):
+            kgraphs[i % LAYERS].replay()
+        k0.record(stream)
+        for i in range(reps):
+            kgraphs[i % LAYERS].replay()
+        k1.record(stream)
+    torch.cuda.synchronize()
+    kern_us = k0.elapsed_time(k1) * 1000.0 / reps
+    clk = clocks.stop()
+
+    # end to end through the public API with host buffers every step
+    hq = torch.empty(1, H, D, dtype=torch.float16, pin_memory=True)
+    hk = torch.empty(1, HKV, 1, D, dtype=torch.float16, pin_memory=True)
+    hv = torch.empty_like(hk, pin_memory=True)
+    hout = torch.empty(1, H, D, dtype=torch.float16, pin_memory=True)
+    hq.copy_(layers[0]["q"].cpu())
+    hk.copy_(layers[0]["kn"].cpu())
+    hv.copy_(layers[0]["vn"].cpu())
+    e2e_steps = max(1, min(args.steps, 2000))
+
+    def e2e_loop(n):
+        with torch.cuda.stream(stream):
+            for i in range(n):
+                Lr = layers[i % LAYERS]
+                Lr["q"].copy_(hq, non_blocking=True)
+                Lr["kn"].copy_(hk, non_blocking=True)
+                Lr["vn"].copy_(hv, non_blocking=True)
+                step(Lr, stream)
+                hout.copy_(Lr["out"], non_blocking=True)
+                stream.synchronize()
+
+    e2e_loop(min(10, e2e_steps))
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ee0 = torch.cuda.Event(enable_timing=True)
+    ee1 = torch.cuda.Event(enable_timing=True)
+    ee0.record(stream)
+    e2e_loop(e2e_steps)
+    ee1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ee0.elapsed_time(ee1)
+    assert tq.device_error() == 0, "a kernel reported a device error"
+
+    # max over ranks
+    tt = torch.tensor([t_ms, e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t_ms, e2e_ms = float(tt[0]), float(tt[1])
+
+    # release graphs before the process group goes away
+    del graphs, kgraphs
+    torch.cuda.synchronize()
+    return dict(t_ms=t_ms, kern_us=kern_us, e2e_ms=e2e_ms, e2e_steps=e2e_steps, clocks=clk,
+                layer0=layers[0])
+
+
+# ----------------------------------------------------------- CPU reference --
+
+def cpu_reference(n_ctx: int, window: int, steps: int, warmup: int, seed: int = 5):
+    """Reference algorithm on the host: quantize the new token, concatenate it
+    onto the packed cache (the reference's append copies the whole cache,
+    engine/gemma4_multilayer.cpp:230-236), dequantize K/V to fp32 and run
+    SDPA (engine/gemma4_multilayer.cpp:307-308,349)."""
+    from oracle import inputs, oracle as O
+    L = inputs.make_layer(seed, H, HKV, D, n_ctx - 1)
+    kq, ks, kb = O.quantize(L["k"])
+    vq, vs, vb = O.quantize(L["v"])
+    q = L["q"].astype(np.float16)
+    kn, vn = L["k_new"], L["v_new"]
+    del L
+
+    def one():
+        nk = O.quantize(kn)
+        nv = O.quantize(vn)
+        ck = [np.concatenate([a, b], axis=2) for a, b in zip((kq, ks, kb), nk)]
+        cv = [np.concatenate([a, b], axis=2) for a, b in zip((vq, vs, vb), nv)]
+        return O.sdpa_int4(q, *ck, *cv, window=window)
+
+    for _ in range(warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    dt = time.perf_counter() - t0
+    return steps / dt, O.num_threads(), dt
+
+
+# --------------------------------------------------------------------- main --
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    n_ctx, window = args.context, args.window
+    bps = bytes_per_step(n_ctx, window)
+    workload = f"cfg1 decode step: append 1 token + sdpa_int4, ctx {n_ctx}, " + \
+               (f"sliding window {window}" if window > 0 else "global")
+    config = {"workload": workload, "batch": 1, "heads": H, "kv_heads": HKV, "head_dim": D,
+              "context": n_ctx, "window": window, "codes": "int4 (group 64)", "scales": "fp16", "q_out": "fp16",
+              "layers_rotated": LAYERS,
+              "l2": f"inputs larger than L2: {LAYERS} rotating layer caches "
+                    f"({LAYERS * bps['attn'] / 1e6:.0f} MB > 126 MB L2)",
+              "parallelism": f"dp{args.gpus} (independent KV heads/sequences per GPU)"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        steps = max(1, min(args.steps, 20))
+        warm = max(0, min(args.warmup, 2))
+        value, cores, dt = cpu_reference(n_ctx, window, steps, warm)
+        line = {"metric": "int4-KV decode-attention tokens/s", "value": value, "unit": "tokens/s",
+                "n_gpus": args.gpus, "steps": steps, "warmup": warm,
+                "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy)",
+                "config": config, "impl": "reference",
+                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores,
+                                 "kind": "port",
+                                 "sample": f"{steps} full decode steps (quantize+concatenate "
+                                           f"append, dequantize, fp32 SDPA) of the same layer"},
+                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    res = run_ours(args, rank, world, local_rank)
+    steps_total = args.steps * world
+    value = steps_total / (res["t_ms"] / 1000.0)
+    peaks = measured_peaks()
+    achieved = bps["attn"] / (res["kern_us"] * 1e-6) / 1e9
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / peaks["hbm_gbs"], "traffic": ncu_traffic(n_ctx, window),
+                "kernel": "tq::decode_kernel<128,2,__half>",
+                "kernel_us": res["kern_us"], "algorithmic_bytes_per_launch": bps["attn"],
+                "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy read+write)",
+                "frac_of_8tbs_nominal": achieved / 8000.0}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cv, cores, dt = cpu_reference(n_ctx, window, steps=10, warmup=1)
+        cpu = {"value": cv, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"10 decode steps of one layer at ctx {n_ctx} ({dt:.1f} s): "
+                         "quantize+concatenate append, dequantize, fp32 SDPA"}
+    e2e_value = res["e2e_steps"] * world / (res["e2e_ms"] / 1000.0)
+    line = {"metric": "int4-KV decode-attention tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": res["t_ms"] / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded torch.randn, RMS-normalised Q/K as task configs[0])",
+            "config": config, "roofline": roofline, "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "tokens/s",
+                    "h2d_bytes_per_step": (H * D + 2 * HKV * D) * 2,
+                    "d2h_bytes_per_step": H * D * 2,
+                    "path": "gemma4metal_b200.turboquant.quantize_append + sdpa_int4 (ctypes C ABI)"},
+            "gpu_launches": 2 * args.steps, "clocks": res["clocks"],
+            "hbm_gbs_step": bps["step"] * value / world / 1e9}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,140 @@
+// Device helpers shared by the sm_100a kernels: dtype loads/stores, the int4
+// unpack, and the mbarrier / bulk-copy (TMA, non-tensor) primitives.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace tq {
+
+enum Dtype : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
+
+// Error codes written to the device error word (see tq_device_error).
+enum DeviceError : uint32_t { kErrNone = 0, kErrBarrierTimeout = 1u };
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+__device__ __forceinline__ float load_as_float(const void* p, long long i, int dtype) {
+  if (dtype == kF16) return __half2float(reinterpret_cast<const __half*>(p)[i]);
+  if (dtype == kBF16) return __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p)[i]);
+  return reinterpret_cast<const float*>(p)[i];
+}
+
+__device__ __forceinline__ void store_from_float(void* p, long long i, int dtype, float v) {
+  if (dtype == kF16) {
+    reinterpret_cast<__half*>(p)[i] = __float2half_rn(v);
+  } else if (dtype == kBF16) {
+    reinterpret_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+  } else {
+    reinterpret_cast<float*>(p)[i] = v;
+  }
+}
+
+// Scale/bias element types of the cache.
+template <typename SB>
+__device__ __forceinline__ float sb_to_float(SB v);
+template <>
+__device__ __forceinline__ float sb_to_float<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float sb_to_float<__half>(__half v) { return __half2float(v); }
+
+// ---- int4 unpack without integer->float conversion instructions ------------
+// Nibble j of a word is OR-ed into the mantissa of 2^23 at its own bit
+// position (j <= 4) or, for j = 5..7, from the word shifted right by 12, so
+// the float equals 2^23 + c * 2^e(j) exactly; subtracting 2^23 (packed
+// fp32x2 add) leaves c * 2^e(j), e(j) = {0,4,8,12,16,8,12,16}. Dot products
+// use q_d * 2^-e(d) (exact power-of-two rescale), V sums are rescaled by
+// 2^-e(d) once at the end, so the result is the exact integer code path.
+constexpr uint32_t kMagic = 0x4B000000u;  // 2^23
+__host__ __device__ constexpr int nib_exp(int j) { return j <= 4 ? 4 * j : 4 * (j - 3); }
+
+__device__ __forceinline__ void unpack_word(uint32_t w, float2 (&c)[4]) {
+  const uint32_t hi = w >> 12;
+  const float2 m = make_float2(-8388608.0f, -8388608.0f);
+  c[0] = __fadd2_rn(make_float2(__uint_as_float(kMagic | (w & 0xFu)),
+                                __uint_as_float(kMagic | (w & 0xF0u))), m);
+  c[1] = __fadd2_rn(make_float2(__uint_as_float(kMagic | (w & 0xF00u)),
+                                __uint_as_float(kMagic | (w & 0xF000u))), m);
+  c[2] = __fadd2_rn(make_float2(__uint_as_float(kMagic | (w & 0xF0000u)),
+                                __uint_as_float(kMagic | (hi & 0xF00u))), m);
+  c[3] = __fadd2_rn(make_float2(__uint_as_float(kMagic | (hi & 0xF000u)),
+                                __uint_as_float(kMagic | (hi & 0xF0000u))), m);
+}
+
+// ---- shared-memory address + mbarrier + bulk async copy --------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait: gives up after ~`budget_cycles` SM clocks, records
+// kErrBarrierTimeout in the device error word and returns false. Callers keep
+// running (on stale shared memory) so the kernel always terminates; the host
+// reads the error word through tq_device_error().
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, uint32_t* err,
+                                                  long long budget_cycles = 4000000000LL) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long start = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - start > budget_cycles) {
+      if (err) atomicOr(err, kErrBarrierTimeout);
+      return false;
+    }
+  }
+  return true;
+}
+
+// cp.async.bulk global -> shared (1-D, non-tensor TMA), completion counted on
+// `bar` in bytes. dst/src 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes,
+                                         uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
+      "[%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+// L2 eviction-priority policy for data that is streamed once per step.
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+}  // namespace tq

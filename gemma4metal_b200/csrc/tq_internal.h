@@ -1,0 +1,69 @@
+// Host-side launch interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace tq {
+
+cudaError_t launch_quantize_rows(const void* x, int x_dtype, long long rows, int D, long long n_new,
+                                 int Hkv, int capacity, long long bstride_tok, int pos,
+                                 const int32_t* positions, uint32_t* codes, void* scales,
+                                 void* biases, int sb_dtype, cudaStream_t stream,
+                                 const void* x2 = nullptr, uint32_t* codes2 = nullptr,
+                                 void* scales2 = nullptr, void* biases2 = nullptr);
+
+cudaError_t launch_dequantize(const uint32_t* codes, const void* scales, const void* biases,
+                              int sb_dtype, long long rows, int D, void* out, int out_dtype,
+                              cudaStream_t stream);
+
+// Split-KV decode attention over an int4 cache.
+struct DecodeArgs {
+  const void* q;  // (B, H, D)
+  int q_dtype;
+  const uint32_t* kq;
+  const void* ks;
+  const void* kb;
+  const uint32_t* vq;
+  const void* vs;
+  const void* vb;
+  int sb_dtype;
+  const int32_t* seq_lens;  // nullable: per-sequence local token count
+  int n_tokens;             // uniform local count (or max when seq_lens given)
+  int B, H, Hkv, D, G;      // G = query heads per KV head
+  int capacity;
+  long long bstride_tok;  // tokens between sequences in the cache arrays
+  float scale;
+  int window;
+  int token_offset;  // global position of local slot 0 (sequence shards)
+  int n_total;       // global sequence length (for the window); <=0: same as local
+  int partial;       // 0: normalised output; 1: (o, m, l) partial state
+  void* out;         // partial == 0: (B, H, D) in out_dtype
+  int out_dtype;
+  float* part_out;   // partial == 1: (B, H*(D+2))
+  void* workspace;
+  size_t workspace_bytes;
+  uint32_t* err;
+};
+
+// Plan: split count etc. Returns workspace bytes needed.
+struct DecodePlan {
+  int gsub;          // query heads per CTA (<= G)
+  int nsub;          // G / gsub
+  int tokens_per_tile;
+  int splits;
+  int tiles_per_split;
+  size_t ws_bytes;
+  size_t ws_o_off, ws_ml_off, ws_cnt_off;
+};
+
+DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_max);
+cudaError_t launch_decode(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
+
+cudaError_t launch_lse_merge(const float* parts, int n_parts, int B, int H, int D, void* out,
+                             int out_dtype, cudaStream_t stream);
+
+int device_sm_count(int device);
+
+}  // namespace tq

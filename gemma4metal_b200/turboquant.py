@@ -1,0 +1,312 @@
+"""Python host mirror of the reference's `turboquant` API over the C ABI.
+
+Same names, argument order and defaults as lib/turboquant.h (MLX arrays become
+torch CUDA tensors; torch is only the device-memory/stream plumbing here):
+
+    set_metallib_path(path)                                  lib/turboquant.h:209
+    sdpa_int4(queries, k_quant, k_scales, k_biases,
+              v_quant, v_scales, v_biases, gqa_factor,
+              scale=1.0, sliding_window=0, s=None)           lib/turboquant.h:202-207
+    quantize(x, group_size=64, bits=4)                       MLX quantize, engine/gemma4_multilayer.cpp:228
+    dequantize(w, scales, biases, group_size=64, bits=4)     MLX dequantize, engine/gemma4_multilayer.cpp:307
+
+plus the pieces the reference does with whole-cache copies or does not have:
+`quantize_append` (replaces quantize + concatenate, engine/gemma4_multilayer.cpp:228-240),
+`sdpa_int4_partial` / `lse_merge` (sequence-split across GPUs) and `KVCache`
+(a preallocated int4 cache). Errors raise RuntimeError, as the reference's
+primitives throw std::runtime_error (lib/turboquant.cpp:363-365).
+
+The CUDA library is mandatory: importing this module without
+libturboquant_b200.so raises; there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional, Sequence
+
+import torch
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libturboquant_b200.so")
+
+F32, F16, BF16 = 0, 1, 2
+_DT = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}
+_TORCH_DT = {v: k for k, v in _DT.items()}
+
+_lib = None
+
+
+def load_library() -> ctypes.CDLL:
+    """Load libturboquant_b200.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(
+            f"{LIB_PATH} is missing: build it with `python -m gemma4metal_b200.build` "
+            "(the int4 attention path has no CPU fallback)")
+    L = ctypes.CDLL(LIB_PATH)
+    P, I, I64, F, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+    L.tq_last_error.restype = ctypes.c_char_p
+    L.tq_version.restype = ctypes.c_char_p
+    L.tq_set_metallib_path.argtypes = [ctypes.c_char_p]
+    L.tq_quantize.argtypes = [P, I, I64, I, P, P, P, I, P]
+    L.tq_dequantize.argtypes = [P, P, P, I, I64, I, P, I, P]
+    L.tq_quantize_append.argtypes = [P, P, I, I, I, I, I, P, P, P, P, P, P, I, I, I, P, P]
+    L.tq_sdpa_int4_workspace_size.restype = SZ
+    L.tq_sdpa_int4_workspace_size.argtypes = [I, I, I, I, I, I]
+    L.tq_workspace_init.argtypes = [P, SZ, P]
+    L.tq_sdpa_int4.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, P, P, I, P, SZ, P]
+    L.tq_sdpa_int4_partial.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, I, I, P,
+                                       P, SZ, P]
+    L.tq_lse_merge.argtypes = [P, I, I, I, I, P, I, P]
+    L.tq_device_error.argtypes = [P, ctypes.POINTER(ctypes.c_uint32)]
+    _register_extra(L)
+    _lib = L
+    return L
+
+
+def _register_extra(L) -> None:
+    """Bind entry points that only some builds export (added incrementally)."""
+    P, I, I64, F, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+    if hasattr(L, "tq_polar_encode"):
+        L.tq_polar_encode.argtypes = [P, I, I64, I, I, P, P, P, P, P, P, P, P, P, P]
+        L.tq_compressed_score.argtypes = [P, I, P, P, P, P, I, I, I, I, I, I, P, P, P, F, P, I, P]
+        L.tq_compressed_sdpa.argtypes = [P, I, P, P, P, P, P, P, P, I, I, I, I, I, I, P, P, P, F,
+                                         I, P, I, P, SZ, P]
+        L.tq_compressed_sdpa_workspace_size.restype = SZ
+        L.tq_compressed_sdpa_workspace_size.argtypes = [I, I, I, I, I]
+
+
+def _check(rc: int) -> None:
+    if rc != 0:
+        msg = load_library().tq_last_error().decode()
+        raise RuntimeError(f"turboquant error {rc}: {msg}")
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise RuntimeError("turboquant tensors must live on a CUDA device")
+    if not t.is_contiguous():
+        raise RuntimeError("turboquant tensors must be contiguous")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(s) -> ctypes.c_void_p:
+    if s is None:
+        s = torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _dt(t: torch.Tensor) -> int:
+    if t.dtype not in _DT:
+        raise RuntimeError(f"unsupported dtype {t.dtype}")
+    return _DT[t.dtype]
+
+
+def version() -> str:
+    return load_library().tq_version().decode()
+
+
+def set_metallib_path(path: str) -> None:
+    """Kept for source compatibility (lib/turboquant.h:209); kernels are linked in."""
+    load_library().tq_set_metallib_path(path.encode())
+
+
+# -------------------------------------------------------------- quantizer --
+
+def quantize(x: torch.Tensor, group_size: int = 64, bits: int = 4,
+             scales_dtype: torch.dtype = torch.float16, s=None):
+    """Affine group-64 4-bit quantization of the last axis (MLX quantize
+    semantics of the task spec). Returns (codes uint32 [..., D/8],
+    scales [..., D/64], biases [..., D/64])."""
+    if group_size != 64 or bits != 4:
+        raise RuntimeError("only group_size=64, bits=4 is implemented")
+    D = x.shape[-1]
+    lead = x.shape[:-1]
+    rows = int(torch.tensor(lead).prod().item()) if len(lead) else 1
+    codes = torch.empty(*lead, D // 8, dtype=torch.int32, device=x.device)
+    scales = torch.empty(*lead, D // 64, dtype=scales_dtype, device=x.device)
+    biases = torch.empty_like(scales)
+    _check(load_library().tq_quantize(_ptr(x.contiguous()), _dt(x), rows, D, _ptr(codes),
+                                      _ptr(scales), _ptr(biases), _dt(scales), _stream(s)))
+    return codes, scales, biases
+
+
+def dequantize(w: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, group_size: int = 64,
+               bits: int = 4, dtype: torch.dtype = torch.float32, s=None) -> torch.Tensor:
+    """value = scale * code + bias (lib/turboquant.metal:718-720)."""
+    if group_size != 64 or bits != 4:
+        raise RuntimeError("only group_size=64, bits=4 is implemented")
+    D = w.shape[-1] * 8
+    lead = w.shape[:-1]
+    rows = int(torch.tensor(lead).prod().item()) if len(lead) else 1
+    out = torch.empty(*lead, D, dtype=dtype, device=w.device)
+    _check(load_library().tq_dequantize(_ptr(w), _ptr(scales), _ptr(biases), _dt(scales), rows, D,
+                                        _ptr(out), _dt(out), _stream(s)))
+    return out
+
+
+# --------------------------------------------------------------- KV cache --
+
+class KVCache:
+    """Preallocated int4 KV cache of one attention layer:
+    codes (B, Hkv, capacity, D/8) int32 (uint32 bit patterns) and scales/biases
+    (B, Hkv, capacity, D/64), the reference's (nkv, N, D/8) layout
+    (lib/turboquant.h:197-200) with a fixed capacity instead of a growing
+    concatenation (engine/gemma4_multilayer.cpp:230-236)."""
+
+    def __init__(self, batch: int, num_kv_heads: int, head_dim: int, capacity: int,
+                 device=None, scales_dtype: torch.dtype = torch.float16):
+        if capacity % 4:
+            raise RuntimeError("capacity must be a multiple of 4")
+        dev = torch.device(device) if device is not None else torch.device("cuda")
+        self.batch, self.num_kv_heads, self.head_dim, self.capacity = batch, num_kv_heads, head_dim, capacity
+        shp = (batch, num_kv_heads, capacity)
+        self.k_quant = torch.zeros(*shp, head_dim // 8, dtype=torch.int32, device=dev)
+        self.v_quant = torch.zeros_like(self.k_quant)
+        self.k_scales = torch.zeros(*shp, head_dim // 64, dtype=scales_dtype, device=dev)
+        self.k_biases = torch.zeros_like(self.k_scales)
+        self.v_scales = torch.zeros_like(self.k_scales)
+        self.v_biases = torch.zeros_like(self.k_scales)
+        self.length = 0
+
+    def tensors(self):
+        return (self.k_quant, self.k_scales, self.k_biases, self.v_quant, self.v_scales,
+                self.v_biases)
+
+    def append(self, k_new: torch.Tensor, v_new: torch.Tensor, pos: Optional[int] = None,
+               positions: Optional[torch.Tensor] = None, s=None) -> None:
+        """Quantize (B, Hkv, n_new, D) new tokens into slots pos.. (default: the
+        current length) and advance the length."""
+        if k_new.dim() == 3:
+            k_new, v_new = k_new.unsqueeze(0), v_new.unsqueeze(0)
+        n_new = k_new.shape[2]
+        p = self.length if pos is None else pos
+        quantize_append(k_new, v_new, *self.tensors(), pos=p, positions=positions, s=s)
+        if positions is None:
+            self.length = max(self.length, p + n_new)
+
+
+def quantize_append(k_new: torch.Tensor, v_new: torch.Tensor, k_quant, k_scales, k_biases,
+                    v_quant, v_scales, v_biases, pos: int = 0,
+                    positions: Optional[torch.Tensor] = None, s=None) -> None:
+    """Quantize-on-append into a preallocated cache (B, Hkv, capacity, ...).
+    k_new, v_new: (B, Hkv, n_new, D)."""
+    if k_new.dim() == 3:
+        k_new, v_new = k_new.unsqueeze(0), v_new.unsqueeze(0)
+    B, Hkv, n_new, D = k_new.shape
+    cap = k_quant.shape[-2]
+    _check(load_library().tq_quantize_append(
+        _ptr(k_new.contiguous()), _ptr(v_new.contiguous()), _dt(k_new), B, Hkv, D, n_new,
+        _ptr(k_quant), _ptr(k_scales), _ptr(k_biases), _ptr(v_quant), _ptr(v_scales),
+        _ptr(v_biases), _dt(k_scales), cap, int(pos), _ptr(positions), _stream(s)))
+
+
+# -------------------------------------------------------------- attention --
+
+_WS = {}
+
+
+def workspace(device: torch.device, nbytes: int, s=None) -> Optional[torch.Tensor]:
+    """Per-device cached, zero-initialised workspace of at least nbytes."""
+    if nbytes == 0:
+        return None
+    key = (device.index if device.index is not None else torch.cuda.current_device())
+    ws = _WS.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _check(load_library().tq_workspace_init(_ptr(ws), ws.numel(), _stream(s)))
+        _WS[key] = ws
+    return ws
+
+
+def sdpa_int4_workspace_size(batch: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                             n_tokens: int, sliding_window: int = 0) -> int:
+    return int(load_library().tq_sdpa_int4_workspace_size(batch, num_heads, num_kv_heads, head_dim,
+                                                          n_tokens, sliding_window))
+
+
+def sdpa_int4(queries: torch.Tensor, k_quant: torch.Tensor, k_scales: torch.Tensor,
+              k_biases: torch.Tensor, v_quant: torch.Tensor, v_scales: torch.Tensor,
+              v_biases: torch.Tensor, gqa_factor: int, scale: float = 1.0,
+              sliding_window: int = 0, s=None, *, n_tokens: Optional[int] = None,
+              seq_lens: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+              out_dtype: Optional[torch.dtype] = None,
+              ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Fused int4 decode attention (lib/turboquant.h:202-207).
+
+    queries (H, D) with a cache of (Hkv, N, D/8) -- the reference's shapes --
+    or batched: queries (B, H, D) with a cache of (B, Hkv, capacity, D/8).
+    n_tokens defaults to the cache's token axis. Returns (…, H, D) in
+    out_dtype (default: the query dtype)."""
+    squeeze = queries.dim() == 2
+    q = queries.unsqueeze(0) if squeeze else queries
+    cache = [k_quant, k_scales, k_biases, v_quant, v_scales, v_biases]
+    if k_quant.dim() == 3:
+        cache = [c.unsqueeze(0) for c in cache]
+    B, H, D = q.shape
+    _, Hkv, cap, _ = cache[0].shape
+    n = cap if n_tokens is None else int(n_tokens)
+    od = out_dtype or q.dtype
+    if out is None:
+        out = torch.empty(B, H, D, dtype=od, device=q.device)
+    nbytes = sdpa_int4_workspace_size(B, H, Hkv, D, n, sliding_window)
+    if ws is None:
+        ws = workspace(q.device, nbytes, s)
+    _check(load_library().tq_sdpa_int4(
+        _ptr(q.contiguous()), _dt(q), *[_ptr(c) for c in cache], _dt(cache[1]), int(gqa_factor),
+        float(scale), int(sliding_window), B, Hkv, D, n, cap, _ptr(seq_lens), _ptr(out), _dt(out),
+        _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
+    return out[0] if squeeze else out
+
+
+def sdpa_int4_partial(queries: torch.Tensor, k_quant, k_scales, k_biases, v_quant, v_scales,
+                      v_biases, gqa_factor: int, scale: float = 1.0, sliding_window: int = 0,
+                      *, n_local: Optional[int] = None, token_offset: int = 0,
+                      n_total: Optional[int] = None, part_out: Optional[torch.Tensor] = None,
+                      ws: Optional[torch.Tensor] = None, s=None) -> torch.Tensor:
+    """Partial softmax state of a sequence shard, returned as (B, H*(D+2))
+    fp32 in the tq_lse_merge layout."""
+    q = queries.unsqueeze(0) if queries.dim() == 2 else queries
+    cache = [k_quant, k_scales, k_biases, v_quant, v_scales, v_biases]
+    if k_quant.dim() == 3:
+        cache = [c.unsqueeze(0) for c in cache]
+    B, H, D = q.shape
+    _, Hkv, cap, _ = cache[0].shape
+    nl = cap if n_local is None else int(n_local)
+    nt = token_offset + nl if n_total is None else int(n_total)
+    if part_out is None:
+        part_out = torch.empty(B, H * (D + 2), dtype=torch.float32, device=q.device)
+    nbytes = sdpa_int4_workspace_size(B, H, Hkv, D, nl, 0)
+    if ws is None:
+        ws = workspace(q.device, nbytes, s)
+    _check(load_library().tq_sdpa_int4_partial(
+        _ptr(q.contiguous()), _dt(q), *[_ptr(c) for c in cache], _dt(cache[1]), int(gqa_factor),
+        float(scale), int(sliding_window), B, Hkv, D, nl, cap, int(token_offset), nt,
+        _ptr(part_out), _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
+    return part_out
+
+
+def lse_merge(parts: torch.Tensor, num_heads: int, head_dim: int,
+              out: Optional[torch.Tensor] = None, out_dtype: torch.dtype = torch.float32,
+              s=None) -> torch.Tensor:
+    """Merge partial states parts (P, B, H*(D+2)) into (B, H, D)."""
+    if parts.dim() == 2:
+        parts = parts.unsqueeze(1)
+    P, B, _ = parts.shape
+    if out is None:
+        out = torch.empty(B, num_heads, head_dim, dtype=out_dtype, device=parts.device)
+    _check(load_library().tq_lse_merge(_ptr(parts), P, B, num_heads, head_dim, _ptr(out), _dt(out),
+                                       _stream(s)))
+    return out
+
+
+def device_error(s=None) -> int:
+    """Read and clear the device error word (0 = no kernel reported an error)."""
+    code = ctypes.c_uint32(0)
+    _check(load_library().tq_device_error(_stream(s), ctypes.byref(code)))
+    return int(code.value)

@@ -1,0 +1,159 @@
+/*
+ * turboquant_c.h -- C ABI of the B200 int4 KV-cache attention library
+ * (libturboquant_b200.so). Plain C types only: device pointers, sizes, dtype
+ * enums and a cudaStream_t passed as void*.
+ *
+ * Conventions shared by every entry point:
+ *   - Return 0 on success, a TQ_ERR_* code otherwise; tq_last_error() gives a
+ *     message for the calling thread. Arguments are validated on the host
+ *     before anything is launched (the reference throws std::runtime_error
+ *     instead: lib/turboquant.cpp:363-365).
+ *   - Nothing here allocates device memory. The caller owns inputs, outputs
+ *     and any workspace (the reference allocates outputs inside eval_gpu:
+ *     lib/turboquant.cpp:372).
+ *   - Work is enqueued asynchronously on `stream` (NULL = legacy default
+ *     stream); no call synchronises, so calls can be captured in CUDA graphs
+ *     once workspaces are allocated.
+ *   - Device pointers must be 16-byte aligned (TMA bulk copies).
+ *
+ * int4 cache layout (the reference's, lib/turboquant.h:197-200, with an
+ * explicit token capacity so the cache can be preallocated):
+ *   codes   uint32 (B, Hkv, capacity, D/8): element 8w+j of a token row at
+ *           bits 4j..4j+3 of word w (lib/turboquant.metal:796-799);
+ *   scales  (B, Hkv, capacity, D/64) in sb_dtype (fp16 by default);
+ *   biases  same shape/dtype; value = scale * code + bias.
+ *   capacity must be a multiple of 4.
+ */
+#ifndef TURBOQUANT_C_H
+#define TURBOQUANT_C_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TQ_API __attribute__((visibility("default")))
+#else
+#define TQ_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum tq_dtype { TQ_F32 = 0, TQ_F16 = 1, TQ_BF16 = 2 } tq_dtype;
+
+enum {
+  TQ_OK = 0,
+  TQ_ERR_INVALID = 1,     /* bad argument (shape, alignment, null pointer) */
+  TQ_ERR_UNSUPPORTED = 2, /* valid but not implemented (e.g. head_dim 96) */
+  TQ_ERR_CUDA = 3,        /* a CUDA runtime call or launch failed */
+  TQ_ERR_WORKSPACE = 4,   /* workspace too small (see *_workspace_size) */
+  TQ_ERR_DEVICE = 5       /* a kernel reported an error through the device error word */
+};
+
+/* Message for the last failing call on this thread ("" if none). */
+TQ_API const char* tq_last_error(void);
+
+/* Library version string. */
+TQ_API const char* tq_version(void);
+
+/* No-op kept for source compatibility with the reference
+ * (lib/turboquant.h:209, set_metallib_path): there is no shader library to
+ * locate; kernels are linked into this shared object. */
+TQ_API void tq_set_metallib_path(const char* path);
+
+/* Affine group-64 4-bit quantization of `rows` contiguous rows of head_dim
+ * values (MLX quantize(x, 64, 4): engine/gemma4_multilayer.cpp:228-229,
+ * tests/test_sdpa_int4.cpp:25-26). scale = (max-min)/15 and bias = min,
+ * rounded to sb_dtype; codes = clamp(rint((x-bias)/scale), 0, 15) computed
+ * with the rounded scale/bias; a constant group gets scale 0 and codes 0.
+ * x: (rows, D) in x_dtype; codes (rows, D/8); scales/biases (rows, D/64). */
+TQ_API int tq_quantize(const void* x, tq_dtype x_dtype, int64_t rows, int head_dim, uint32_t* codes,
+                void* scales, void* biases, tq_dtype sb_dtype, void* stream);
+
+/* value = scale * code + bias (MLX dequantize(w, s, b, 64, 4):
+ * engine/gemma4_multilayer.cpp:307-308, tests/test_sdpa_int4.cpp:31-32).
+ * out: (rows, D) in out_dtype. */
+TQ_API int tq_dequantize(const uint32_t* codes, const void* scales, const void* biases,
+                  tq_dtype sb_dtype, int64_t rows, int head_dim, void* out, tq_dtype out_dtype,
+                  void* stream);
+
+/* Quantize-on-append: quantize n_new new tokens per (sequence, KV head) of K
+ * and V and write them in place at token slots pos .. pos+n_new-1 of a
+ * preallocated cache. Replaces the reference's quantize + concatenate of the
+ * whole cache per token (engine/gemma4_multilayer.cpp:228-240).
+ * k_new, v_new: (B, Hkv, n_new, D) contiguous in in_dtype.
+ * positions: NULL (every sequence appends at `pos`) or a device int32[B]
+ * of per-sequence positions. Slots must satisfy slot + n_new <= capacity. */
+TQ_API int tq_quantize_append(const void* k_new, const void* v_new, tq_dtype in_dtype, int batch,
+                       int num_kv_heads, int head_dim, int n_new, uint32_t* k_quant,
+                       void* k_scales, void* k_biases, uint32_t* v_quant, void* v_scales,
+                       void* v_biases, tq_dtype sb_dtype, int capacity, int pos,
+                       const int32_t* positions, void* stream);
+
+/* Workspace bytes that tq_sdpa_int4 / tq_sdpa_int4_partial need for these
+ * sizes (split-KV partials + merge counters). n_tokens is the largest
+ * sequence length the call will see. The workspace must be zero-filled once
+ * before first use (tq_workspace_init); kernels leave it reusable. */
+TQ_API size_t tq_sdpa_int4_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim,
+                                   int n_tokens, int sliding_window);
+
+/* Zero a workspace (cudaMemsetAsync on `stream`). */
+TQ_API int tq_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Fused single-query decode attention straight from the int4 cache
+ * (replaces turboquant::sdpa_int4, lib/turboquant.h:202-207 /
+ * lib/turboquant.cpp:405-417; same argument order, then sizes).
+ *   queries: (B, H, D) in q_dtype, H = num_kv_heads * gqa_factor,
+ *            query head h reads KV head h / gqa_factor;
+ *   out:     (B, H, D) in out_dtype;
+ *   n_tokens: tokens in every sequence, or the maximum when seq_lens (device
+ *            int32[B]) is given;
+ *   scale multiplies q.k (reference default 1.0);
+ *   sliding_window > 0 masks tokens t with (N-1-t) >= sliding_window
+ *   (lib/turboquant.metal:779); 0 = global attention.
+ * Long contexts are split across CTAs and merged in-kernel; the workspace
+ * must hold tq_sdpa_int4_workspace_size(...) bytes (may be NULL when that is
+ * 0). head_dim in {128, 256, 512}; gqa_factor in {1, 2, 4, 8}. */
+TQ_API int tq_sdpa_int4(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,
+                 const void* k_scales, const void* k_biases, const uint32_t* v_quant,
+                 const void* v_scales, const void* v_biases, tq_dtype sb_dtype, int gqa_factor,
+                 float scale, int sliding_window, int batch, int num_kv_heads, int head_dim,
+                 int n_tokens, int capacity, const int32_t* seq_lens, void* out,
+                 tq_dtype out_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Sequence-split shard of decode attention: this cache holds global token
+ * positions [token_offset, token_offset + n_local) of a sequence whose total
+ * length is n_total (all sequences of the batch share both). Writes the
+ * shard's partial softmax state per query head in the merge layout of
+ * tq_lse_merge, fp32: part_out[b] = { o (H, D) unnormalised, ml (H, 2) with
+ * m = max score (natural-log units) and l = sum exp(score - m) }.
+ * A shard with no visible token writes m = -inf, l = 0, o = 0.
+ * No counterpart in the reference (it has no multi-GPU code); it is the
+ * per-GPU half of the NCCL all-gather + merge path. */
+TQ_API int tq_sdpa_int4_partial(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,
+                         const void* k_scales, const void* k_biases, const uint32_t* v_quant,
+                         const void* v_scales, const void* v_biases, tq_dtype sb_dtype,
+                         int gqa_factor, float scale, int sliding_window, int batch,
+                         int num_kv_heads, int head_dim, int n_local, int capacity,
+                         int token_offset, int n_total, float* part_out, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* Log-sum-exp merge of n_parts partial states (e.g. one per GPU after an
+ * all-gather). parts: n_parts blocks of (H*(D+2)) floats per batch entry,
+ * laid out [part][batch][H*(D+2)]; out: (B, H, D) in out_dtype.
+ * out = sum_p e^(m_p - M) o_p / sum_p e^(m_p - M) l_p, M = max_p m_p; a head
+ * whose total l is 0 gets 0 (lib/turboquant.metal:838-888 merges the same
+ * state across simdgroups). */
+TQ_API int tq_lse_merge(const float* parts, int n_parts, int batch, int num_heads, int head_dim,
+                 void* out, tq_dtype out_dtype, void* stream);
+
+/* Read and clear the device error word that kernels set when a bounded wait
+ * gives up (0 = no error). Synchronises `stream`. */
+TQ_API int tq_device_error(void* stream, uint32_t* code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TURBOQUANT_C_H */

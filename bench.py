@@ -188,60 +188,71 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         tq.sdpa_int4(Lr["q"], *c.tensors(), H // HKV, 1.0, window, s=s, n_tokens=n_ctx,
                      out=Lr["out"], ws=ws)
 
-    # eager warm-up (plans, occupancy, attributes) then one graph per layer
+    # eager warm-up (plans, occupancy, attributes), then CUDA graphs: one per
+    # layer (1 step) and one of CHUNK consecutive steps over the rotation, so
+    # host launch overhead is amortised over CHUNK steps.
     with torch.cuda.stream(stream):
         for Lr in layers:
             step(Lr, stream)
     torch.cuda.synchronize()
-    graphs, kgraphs = [], []
-    for Lr in layers:
+
+    def capture(steps, with_append=True):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
             with torch.cuda.graph(g, stream=stream):
-                step(Lr, stream)
-        graphs.append(g)
-        g2 = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            with torch.cuda.graph(g2, stream=stream):
-                step(Lr, stream, with_append=False)
-        kgraphs.append(g2)
+                for i in steps:
+                    step(layers[i % LAYERS], stream, with_append)
+        return g
+
+    CHUNK = 8 * LAYERS
+    single = [capture([i]) for i in range(LAYERS)]
+    chunk = capture(range(CHUNK))
+    kchunk = capture(range(CHUNK), with_append=False)
     torch.cuda.synchronize()
+
+    def run_steps(n):
+        with torch.cuda.stream(stream):
+            for _ in range(n // CHUNK):
+                chunk.replay()
+            for i in range(n % CHUNK):
+                single[i % LAYERS].replay()
 
     clocks = Clocks(local_rank)
     clocks.start()
-    with torch.cuda.stream(stream):
-        for i in range(args.warmup):
-            graphs[i % LAYERS].replay()
+    run_steps(args.warmup)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        e0.record(stream)
-        for i in range(args.steps):
-            graphs[i % LAYERS].replay()
-        e1.record(stream)
+    e0.record(stream)
+    run_steps(args.steps)
+    e1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
     t_ms = e0.elapsed_time(e1)
 
-    # decode kernel alone (same rotation), for the roofline
-    reps = max(LAYERS * 50, 2000)
+    # decode kernel alone (same rotation, CHUNK launches per graph) for the
+    # roofline; runs >= 1.5 s so the clock sampler sees it
+    with torch.cuda.stream(stream):
+        kchunk.replay()
+    torch.cuda.synchronize()
     k0 = torch.cuda.Event(enable_timing=True)
     k1 = torch.cuda.Event(enable_timing=True)
+    reps, t_start = 0, time.perf_counter()
+    k0.record(stream)
     with torch.cuda.stream(stream):
-        for i in range(LAYERS * 4):
-            kgraphs[i % LAYERS].replay()
-        k0.record(stream)
-        for i in range(reps):
-            kgraphs[i % LAYERS].replay()
-        k1.record(stream)
+        while time.perf_counter() - t_start < 1.5 or reps < 8:
+            for _ in range(8):
+                kchunk.replay()
+            reps += 8
+            torch.cuda.current_stream().synchronize() if reps % 64 == 0 else None
+    k1.record(stream)
     torch.cuda.synchronize()
-    kern_us = k0.elapsed_time(k1) * 1000.0 / reps
+    kern_us = k0.elapsed_time(k1) * 1000.0 / (reps * CHUNK)
     clk = clocks.stop()
 
     # end to end through the public API with host buffers every step
@@ -285,7 +296,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     t_ms, e2e_ms = float(tt[0]), float(tt[1])
 
     # release graphs before the process group goes away
-    del graphs, kgraphs
+    del single, chunk, kchunk
     torch.cuda.synchronize()
     return dict(t_ms=t_ms, kern_us=kern_us, e2e_ms=e2e_ms, e2e_steps=e2e_steps, clocks=clk,
                 layer0=layers[0])
@@ -372,7 +383,9 @@ def main():
     achieved = bps["attn"] / (res["kern_us"] * 1e-6) / 1e9
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                 "frac": achieved / peaks["hbm_gbs"], "traffic": ncu_traffic(n_ctx, window),
-                "kernel": "tq::decode_kernel<128,2,__half>",
+                "kernel": ("tq::decode_kernel<128,2,__half> (CUDA cores)"
+                           if os.environ.get("TQ_DECODE_KERNEL") == "simt" else
+                           "tq::decode_mma_kernel<128,2,__half,false> (mma.sync)"),
                 "kernel_us": res["kern_us"], "algorithmic_bytes_per_launch": bps["attn"],
                 "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs, copy read+write)",
                 "frac_of_8tbs_nominal": achieved / 8000.0}
@@ -393,7 +406,8 @@ def main():
                     "h2d_bytes_per_step": (H * D + 2 * HKV * D) * 2,
                     "d2h_bytes_per_step": H * D * 2,
                     "path": "gemma4metal_b200.turboquant.quantize_append + sdpa_int4 (ctypes C ABI)"},
-            "gpu_launches": 2 * args.steps, "clocks": res["clocks"],
+            "gpu_launches": 2 * args.steps,
+            "launches_per_step": "2 (quantize_rows_kernel for K+V, decode_kernel)", "clocks": res["clocks"],
             "hbm_gbs_step": bps["step"] * value / world / 1e9}
     if rank == 0:
         print(json.dumps(line), flush=True)

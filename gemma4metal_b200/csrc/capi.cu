@@ -193,6 +193,8 @@ static int decode_common(const DecodeCommon& c, const char* fn, const int32_t* s
   if (e != cudaSuccess) return cuda_fail(e, fn);
   const int vis = partial ? c.n_tokens : visible_max(c.n_tokens, c.window);
   tq::DecodePlan pl = tq::plan_decode(dev, c.B, H, c.Hkv, c.D, vis);
+  if (pl.splits < 0)
+    return fail(TQ_ERR_UNSUPPORTED, "%s: batch * kv_heads too large for one launch", fn);
   if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < pl.ws_bytes))
     return fail(TQ_ERR_WORKSPACE, "%s: workspace of %zu bytes needed, %zu given", fn, pl.ws_bytes,
                 workspace ? workspace_bytes : static_cast<size_t>(0));

@@ -22,6 +22,8 @@
 //     when the caller asked for it, for the multi-GPU sequence split).
 // All waits on barriers are bounded (see mbar_wait_bounded).
 #include <algorithm>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -36,6 +38,9 @@ constexpr int kThreads = 128;
 constexpr int kStages = 4;
 constexpr int kMaxSplits = 1024;
 constexpr int kMinBlocksPerSM = 3;
+}  // namespace
+const size_t kCounterRegionBytes = 64 * 1024;  // 16384 merge counters
+namespace {
 
 template <int D, int G>
 struct Cfg {
@@ -609,12 +614,20 @@ int device_sm_count(int device) {
   return n;
 }
 
+int choose_decode_variant(int D, int G) {
+  const char* env = getenv("TQ_DECODE_KERNEL");
+  const bool force_simt = env && strcmp(env, "simt") == 0;
+  if (!force_simt && mma_supported(D, std::min(G, 8))) return kDecodeMma;
+  return kDecodeSimt;
+}
+
 DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_max) {
   DecodePlan pl{};
   const int G = H / Hkv;
-  pl.gsub = std::min(G, max_gsub(D));
+  pl.variant = choose_decode_variant(D, G);
+  pl.gsub = std::min(G, pl.variant == kDecodeMma ? 8 : max_gsub(D));
   pl.nsub = G / pl.gsub;
-  pl.tokens_per_tile = 8192 / D;
+  pl.tokens_per_tile = pl.variant == kDecodeMma ? mma_tokens_per_tile() : 8192 / D;
   const int T = pl.tokens_per_tile;
   // +1 tile: a window that does not start on a tile boundary spans one more
   const int tiles = std::max(1, (n_visible_max + T - 1) / T + 1);
@@ -622,8 +635,12 @@ DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_m
   int per_sm = kMinBlocksPerSM;
   if (device >= 0) {
     // occupancy of the f16-scale kernel (the f32 variant differs by 1 KB smem)
-    KernelInfo k = pick_kernel(D, pl.gsub, kF16);
-    if (k.fn) per_sm = blocks_per_sm(device, k);
+    if (pl.variant == kDecodeMma) {
+      per_sm = mma_occupancy(device, D, pl.gsub);
+    } else {
+      KernelInfo k = pick_kernel(D, pl.gsub, kF16);
+      if (k.fn) per_sm = blocks_per_sm(device, k);
+    }
   }
   const long long target = static_cast<long long>(device_sm_count(device < 0 ? 0 : device)) * per_sm;
   long long splits = (target + units - 1) / units;
@@ -637,16 +654,21 @@ DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_m
   pl.splits = static_cast<int>(splits);
   pl.tiles_per_split = tps;
   if (pl.splits > 1) {
+    // Merge counters live in a fixed region at the start of every workspace,
+    // so that no plan's partials ever overlap another plan's counters: kernels
+    // leave counters at zero, partial data is only ever written after them.
     const size_t n_part = static_cast<size_t>(units) * pl.splits * pl.gsub;
-    pl.ws_o_off = 0;
-    pl.ws_ml_off = align256(n_part * D * sizeof(float));
-    pl.ws_cnt_off = pl.ws_ml_off + align256(n_part * 2 * sizeof(float));
-    pl.ws_bytes = pl.ws_cnt_off + align256(static_cast<size_t>(units) * sizeof(unsigned));
+    pl.ws_cnt_off = 0;
+    pl.ws_o_off = kCounterRegionBytes;
+    pl.ws_ml_off = pl.ws_o_off + align256(n_part * D * sizeof(float));
+    pl.ws_bytes = pl.ws_ml_off + align256(n_part * 2 * sizeof(float));
+    if (units * sizeof(unsigned) > kCounterRegionBytes) pl.ws_bytes = 0, pl.splits = -1;
   }
   return pl;
 }
 
 cudaError_t launch_decode(const DecodeArgs& a, const DecodePlan& pl, cudaStream_t stream) {
+  if (pl.variant == kDecodeMma) return launch_decode_mma(a, pl, stream);
   KernelInfo k = pick_kernel(a.D, pl.gsub, a.sb_dtype);
   if (!k.fn) return cudaErrorInvalidValue;
   int device = 0;

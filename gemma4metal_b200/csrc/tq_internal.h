@@ -47,8 +47,20 @@ struct DecodeArgs {
   uint32_t* err;
 };
 
+// Decode kernel variants: the CUDA-core kernel (sdpa_decode.cu) and the
+// warp-level tensor-core kernel (sdpa_decode_mma.cu).
+enum DecodeVariant : int { kDecodeSimt = 0, kDecodeMma = 1 };
+
+// Variant used for (D, heads per CTA); TQ_DECODE_KERNEL=simt|mma overrides.
+int choose_decode_variant(int D, int G);
+
+bool mma_supported(int D, int G);
+int mma_tokens_per_tile();
+int mma_occupancy(int device, int D, int gsub);
+
 // Plan: split count etc. Returns workspace bytes needed.
 struct DecodePlan {
+  int variant;
   int gsub;          // query heads per CTA (<= G)
   int nsub;          // G / gsub
   int tokens_per_tile;
@@ -58,7 +70,13 @@ struct DecodePlan {
   size_t ws_o_off, ws_ml_off, ws_cnt_off;
 };
 
+// Bytes reserved at the start of every decode workspace for merge counters.
+extern const size_t kCounterRegionBytes;
+
+// splits == -1 marks a problem with more (batch x head-group) units than
+// counters.
 DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_max);
+cudaError_t launch_decode_mma(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 cudaError_t launch_decode(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 
 cudaError_t launch_lse_merge(const float* parts, int n_parts, int B, int H, int D, void* out,

@@ -94,7 +94,10 @@ TQ_API int tq_quantize_append(const void* k_new, const void* v_new, tq_dtype in_
 /* Workspace bytes that tq_sdpa_int4 / tq_sdpa_int4_partial need for these
  * sizes (split-KV partials + merge counters). n_tokens is the largest
  * sequence length the call will see. The workspace must be zero-filled once
- * before first use (tq_workspace_init); kernels leave it reusable. */
+ * before first use (tq_workspace_init); kernels leave it reusable, and one
+ * workspace may serve calls of any size that fits (its first 64 KiB hold
+ * merge counters that every call leaves at zero). Calls that share a
+ * workspace must not run concurrently. */
 TQ_API size_t tq_sdpa_int4_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim,
                                    int n_tokens, int sliding_window);
 

@@ -3,6 +3,8 @@ against the CPU oracle: quantize / quantize-on-append bit-exact, decode
 attention within max-abs 2e-3 and cosine >= 0.99999 of the oracle's
 dequantize + fp64 SDPA (the reference's baseline path,
 engine/gemma4_multilayer.cpp:307-308,349)."""
+import os
+
 import numpy as np
 import pytest
 
@@ -106,6 +108,18 @@ def test_quantize_append_bitexact_and_in_place():
 
 # ------------------------------------------------------------------ decode --
 
+@pytest.fixture(params=["mma", "simt"])
+def variant(request):
+    """Run the test against each decode kernel (tensor-core and CUDA-core)."""
+    old = os.environ.get("TQ_DECODE_KERNEL")
+    os.environ["TQ_DECODE_KERNEL"] = request.param
+    yield request.param
+    if old is None:
+        os.environ.pop("TQ_DECODE_KERNEL", None)
+    else:
+        os.environ["TQ_DECODE_KERNEL"] = old
+
+
 def run_decode(H, Hkv, D, N, seed=0, window=0, sb="f16", qdt="f16", odt="f16", batch=1,
                seq_lens=None, cap=None, scale=1.0, append_last=False):
     L = inputs.make_layer(seed, H, Hkv, D, N, batch=batch)
@@ -141,7 +155,7 @@ def run_decode(H, Hkv, D, N, seed=0, window=0, sb="f16", qdt="f16", odt="f16", b
     return host(out).astype(np.float32), ref
 
 
-def test_config0_parity():
+def test_config0_parity(variant):
     cfg = inputs.CONFIGS[0]
     out, ref = run_decode(cfg["H"], cfg["Hkv"], cfg["D"], cfg["N"], seed=cfg["seed"])
     parity(out, ref)
@@ -149,7 +163,7 @@ def test_config0_parity():
 
 @pytest.mark.parametrize("N", [1024, 4096, 8192, 16384, 32768])
 @pytest.mark.parametrize("window", [1024, 0])
-def test_config1_sweep(N, window):
+def test_config1_sweep(N, window, variant):
     seed = {1024: 1, 4096: 2, 8192: 3, 16384: 4, 32768: 5}[N]
     out, ref = run_decode(32, 16, 128, N, seed=seed, window=window, append_last=True)
     parity(out, ref)
@@ -176,7 +190,7 @@ SHAPES = [
 
 
 @pytest.mark.parametrize("H,Hkv,D,N,window,sb,qdt,odt", SHAPES)
-def test_shapes(H, Hkv, D, N, window, sb, qdt, odt):
+def test_shapes(H, Hkv, D, N, window, sb, qdt, odt, variant):
     out, ref = run_decode(H, Hkv, D, N, seed=N % 97, window=window, sb=sb, qdt=qdt, odt=odt)
     if odt == "bf16":
         parity(out, ref, max_abs=1.6e-2, min_cos=0.9999)  # bf16 output rounding alone is 2^-9
@@ -184,7 +198,7 @@ def test_shapes(H, Hkv, D, N, window, sb, qdt, odt):
         parity(out, ref)
 
 
-def test_reference_test_shape_fp32():
+def test_reference_test_shape_fp32(variant):
     """Mirror of tests/test_sdpa_int4.cpp:13-45: nh=16, nkv=16, N=10, hd=256,
     gqa=1, scale 1, window 0, fp32 everywhere -- with a seeded input and the
     task tolerance instead of the reference's 0.1 (tests/test_sdpa_int4.cpp:77)."""
@@ -192,22 +206,22 @@ def test_reference_test_shape_fp32():
     parity(out, ref)
 
 
-def test_batch_with_seq_lens():
+def test_batch_with_seq_lens(variant):
     out, ref = run_decode(16, 8, 128, 900, seed=3, batch=3, seq_lens=[900, 1, 517], window=300)
     parity(out, ref)
 
 
-def test_empty_context_is_zero():
+def test_empty_context_is_zero(variant):
     out, _ = run_decode(8, 4, 128, 8, seq_lens=[0])
     assert np.all(out == 0)
 
 
-def test_scale_parameter():
+def test_scale_parameter(variant):
     out, ref = run_decode(16, 8, 128, 700, seed=8, scale=0.0884)
     parity(out, ref)
 
 
-def test_partial_shards_merge_to_full():
+def test_partial_shards_merge_to_full(variant):
     """Sequence split: 3 shards -> partial states -> LSE merge == unsplit."""
     H, Hkv, D, N = 16, 4, 256, 5003
     L = inputs.make_layer(21, H, Hkv, D, N)
@@ -226,15 +240,21 @@ def test_partial_shards_merge_to_full():
             parts.append(tq.sdpa_int4_partial(q, *dc, H // Hkv, 1.0, window, n_local=n,
                                               token_offset=t0, n_total=N).clone())
         merged = tq.lse_merge(torch.stack(parts), H, D)
-        c = [*O.quantize(L["k"]), *O.quantize(L["v"])]
-        full = tq.sdpa_int4(q, *[dev(a) for a in c], H // Hkv, 1.0, window, out_dtype=torch.float32)
-        ref = O.sdpa_int4(L["q"].astype(np.float16), *c, window=window, f64=True)
+        capf = (N + 3) // 4 * 4
+        kf = np.zeros((1, Hkv, capf, D), np.float32)
+        vf = np.zeros_like(kf)
+        kf[:, :, :N] = L["k"]
+        vf[:, :, :N] = L["v"]
+        c = [*O.quantize(kf), *O.quantize(vf)]
+        full = tq.sdpa_int4(q, *[dev(a) for a in c], H // Hkv, 1.0, window, n_tokens=N,
+                            out_dtype=torch.float32)
+        ref = O.sdpa_int4(L["q"].astype(np.float16), *c, window=window, n_tokens=[N], f64=True)
         torch.cuda.synchronize()
         parity(host(merged), ref)
         np.testing.assert_allclose(host(merged), host(full), rtol=0, atol=2e-5)
 
 
-def test_graph_capture_replay():
+def test_graph_capture_replay(variant):
     """append + decode captured in a CUDA graph replay to the same result."""
     H, Hkv, D, N = 32, 16, 128, 4096
     L = inputs.make_layer(4, H, Hkv, D, N)

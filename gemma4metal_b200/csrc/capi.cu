@@ -92,6 +92,17 @@ int visible_max(int n_tokens, int window) {
 
 }  // namespace
 
+namespace tq {
+void set_last_error(const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+}
+}  // namespace tq
+
 extern "C" {
 
 const char* tq_last_error(void) { return t_err.c_str(); }

@@ -84,4 +84,7 @@ cudaError_t launch_lse_merge(const float* parts, int n_parts, int B, int H, int 
 
 int device_sm_count(int device);
 
+// Set the calling thread's tq_last_error() message (printf-style).
+void set_last_error(const char* fmt, ...);
+
 }  // namespace tq

@@ -151,6 +151,28 @@ TQ_API int tq_sdpa_int4_partial(const void* queries, tq_dtype q_dtype, const uin
 TQ_API int tq_lse_merge(const float* parts, int n_parts, int batch, int num_heads, int head_dim,
                  void* out, tq_dtype out_dtype, void* stream);
 
+/* Same as tq_sdpa_int4, but with no workspace argument and no allocation of
+ * any kind: for callers that cannot call cudaMalloc (for example code running
+ * inside a host callback or a custom allocator, or a process whose device
+ * memory is fully reserved up front), the split-KV scratch comes from a
+ * 2 MiB array built into the library, which every GPU that loads the library
+ * keeps until the process exits. Sizes whose scratch does not fit are
+ * rejected with TQ_ERR_WORKSPACE.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call outside any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU
+ * (different streams, or concurrent graphs) race and must be serialised.
+ * No counterpart in the reference (its outputs and temporaries come from
+ * MLX's allocator). */
+TQ_API int tq_sdpa_int4_noalloc(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,
+                                const void* k_scales, const void* k_biases,
+                                const uint32_t* v_quant, const void* v_scales,
+                                const void* v_biases, tq_dtype sb_dtype, int gqa_factor,
+                                float scale, int sliding_window, int batch, int num_kv_heads,
+                                int head_dim, int n_tokens, int capacity,
+                                const int32_t* seq_lens, void* out, tq_dtype out_dtype,
+                                void* stream);
+
 /* Read and clear the device error word that kernels set when a bounded wait
  * gives up (0 = no error). Synchronises `stream`. */
 TQ_API int tq_device_error(void* stream, uint32_t* code);

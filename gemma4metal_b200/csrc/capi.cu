@@ -1,5 +1,6 @@
 // extern "C" ABI of libturboquant_b200.so (declared in include/turboquant_c.h):
 // host-side validation, planning and dispatch onto the caller's CUDA stream.
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -83,6 +84,7 @@ int validate_decode(const DecodeCommon& c, const char* fn) {
   const void* ptrs[] = {c.kq, c.ks, c.kb, c.vq, c.vs, c.vb};
   for (const void* p : ptrs)
     if (!aligned16(p)) return fail(TQ_ERR_INVALID, "%s: cache pointers must be 16-byte aligned", fn);
+  if (!aligned16(c.q)) return fail(TQ_ERR_INVALID, "%s: queries must be 16-byte aligned", fn);
   return TQ_OK;
 }
 
@@ -182,7 +184,7 @@ size_t tq_sdpa_int4_workspace_size(int batch, int num_heads, int num_kv_heads, i
   int dev = 0;
   cudaGetDevice(&dev);
   tq::DecodePlan pl = tq::plan_decode(dev, batch, num_heads, num_kv_heads, head_dim,
-                                      visible_max(n_tokens, sliding_window));
+                                      visible_max(n_tokens, sliding_window), sliding_window > 0);
   return pl.ws_bytes;
 }
 
@@ -202,8 +204,13 @@ static int decode_common(const DecodeCommon& c, const char* fn, const int32_t* s
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, fn);
-  const int vis = partial ? c.n_tokens : visible_max(c.n_tokens, c.window);
-  tq::DecodePlan pl = tq::plan_decode(dev, c.B, H, c.Hkv, c.D, vis);
+  // visible tokens of the largest sequence; a sequence shard sees the part of
+  // its tokens that lies inside the window of the whole sequence
+  const int vis = !partial       ? visible_max(c.n_tokens, c.window)
+                  : c.window > 0 ? std::max(0, c.n_tokens - std::max(0, n_total - c.window -
+                                                                          token_offset))
+                                 : c.n_tokens;
+  tq::DecodePlan pl = tq::plan_decode(dev, c.B, H, c.Hkv, c.D, vis, c.window > 0);
   if (pl.splits < 0)
     return fail(TQ_ERR_UNSUPPORTED, "%s: batch * kv_heads too large for one launch", fn);
   if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < pl.ws_bytes))
@@ -241,8 +248,13 @@ static int decode_common(const DecodeCommon& c, const char* fn, const int32_t* s
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
   a.err = device_error_ptr();
+  tq::launch_detail().clear();
   e = tq::launch_decode(a, pl, static_cast<cudaStream_t>(stream));
-  if (e != cudaSuccess) return cuda_fail(e, fn);
+  if (e != cudaSuccess) {
+    if (!tq::launch_detail().empty())
+      return fail(TQ_ERR_CUDA, "%s: %s (%s)", fn, cudaGetErrorString(e), tq::launch_detail().c_str());
+    return cuda_fail(e, fn);
+  }
   return TQ_OK;
 }
 

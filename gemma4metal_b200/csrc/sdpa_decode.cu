@@ -621,7 +621,7 @@ int choose_decode_variant(int D, int G) {
   return kDecodeSimt;
 }
 
-DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_max) {
+DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_max, bool windowed) {
   DecodePlan pl{};
   const int G = H / Hkv;
   pl.variant = choose_decode_variant(D, G);
@@ -630,7 +630,7 @@ DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_m
   pl.tokens_per_tile = pl.variant == kDecodeMma ? mma_tokens_per_tile() : 8192 / D;
   const int T = pl.tokens_per_tile;
   // +1 tile: a window that does not start on a tile boundary spans one more
-  const int tiles = std::max(1, (n_visible_max + T - 1) / T + 1);
+  const int tiles = std::max(1, (n_visible_max + T - 1) / T + (windowed ? 1 : 0));
   const long long units = static_cast<long long>(B) * Hkv * pl.nsub;
   int per_sm = kMinBlocksPerSM;
   if (device >= 0) {
@@ -643,7 +643,8 @@ DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_m
     }
   }
   const long long target = static_cast<long long>(device_sm_count(device < 0 ? 0 : device)) * per_sm;
-  long long splits = (target + units - 1) / units;
+  // at most one wave: splits * units <= resident CTAs
+  long long splits = target / units;
   splits = std::max<long long>(1, std::min<long long>(splits, tiles));
   int tps = static_cast<int>((tiles + splits - 1) / splits);
   splits = (tiles + tps - 1) / tps;

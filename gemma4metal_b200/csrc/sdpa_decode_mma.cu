@@ -7,30 +7,38 @@
 //
 // Data path per CTA (grid = splits x KV-head groups x batch):
 //   * producer warp: 2-D TMA tensor copies of the K and V code tiles
-//     (64 tokens x D/2 bytes, 64B/128B-swizzled so the transposed ldmatrix
-//     reads below are bank-conflict free) + 1-D bulk copies of the fp16
-//     scales/biases, into a 4-stage full/empty mbarrier ring;
+//     (64 tokens x D/2 bytes, 64B/128B-swizzled so the K-side row reads and
+//     the transposed ldmatrix reads below are bank-conflict free) + 1-D bulk
+//     copies of the fp16 scales/biases, into a 6-stage full/empty mbarrier
+//     ring;
 //   * 4 consumer warps, 16 tokens of every tile each, each with its own
 //     online-softmax state (no CTA barrier in the main loop):
-//       K side:  S[head][token] = sum_d q[head][d] * (1 + c[token][d]/16)
-//                as mma(A = q (rows = query heads), B = codes); the codes are
-//                made exact fp16 values 1 + c/16 by one shift + one LOP3 per
-//                two nibbles, and the offset is removed through sum_d q:
-//                score = s*(16*S - 16*sum q) + b*sum q per 64-group;
-//       softmax: exp2 in log2 units; weights w = p*s split into fp16 hi+lo
-//                (22 significant bits) -- the K-side accumulator layout is
-//                exactly the B-operand layout the V side needs;
-//       V side:  O[dim][head] += (1 + c/16)^T * w as mma(A = codes read
+//       K side:  S[token][col] = sum_d (1 + c[token][d]/64) * q[col][d] as
+//                mma(A = codes, rows = tokens; B = q). The codes become exact
+//                fp16 values 1 + c/64 with one LOP3 (and at most one shift)
+//                per two nibbles; every B column holds one query head on a
+//                subset of the dims, so all 8 columns work at any GQA factor
+//                and a cheap in-register/one-shuffle sum completes the dot
+//                products. The offset is removed through sum_d q:
+//                score = s*64*(S - sum q) + b*sum q per 64-group;
+//       softmax: exp2 in log2 units, one (head, token) item per lane at
+//                GQA <= 2; weights w = p*s split into fp16 hi+lo (22
+//                significant bits) and moved to the V-side B layout with four
+//                shuffles per group;
+//       V side:  O[dim][head] += (1 + c/64)^T * w as mma(A = codes read
 //                transposed by ldmatrix.trans, B = w hi/lo); the constant part
-//                is removed with corr = sum_t p*(b - 16*s) at the end:
-//                out = 16*O + corr.
+//                is removed with corr = sum_t p*(b - 64*s) at the end:
+//                out = 64*O + corr.
 //   * the 4 warp states are LSE-merged in shared memory; the CTA writes its
-//     split partial and the last CTA of the KV head merges all splits.
+//     split partial and the last CTA of the KV head merges all splits with
+//     float4 loads spread over all its threads.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <mutex>
+#include <string>
+#include <type_traits>
 #include <unordered_map>
 
 #include "tq_common.cuh"
@@ -43,7 +51,7 @@ namespace {
 constexpr int kConsumerWarps = 4;
 constexpr int kMThreads = (kConsumerWarps + 1) * 32;  // + one TMA producer warp
 constexpr int kMTile = 64;                             // tokens per stage
-constexpr int kMStages = 4;
+constexpr int kMStages = 6;
 constexpr int kMMaxSplits = 1024;
 
 template <int D, int G, typename SB>
@@ -54,14 +62,17 @@ struct MLayout {
   static constexpr int SBB = kMTile * NG * static_cast<int>(sizeof(SB));
   static constexpr int STAGE = (2 * CODE + 4 * SBB + 1023) / 1024 * 1024;
   static constexpr int STAGES = kMStages * STAGE;
-  static constexpr int BAR = STAGES;                     // full[kMStages], empty[kMStages]
-  static constexpr int FLAG = BAR + 2 * kMStages * 8;
+  static constexpr int BAR = STAGES;  // full[kMStages], empty[kMStages], q
+  static constexpr int FLAG = BAR + ((2 * kMStages + 1) * 8 + 15) / 16 * 16;
   static constexpr int RED = FLAG + 16;                  // float scratch (merge reductions)
-  static constexpr int BYTES = RED + 2 * 4 * 8 * 4 + 1024;  // + alignment slack
+  static constexpr int QB = RED + 2 * 4 * 8 * 4;         // the CTA's G query rows (<= f32)
+  static_assert(QB % 16 == 0, "bulk-copy destination must be 16-byte aligned");
+  static constexpr int BYTES = QB + G * D * 4 + 1024;    // + alignment slack
   // end-of-range combine: per warp m, l, corr[NG], o[D] for G heads
   static constexpr int WST = G * (2 + NG + D);
   static_assert(kConsumerWarps * WST * 4 <= STAGES, "warp states reuse the stages");
-  static_assert(G * kMMaxSplits * 4 <= STAGES, "merge weights reuse the stages");
+  static_assert(G * kMMaxSplits * 4 + G * D * 4 * (G * D / 4 >= 128 ? 1 : 128 / (G * D / 4)) <= STAGES,
+                "merge weights and partial sums reuse the stages");
 };
 
 struct MParams {
@@ -124,12 +135,15 @@ __device__ __forceinline__ void consumers_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
 }
 
-// Two nibbles (bits 4j and 16+4j of x) -> fp16x2 (1 + c/16): the nibble is
-// moved to mantissa bits 6..9 of each half and OR-ed into 1.0 (0x3C00).
+// Two nibbles (bits 4j and 16+4j of x) -> fp16x2 (1 + c/64): the nibble is
+// moved to mantissa bits 4..7 of each half (nibble 1 is already there) and
+// OR-ed into 1.0 (0x3C00). Three shifts and four LOP3 per 8 nibbles.
 template <int J>
-__device__ __forceinline__ uint32_t nib2h(uint32_t x) {
-  const uint32_t s = (J == 0) ? (x << 6) : (J == 1) ? (x << 2) : (J == 2) ? (x >> 2) : (x >> 6);
-  return (s & 0x03C003C0u) | 0x3C003C00u;
+__device__ __forceinline__ uint32_t nib64(uint32_t x, uint32_t magic) {
+  const uint32_t s = (J == 0) ? (x << 4) : (J == 1) ? x : (J == 2) ? (x >> 4) : (x >> 8);
+  uint32_t d;  // (s & 0x00F000F0) | magic in one LOP3 (lut 0xEA = (a & b) | c)
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(s), "n"(0x00F000F0), "r"(magic));
+  return d;
 }
 
 // Byte offset of 16-byte chunk k of tile row t (TMA swizzle of the code tile).
@@ -151,25 +165,33 @@ __device__ __forceinline__ float2 unpack_h2(uint32_t v) {
   return __half22float2(*reinterpret_cast<const __half2*>(&v));
 }
 
-// scales/biases of two consecutive tokens (2*NG values) as floats
+// The NG scales (or biases) of one token row as floats.
 template <typename SB, int NG>
-__device__ __forceinline__ void load_sb2(const SB* p, float (&v)[2][NG]) {
+__device__ __forceinline__ void load_sb_row(const SB* p, float (&v)[NG]) {
   if constexpr (sizeof(SB) == 2 && NG == 2) {
+    const float2 a = unpack_h2(*reinterpret_cast<const uint32_t*>(p));
+    v[0] = a.x;
+    v[1] = a.y;
+  } else if constexpr (sizeof(SB) == 2 && NG == 4) {
     const uint2 raw = *reinterpret_cast<const uint2*>(p);
     const float2 a = unpack_h2(raw.x), b = unpack_h2(raw.y);
-    v[0][0] = a.x; v[0][1] = a.y; v[1][0] = b.x; v[1][1] = b.y;
-  } else if constexpr (sizeof(SB) == 2 && NG == 4) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(p);
-    float2 f;
-    f = unpack_h2(raw.x); v[0][0] = f.x; v[0][1] = f.y;
-    f = unpack_h2(raw.y); v[0][2] = f.x; v[0][3] = f.y;
-    f = unpack_h2(raw.z); v[1][0] = f.x; v[1][1] = f.y;
-    f = unpack_h2(raw.w); v[1][2] = f.x; v[1][3] = f.y;
+    v[0] = a.x;
+    v[1] = a.y;
+    v[2] = b.x;
+    v[3] = b.y;
+  } else if constexpr (sizeof(SB) == 4 && NG == 2) {
+    const float2 a = *reinterpret_cast<const float2*>(p);
+    v[0] = a.x;
+    v[1] = a.y;
+  } else if constexpr (sizeof(SB) == 4 && NG == 4) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    v[0] = a.x;
+    v[1] = a.y;
+    v[2] = a.z;
+    v[3] = a.w;
   } else {
 #pragma unroll
-    for (int e = 0; e < 2; ++e)
-#pragma unroll
-      for (int g = 0; g < NG; ++g) v[e][g] = sb_to_float<SB>(p[e * NG + g]);
+    for (int g = 0; g < NG; ++g) v[g] = sb_to_float<SB>(p[g]);
   }
 }
 
@@ -185,6 +207,12 @@ __device__ __forceinline__ float wsum(float v) {
   return v;
 }
 
+// Token order of a warp's 16-token block: A-operand row r of the K-side mma
+// and V-side contraction index k < 8 both stand for token sigma(r) (bits 1
+// and 2 swapped); with the 64B/128B TMA swizzle this makes the K-side 8-byte
+// row reads and the ldmatrix reads bank-conflict free. sigma is an involution.
+__device__ __forceinline__ int sigma8(int r) { return (r & 1) | ((r & 2) << 1) | ((r & 4) >> 1); }
+
 template <int D, int G, typename SB, bool QSPLIT>
 __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
     decode_mma_kernel(const __grid_constant__ CUtensorMap tmk,
@@ -192,12 +220,22 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
   using Lyt = MLayout<D, G, SB>;
   constexpr int NG = Lyt::NG;
   constexpr int NCH = D / 32;          // 16-byte code chunks per token
-  constexpr bool kPaired = G <= 4;     // hi/lo weights share one mma (N = 2G <= 8)
+  constexpr bool kPaired = G <= 4;     // V side: hi/lo weights share one mma (N = 2G <= 8)
+  // K side: mma(A = codes, rows = tokens; B = q, columns n = hb*P + phi). A
+  // column (hb, phi) carries q_hb only on the k-rows of the lanes whose
+  // thread-in-group c has c*P/4 == phi, so every accumulator column is a
+  // partial dot product over a quarter (P=4), half (P=2) or all (P=1) of the
+  // 64 dims of a group, and all 8 columns are used for any GQA factor.
+  constexpr int P = G <= 2 ? 4 : 8 / G;
+  constexpr int IPL = G <= 2 ? 1 : G / 2;  // complete (head, token) items per lane
+  constexpr int IH = G == 8 ? 2 : 1;       // distinct item heads per lane
+  constexpr int NTK = G <= 2 ? 1 : 2;      // distinct item tokens per lane
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lyt::BAR);
   uint64_t* empty = full + kMStages;
+  uint64_t* qbar = empty + kMStages;
   int* s_flag = reinterpret_cast<int*>(smem + Lyt::FLAG);
   float* s_red = reinterpret_cast<float*>(smem + Lyt::RED);
 
@@ -233,6 +271,7 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumerWarps);
     }
+    mbar_init(qbar, 1);
     fence_barrier_init();
   }
   __syncthreads();
@@ -240,15 +279,25 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
   // ======================= producer warp ========================================
   if (warp == kConsumerWarps) {
     if (lane == 0) {
+      prefetch_tensormap(&tmk);
+      prefetch_tensormap(&tmv);
+      // the CTA's query rows: one bulk copy, shared through shared memory
+      const int qel = p.q_dtype == kF32 ? 4 : 2;
+      const uint32_t qbytes = static_cast<uint32_t>(G * D * qel);
+      mbar_arrive_expect_tx(qbar, qbytes);
+      bulk_g2s(smem + Lyt::QB,
+               static_cast<const unsigned char*>(p.q) + (static_cast<long long>(b) * p.H + h0) * D * qel,
+               qbytes, qbar, policy_evict_last());
       const uint64_t pol = policy_evict_first();
       const int t_hi4 = (t_hi + 3) & ~3;
       const SB* ksb = reinterpret_cast<const SB*>(p.ks) + tok_base * NG;
       const SB* kbb = reinterpret_cast<const SB*>(p.kb) + tok_base * NG;
       const SB* vsb = reinterpret_cast<const SB*>(p.vs) + tok_base * NG;
       const SB* vbb = reinterpret_cast<const SB*>(p.vb) + tok_base * NG;
+      int st = 0;
+      uint32_t par = 0;
       for (int i = 0; i < ntiles; ++i) {
-        const int st = i % kMStages;
-        if (i >= kMStages) mbar_wait_bounded(&empty[st], ((i / kMStages) + 1) & 1, p.err);
+        if (i >= kMStages) mbar_wait_bounded(&empty[st], par ^ 1u, p.err);
         const int t0 = (tile_begin + i) * kMTile;
         const int nt = min(kMTile, t_hi4 - t0);
         const uint32_t sbb = static_cast<uint32_t>(nt * NG * sizeof(SB));
@@ -265,6 +314,10 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
         bulk_g2s(sbp + Lyt::SBB, kbb + static_cast<long long>(t0) * NG, sbb, &full[st], pol);
         bulk_g2s(sbp + 2 * Lyt::SBB, vsb + static_cast<long long>(t0) * NG, sbb, &full[st], pol);
         bulk_g2s(sbp + 3 * Lyt::SBB, vbb + static_cast<long long>(t0) * NG, sbb, &full[st], pol);
+        if (++st == kMStages) {
+          st = 0;
+          par ^= 1u;
+        }
       }
     }
     return;
@@ -273,17 +326,22 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
   // ======================= consumer warps =======================================
   const int r = lane >> 2;  // mma groupID
   const int c = lane & 3;   // mma thread-in-group
-  const int hr = kPaired ? (r >> 1) : r;  // query head of K-side row r
-  const bool hr_ok = hr < G;
 
-  // q as the K-side A operand: row r = head hr; k-step ks of group g covers
-  // word w = 8g + 2c + ks/2, nibbles jb, jb+4 (cols 2c, 2c+1) and jb+1, jb+5
-  // (cols 2c+8, 2c+9), jb = 2*(ks%2).
-  uint32_t qa[NG][4][2];
-  uint32_t qa_lo[QSPLIT ? NG : 1][4][2];
-  float qsum[NG];
+  // ---- q as the K-side B operand (column n = r) -----------------------------
+  // k-step ks of group g covers word w = 8g + 2c + ks/2 of the token rows:
+  // b0 = k-rows 2c, 2c+1 -> dims 8w+jb, 8w+jb+4; b1 = k-rows 2c+8, 2c+9 ->
+  // dims 8w+jb+1, 8w+jb+5 (jb = 2*(ks%2)) -- the dims nib64<jb>/<jb+1> give
+  // the A operand.
+  uint32_t qb[NG][4][2];
+  uint32_t qb_lo[QSPLIT ? NG : 1][4][2];
+  float qs_col[NG];  // sum of q_hb over each group (identical in the 4 lanes of row r)
+  mbar_wait_bounded(qbar, 0, p.err);
   {
-    const long long qrow = (static_cast<long long>(b) * p.H + h0 + (hr_ok ? hr : 0)) * D;
+    const int hb = r / P;
+    const int phib = r % P;
+    const bool on = hb < G && phib == (c * P) / 4;
+    const void* sq = smem + Lyt::QB;
+    const int qrow = (hb < G ? hb : 0) * D;
 #pragma unroll
     for (int g = 0; g < NG; ++g) {
       float part = 0.0f;
@@ -291,209 +349,375 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
       for (int ks = 0; ks < 4; ++ks) {
         const int w = 8 * g + 2 * c + (ks >> 1);
         const int jb = 2 * (ks & 1);
-        float v[4];
         const int dd[4] = {8 * w + jb, 8 * w + jb + 4, 8 * w + jb + 1, 8 * w + jb + 5};
+        float v[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) v[e] = hr_ok ? load_as_float(p.q, qrow + dd[e], p.q_dtype) : 0.0f;
+        for (int e = 0; e < 4; ++e) v[e] = load_as_float(sq, qrow + dd[e], p.q_dtype);
         part += (v[0] + v[1]) + (v[2] + v[3]);
-        qa[g][ks][0] = pack_h2(v[0], v[1]);
-        qa[g][ks][1] = pack_h2(v[2], v[3]);
+        const uint32_t h01 = pack_h2(v[0], v[1]), h23 = pack_h2(v[2], v[3]);
+        qb[g][ks][0] = on ? h01 : 0u;
+        qb[g][ks][1] = on ? h23 : 0u;
         if constexpr (QSPLIT) {
-          const float2 h01 = unpack_h2(qa[g][ks][0]);
-          const float2 h23 = unpack_h2(qa[g][ks][1]);
-          qa_lo[g][ks][0] = pack_h2(v[0] - h01.x, v[1] - h01.y);
-          qa_lo[g][ks][1] = pack_h2(v[2] - h23.x, v[3] - h23.y);
+          const float2 f01 = unpack_h2(h01), f23 = unpack_h2(h23);
+          qb_lo[g][ks][0] = on ? pack_h2(v[0] - f01.x, v[1] - f01.y) : 0u;
+          qb_lo[g][ks][1] = on ? pack_h2(v[2] - f23.x, v[3] - f23.y) : 0u;
         }
       }
       part += __shfl_xor_sync(0xffffffffu, part, 1);
       part += __shfl_xor_sync(0xffffffffu, part, 2);
-      qsum[g] = part;
+      qs_col[g] = part;
     }
   }
 
-  // O[dim][col] accumulators: chunk kk (32 dims), sub-tile sub; rows r / r+8 =
-  // dims 32kk + 4r + 2sub (+1); cols 2c, 2c+1 = (head c: hi, lo) when paired,
+  // ---- this lane's items: complete (head, token) scores after the reduce ----
+  // G <= 2: head c/2, token sigma(r) + 8*(c&1); G = 4: head c, tokens
+  // sigma(r) + 8f; G = 8: heads 2c + e, tokens sigma(r) + 8f (item 2f + e).
+  int ihead[IH];
+#pragma unroll
+  for (int e = 0; e < IH; ++e) ihead[e] = G <= 2 ? (c >> 1) : (G == 4 ? c : 2 * c + e);
+  const bool hvalid = ihead[0] < G;  // false only for G = 1, c >= 2
+  float qsum[IH][NG];                // sum of q over each group for the item heads
+#pragma unroll
+  for (int e = 0; e < IH; ++e)
+#pragma unroll
+    for (int g = 0; g < NG; ++g)
+      qsum[e][g] = __shfl_sync(0xffffffffu, qs_col[g], 4 * ((hvalid ? ihead[e] : 0) * P));
+
+  const int wt0 = warp * 16;  // this warp's first row of every tile
+  const int sr = sigma8(r);
+  int trow[NTK];              // tile rows of the item tokens
+#pragma unroll
+  for (int f = 0; f < NTK; ++f) trow[f] = wt0 + sr + 8 * (G <= 2 ? (c & 1) : f);
+  int koff[2][NG];            // K-side A operand: rows sigma(r), sigma(r)+8; words 8g+2c, +1
+#pragma unroll
+  for (int f = 0; f < 2; ++f)
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const int word = 8 * g + 2 * c;
+      koff[f][g] = swz<D>(wt0 + sr + 8 * f, word >> 2) + 4 * (word & 3);
+    }
+  int voff[NCH / 2];          // ldmatrix row address of this lane (token sigma(row))
+  {
+    const int mi = lane >> 3, mrow = lane & 7;
+#pragma unroll
+    for (int q2 = 0; q2 < NCH / 2; ++q2)
+      voff[q2] = swz<D>(wt0 + 8 * (mi & 1) + sigma8(mrow), 2 * q2 + (mi >> 1));
+  }
+
+  // O[dim][col] accumulators: chunk kk (32 dims), sub-tile s2; rows r / r+8 =
+  // dims 32kk + 4r + 2s2 (+1); cols 2c, 2c+1 = (head c: hi, lo) when paired,
   // heads 2c, 2c+1 otherwise.
   float o[NCH][2][4];
 #pragma unroll
   for (int kk = 0; kk < NCH; ++kk)
 #pragma unroll
-    for (int s = 0; s < 2; ++s)
+    for (int s2 = 0; s2 < 2; ++s2)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) o[kk][s][e] = 0.0f;
-  float m_run = -INFINITY;  // for head hr (K-side layout)
-  float l_run = 0.0f;       // partial over this thread's tokens
-  float corr[NG];
+      for (int e = 0; e < 4; ++e) o[kk][s2][e] = 0.0f;
+  float m_run[IH], l_run[IH], corr[IH][NG];
 #pragma unroll
-  for (int g = 0; g < NG; ++g) corr[g] = 0.0f;
+  for (int e = 0; e < IH; ++e) {
+    m_run[e] = -INFINITY;
+    l_run[e] = 0.0f;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) corr[e][g] = 0.0f;
+  }
 
-  const int wt0 = warp * 16;  // this warp's first row of every tile
   const uint32_t smem_base = smem_addr(smem);
+  uint32_t mg = 0x3C003C00u;  // fp16x2 1.0, kept in a register for the LOP3s
+  asm volatile("" : "+r"(mg));
 
-  for (int i = 0; i < ntiles; ++i) {
-    const int st = i % kMStages;
+  auto tile = [&](auto masked_c, int st, int tile_t0) {
+    constexpr bool MASKED = decltype(masked_c)::value;
     const unsigned char* stg = smem + st * Lyt::STAGE;
-    const uint32_t stg_addr = smem_base + st * Lyt::STAGE;
     const SB* s_ks = reinterpret_cast<const SB*>(stg + 2 * Lyt::CODE);
     const SB* s_kb = s_ks + kMTile * NG;
     const SB* s_vs = s_kb + kMTile * NG;
     const SB* s_vb = s_vs + kMTile * NG;
-    const int tile_t0 = (tile_begin + i) * kMTile;
-    mbar_wait_bounded(&full[st], static_cast<uint32_t>((i / kMStages) & 1), p.err);
 
-    // ---- K side: S[head][token], then the scores of (head hr, tokens
-    // 8nt + 2c + e), one n-tile at a time to keep few accumulators live -------
-    float sc[2][2];
-    float bmax = -INFINITY;
+    // ---- K side: partial S[token][column] per group --------------------------
+    float acc[NG][4];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const int trow = wt0 + 8 * nt + r;  // token (B-operand column r) of this n-tile
-      float acc[NG][4];
+    for (int g = 0; g < NG; ++g) {
 #pragma unroll
-      for (int g = 0; g < NG; ++g) {
+      for (int e = 0; e < 4; ++e) acc[g][e] = 0.0f;
+      const uint2 w0 = *reinterpret_cast<const uint2*>(stg + koff[0][g]);  // token sigma(r)
+      const uint2 w1 = *reinterpret_cast<const uint2*>(stg + koff[1][g]);  // token sigma(r)+8
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[g][e] = 0.0f;
-        const int word = 8 * g + 2 * c;
-        const uint2 wv = *reinterpret_cast<const uint2*>(stg + swz<D>(trow, word >> 2) + 4 * (word & 3));
-        mma16816(acc[g], qa[g][0][0], 0u, qa[g][0][1], 0u, nib2h<0>(wv.x), nib2h<1>(wv.x));
-        mma16816(acc[g], qa[g][1][0], 0u, qa[g][1][1], 0u, nib2h<2>(wv.x), nib2h<3>(wv.x));
-        mma16816(acc[g], qa[g][2][0], 0u, qa[g][2][1], 0u, nib2h<0>(wv.y), nib2h<1>(wv.y));
-        mma16816(acc[g], qa[g][3][0], 0u, qa[g][3][1], 0u, nib2h<2>(wv.y), nib2h<3>(wv.y));
-        if constexpr (QSPLIT) {
-          mma16816(acc[g], qa_lo[g][0][0], 0u, qa_lo[g][0][1], 0u, nib2h<0>(wv.x), nib2h<1>(wv.x));
-          mma16816(acc[g], qa_lo[g][1][0], 0u, qa_lo[g][1][1], 0u, nib2h<2>(wv.x), nib2h<3>(wv.x));
-          mma16816(acc[g], qa_lo[g][2][0], 0u, qa_lo[g][2][1], 0u, nib2h<0>(wv.y), nib2h<1>(wv.y));
-          mma16816(acc[g], qa_lo[g][3][0], 0u, qa_lo[g][3][1], 0u, nib2h<2>(wv.y), nib2h<3>(wv.y));
+      for (int ks = 0; ks < 4; ++ks) {
+        const uint32_t x0 = (ks >> 1) ? w0.y : w0.x;
+        const uint32_t x1 = (ks >> 1) ? w1.y : w1.x;
+        uint32_t a0, a1, a2, a3;
+        if (ks & 1) {
+          a0 = nib64<2>(x0, mg); a1 = nib64<2>(x1, mg); a2 = nib64<3>(x0, mg); a3 = nib64<3>(x1, mg);
+        } else {
+          a0 = nib64<0>(x0, mg); a1 = nib64<0>(x1, mg); a2 = nib64<1>(x0, mg); a3 = nib64<1>(x1, mg);
         }
-      }
-      const int tt = wt0 + 8 * nt + 2 * c;
-      float sk[2][NG], bk[2][NG];
-      load_sb2<SB, NG>(s_ks + tt * NG, sk);
-      load_sb2<SB, NG>(s_kb + tt * NG, bk);
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        float s = 0.0f;
-#pragma unroll
-        for (int g = 0; g < NG; ++g)
-          s += sk[e][g] * (16.0f * acc[g][e] - 16.0f * qsum[g]) + bk[e][g] * qsum[g];
-        const int tg = tile_t0 + tt + e;
-        const bool ok = hr_ok && tg >= t_lo && tg < t_hi;
-        sc[nt][e] = ok ? s * p.qscale : -INFINITY;
-        bmax = fmaxf(bmax, sc[nt][e]);
+        mma16816(acc[g], a0, a1, a2, a3, qb[g][ks][0], qb[g][ks][1]);
+        if constexpr (QSPLIT) mma16816(acc[g], a0, a1, a2, a3, qb_lo[g][ks][0], qb_lo[g][ks][1]);
       }
     }
-    bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 1));
-    bmax = fmaxf(bmax, __shfl_xor_sync(0xffffffffu, bmax, 2));
 
-    // ---- online softmax for head hr -------------------------------------------
-    const float m_new = fmaxf(m_run, bmax);
-    const float alpha = (m_new == -INFINITY) ? 1.0f : fast_exp2(m_run - m_new);
-    m_run = m_new;
-    float pr[2][2];
-    float lsum = 0.0f;
+    // ---- complete S per item (sum over the dim subsets phi) ------------------
+    float S[IPL][NG];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+    for (int g = 0; g < NG; ++g) {
+      if constexpr (G <= 2) {
+        // cols 2c, 2c+1 = phis {0,1} (c even) or {2,3} (c odd) of head c/2;
+        // lane c even keeps token sigma(r), c odd keeps sigma(r)+8.
+        const float x0 = acc[g][0] + acc[g][1];
+        const float x1 = acc[g][2] + acc[g][3];
+        const bool odd = (c & 1) != 0;
+        const float keep = odd ? x1 : x0;
+        const float send = odd ? x0 : x1;
+        S[0][g] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+      } else if constexpr (G == 4) {
+        S[0][g] = acc[g][0] + acc[g][1];
+        S[1][g] = acc[g][2] + acc[g][3];
+      } else {
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        pr[nt][e] = (sc[nt][e] == -INFINITY) ? 0.0f : fast_exp2(sc[nt][e] - m_new);
-        lsum += pr[nt][e];
+        for (int it = 0; it < 4; ++it) S[it][g] = acc[g][it];  // it = 2f + e
       }
-    l_run = l_run * alpha + lsum;
+    }
 
-    // weights w = p*s (V-side B operand, hi/lo) and the constant correction
-    uint32_t bw[NG][2];
-    uint32_t bw_lo[kPaired ? 1 : NG][2];
+    // ---- scores (log2 units) ---------------------------------------------------
+    // score = sum_g s_g * sum_d q_d c_d + b_g * sum_d q_d, sum q c = 64 (S - sum q)
+    float sk[NTK][NG], bk[NTK][NG];
 #pragma unroll
-    for (int g = 0; g < NG; ++g) corr[g] *= alpha;
+    for (int f = 0; f < NTK; ++f) {
+      load_sb_row<SB, NG>(s_ks + trow[f] * NG, sk[f]);
+      load_sb_row<SB, NG>(s_kb + trow[f] * NG, bk[f]);
+    }
+    float sc[IPL];
+    float bmax[IH];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const int tt = wt0 + 8 * nt + 2 * c;
-      float sv[2][NG], bv[2][NG];
-      load_sb2<SB, NG>(s_vs + tt * NG, sv);
-      load_sb2<SB, NG>(s_vb + tt * NG, bv);
+    for (int e = 0; e < IH; ++e) bmax[e] = -INFINITY;
+#pragma unroll
+    for (int it = 0; it < IPL; ++it) {
+      const int f = G <= 2 ? 0 : (G == 4 ? it : it >> 1);
+      const int e = G == 8 ? (it & 1) : 0;
+      float a = 0.0f, bsum = 0.0f;
 #pragma unroll
       for (int g = 0; g < NG; ++g) {
-        // masked tokens have p == 0 but their scales may be stale: select
-        const float w0 = pr[nt][0] > 0.0f ? pr[nt][0] * sv[0][g] : 0.0f;
-        const float w1 = pr[nt][1] > 0.0f ? pr[nt][1] * sv[1][g] : 0.0f;
-        corr[g] += (pr[nt][0] > 0.0f ? pr[nt][0] * (bv[0][g] - 16.0f * sv[0][g]) : 0.0f) +
-                   (pr[nt][1] > 0.0f ? pr[nt][1] * (bv[1][g] - 16.0f * sv[1][g]) : 0.0f);
-        const uint32_t hi = pack_h2(w0, w1);
-        const float2 hf = unpack_h2(hi);
-        const uint32_t lo = pack_h2(w0 - hf.x, w1 - hf.y);
-        if constexpr (kPaired) {
-          bw[g][nt] = (r & 1) ? lo : hi;
-        } else {
-          bw[g][nt] = hi;
-          bw_lo[g][nt] = lo;
+        a = fmaf(sk[f][g], S[it][g] - qsum[e][g], a);
+        bsum = fmaf(bk[f][g], qsum[e][g], bsum);
+      }
+      float v = fmaf(64.0f, a, bsum) * p.qscale;
+      if constexpr (MASKED) {
+        const int tg = tile_t0 + trow[f];
+        v = (hvalid && tg >= t_lo && tg < t_hi) ? v : -INFINITY;
+      }
+      sc[it] = v;
+      bmax[e] = fmaxf(bmax[e], v);
+    }
+    // max over the lanes of each item head
+#pragma unroll
+    for (int e = 0; e < IH; ++e) {
+      if constexpr (G <= 2) bmax[e] = fmaxf(bmax[e], __shfl_xor_sync(0xffffffffu, bmax[e], 1));
+      bmax[e] = fmaxf(bmax[e], __shfl_xor_sync(0xffffffffu, bmax[e], 4));
+      bmax[e] = fmaxf(bmax[e], __shfl_xor_sync(0xffffffffu, bmax[e], 8));
+      bmax[e] = fmaxf(bmax[e], __shfl_xor_sync(0xffffffffu, bmax[e], 16));
+    }
+
+    // ---- online softmax -------------------------------------------------------
+    float alpha[IH];
+#pragma unroll
+    for (int e = 0; e < IH; ++e) {
+      const float m_new = fmaxf(m_run[e], bmax[e]);
+      alpha[e] = (m_new == -INFINITY) ? 1.0f : fast_exp2(m_run[e] - m_new);
+      m_run[e] = m_new;
+      l_run[e] *= alpha[e];
+#pragma unroll
+      for (int g = 0; g < NG; ++g) corr[e][g] *= alpha[e];
+    }
+    float pr[IPL];
+#pragma unroll
+    for (int it = 0; it < IPL; ++it) {
+      const int e = G == 8 ? (it & 1) : 0;
+      pr[it] = MASKED ? ((sc[it] == -INFINITY) ? 0.0f : fast_exp2(sc[it] - m_run[e]))
+                      : fast_exp2(sc[it] - m_run[e]);
+      l_run[e] += pr[it];
+    }
+
+    // ---- weights w = p*s (fp16 hi + lo) and the constant correction ------------
+    float sv[NTK][NG], bv[NTK][NG];
+#pragma unroll
+    for (int f = 0; f < NTK; ++f) {
+      load_sb_row<SB, NG>(s_vs + trow[f] * NG, sv[f]);
+      load_sb_row<SB, NG>(s_vb + trow[f] * NG, bv[f]);
+    }
+    uint32_t hl[IPL][NG];  // packed (hi | lo << 16) of w per item and group
+#pragma unroll
+    for (int it = 0; it < IPL; ++it) {
+      const int f = G <= 2 ? 0 : (G == 4 ? it : it >> 1);
+      const int e = G == 8 ? (it & 1) : 0;
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        float w = pr[it] * sv[f][g];
+        float cb = pr[it] * fmaf(-64.0f, sv[f][g], bv[f][g]);
+        if constexpr (MASKED) {  // stale scales of masked tokens must not leak
+          w = pr[it] > 0.0f ? w : 0.0f;
+          cb = pr[it] > 0.0f ? cb : 0.0f;
         }
+        corr[e][g] += cb;
+        const __half wh = __float2half_rn(w);
+        const __half wl = __float2half_rn(w - __half2float(wh));
+        hl[it][g] = static_cast<uint32_t>(__half_as_ushort(wh)) |
+                    (static_cast<uint32_t>(__half_as_ushort(wl)) << 16);
+      }
+    }
+
+    // ---- V-side B operand: rows k = 2c, 2c+1 (b0), 2c+8, 2c+9 (b1) stand for
+    // tokens sigma(k&7) + 8(k>>3), whose items live in lanes with r' = k & 7.
+    uint32_t bw[NG][2];
+    uint32_t bw_lo[kPaired ? 1 : NG][2];
+    (void)bw_lo;
+    if constexpr (G <= 2) {
+      const int hp = r >> 1;  // column r = (head r/2, hi or lo)
+      const uint32_t sel = (r & 1) ? 0x7632u : 0x5410u;
+      const bool ok = hp < G;
+      const int l0 = 8 * c + 2 * hp;
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const uint32_t x0 = __shfl_sync(0xffffffffu, hl[0][g], l0);
+        const uint32_t x1 = __shfl_sync(0xffffffffu, hl[0][g], l0 + 4);
+        const uint32_t x2 = __shfl_sync(0xffffffffu, hl[0][g], l0 + 1);
+        const uint32_t x3 = __shfl_sync(0xffffffffu, hl[0][g], l0 + 5);
+        bw[g][0] = ok ? __byte_perm(x0, x1, sel) : 0u;
+        bw[g][1] = ok ? __byte_perm(x2, x3, sel) : 0u;
+      }
+    } else if constexpr (G == 4) {
+      const int hp = r >> 1;
+      const uint32_t sel = (r & 1) ? 0x7632u : 0x5410u;
+      const int l0 = 8 * c + hp;
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const uint32_t x0 = __shfl_sync(0xffffffffu, hl[0][g], l0);
+        const uint32_t x1 = __shfl_sync(0xffffffffu, hl[0][g], l0 + 4);
+        const uint32_t x2 = __shfl_sync(0xffffffffu, hl[1][g], l0);
+        const uint32_t x3 = __shfl_sync(0xffffffffu, hl[1][g], l0 + 4);
+        bw[g][0] = __byte_perm(x0, x1, sel);
+        bw[g][1] = __byte_perm(x2, x3, sel);
+      }
+    } else {
+      // column r = head r: item (head r, token k) is register 2(k>>3) + (r&1)
+      // of lane 4(k&7) + r/2
+      const int l0 = 8 * c + (r >> 1);
+      const bool odd = (r & 1) != 0;
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        uint32_t y[4];
+#pragma unroll
+        for (int f = 0; f < 2; ++f) {
+          const uint32_t u0 = __shfl_sync(0xffffffffu, hl[2 * f][g], l0);
+          const uint32_t u1 = __shfl_sync(0xffffffffu, hl[2 * f + 1][g], l0);
+          const uint32_t v0 = __shfl_sync(0xffffffffu, hl[2 * f][g], l0 + 4);
+          const uint32_t v1 = __shfl_sync(0xffffffffu, hl[2 * f + 1][g], l0 + 4);
+          y[2 * f] = odd ? u1 : u0;
+          y[2 * f + 1] = odd ? v1 : v0;
+        }
+        bw[g][0] = __byte_perm(y[0], y[1], 0x5410u);
+        bw[g][1] = __byte_perm(y[2], y[3], 0x5410u);
+        bw_lo[g][0] = __byte_perm(y[0], y[1], 0x7632u);
+        bw_lo[g][1] = __byte_perm(y[2], y[3], 0x7632u);
       }
     }
 
     // rescale O when any head's max moved (warp-uniform decision)
-    if (__any_sync(0xffffffffu, alpha != 1.0f)) {
+    bool moved = false;
+#pragma unroll
+    for (int e = 0; e < IH; ++e) moved |= alpha[e] != 1.0f;
+    if (__any_sync(0xffffffffu, moved)) {
       float a0, a1;
-      if constexpr (kPaired) {
-        a0 = a1 = __shfl_sync(0xffffffffu, alpha, 8 * c);
+      if constexpr (G <= 2) {
+        a0 = a1 = __shfl_sync(0xffffffffu, alpha[0], 2 * c);
+      } else if constexpr (G == 4) {
+        a0 = a1 = __shfl_sync(0xffffffffu, alpha[0], c);
       } else {
-        a0 = __shfl_sync(0xffffffffu, alpha, 8 * c);
-        a1 = __shfl_sync(0xffffffffu, alpha, 8 * c + 4);
+        a0 = __shfl_sync(0xffffffffu, alpha[0], c);
+        a1 = __shfl_sync(0xffffffffu, alpha[IH - 1], c);
       }
 #pragma unroll
       for (int kk = 0; kk < NCH; ++kk)
 #pragma unroll
-        for (int s = 0; s < 2; ++s) {
-          o[kk][s][0] *= a0;
-          o[kk][s][1] *= a1;
-          o[kk][s][2] *= a0;
-          o[kk][s][3] *= a1;
+        for (int s2 = 0; s2 < 2; ++s2) {
+          o[kk][s2][0] *= a0;
+          o[kk][s2][1] *= a1;
+          o[kk][s2][2] *= a0;
+          o[kk][s2][3] *= a1;
         }
     }
 
-    // ---- V side: O += V^T * w -------------------------------------------------
-    const uint32_t vbase = stg_addr + Lyt::CODE;
-    const int mi = lane >> 3;  // ldmatrix matrix served by this lane's row address
-    const int mrow = lane & 7;
+    // ---- V side: O += V^T * w ---------------------------------------------------
+    const uint32_t vbase = smem_base + st * Lyt::STAGE + Lyt::CODE;
 #pragma unroll
     for (int q2 = 0; q2 < NCH / 2; ++q2) {
-      // matrices: (chunk 2q2, tokens 0-7), (2q2, 8-15), (2q2+1, 0-7), (2q2+1, 8-15)
-      const int kk_l = 2 * q2 + (mi >> 1);
-      const int trow = wt0 + 8 * (mi & 1) + mrow;
       uint32_t d[4];
-      ldsm_x4_trans(vbase + swz<D>(trow, kk_l), d);
+      ldsm_x4_trans(vbase + voff[q2], d);
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int kk = 2 * q2 + h;
+      for (int hh = 0; hh < 2; ++hh) {
+        const int kk = 2 * q2 + hh;
         const int g = kk >> 1;
-        const uint32_t R0 = d[2 * h], R1 = d[2 * h + 1];
-        mma16816(o[kk][0], nib2h<0>(R0), nib2h<1>(R0), nib2h<0>(R1), nib2h<1>(R1), bw[g][0], bw[g][1]);
-        mma16816(o[kk][1], nib2h<2>(R0), nib2h<3>(R0), nib2h<2>(R1), nib2h<3>(R1), bw[g][0], bw[g][1]);
+        const uint32_t R0 = d[2 * hh], R1 = d[2 * hh + 1];
+        const uint32_t a00 = nib64<0>(R0, mg), a01 = nib64<1>(R0, mg), a02 = nib64<2>(R0, mg), a03 = nib64<3>(R0, mg);
+        const uint32_t a10 = nib64<0>(R1, mg), a11 = nib64<1>(R1, mg), a12 = nib64<2>(R1, mg), a13 = nib64<3>(R1, mg);
+        mma16816(o[kk][0], a00, a01, a10, a11, bw[g][0], bw[g][1]);
+        mma16816(o[kk][1], a02, a03, a12, a13, bw[g][0], bw[g][1]);
         if constexpr (!kPaired) {
-          mma16816(o[kk][0], nib2h<0>(R0), nib2h<1>(R0), nib2h<0>(R1), nib2h<1>(R1), bw_lo[g][0], bw_lo[g][1]);
-          mma16816(o[kk][1], nib2h<2>(R0), nib2h<3>(R0), nib2h<2>(R1), nib2h<3>(R1), bw_lo[g][0], bw_lo[g][1]);
+          mma16816(o[kk][0], a00, a01, a10, a11, bw_lo[g][0], bw_lo[g][1]);
+          mma16816(o[kk][1], a02, a03, a12, a13, bw_lo[g][0], bw_lo[g][1]);
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[st]);
+  };
+
+  {
+    int st = 0;
+    uint32_t par = 0;
+    for (int i = 0; i < ntiles; ++i) {
+      mbar_wait_bounded(&full[st], par, p.err);
+      const int tile_t0 = (tile_begin + i) * kMTile;
+      if (tile_t0 >= t_lo && tile_t0 + kMTile <= t_hi) {
+        tile(std::integral_constant<bool, false>{}, st, tile_t0);
+      } else {
+        tile(std::integral_constant<bool, true>{}, st, tile_t0);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      if (++st == kMStages) {
+        st = 0;
+        par ^= 1u;
+      }
+    }
   }
 
   // ---- combine the 4 consumer warps -------------------------------------------
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
-  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  // l and corr: sum over the lanes of each item head
 #pragma unroll
-  for (int g = 0; g < NG; ++g) {
-    corr[g] += __shfl_xor_sync(0xffffffffu, corr[g], 1);
-    corr[g] += __shfl_xor_sync(0xffffffffu, corr[g], 2);
+  for (int e = 0; e < IH; ++e) {
+    if constexpr (G <= 2) l_run[e] += __shfl_xor_sync(0xffffffffu, l_run[e], 1);
+    l_run[e] += __shfl_xor_sync(0xffffffffu, l_run[e], 4);
+    l_run[e] += __shfl_xor_sync(0xffffffffu, l_run[e], 8);
+    l_run[e] += __shfl_xor_sync(0xffffffffu, l_run[e], 16);
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      if constexpr (G <= 2) corr[e][g] += __shfl_xor_sync(0xffffffffu, corr[e][g], 1);
+      corr[e][g] += __shfl_xor_sync(0xffffffffu, corr[e][g], 4);
+      corr[e][g] += __shfl_xor_sync(0xffffffffu, corr[e][g], 8);
+      corr[e][g] += __shfl_xor_sync(0xffffffffu, corr[e][g], 16);
+    }
   }
   consumers_sync();  // every warp is past its last tile: the stage area is free
   float* wst = reinterpret_cast<float*>(smem) + warp * Lyt::WST;  // [G][2 + NG + D]
-  if (c == 0 && hr_ok && (!kPaired || (r & 1) == 0)) {
-    float* hs = wst + hr * (2 + NG + D);
-    hs[0] = m_run;
-    hs[1] = l_run;
+  if (r == 0 && (G > 2 || (c & 1) == 0) && hvalid) {
 #pragma unroll
-    for (int g = 0; g < NG; ++g) hs[2 + g] = corr[g];
+    for (int e = 0; e < IH; ++e) {
+      float* hs = wst + ihead[e] * (2 + NG + D);
+      hs[0] = m_run[e];
+      hs[1] = l_run[e];
+#pragma unroll
+      for (int g = 0; g < NG; ++g) hs[2 + g] = corr[e][g];
+    }
   }
 #pragma unroll
   for (int kk = 0; kk < NCH; ++kk)
@@ -520,7 +744,8 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
   const bool direct = p.splits == 1;
   const long long unit = static_cast<long long>(b) * gridDim.y + hg;
   const float* wall = reinterpret_cast<const float*>(smem);
-  for (int it = tid; it < G * D; it += kConsumerWarps * 32) {
+  constexpr int NTH = kConsumerWarps * 32;
+  for (int it = tid; it < G * D; it += NTH) {
     const int g = it / D;
     const int d = it % D;
     float M = -INFINITY;
@@ -532,7 +757,7 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
       const float* hs = wall + w * Lyt::WST + g * (2 + NG + D);
       const float e = (M == -INFINITY || hs[0] == -INFINITY) ? 0.0f : fast_exp2(hs[0] - M);
       L += e * hs[1];
-      acc += e * (16.0f * hs[2 + NG + d] + hs[2 + d / 64]);
+      acc += e * (64.0f * hs[2 + NG + d] + hs[2 + d / 64]);
     }
     const int h = h0 + g;
     if (direct) {
@@ -569,63 +794,95 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
   if (s_flag[0] == 0) return;
   __threadfence();
 
-  constexpr int NT = kConsumerWarps * 32;
   const int S_ = p.splits;
-  float* ew = reinterpret_cast<float*>(smem);  // [G][S_]
   const long long base = unit * S_ * G;
-  float Mg[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
+  float* ew = reinterpret_cast<float*>(smem);  // [G][S_] merge weights
+  // 1) per head (one warp each): M = max m_s, weights e_s = 2^(m_s - M), L
+  for (int g = warp; g < G; g += kConsumerWarps) {
     float m = -INFINITY;
-    for (int s = tid; s < S_; s += NT) m = fmaxf(m, __ldcg(&p.ws_ml[(base + s * G + g) * 2]));
+    for (int s = lane; s < S_; s += 32) m = fmaxf(m, __ldcg(&p.ws_ml[(base + s * G + g) * 2]));
     m = wmax(m);
-    if (lane == 0) s_red[warp * G + g] = m;
-  }
-  consumers_sync();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float m = s_red[g];
-#pragma unroll
-    for (int ww = 1; ww < kConsumerWarps; ++ww) m = fmaxf(m, s_red[ww * G + g]);
-    Mg[g] = m;
-  }
-  consumers_sync();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
     float l = 0.0f;
-    for (int s = tid; s < S_; s += NT) {
-      const float ms = __ldcg(&p.ws_ml[(base + s * G + g) * 2]);
-      const float ls = __ldcg(&p.ws_ml[(base + s * G + g) * 2 + 1]);
-      const float e = (ms == -INFINITY || Mg[g] == -INFINITY) ? 0.0f : fast_exp2(ms - Mg[g]);
+    for (int s = lane; s < S_; s += 32) {
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(&p.ws_ml[(base + s * G + g) * 2]));
+      const float e = (ml.x == -INFINITY || m == -INFINITY) ? 0.0f : fast_exp2(ml.x - m);
       ew[g * S_ + s] = e;
-      l += e * ls;
+      l += e * ml.y;
     }
     l = wsum(l);
-    if (lane == 0) s_red[4 * G + warp * G + g] = l;
+    if (lane == 0) {
+      s_red[2 * g] = m;
+      s_red[2 * g + 1] = l;
+    }
   }
   consumers_sync();
-  for (int it = tid; it < G * D; it += NT) {
-    const int g = it / D;
-    const int d = it % D;
-    float L = 0.0f;
+  // 2) o = sum_s e_s o_s: float4 items (head, 4 dims), the splits spread over
+  //    R thread subsets so that every thread has several loads in flight
+  constexpr int NI = G * D / 4;
+  constexpr int R = NI >= NTH ? 1 : NTH / NI;
+  float4* red = reinterpret_cast<float4*>(smem + ((G * S_ * 4 + 15) & ~15));  // [R][NI]
+  for (int it = tid; it < NI * R; it += NTH) {
+    const int item = it % NI, sub = it / NI;
+    const int g = item / (D / 4);
+    const float* ow = p.ws_o + (base + g) * D + 4 * (item % (D / 4));
+    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    int s = sub;
+    for (; s + 3 * R < S_; s += 4 * R) {
+      float4 v[4];
+      float e[4];
 #pragma unroll
-    for (int ww = 0; ww < kConsumerWarps; ++ww) L += s_red[4 * G + ww * G + g];
-    float acc = 0.0f;
-    for (int s = 0; s < S_; ++s) acc += ew[g * S_ + s] * __ldcg(&p.ws_o[(base + s * G + g) * D + d]);
+      for (int j = 0; j < 4; ++j) {
+        v[j] = __ldcg(reinterpret_cast<const float4*>(ow + static_cast<long long>(s + j * R) * G * D));
+        e[j] = ew[g * S_ + s + j * R];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        a.x = fmaf(e[j], v[j].x, a.x);
+        a.y = fmaf(e[j], v[j].y, a.y);
+        a.z = fmaf(e[j], v[j].z, a.z);
+        a.w = fmaf(e[j], v[j].w, a.w);
+      }
+    }
+    for (; s < S_; s += R) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(ow + static_cast<long long>(s) * G * D));
+      const float e = ew[g * S_ + s];
+      a.x = fmaf(e, v.x, a.x);
+      a.y = fmaf(e, v.y, a.y);
+      a.z = fmaf(e, v.z, a.z);
+      a.w = fmaf(e, v.w, a.w);
+    }
+    red[sub * NI + item] = a;
+  }
+  consumers_sync();
+  for (int item = tid; item < NI; item += NTH) {
+    float4 a = red[item];
+#pragma unroll
+    for (int sub = 1; sub < R; ++sub) {
+      const float4 v = red[sub * NI + item];
+      a.x += v.x;
+      a.y += v.y;
+      a.z += v.z;
+      a.w += v.w;
+    }
+    const int g = item / (D / 4);
+    const int d = 4 * (item % (D / 4));
     const int h = h0 + g;
-    float Mv = Mg[0];
-#pragma unroll
-    for (int gg = 1; gg < G; ++gg) Mv = (g == gg) ? Mg[gg] : Mv;
+    const float M = s_red[2 * g], L = s_red[2 * g + 1];
+    const float av[4] = {a.x, a.y, a.z, a.w};
     if (p.partial) {
       float* blk = p.part_out + static_cast<long long>(b) * p.H * (D + 2);
-      blk[static_cast<long long>(h) * D + d] = acc;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) blk[static_cast<long long>(h) * D + d + j] = av[j];
       if (d == 0) {
-        blk[static_cast<long long>(p.H) * D + 2 * h] = L > 0.0f ? Mv * kLn2 : -INFINITY;
+        blk[static_cast<long long>(p.H) * D + 2 * h] = L > 0.0f ? M * kLn2 : -INFINITY;
         blk[static_cast<long long>(p.H) * D + 2 * h + 1] = L;
       }
     } else {
-      store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * D + d, p.out_dtype,
-                       L > 0.0f ? acc / L : 0.0f);
+      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * D + d + j, p.out_dtype,
+                         av[j] * inv);
     }
   }
   if (tid == 0) p.counters[unit] = 0u;
@@ -711,6 +968,11 @@ bool encode_codes_map(CUtensorMap* m, const uint32_t* base, int D, long long row
 
 }  // namespace
 
+std::string& launch_detail() {
+  static thread_local std::string d;
+  return d;
+}
+
 bool mma_supported(int D, int G) { return (D == 128 || D == 256) && G >= 1 && G <= 8 && (G & (G - 1)) == 0; }
 
 int mma_tokens_per_tile() { return kMTile; }
@@ -728,10 +990,15 @@ cudaError_t launch_decode_mma(const DecodeArgs& a, const DecodePlan& pl, cudaStr
   cudaGetDevice(&device);
   mma_blocks_per_sm(device, k);
   const long long rows = static_cast<long long>(a.B) * a.bstride_tok;
-  if (rows >= (1LL << 31)) return cudaErrorInvalidValue;
-  CUtensorMap tmk, tmv;
-  if (!encode_codes_map(&tmk, a.kq, a.D, rows) || !encode_codes_map(&tmv, a.vq, a.D, rows))
+  if (rows >= (1LL << 31)) {
+    launch_detail() = "batch * kv_heads * capacity must be below 2^31 tokens";
     return cudaErrorInvalidValue;
+  }
+  CUtensorMap tmk, tmv;
+  if (!encode_codes_map(&tmk, a.kq, a.D, rows) || !encode_codes_map(&tmv, a.vq, a.D, rows)) {
+    launch_detail() = "cuTensorMapEncodeTiled failed for the code tiles";
+    return cudaErrorInvalidValue;
+  }
   MParams p{};
   p.q = a.q;
   p.q_dtype = a.q_dtype;

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <string>
+
 namespace tq {
 
 cudaError_t launch_quantize_rows(const void* x, int x_dtype, long long rows, int D, long long n_new,
@@ -75,7 +77,8 @@ extern const size_t kCounterRegionBytes;
 
 // splits == -1 marks a problem with more (batch x head-group) units than
 // counters.
-DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_max);
+DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_max,
+                       bool windowed);
 cudaError_t launch_decode_mma(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 cudaError_t launch_decode(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 
@@ -83,6 +86,10 @@ cudaError_t launch_lse_merge(const float* parts, int n_parts, int B, int H, int 
                              int out_dtype, cudaStream_t stream);
 
 int device_sm_count(int device);
+
+// Why the last launch_* call on this thread failed before reaching the GPU
+// ("" if it did not); the C ABI appends it to tq_last_error().
+std::string& launch_detail();
 
 // Set the calling thread's tq_last_error() message (printf-style).
 void set_last_error(const char* fmt, ...);

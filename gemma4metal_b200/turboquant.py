@@ -281,7 +281,7 @@ def sdpa_int4_partial(queries: torch.Tensor, k_quant, k_scales, k_biases, v_quan
     nt = token_offset + nl if n_total is None else int(n_total)
     if part_out is None:
         part_out = torch.empty(B, H * (D + 2), dtype=torch.float32, device=q.device)
-    nbytes = sdpa_int4_workspace_size(B, H, Hkv, D, nl, 0)
+    nbytes = sdpa_int4_workspace_size(B, H, Hkv, D, nl, sliding_window)
     if ws is None:
         ws = workspace(q.device, nbytes, s)
     _check(load_library().tq_sdpa_int4_partial(

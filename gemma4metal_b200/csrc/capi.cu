@@ -210,7 +210,8 @@ static int decode_common(const DecodeCommon& c, const char* fn, const int32_t* s
                   : c.window > 0 ? std::max(0, c.n_tokens - std::max(0, n_total - c.window -
                                                                           token_offset))
                                  : c.n_tokens;
-  tq::DecodePlan pl = tq::plan_decode(dev, c.B, H, c.Hkv, c.D, vis, c.window > 0);
+  tq::DecodePlan pl = tq::plan_decode(dev, c.B, H, c.Hkv, c.D, vis, c.window > 0,
+                                      c.q_dtype != TQ_F16);
   if (pl.splits < 0)
     return fail(TQ_ERR_UNSUPPORTED, "%s: batch * kv_heads too large for one launch", fn);
   if (pl.ws_bytes > 0 && (!workspace || workspace_bytes < pl.ws_bytes))

@@ -80,6 +80,8 @@ __device__ __forceinline__ float round_store(float v, int dtype, void* dst, long
 }
 
 __global__ void __launch_bounds__(256) quantize_rows_kernel(QuantRows p) {
+  pdl_wait();
+  pdl_trigger();
   if (blockIdx.y == 1) {  // second tensor: same geometry, other buffers
     p.x = p.x2;
     p.codes = p.codes2;
@@ -194,8 +196,7 @@ cudaError_t launch_quantize_rows(const void* x, int x_dtype, long long rows, int
   const long long words = rows * (D / 8);
   if (words == 0) return cudaSuccess;
   const unsigned blocks = static_cast<unsigned>((words + 255) / 256);
-  quantize_rows_kernel<<<dim3(blocks, x2 ? 2 : 1), 256, 0, stream>>>(p);
-  return cudaGetLastError();
+  return launch_pdl(quantize_rows_kernel, dim3(blocks, x2 ? 2 : 1), dim3(256), 0, stream, p);
 }
 
 cudaError_t launch_dequantize(const uint32_t* codes, const void* scales, const void* biases,

@@ -621,7 +621,8 @@ int choose_decode_variant(int D, int G) {
   return kDecodeSimt;
 }
 
-DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_max, bool windowed) {
+DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_max, bool windowed,
+                       bool qsplit) {
   DecodePlan pl{};
   const int G = H / Hkv;
   pl.variant = choose_decode_variant(D, G);
@@ -636,7 +637,7 @@ DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_m
   if (device >= 0) {
     // occupancy of the f16-scale kernel (the f32 variant differs by 1 KB smem)
     if (pl.variant == kDecodeMma) {
-      per_sm = mma_occupancy(device, D, pl.gsub);
+      per_sm = mma_occupancy(device, D, pl.gsub, qsplit);
     } else {
       KernelInfo k = pick_kernel(D, pl.gsub, kF16);
       if (k.fn) per_sm = blocks_per_sm(device, k);

@@ -9,10 +9,11 @@
 //   * producer warp: 2-D TMA tensor copies of the K and V code tiles
 //     (64 tokens x D/2 bytes, 64B/128B-swizzled so the K-side row reads and
 //     the transposed ldmatrix reads below are bank-conflict free) + 1-D bulk
-//     copies of the fp16 scales/biases, into a 6-stage full/empty mbarrier
-//     ring;
-//   * 4 consumer warps, 16 tokens of every tile each, each with its own
-//     online-softmax state (no CTA barrier in the main loop):
+//     copies of the fp16 scales/biases, into a 5-stage full/empty mbarrier
+//     ring (64-token boxes; a CTA's token range is a whole number of boxes);
+//   * 4 consumer warps, 32 (D=128) or 16 (D=256) tokens of every tile each
+//     (as independent 16-token blocks), each warp with its own online-softmax
+//     state (no CTA barrier in the main loop), 2 CTAs per SM:
 //       K side:  S[token][col] = sum_d (1 + c[token][d]/64) * q[col][d] as
 //                mma(A = codes, rows = tokens; B = q). The codes become exact
 //                fp16 values 1 + c/64 with one LOP3 (and at most one shift)
@@ -29,9 +30,9 @@
 //                transposed by ldmatrix.trans, B = w hi/lo); the constant part
 //                is removed with corr = sum_t p*(b - 64*s) at the end:
 //                out = 64*O + corr.
-//   * the 4 warp states are LSE-merged in shared memory; the CTA writes its
-//     split partial and the last CTA of the KV head merges all splits with
-//     float4 loads spread over all its threads.
+//   * the warp states are LSE-merged in shared memory; the CTA writes its
+//     split partial and the last CTA of the KV head merges all splits with an
+//     online LSE merge, 8 splits' loads in flight per thread.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -48,31 +49,45 @@ namespace tq {
 
 namespace {
 
-constexpr int kConsumerWarps = 4;
-constexpr int kMThreads = (kConsumerWarps + 1) * 32;  // + one TMA producer warp
-constexpr int kMTile = 64;                             // tokens per stage
-constexpr int kMStages = 6;
-constexpr int kMMaxSplits = 1024;
+constexpr int kChunk = 64;  // tokens per TMA box; splits are whole chunks
+
+// Per head_dim: W consumer warps (+ one TMA producer warp), each taking TB
+// independent 16-token blocks of every tile (two interleaved dependency
+// chains at D=128); a stage of W*TB*16 tokens (18 KB at D=128 and at D=256),
+// 2 CTAs per SM.
+template <int D>
+struct MCfg {
+  static constexpr int W = 4;
+  static constexpr int TB = D == 128 ? 2 : 1;  // 16-token blocks per warp per tile
+  static constexpr int THREADS = (W + 1) * 32;
+  static constexpr int TILE = 16 * W * TB;
+  static constexpr int CPT = TILE / kChunk;  // chunks per tile
+  static constexpr int MINB = D == 128 ? 3 : 2;  // CTAs per SM with f16 queries; f32/bf16
+                                                 // queries (hi+lo split) run 1 per SM
+  static constexpr int STAGES = D == 128 ? 3 : 5;
+};
 
 template <int D, int G, typename SB>
 struct MLayout {
+  static constexpr int W = MCfg<D>::W;
+  static constexpr int TILE = MCfg<D>::TILE;
   static constexpr int NG = D / 64;
   static constexpr int ROWB = D / 2;                     // code bytes per token
-  static constexpr int CODE = kMTile * ROWB;             // one code tile
-  static constexpr int SBB = kMTile * NG * static_cast<int>(sizeof(SB));
+  static constexpr int CHUNK = kChunk * ROWB;            // code bytes of one TMA box
+  static constexpr int CODE = TILE * ROWB;               // one code tile
+  static constexpr int SBB = TILE * NG * static_cast<int>(sizeof(SB));
   static constexpr int STAGE = (2 * CODE + 4 * SBB + 1023) / 1024 * 1024;
-  static constexpr int STAGES = kMStages * STAGE;
-  static constexpr int BAR = STAGES;  // full[kMStages], empty[kMStages], q
-  static constexpr int FLAG = BAR + ((2 * kMStages + 1) * 8 + 15) / 16 * 16;
-  static constexpr int RED = FLAG + 16;                  // float scratch (merge reductions)
-  static constexpr int QB = RED + 2 * 4 * 8 * 4;         // the CTA's G query rows (<= f32)
+  static constexpr int STAGES = MCfg<D>::STAGES * STAGE;
+  static constexpr int BAR = STAGES;  // full[MCfg<D>::STAGES], empty[MCfg<D>::STAGES], q
+  static constexpr int FLAG = BAR + ((2 * MCfg<D>::STAGES + 1) * 8 + 15) / 16 * 16;
+  static constexpr int QB = FLAG + 16;                   // the CTA's G query rows (<= f32)
   static_assert(QB % 16 == 0, "bulk-copy destination must be 16-byte aligned");
   static constexpr int BYTES = QB + G * D * 4 + 1024;    // + alignment slack
   // end-of-range combine: per warp m, l, corr[NG], o[D] for G heads
   static constexpr int WST = G * (2 + NG + D);
-  static_assert(kConsumerWarps * WST * 4 <= STAGES, "warp states reuse the stages");
-  static_assert(G * kMMaxSplits * 4 + G * D * 4 * (G * D / 4 >= 128 ? 1 : 128 / (G * D / 4)) <= STAGES,
-                "merge weights and partial sums reuse the stages");
+  static_assert(W * WST * 4 <= STAGES, "warp states reuse the stages");
+  // split merge: per thread (M, L) + a float4 of o
+  static_assert(W * 32 * 24 <= STAGES, "merge states reuse the stages");
 };
 
 struct MParams {
@@ -95,7 +110,7 @@ struct MParams {
   void* out;
   int out_dtype;
   float* part_out;
-  int splits, tiles_per_split;
+  int splits, chunks_per_split;
   float* ws_o;
   float* ws_ml;
   unsigned* counters;
@@ -131,8 +146,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
 }
 
+template <int W>
 __device__ __forceinline__ void consumers_sync() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
+  asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
 }
 
 // Two nibbles (bits 4j and 16+4j of x) -> fp16x2 (1 + c/64): the nibble is
@@ -214,10 +230,14 @@ __device__ __forceinline__ float wsum(float v) {
 __device__ __forceinline__ int sigma8(int r) { return (r & 1) | ((r & 2) << 1) | ((r & 4) >> 1); }
 
 template <int D, int G, typename SB, bool QSPLIT>
-__global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
+__global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     decode_mma_kernel(const __grid_constant__ CUtensorMap tmk,
                       const __grid_constant__ CUtensorMap tmv, const MParams p) {
   using Lyt = MLayout<D, G, SB>;
+  constexpr int W = MCfg<D>::W;
+  constexpr int TILE = MCfg<D>::TILE;
+  constexpr int TB = MCfg<D>::TB;
+  constexpr int CPT = MCfg<D>::CPT;
   constexpr int NG = Lyt::NG;
   constexpr int NCH = D / 32;          // 16-byte code chunks per token
   constexpr bool kPaired = G <= 4;     // V side: hi/lo weights share one mma (N = 2G <= 8)
@@ -234,10 +254,9 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lyt::BAR);
-  uint64_t* empty = full + kMStages;
-  uint64_t* qbar = empty + kMStages;
+  uint64_t* empty = full + MCfg<D>::STAGES;
+  uint64_t* qbar = empty + MCfg<D>::STAGES;
   int* s_flag = reinterpret_cast<int*>(smem + Lyt::FLAG);
-  float* s_red = reinterpret_cast<float*>(smem + Lyt::RED);
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -248,6 +267,9 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
   const int kv = hg / p.nsub;
   const int h0 = kv * p.Gtot + (hg % p.nsub) * G;
 
+  pdl_wait();     // inputs of the preceding kernels are visible from here on
+  pdl_trigger();  // every CTA of this grid has started: the next may launch
+
   // ---- visible token range (local coordinates), as in decode_kernel --------
   const int n_local = max(0, min(p.seq_lens ? p.seq_lens[b] : p.n_tokens, p.capacity));
   int t_lo = 0;
@@ -256,20 +278,21 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
     const int n_glob = p.n_total > 0 ? p.n_total : n_local + p.token_offset;
     t_lo = max(0, n_glob - p.window - p.token_offset);
   }
-  int ntiles = 0, tile_begin = 0;
+  // this CTA's chunks [cb, ce); tiles of CPT chunks from cb (the last may be short)
+  int cb = 0, ce = 0;
   if (t_hi > t_lo) {
-    const int tb = t_lo / kMTile;
-    const int te = (t_hi + kMTile - 1) / kMTile;
-    tile_begin = tb + split * p.tiles_per_split;
-    ntiles = max(0, min(te, tile_begin + p.tiles_per_split) - tile_begin);
+    cb = t_lo / kChunk + split * p.chunks_per_split;
+    ce = min((t_hi + kChunk - 1) / kChunk, cb + p.chunks_per_split);
   }
+  const int ntiles = ce > cb ? (ce - cb + CPT - 1) / CPT : 0;
+  const int r_hi = min(t_hi, ce * kChunk);  // tokens at or past r_hi are masked
   const long long tok_base =
       static_cast<long long>(b) * p.bstride_tok + static_cast<long long>(kv) * p.capacity;
 
   if (tid == 0) {
-    for (int s = 0; s < kMStages; ++s) {
+    for (int s = 0; s < MCfg<D>::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
+      mbar_init(&empty[s], W);
     }
     mbar_init(qbar, 1);
     fence_barrier_init();
@@ -277,7 +300,7 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
   __syncthreads();
 
   // ======================= producer warp ========================================
-  if (warp == kConsumerWarps) {
+  if (warp == W) {
     if (lane == 0) {
       prefetch_tensormap(&tmk);
       prefetch_tensormap(&tmv);
@@ -297,24 +320,25 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
       int st = 0;
       uint32_t par = 0;
       for (int i = 0; i < ntiles; ++i) {
-        if (i >= kMStages) mbar_wait_bounded(&empty[st], par ^ 1u, p.err);
-        const int t0 = (tile_begin + i) * kMTile;
-        const int nt = min(kMTile, t_hi4 - t0);
+        if (i >= MCfg<D>::STAGES) mbar_wait_bounded(&empty[st], par ^ 1u, p.err);
+        const int c0 = cb + i * CPT;
+        const int nc = min(CPT, ce - c0);
+        const int t0 = c0 * kChunk;
+        const int nt = min(nc * kChunk, t_hi4 - t0);  // scale rows: a positive multiple of 4
         const uint32_t sbb = static_cast<uint32_t>(nt * NG * sizeof(SB));
         unsigned char* sb = smem + st * Lyt::STAGE;
-        mbar_arrive_expect_tx(&full[st], 2 * Lyt::CODE + 4 * sbb);
+        mbar_arrive_expect_tx(&full[st], 2 * nc * Lyt::CHUNK + 4 * sbb);
         const int row = static_cast<int>(tok_base + t0);
-#pragma unroll
-        for (int half = 0; half < (D > 256 ? 2 : 1); ++half) {
-          tma_load_2d(sb + half * (Lyt::CODE / 2), &tmk, half * 32, row, &full[st], pol);
-          tma_load_2d(sb + Lyt::CODE + half * (Lyt::CODE / 2), &tmv, half * 32, row, &full[st], pol);
+        for (int j = 0; j < nc; ++j) {
+          tma_load_2d(sb + j * Lyt::CHUNK, &tmk, 0, row + j * kChunk, &full[st], pol);
+          tma_load_2d(sb + Lyt::CODE + j * Lyt::CHUNK, &tmv, 0, row + j * kChunk, &full[st], pol);
         }
         unsigned char* sbp = sb + 2 * Lyt::CODE;
         bulk_g2s(sbp, ksb + static_cast<long long>(t0) * NG, sbb, &full[st], pol);
         bulk_g2s(sbp + Lyt::SBB, kbb + static_cast<long long>(t0) * NG, sbb, &full[st], pol);
         bulk_g2s(sbp + 2 * Lyt::SBB, vsb + static_cast<long long>(t0) * NG, sbb, &full[st], pol);
         bulk_g2s(sbp + 3 * Lyt::SBB, vbb + static_cast<long long>(t0) * NG, sbb, &full[st], pol);
-        if (++st == kMStages) {
+        if (++st == MCfg<D>::STAGES) {
           st = 0;
           par ^= 1u;
         }
@@ -383,9 +407,13 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
     for (int g = 0; g < NG; ++g)
       qsum[e][g] = __shfl_sync(0xffffffffu, qs_col[g], 4 * ((hvalid ? ihead[e] : 0) * P));
 
-  const int wt0 = warp * 16;  // this warp's first row of every tile
+  // this warp's blocks of 16 tokens start at tile rows wt0 + 16*bt; the
+  // swizzle pattern repeats every 8 rows, so block bt's offsets are block 0's
+  // plus 16*bt rows
+  const int wt0 = warp * 16 * TB;
+  constexpr int BROW = 16 * Lyt::ROWB;  // bytes of 16 code rows
   const int sr = sigma8(r);
-  int trow[NTK];              // tile rows of the item tokens
+  int trow[NTK];              // tile rows of the item tokens (block 0)
 #pragma unroll
   for (int f = 0; f < NTK; ++f) trow[f] = wt0 + sr + 8 * (G <= 2 ? (c & 1) : f);
   int koff[2][NG];            // K-side A operand: rows sigma(r), sigma(r)+8; words 8g+2c, +1
@@ -431,85 +459,93 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
     constexpr bool MASKED = decltype(masked_c)::value;
     const unsigned char* stg = smem + st * Lyt::STAGE;
     const SB* s_ks = reinterpret_cast<const SB*>(stg + 2 * Lyt::CODE);
-    const SB* s_kb = s_ks + kMTile * NG;
-    const SB* s_vs = s_kb + kMTile * NG;
-    const SB* s_vb = s_vs + kMTile * NG;
+    const SB* s_kb = s_ks + TILE * NG;
+    const SB* s_vs = s_kb + TILE * NG;
+    const SB* s_vb = s_vs + TILE * NG;
 
-    // ---- K side: partial S[token][column] per group --------------------------
-    float acc[NG][4];
+    // ---- K side: partial S[token][column] per block and group ------------------
+    float acc[TB][NG][4];
 #pragma unroll
-    for (int g = 0; g < NG; ++g) {
+    for (int bt = 0; bt < TB; ++bt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) acc[g][e] = 0.0f;
-      const uint2 w0 = *reinterpret_cast<const uint2*>(stg + koff[0][g]);  // token sigma(r)
-      const uint2 w1 = *reinterpret_cast<const uint2*>(stg + koff[1][g]);  // token sigma(r)+8
+      for (int g = 0; g < NG; ++g) {
 #pragma unroll
-      for (int ks = 0; ks < 4; ++ks) {
-        const uint32_t x0 = (ks >> 1) ? w0.y : w0.x;
-        const uint32_t x1 = (ks >> 1) ? w1.y : w1.x;
-        uint32_t a0, a1, a2, a3;
-        if (ks & 1) {
-          a0 = nib64<2>(x0, mg); a1 = nib64<2>(x1, mg); a2 = nib64<3>(x0, mg); a3 = nib64<3>(x1, mg);
-        } else {
-          a0 = nib64<0>(x0, mg); a1 = nib64<0>(x1, mg); a2 = nib64<1>(x0, mg); a3 = nib64<1>(x1, mg);
+        for (int e = 0; e < 4; ++e) acc[bt][g][e] = 0.0f;
+        const uint2 w0 = *reinterpret_cast<const uint2*>(stg + bt * BROW + koff[0][g]);  // sigma(r)
+        const uint2 w1 = *reinterpret_cast<const uint2*>(stg + bt * BROW + koff[1][g]);  // sigma(r)+8
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          const uint32_t x0 = (ks >> 1) ? w0.y : w0.x;
+          const uint32_t x1 = (ks >> 1) ? w1.y : w1.x;
+          uint32_t a0, a1, a2, a3;
+          if (ks & 1) {
+            a0 = nib64<2>(x0, mg); a1 = nib64<2>(x1, mg); a2 = nib64<3>(x0, mg); a3 = nib64<3>(x1, mg);
+          } else {
+            a0 = nib64<0>(x0, mg); a1 = nib64<0>(x1, mg); a2 = nib64<1>(x0, mg); a3 = nib64<1>(x1, mg);
+          }
+          mma16816(acc[bt][g], a0, a1, a2, a3, qb[g][ks][0], qb[g][ks][1]);
+          if constexpr (QSPLIT) mma16816(acc[bt][g], a0, a1, a2, a3, qb_lo[g][ks][0], qb_lo[g][ks][1]);
         }
-        mma16816(acc[g], a0, a1, a2, a3, qb[g][ks][0], qb[g][ks][1]);
-        if constexpr (QSPLIT) mma16816(acc[g], a0, a1, a2, a3, qb_lo[g][ks][0], qb_lo[g][ks][1]);
       }
-    }
 
     // ---- complete S per item (sum over the dim subsets phi) ------------------
-    float S[IPL][NG];
+    float S[TB][IPL][NG];
 #pragma unroll
-    for (int g = 0; g < NG; ++g) {
-      if constexpr (G <= 2) {
-        // cols 2c, 2c+1 = phis {0,1} (c even) or {2,3} (c odd) of head c/2;
-        // lane c even keeps token sigma(r), c odd keeps sigma(r)+8.
-        const float x0 = acc[g][0] + acc[g][1];
-        const float x1 = acc[g][2] + acc[g][3];
-        const bool odd = (c & 1) != 0;
-        const float keep = odd ? x1 : x0;
-        const float send = odd ? x0 : x1;
-        S[0][g] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
-      } else if constexpr (G == 4) {
-        S[0][g] = acc[g][0] + acc[g][1];
-        S[1][g] = acc[g][2] + acc[g][3];
-      } else {
+    for (int bt = 0; bt < TB; ++bt)
 #pragma unroll
-        for (int it = 0; it < 4; ++it) S[it][g] = acc[g][it];  // it = 2f + e
+      for (int g = 0; g < NG; ++g) {
+        if constexpr (G <= 2) {
+          // cols 2c, 2c+1 = phis {0,1} (c even) or {2,3} (c odd) of head c/2;
+          // lane c even keeps token sigma(r), c odd keeps sigma(r)+8.
+          const float x0 = acc[bt][g][0] + acc[bt][g][1];
+          const float x1 = acc[bt][g][2] + acc[bt][g][3];
+          const bool odd = (c & 1) != 0;
+          const float keep = odd ? x1 : x0;
+          const float send = odd ? x0 : x1;
+          S[bt][0][g] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
+        } else if constexpr (G == 4) {
+          S[bt][0][g] = acc[bt][g][0] + acc[bt][g][1];
+          S[bt][1][g] = acc[bt][g][2] + acc[bt][g][3];
+        } else {
+#pragma unroll
+          for (int it = 0; it < 4; ++it) S[bt][it][g] = acc[bt][g][it];  // it = 2f + e
+        }
       }
-    }
 
     // ---- scores (log2 units) ---------------------------------------------------
     // score = sum_g s_g * sum_d q_d c_d + b_g * sum_d q_d, sum q c = 64 (S - sum q)
-    float sk[NTK][NG], bk[NTK][NG];
+    float sk[TB][NTK][NG], bk[TB][NTK][NG];
 #pragma unroll
-    for (int f = 0; f < NTK; ++f) {
-      load_sb_row<SB, NG>(s_ks + trow[f] * NG, sk[f]);
-      load_sb_row<SB, NG>(s_kb + trow[f] * NG, bk[f]);
-    }
-    float sc[IPL];
+    for (int bt = 0; bt < TB; ++bt)
+#pragma unroll
+      for (int f = 0; f < NTK; ++f) {
+        load_sb_row<SB, NG>(s_ks + (trow[f] + 16 * bt) * NG, sk[bt][f]);
+        load_sb_row<SB, NG>(s_kb + (trow[f] + 16 * bt) * NG, bk[bt][f]);
+      }
+    float sc[TB][IPL];
     float bmax[IH];
 #pragma unroll
     for (int e = 0; e < IH; ++e) bmax[e] = -INFINITY;
 #pragma unroll
-    for (int it = 0; it < IPL; ++it) {
-      const int f = G <= 2 ? 0 : (G == 4 ? it : it >> 1);
-      const int e = G == 8 ? (it & 1) : 0;
-      float a = 0.0f, bsum = 0.0f;
+    for (int bt = 0; bt < TB; ++bt)
 #pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        a = fmaf(sk[f][g], S[it][g] - qsum[e][g], a);
-        bsum = fmaf(bk[f][g], qsum[e][g], bsum);
+      for (int it = 0; it < IPL; ++it) {
+        const int f = G <= 2 ? 0 : (G == 4 ? it : it >> 1);
+        const int e = G == 8 ? (it & 1) : 0;
+        float a = 0.0f, bsum = 0.0f;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          a = fmaf(sk[bt][f][g], S[bt][it][g] - qsum[e][g], a);
+          bsum = fmaf(bk[bt][f][g], qsum[e][g], bsum);
+        }
+        float v = fmaf(64.0f, a, bsum) * p.qscale;
+        if constexpr (MASKED) {
+          const int tg = tile_t0 + trow[f] + 16 * bt;
+          v = (hvalid && tg >= t_lo && tg < r_hi) ? v : -INFINITY;
+        }
+        sc[bt][it] = v;
+        bmax[e] = fmaxf(bmax[e], v);
       }
-      float v = fmaf(64.0f, a, bsum) * p.qscale;
-      if constexpr (MASKED) {
-        const int tg = tile_t0 + trow[f];
-        v = (hvalid && tg >= t_lo && tg < t_hi) ? v : -INFINITY;
-      }
-      sc[it] = v;
-      bmax[e] = fmaxf(bmax[e], v);
-    }
     // max over the lanes of each item head
 #pragma unroll
     for (int e = 0; e < IH; ++e) {
@@ -530,96 +566,113 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
 #pragma unroll
       for (int g = 0; g < NG; ++g) corr[e][g] *= alpha[e];
     }
-    float pr[IPL];
+    float pr[TB][IPL];
 #pragma unroll
-    for (int it = 0; it < IPL; ++it) {
-      const int e = G == 8 ? (it & 1) : 0;
-      pr[it] = MASKED ? ((sc[it] == -INFINITY) ? 0.0f : fast_exp2(sc[it] - m_run[e]))
-                      : fast_exp2(sc[it] - m_run[e]);
-      l_run[e] += pr[it];
-    }
+    for (int bt = 0; bt < TB; ++bt)
+#pragma unroll
+      for (int it = 0; it < IPL; ++it) {
+        const int e = G == 8 ? (it & 1) : 0;
+        pr[bt][it] = MASKED ? ((sc[bt][it] == -INFINITY) ? 0.0f : fast_exp2(sc[bt][it] - m_run[e]))
+                            : fast_exp2(sc[bt][it] - m_run[e]);
+        l_run[e] += pr[bt][it];
+      }
 
     // ---- weights w = p*s (fp16 hi + lo) and the constant correction ------------
-    float sv[NTK][NG], bv[NTK][NG];
+    float sv[TB][NTK][NG], bv[TB][NTK][NG];
 #pragma unroll
-    for (int f = 0; f < NTK; ++f) {
-      load_sb_row<SB, NG>(s_vs + trow[f] * NG, sv[f]);
-      load_sb_row<SB, NG>(s_vb + trow[f] * NG, bv[f]);
-    }
-    uint32_t hl[IPL][NG];  // packed (hi | lo << 16) of w per item and group
+    for (int bt = 0; bt < TB; ++bt)
 #pragma unroll
-    for (int it = 0; it < IPL; ++it) {
-      const int f = G <= 2 ? 0 : (G == 4 ? it : it >> 1);
-      const int e = G == 8 ? (it & 1) : 0;
-#pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        float w = pr[it] * sv[f][g];
-        float cb = pr[it] * fmaf(-64.0f, sv[f][g], bv[f][g]);
-        if constexpr (MASKED) {  // stale scales of masked tokens must not leak
-          w = pr[it] > 0.0f ? w : 0.0f;
-          cb = pr[it] > 0.0f ? cb : 0.0f;
-        }
-        corr[e][g] += cb;
-        const __half wh = __float2half_rn(w);
-        const __half wl = __float2half_rn(w - __half2float(wh));
-        hl[it][g] = static_cast<uint32_t>(__half_as_ushort(wh)) |
-                    (static_cast<uint32_t>(__half_as_ushort(wl)) << 16);
+      for (int f = 0; f < NTK; ++f) {
+        load_sb_row<SB, NG>(s_vs + (trow[f] + 16 * bt) * NG, sv[bt][f]);
+        load_sb_row<SB, NG>(s_vb + (trow[f] + 16 * bt) * NG, bv[bt][f]);
       }
-    }
+    uint32_t hl[TB][IPL][NG];  // packed (hi | lo << 16) of w per item and group
+#pragma unroll
+    for (int bt = 0; bt < TB; ++bt)
+#pragma unroll
+      for (int it = 0; it < IPL; ++it) {
+        const int f = G <= 2 ? 0 : (G == 4 ? it : it >> 1);
+        const int e = G == 8 ? (it & 1) : 0;
+        float w[NG];
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          w[g] = pr[bt][it] * sv[bt][f][g];
+          float cb = pr[bt][it] * fmaf(-64.0f, sv[bt][f][g], bv[bt][f][g]);
+          if constexpr (MASKED) {  // stale scales of masked tokens must not leak
+            w[g] = pr[bt][it] > 0.0f ? w[g] : 0.0f;
+            cb = pr[bt][it] > 0.0f ? cb : 0.0f;
+          }
+          corr[e][g] += cb;
+        }
+        // hi = fp16(w), lo = fp16(w - hi), two groups per conversion
+#pragma unroll
+        for (int g = 0; g < NG; g += 2) {
+          const uint32_t hi2 = pack_h2(w[g], w[g + 1]);
+          const float2 hf = unpack_h2(hi2);
+          const uint32_t lo2 = pack_h2(w[g] - hf.x, w[g + 1] - hf.y);
+          hl[bt][it][g] = __byte_perm(hi2, lo2, 0x5410u);
+          hl[bt][it][g + 1] = __byte_perm(hi2, lo2, 0x7632u);
+        }
+      }
 
     // ---- V-side B operand: rows k = 2c, 2c+1 (b0), 2c+8, 2c+9 (b1) stand for
     // tokens sigma(k&7) + 8(k>>3), whose items live in lanes with r' = k & 7.
-    uint32_t bw[NG][2];
-    uint32_t bw_lo[kPaired ? 1 : NG][2];
+    uint32_t bw[TB][NG][2];
+    uint32_t bw_lo[TB][kPaired ? 1 : NG][2];
     (void)bw_lo;
-    if constexpr (G <= 2) {
-      const int hp = r >> 1;  // column r = (head r/2, hi or lo)
-      const uint32_t sel = (r & 1) ? 0x7632u : 0x5410u;
-      const bool ok = hp < G;
-      const int l0 = 8 * c + 2 * hp;
 #pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        const uint32_t x0 = __shfl_sync(0xffffffffu, hl[0][g], l0);
-        const uint32_t x1 = __shfl_sync(0xffffffffu, hl[0][g], l0 + 4);
-        const uint32_t x2 = __shfl_sync(0xffffffffu, hl[0][g], l0 + 1);
-        const uint32_t x3 = __shfl_sync(0xffffffffu, hl[0][g], l0 + 5);
-        bw[g][0] = ok ? __byte_perm(x0, x1, sel) : 0u;
-        bw[g][1] = ok ? __byte_perm(x2, x3, sel) : 0u;
-      }
-    } else if constexpr (G == 4) {
-      const int hp = r >> 1;
-      const uint32_t sel = (r & 1) ? 0x7632u : 0x5410u;
-      const int l0 = 8 * c + hp;
+    for (int bt = 0; bt < TB; ++bt) {
+      if constexpr (G <= 2) {
+        // column r = (head r/2, hi or lo); columns of heads >= G carry other
+        // heads' weights into O columns that are never read (each mma output
+        // column depends on its B column only)
+        const int hp = r >> 1;
+        const uint32_t sel = (r & 1) ? 0x7632u : 0x5410u;
+        const int l0 = 8 * c + 2 * hp;
 #pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        const uint32_t x0 = __shfl_sync(0xffffffffu, hl[0][g], l0);
-        const uint32_t x1 = __shfl_sync(0xffffffffu, hl[0][g], l0 + 4);
-        const uint32_t x2 = __shfl_sync(0xffffffffu, hl[1][g], l0);
-        const uint32_t x3 = __shfl_sync(0xffffffffu, hl[1][g], l0 + 4);
-        bw[g][0] = __byte_perm(x0, x1, sel);
-        bw[g][1] = __byte_perm(x2, x3, sel);
-      }
-    } else {
-      // column r = head r: item (head r, token k) is register 2(k>>3) + (r&1)
-      // of lane 4(k&7) + r/2
-      const int l0 = 8 * c + (r >> 1);
-      const bool odd = (r & 1) != 0;
-#pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        uint32_t y[4];
-#pragma unroll
-        for (int f = 0; f < 2; ++f) {
-          const uint32_t u0 = __shfl_sync(0xffffffffu, hl[2 * f][g], l0);
-          const uint32_t u1 = __shfl_sync(0xffffffffu, hl[2 * f + 1][g], l0);
-          const uint32_t v0 = __shfl_sync(0xffffffffu, hl[2 * f][g], l0 + 4);
-          const uint32_t v1 = __shfl_sync(0xffffffffu, hl[2 * f + 1][g], l0 + 4);
-          y[2 * f] = odd ? u1 : u0;
-          y[2 * f + 1] = odd ? v1 : v0;
+        for (int g = 0; g < NG; ++g) {
+          const uint32_t x0 = __shfl_sync(0xffffffffu, hl[bt][0][g], l0);
+          const uint32_t x1 = __shfl_sync(0xffffffffu, hl[bt][0][g], l0 + 4);
+          const uint32_t x2 = __shfl_sync(0xffffffffu, hl[bt][0][g], l0 + 1);
+          const uint32_t x3 = __shfl_sync(0xffffffffu, hl[bt][0][g], l0 + 5);
+          bw[bt][g][0] = __byte_perm(x0, x1, sel);
+          bw[bt][g][1] = __byte_perm(x2, x3, sel);
         }
-        bw[g][0] = __byte_perm(y[0], y[1], 0x5410u);
-        bw[g][1] = __byte_perm(y[2], y[3], 0x5410u);
-        bw_lo[g][0] = __byte_perm(y[0], y[1], 0x7632u);
-        bw_lo[g][1] = __byte_perm(y[2], y[3], 0x7632u);
+      } else if constexpr (G == 4) {
+        const int hp = r >> 1;
+        const uint32_t sel = (r & 1) ? 0x7632u : 0x5410u;
+        const int l0 = 8 * c + hp;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          const uint32_t x0 = __shfl_sync(0xffffffffu, hl[bt][0][g], l0);
+          const uint32_t x1 = __shfl_sync(0xffffffffu, hl[bt][0][g], l0 + 4);
+          const uint32_t x2 = __shfl_sync(0xffffffffu, hl[bt][1][g], l0);
+          const uint32_t x3 = __shfl_sync(0xffffffffu, hl[bt][1][g], l0 + 4);
+          bw[bt][g][0] = __byte_perm(x0, x1, sel);
+          bw[bt][g][1] = __byte_perm(x2, x3, sel);
+        }
+      } else {
+        // column r = head r: item (head r, token k) is register 2(k>>3) + (r&1)
+        // of lane 4(k&7) + r/2
+        const int l0 = 8 * c + (r >> 1);
+        const bool odd = (r & 1) != 0;
+#pragma unroll
+        for (int g = 0; g < NG; ++g) {
+          uint32_t y[4];
+#pragma unroll
+          for (int f = 0; f < 2; ++f) {
+            const uint32_t u0 = __shfl_sync(0xffffffffu, hl[bt][2 * f][g], l0);
+            const uint32_t u1 = __shfl_sync(0xffffffffu, hl[bt][2 * f + 1][g], l0);
+            const uint32_t v0 = __shfl_sync(0xffffffffu, hl[bt][2 * f][g], l0 + 4);
+            const uint32_t v1 = __shfl_sync(0xffffffffu, hl[bt][2 * f + 1][g], l0 + 4);
+            y[2 * f] = odd ? u1 : u0;
+            y[2 * f + 1] = odd ? v1 : v0;
+          }
+          bw[bt][g][0] = __byte_perm(y[0], y[1], 0x5410u);
+          bw[bt][g][1] = __byte_perm(y[2], y[3], 0x5410u);
+          bw_lo[bt][g][0] = __byte_perm(y[0], y[1], 0x7632u);
+          bw_lo[bt][g][1] = __byte_perm(y[2], y[3], 0x7632u);
+        }
       }
     }
 
@@ -651,24 +704,26 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
     // ---- V side: O += V^T * w ---------------------------------------------------
     const uint32_t vbase = smem_base + st * Lyt::STAGE + Lyt::CODE;
 #pragma unroll
-    for (int q2 = 0; q2 < NCH / 2; ++q2) {
-      uint32_t d[4];
-      ldsm_x4_trans(vbase + voff[q2], d);
+    for (int bt = 0; bt < TB; ++bt)
 #pragma unroll
-      for (int hh = 0; hh < 2; ++hh) {
-        const int kk = 2 * q2 + hh;
-        const int g = kk >> 1;
-        const uint32_t R0 = d[2 * hh], R1 = d[2 * hh + 1];
-        const uint32_t a00 = nib64<0>(R0, mg), a01 = nib64<1>(R0, mg), a02 = nib64<2>(R0, mg), a03 = nib64<3>(R0, mg);
-        const uint32_t a10 = nib64<0>(R1, mg), a11 = nib64<1>(R1, mg), a12 = nib64<2>(R1, mg), a13 = nib64<3>(R1, mg);
-        mma16816(o[kk][0], a00, a01, a10, a11, bw[g][0], bw[g][1]);
-        mma16816(o[kk][1], a02, a03, a12, a13, bw[g][0], bw[g][1]);
-        if constexpr (!kPaired) {
-          mma16816(o[kk][0], a00, a01, a10, a11, bw_lo[g][0], bw_lo[g][1]);
-          mma16816(o[kk][1], a02, a03, a12, a13, bw_lo[g][0], bw_lo[g][1]);
+      for (int q2 = 0; q2 < NCH / 2; ++q2) {
+        uint32_t d[4];
+        ldsm_x4_trans(vbase + bt * BROW + voff[q2], d);
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          const int kk = 2 * q2 + hh;
+          const int g = kk >> 1;
+          const uint32_t R0 = d[2 * hh], R1 = d[2 * hh + 1];
+          const uint32_t a00 = nib64<0>(R0, mg), a01 = nib64<1>(R0, mg), a02 = nib64<2>(R0, mg), a03 = nib64<3>(R0, mg);
+          const uint32_t a10 = nib64<0>(R1, mg), a11 = nib64<1>(R1, mg), a12 = nib64<2>(R1, mg), a13 = nib64<3>(R1, mg);
+          mma16816(o[kk][0], a00, a01, a10, a11, bw[bt][g][0], bw[bt][g][1]);
+          mma16816(o[kk][1], a02, a03, a12, a13, bw[bt][g][0], bw[bt][g][1]);
+          if constexpr (!kPaired) {
+            mma16816(o[kk][0], a00, a01, a10, a11, bw_lo[bt][g][0], bw_lo[bt][g][1]);
+            mma16816(o[kk][1], a02, a03, a12, a13, bw_lo[bt][g][0], bw_lo[bt][g][1]);
+          }
         }
       }
-    }
   };
 
   {
@@ -676,15 +731,15 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
     uint32_t par = 0;
     for (int i = 0; i < ntiles; ++i) {
       mbar_wait_bounded(&full[st], par, p.err);
-      const int tile_t0 = (tile_begin + i) * kMTile;
-      if (tile_t0 >= t_lo && tile_t0 + kMTile <= t_hi) {
+      const int tile_t0 = (cb + i * CPT) * kChunk;
+      if (tile_t0 >= t_lo && tile_t0 + TILE <= r_hi) {
         tile(std::integral_constant<bool, false>{}, st, tile_t0);
       } else {
         tile(std::integral_constant<bool, true>{}, st, tile_t0);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
-      if (++st == kMStages) {
+      if (++st == MCfg<D>::STAGES) {
         st = 0;
         par ^= 1u;
       }
@@ -707,7 +762,7 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
       corr[e][g] += __shfl_xor_sync(0xffffffffu, corr[e][g], 16);
     }
   }
-  consumers_sync();  // every warp is past its last tile: the stage area is free
+  consumers_sync<W>();  // every warp is past its last tile: the stage area is free
   float* wst = reinterpret_cast<float*>(smem) + warp * Lyt::WST;  // [G][2 + NG + D]
   if (r == 0 && (G > 2 || (c & 1) == 0) && hvalid) {
 #pragma unroll
@@ -739,21 +794,21 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
         h1s[d0 + 1] = o[kk][s][3];
       }
     }
-  consumers_sync();
+  consumers_sync<W>();
 
   const bool direct = p.splits == 1;
   const long long unit = static_cast<long long>(b) * gridDim.y + hg;
   const float* wall = reinterpret_cast<const float*>(smem);
-  constexpr int NTH = kConsumerWarps * 32;
+  constexpr int NTH = W * 32;
   for (int it = tid; it < G * D; it += NTH) {
     const int g = it / D;
     const int d = it % D;
     float M = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, wall[w * Lyt::WST + g * (2 + NG + D)]);
+    for (int w = 0; w < W; ++w) M = fmaxf(M, wall[w * Lyt::WST + g * (2 + NG + D)]);
     float L = 0.0f, acc = 0.0f;
 #pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w) {
+    for (int w = 0; w < W; ++w) {
       const float* hs = wall + w * Lyt::WST + g * (2 + NG + D);
       const float e = (M == -INFINITY || hs[0] == -INFINITY) ? 0.0f : fast_exp2(hs[0] - M);
       L += e * hs[1];
@@ -784,90 +839,91 @@ __global__ void __launch_bounds__(kMThreads, D == 128 ? 3 : 1)
   if (direct) return;
 
   // ---- last CTA of this (b, head group) merges the splits -------------------
-  __threadfence();
-  consumers_sync();
+  // Release: the CTA barrier orders every thread's partial stores before
+  // thread 0's acquire-release ticket; the CTA that draws the last ticket has
+  // acquired every other CTA's partials, and its barrier passes that on.
+  consumers_sync<W>();
   if (tid == 0) {
-    const unsigned prev = atomicAdd(&p.counters[unit], 1u);
+    const unsigned prev = atomic_add_acq_rel(&p.counters[unit], 1u);
     s_flag[0] = (prev == static_cast<unsigned>(p.splits - 1)) ? 1 : 0;
   }
-  consumers_sync();
+  consumers_sync<W>();
   if (s_flag[0] == 0) return;
-  __threadfence();
 
+  // float4 items (head, 4 dims); the splits of an item are spread over R
+  // thread subsets, each running an online log-sum-exp merge with 8 splits'
+  // (m, l, o) loads in flight per step, then the R states are combined.
   const int S_ = p.splits;
   const long long base = unit * S_ * G;
-  float* ew = reinterpret_cast<float*>(smem);  // [G][S_] merge weights
-  // 1) per head (one warp each): M = max m_s, weights e_s = 2^(m_s - M), L
-  for (int g = warp; g < G; g += kConsumerWarps) {
-    float m = -INFINITY;
-    for (int s = lane; s < S_; s += 32) m = fmaxf(m, __ldcg(&p.ws_ml[(base + s * G + g) * 2]));
-    m = wmax(m);
-    float l = 0.0f;
-    for (int s = lane; s < S_; s += 32) {
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(&p.ws_ml[(base + s * G + g) * 2]));
-      const float e = (ml.x == -INFINITY || m == -INFINITY) ? 0.0f : fast_exp2(ml.x - m);
-      ew[g * S_ + s] = e;
-      l += e * ml.y;
-    }
-    l = wsum(l);
-    if (lane == 0) {
-      s_red[2 * g] = m;
-      s_red[2 * g + 1] = l;
-    }
-  }
-  consumers_sync();
-  // 2) o = sum_s e_s o_s: float4 items (head, 4 dims), the splits spread over
-  //    R thread subsets so that every thread has several loads in flight
   constexpr int NI = G * D / 4;
   constexpr int R = NI >= NTH ? 1 : NTH / NI;
-  float4* red = reinterpret_cast<float4*>(smem + ((G * S_ * 4 + 15) & ~15));  // [R][NI]
+  float2* mst = reinterpret_cast<float2*>(smem);           // [R][NI] (M, L)
+  float4* ost = reinterpret_cast<float4*>(smem + R * NI * 8);  // [R][NI] o
   for (int it = tid; it < NI * R; it += NTH) {
     const int item = it % NI, sub = it / NI;
     const int g = item / (D / 4);
     const float* ow = p.ws_o + (base + g) * D + 4 * (item % (D / 4));
+    const float* mw = p.ws_ml + (base + g) * 2;
+    float M = -INFINITY, L = 0.0f;
     float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    int s = sub;
-    for (; s + 3 * R < S_; s += 4 * R) {
-      float4 v[4];
-      float e[4];
+    for (int s0 = sub; s0 < S_; s0 += 8 * R) {
+      float2 ml[8];
+      float4 v[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        v[j] = __ldcg(reinterpret_cast<const float4*>(ow + static_cast<long long>(s + j * R) * G * D));
-        e[j] = ew[g * S_ + s + j * R];
+      for (int j = 0; j < 8; ++j) {
+        const int s = s0 + j * R;
+        if (s < S_) {
+          ml[j] = __ldcg(reinterpret_cast<const float2*>(mw + static_cast<long long>(s) * G * 2));
+          v[j] = __ldcg(reinterpret_cast<const float4*>(ow + static_cast<long long>(s) * G * D));
+        } else {
+          ml[j] = make_float2(-INFINITY, 0.0f);
+          v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
       }
+      float mb = M;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        a.x = fmaf(e[j], v[j].x, a.x);
-        a.y = fmaf(e[j], v[j].y, a.y);
-        a.z = fmaf(e[j], v[j].z, a.z);
-        a.w = fmaf(e[j], v[j].w, a.w);
+      for (int j = 0; j < 8; ++j) mb = fmaxf(mb, ml[j].x);
+      const float sc = M == -INFINITY ? 0.0f : fast_exp2(M - mb);
+      L *= sc;
+      a.x *= sc;
+      a.y *= sc;
+      a.z *= sc;
+      a.w *= sc;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float e = ml[j].x == -INFINITY ? 0.0f : fast_exp2(ml[j].x - mb);
+        L = fmaf(e, ml[j].y, L);
+        a.x = fmaf(e, v[j].x, a.x);
+        a.y = fmaf(e, v[j].y, a.y);
+        a.z = fmaf(e, v[j].z, a.z);
+        a.w = fmaf(e, v[j].w, a.w);
       }
+      M = mb;
     }
-    for (; s < S_; s += R) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(ow + static_cast<long long>(s) * G * D));
-      const float e = ew[g * S_ + s];
+    mst[sub * NI + item] = make_float2(M, L);
+    ost[sub * NI + item] = a;
+  }
+  consumers_sync<W>();
+  for (int item = tid; item < NI; item += NTH) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int sub = 0; sub < R; ++sub) M = fmaxf(M, mst[sub * NI + item].x);
+    float L = 0.0f;
+    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+    for (int sub = 0; sub < R; ++sub) {
+      const float2 ml = mst[sub * NI + item];
+      const float4 v = ost[sub * NI + item];
+      const float e = ml.x == -INFINITY ? 0.0f : fast_exp2(ml.x - M);
+      L = fmaf(e, ml.y, L);
       a.x = fmaf(e, v.x, a.x);
       a.y = fmaf(e, v.y, a.y);
       a.z = fmaf(e, v.z, a.z);
       a.w = fmaf(e, v.w, a.w);
     }
-    red[sub * NI + item] = a;
-  }
-  consumers_sync();
-  for (int item = tid; item < NI; item += NTH) {
-    float4 a = red[item];
-#pragma unroll
-    for (int sub = 1; sub < R; ++sub) {
-      const float4 v = red[sub * NI + item];
-      a.x += v.x;
-      a.y += v.y;
-      a.z += v.z;
-      a.w += v.w;
-    }
     const int g = item / (D / 4);
     const int d = 4 * (item % (D / 4));
     const int h = h0 + g;
-    const float M = s_red[2 * g], L = s_red[2 * g + 1];
     const float av[4] = {a.x, a.y, a.z, a.w};
     if (p.partial) {
       float* blk = p.part_out + static_cast<long long>(b) * p.H * (D + 2);
@@ -895,6 +951,7 @@ using MKernelFn = void (*)(CUtensorMap, CUtensorMap, MParams);
 struct MKernelInfo {
   MKernelFn fn = nullptr;
   int smem = 0;
+  int threads = 0;
 };
 
 template <int D, int G, typename SB>
@@ -902,6 +959,7 @@ MKernelInfo mk(bool qsplit) {
   MKernelInfo k;
   k.fn = qsplit ? decode_mma_kernel<D, G, SB, true> : decode_mma_kernel<D, G, SB, false>;
   k.smem = MLayout<D, G, SB>::BYTES;
+  k.threads = MCfg<D>::THREADS;
   return k;
 }
 
@@ -933,7 +991,7 @@ int mma_blocks_per_sm(int device, const MKernelInfo& k) {
   if (it != g_mocc.end()) return it->second;
   cudaFuncSetAttribute(k.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, k.smem);
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k.fn, kMThreads, k.smem) != cudaSuccess || n < 1)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, k.fn, k.threads, k.smem) != cudaSuccess || n < 1)
     n = 1;
   g_mocc[key] = n;
   return n;
@@ -957,7 +1015,7 @@ bool encode_codes_map(CUtensorMap* m, const uint32_t* base, int D, long long row
   if (!fn) return false;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(D / 8), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(D / 2)};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(D == 128 ? 16 : 32), static_cast<cuuint32_t>(kMTile)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(D / 8), static_cast<cuuint32_t>(kChunk)};
   cuuint32_t estr[2] = {1, 1};
   const CUtensorMapSwizzle swz = D == 128 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(base), dims, strides,
@@ -975,10 +1033,10 @@ std::string& launch_detail() {
 
 bool mma_supported(int D, int G) { return (D == 128 || D == 256) && G >= 1 && G <= 8 && (G & (G - 1)) == 0; }
 
-int mma_tokens_per_tile() { return kMTile; }
+int mma_tokens_per_tile() { return kChunk; }
 
-int mma_occupancy(int device, int D, int gsub) {
-  MKernelInfo k = pick_mma(D, gsub, kF16, false);
+int mma_occupancy(int device, int D, int gsub, bool qsplit) {
+  MKernelInfo k = pick_mma(D, gsub, kF16, qsplit);
   return k.fn ? mma_blocks_per_sm(device, k) : 1;
 }
 
@@ -1023,7 +1081,7 @@ cudaError_t launch_decode_mma(const DecodeArgs& a, const DecodePlan& pl, cudaStr
   p.out_dtype = a.out_dtype;
   p.part_out = a.part_out;
   p.splits = pl.splits;
-  p.tiles_per_split = pl.tiles_per_split;
+  p.chunks_per_split = pl.tiles_per_split;  // the planner's tiles are 64-token chunks here
   if (pl.splits > 1) {
     unsigned char* ws = static_cast<unsigned char*>(a.workspace);
     p.ws_o = reinterpret_cast<float*>(ws + pl.ws_o_off);
@@ -1032,8 +1090,7 @@ cudaError_t launch_decode_mma(const DecodeArgs& a, const DecodePlan& pl, cudaStr
   }
   p.err = a.err;
   dim3 grid(pl.splits, a.Hkv * pl.nsub, a.B);
-  k.fn<<<grid, kMThreads, k.smem, stream>>>(tmk, tmv, p);
-  return cudaGetLastError();
+  return launch_pdl(k.fn, grid, dim3(k.threads), static_cast<size_t>(k.smem), stream, tmk, tmv, p);
 }
 
 }  // namespace tq

@@ -145,6 +145,25 @@ __device__ __forceinline__ void prefetch_tensormap(const void* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// Programmatic dependent launch. pdl_wait blocks until the kernels this grid
+// depends on (launched before it on the stream) have completed and their
+// writes are visible; without the launch attribute it returns at once.
+// pdl_trigger lets the next kernel on the stream start launching (its CTAs
+// then wait in their own pdl_wait), which hides its launch latency behind
+// this kernel's tail.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Atomic add with acquire-release semantics at GPU scope (a split-merge ticket:
+// releases this CTA's partials, acquires the other CTAs').
+__device__ __forceinline__ unsigned atomic_add_acq_rel(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));

@@ -58,7 +58,7 @@ int choose_decode_variant(int D, int G);
 
 bool mma_supported(int D, int G);
 int mma_tokens_per_tile();
-int mma_occupancy(int device, int D, int gsub);
+int mma_occupancy(int device, int D, int gsub, bool qsplit);
 
 // Plan: split count etc. Returns workspace bytes needed.
 struct DecodePlan {
@@ -77,8 +77,10 @@ extern const size_t kCounterRegionBytes;
 
 // splits == -1 marks a problem with more (batch x head-group) units than
 // counters.
+// qsplit: f32/bf16 queries (their kernels run fewer CTAs per SM, so they get
+// no more splits than the f16 plan the workspace size is computed from).
 DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_max,
-                       bool windowed);
+                       bool windowed, bool qsplit = false);
 cudaError_t launch_decode_mma(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 cudaError_t launch_decode(const DecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 
@@ -86,6 +88,25 @@ cudaError_t launch_lse_merge(const float* parts, int n_parts, int B, int H, int 
                              int out_dtype, cudaStream_t stream);
 
 int device_sm_count(int device);
+
+// Launch `kernel` with programmatic stream serialization, so it may start
+// while the preceding kernel of the stream finishes (the kernel must call
+// pdl_wait() before it touches global memory).
+template <typename... K, typename... A>
+cudaError_t launch_pdl(void (*kernel)(K...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, A&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
+}
 
 // Why the last launch_* call on this thread failed before reaching the GPU
 // ("" if it did not); the C ABI appends it to tq_last_error().

@@ -93,6 +93,8 @@ struct MLayout {
 struct MParams {
   const void* q;
   int q_dtype;
+  const uint32_t* kq;  // code bases (the TMA maps hold them too; used for L2 prefetch)
+  const uint32_t* vq;
   const void* ks;
   const void* kb;
   const void* vs;
@@ -267,27 +269,55 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   const int kv = hg / p.nsub;
   const int h0 = kv * p.Gtot + (hg % p.nsub) * G;
 
+  const long long tok_base =
+      static_cast<long long>(b) * p.bstride_tok + static_cast<long long>(kv) * p.capacity;
+  // visible token range [t_lo, t_hi) of a sequence of n_local tokens and this
+  // CTA's chunks [cb, ce) of it (tiles of CPT chunks from cb, the last may be short)
+  auto range = [&](int n_local, int& t_lo, int& cb, int& ce) {
+    t_lo = 0;
+    if (p.window > 0) {
+      const int n_glob = p.n_total > 0 ? p.n_total : n_local + p.token_offset;
+      t_lo = max(0, n_glob - p.window - p.token_offset);
+    }
+    cb = ce = 0;
+    if (n_local > t_lo) {
+      cb = t_lo / kChunk + split * p.chunks_per_split;
+      ce = min((n_local + kChunk - 1) / kChunk, cb + p.chunks_per_split);
+    }
+  };
+
+  // Before waiting for the preceding kernel, warm L2 with the first tiles of
+  // the range that n_tokens (the largest sequence) gives: a prefetch reads
+  // nothing into this kernel, so data the preceding kernel still writes (the
+  // appended token) is read coherently after pdl_wait.
+  if (tid == W * 32) {
+    const int n_pf = max(0, min(p.n_tokens, p.capacity));
+    const int n_pf4 = (n_pf + 3) & ~3;  // <= capacity: rows past it are never touched
+    int lo, c0, c1;
+    range(n_pf, lo, c0, c1);
+    for (int c = c0; c < min(c1, c0 + 2 * CPT); c += CPT) {
+      const int rows = min(min(CPT, c1 - c) * kChunk, n_pf4 - c * kChunk);
+      const long long t0 = tok_base + static_cast<long long>(c) * kChunk;
+      const uint32_t cbytes = static_cast<uint32_t>(rows * (D / 2));
+      const uint32_t sbytes = static_cast<uint32_t>(rows * NG * sizeof(SB));
+      prefetch_l2(p.kq + t0 * (D / 8), cbytes);
+      prefetch_l2(p.vq + t0 * (D / 8), cbytes);
+      prefetch_l2(reinterpret_cast<const SB*>(p.ks) + t0 * NG, sbytes);
+      prefetch_l2(reinterpret_cast<const SB*>(p.kb) + t0 * NG, sbytes);
+      prefetch_l2(reinterpret_cast<const SB*>(p.vs) + t0 * NG, sbytes);
+      prefetch_l2(reinterpret_cast<const SB*>(p.vb) + t0 * NG, sbytes);
+    }
+  }
+
   pdl_wait();     // inputs of the preceding kernels are visible from here on
   pdl_trigger();  // every CTA of this grid has started: the next may launch
 
-  // ---- visible token range (local coordinates), as in decode_kernel --------
   const int n_local = max(0, min(p.seq_lens ? p.seq_lens[b] : p.n_tokens, p.capacity));
-  int t_lo = 0;
   const int t_hi = n_local;
-  if (p.window > 0) {
-    const int n_glob = p.n_total > 0 ? p.n_total : n_local + p.token_offset;
-    t_lo = max(0, n_glob - p.window - p.token_offset);
-  }
-  // this CTA's chunks [cb, ce); tiles of CPT chunks from cb (the last may be short)
-  int cb = 0, ce = 0;
-  if (t_hi > t_lo) {
-    cb = t_lo / kChunk + split * p.chunks_per_split;
-    ce = min((t_hi + kChunk - 1) / kChunk, cb + p.chunks_per_split);
-  }
+  int t_lo, cb, ce;
+  range(n_local, t_lo, cb, ce);
   const int ntiles = ce > cb ? (ce - cb + CPT - 1) / CPT : 0;
   const int r_hi = min(t_hi, ce * kChunk);  // tokens at or past r_hi are masked
-  const long long tok_base =
-      static_cast<long long>(b) * p.bstride_tok + static_cast<long long>(kv) * p.capacity;
 
   if (tid == 0) {
     for (int s = 0; s < MCfg<D>::STAGES; ++s) {
@@ -1060,6 +1090,8 @@ cudaError_t launch_decode_mma(const DecodeArgs& a, const DecodePlan& pl, cudaStr
   MParams p{};
   p.q = a.q;
   p.q_dtype = a.q_dtype;
+  p.kq = a.kq;
+  p.vq = a.vq;
   p.ks = a.ks;
   p.kb = a.kb;
   p.vs = a.vs;

@@ -126,6 +126,12 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// Bulk prefetch of [src, src + bytes) into L2 (16-byte aligned, bytes a
+// multiple of 16). Only warms the cache: it reads nothing into the kernel.
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // L2 eviction-priority policy for data that is streamed once per step.
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;

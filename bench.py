@@ -52,6 +52,9 @@ def parse():
     ap.add_argument("--context", type=int, default=32768)
     ap.add_argument("--window", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg4"],
+                    help="cfg1: config 1 decode step (default, weak scaling over GPUs); "
+                         "cfg4: config 4, one 256K-token sequence split over the GPUs")
     return ap.parse_args()
 
 
@@ -302,6 +305,146 @@ def run_ours(args, rank: int, world: int, local_rank: int):
                 layer0=layers[0])
 
 
+# ------------------------------------------------- config 4: sequence split --
+
+C4_H, C4_HKV, C4_D, C4_N = 32, 8, 256, 262144
+
+
+def run_cfg4(args, rank: int, world: int, local_rank: int):
+    """Config 4: one decode step of a 262144-token global-attention layer
+    (H=32, Hkv=8, D=256) whose int4 cache is split by sequence over the GPUs.
+    Step = append the new token on the last rank + partial decode on every
+    rank + NCCL all-gather of the fp32 (o, m, l) states + LSE merge, captured
+    in CUDA graphs. Layers rotate so every step streams its shard from HBM."""
+    import math
+
+    import torch
+    import torch.distributed as dist
+
+    import gemma4metal_b200.turboquant as tq
+    from gemma4metal_b200 import seqsplit
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(13)
+    t0, t1 = seqsplit.shard_bounds(C4_N - 1, world, rank)
+    shard_bytes = (t1 - t0) * C4_HKV * 2 * (C4_D // 2 + 4 * (C4_D // 64))
+    layers_n = max(2, math.ceil(400e6 / max(shard_bytes, 1)))
+
+    def rms_norm(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True)) * w
+
+    wq = 1 + 0.1 * torch.randn(C4_D, device=dev, generator=gen)
+    wk = 1 + 0.1 * torch.randn(C4_D, device=dev, generator=gen)
+    layers = []
+    for _ in range(layers_n):
+        sc = seqsplit.SeqSplitCache(C4_N - 1, C4_HKV, C4_D, capacity_extra=4, device=dev)
+        # every rank draws the same full-sequence chunks, quantizes its own slice
+        step_tok = 16384
+        for c0 in range(0, C4_N - 1, step_tok):
+            c1 = min(C4_N - 1, c0 + step_tok)
+            k = rms_norm(torch.randn(1, C4_HKV, c1 - c0, C4_D, device=dev, generator=gen), wk).half()
+            v = torch.randn(1, C4_HKV, c1 - c0, C4_D, device=dev, generator=gen).half()
+            a, b = max(c0, sc.t0), min(c1, sc.t1)
+            if b > a:
+                sc.cache.append(k[:, :, a - c0:b - c0], v[:, :, a - c0:b - c0], pos=a - sc.t0)
+        q = rms_norm(torch.randn(1, C4_H, C4_D, device=dev, generator=gen), wq).half()
+        kn = rms_norm(torch.randn(1, C4_HKV, 1, C4_D, device=dev, generator=gen), wk).half()
+        vn = torch.randn(1, C4_HKV, 1, C4_D, device=dev, generator=gen).half()
+        out = torch.empty(1, C4_H, C4_D, dtype=torch.float16, device=dev)
+        part = torch.empty(1, C4_H * (C4_D + 2), dtype=torch.float32, device=dev)
+        parts = torch.empty(world, 1, C4_H * (C4_D + 2), dtype=torch.float32, device=dev)
+        layers.append(dict(sc=sc, q=q, kn=kn, vn=vn, out=out, part=part, parts=parts))
+    n_local = layers[0]["sc"].n_local
+    last = rank == world - 1
+    ws = tq.workspace(dev, tq.sdpa_int4_workspace_size(1, C4_H, C4_HKV, C4_D, n_local + 1, 0))
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(Lr):
+        sc = Lr["sc"]
+        if last:  # the appended token rewrites the same slot every rotation
+            tq.quantize_append(Lr["kn"], Lr["vn"], *sc.cache.tensors(), pos=n_local, s=stream)
+        nl = n_local + (1 if last else 0)
+        tq.sdpa_int4_partial(Lr["q"], *sc.cache.tensors(), C4_H // C4_HKV, 1.0, 0, n_local=nl,
+                             token_offset=sc.t0, n_total=C4_N, part_out=Lr["part"], ws=ws, s=stream)
+        if world > 1:
+            dist.all_gather_into_tensor(Lr["parts"], Lr["part"])
+        else:
+            Lr["parts"][0].copy_(Lr["part"])
+        tq.lse_merge(Lr["parts"], C4_H, C4_D, out=Lr["out"], s=stream)
+
+    with torch.cuda.stream(stream):
+        for Lr in layers:
+            step(Lr)
+    torch.cuda.synchronize()
+    CH = 4 * layers_n
+    graph = None
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(CH):
+                    step(layers[i % layers_n])
+        graph = g
+    except Exception as e:  # NCCL capture not available: time the eager loop
+        print(f"[bench] CUDA graph capture failed ({e}); timing eagerly", file=sys.stderr)
+        torch.cuda.synchronize()
+
+    def run_steps(n):
+        with torch.cuda.stream(stream):
+            if graph is not None:
+                for _ in range(max(1, n // CH)):
+                    graph.replay()
+                return max(1, n // CH) * CH
+            for i in range(n):
+                step(layers[i % layers_n])
+            return n
+
+    clocks = Clocks(local_rank)
+    clocks.start()
+    run_steps(args.warmup)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    steps = run_steps(args.steps)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    t_ms = e0.elapsed_time(e1)
+    tt = torch.tensor([t_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t_ms = float(tt[0])
+    assert tq.device_error() == 0, "a kernel reported a device error"
+    del graph
+    torch.cuda.synchronize()
+    value = steps / (t_ms / 1000.0)
+    total_bytes = C4_N * C4_HKV * 2 * (C4_D // 2 + 4 * (C4_D // 64))
+    line = {"metric": "int4-KV decode-attention tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": steps, "warmup": args.warmup,
+            "ms_per_step": t_ms / steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded torch.randn, RMS-normalised Q/K as task configs[0])",
+            "config": {"workload": "cfg4 decode step: 262144-token global layer split by sequence, "
+                                   "append + partial decode + NCCL all-gather + LSE merge",
+                       "batch": 1, "heads": C4_H, "kv_heads": C4_HKV, "head_dim": C4_D,
+                       "context": C4_N, "layers_rotated": layers_n,
+                       "l2": f"inputs larger than L2: {layers_n} rotating shards of {shard_bytes / 1e6:.0f} MB",
+                       "parallelism": f"sequence split over {world} GPU(s)"},
+            "hbm_gbs_per_gpu": shard_bytes / (t_ms / steps * 1e-3) / 1e9,
+            "hbm_gbs_total": total_bytes / (t_ms / steps * 1e-3) / 1e9,
+            "clocks": clk}
+    return line
+
+
 # ----------------------------------------------------------- CPU reference --
 
 def cpu_reference(n_ctx: int, window: int, steps: int, warmup: int, seed: int = 5):
@@ -376,6 +519,14 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120))
+    if args.workload == "cfg4":
+        line = run_cfg4(args, rank, world, local_rank)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     res = run_ours(args, rank, world, local_rank)
     steps_total = args.steps * world
     value = steps_total / (res["t_ms"] / 1000.0)

@@ -40,8 +40,43 @@ def sources():
 def headers():
     hs = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
     inc = os.path.join(ROOT, "include")
-    hs += [os.path.join(inc, f) for f in os.listdir(inc) if f.endswith(".h")]
+    hs += [os.path.join(inc, f) for f in os.listdir(inc) if f.endswith((".h", ".hpp"))]
     return hs
+
+
+CPP_TESTS = os.path.join(ROOT, "tests", "cpp")
+
+
+def cpp_test_binary(name: str) -> str:
+    """Path of the built C++ test program tests/cpp/<name>.cpp."""
+    return os.path.join(OBJ, name + "_cpp")
+
+
+def build_cpp_tests(verbose: bool = False) -> list:
+    """Compile tests/cpp/*.cpp against the C++ API (include/turboquant.hpp) and
+    the built library; binaries go to _build/ and find the library by rpath."""
+    out = []
+    if not os.path.isdir(CPP_TESTS):
+        return out
+    for f in sorted(os.listdir(CPP_TESTS)):
+        if not f.endswith(".cpp"):
+            continue
+        src = os.path.join(CPP_TESTS, f)
+        exe = cpp_test_binary(f[:-4])
+        if os.path.exists(exe) and os.path.getmtime(exe) >= max(
+                os.path.getmtime(src), os.path.getmtime(LIB), max(os.path.getmtime(h) for h in headers())):
+            out.append(exe)
+            continue
+        cmd = [nvcc(), "-O2", "-std=c++17", "-I" + os.path.join(ROOT, "include"), src, "-o", exe,
+               "-L" + PKG, "-lturboquant_b200", "-lcudart", "-Xlinker", "-rpath=" + PKG,
+               "-Xlinker", "-rpath=$ORIGIN/.."]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"C++ test build failed for {src}:\n{r.stdout}\n{r.stderr}")
+        out.append(exe)
+    return out
 
 
 def _compile(src: str, verbose: bool, ptxas_v: bool) -> str:
@@ -79,6 +114,7 @@ def build(force: bool = False, verbose: bool = False, ptxas_v: bool = False) -> 
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
         os.replace(LIB + ".tmp", LIB)
+    build_cpp_tests(verbose)
     return LIB
 
 

@@ -1,0 +1,286 @@
+// C++ host API (include/turboquant.hpp) over the C ABI (include/turboquant_c.h):
+// the reference's turboquant:: entry points (lib/turboquant.h) with a minimal
+// ref-counted device array in place of mlx::core::array. Host code only.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <utility>
+
+#include "../../include/turboquant.hpp"
+#include "../../include/turboquant_c.h"
+
+namespace turboquant {
+
+namespace {
+
+[[noreturn]] void raise(const std::string& where, const std::string& what) {
+  throw std::runtime_error("turboquant::" + where + ": " + what);
+}
+
+void check(int rc, const char* where) {
+  if (rc != TQ_OK) raise(where, tq_last_error());
+}
+
+void check_cuda(cudaError_t e, const char* where) {
+  if (e != cudaSuccess) raise(where, cudaGetErrorString(e));
+}
+
+tq_dtype to_c(Dtype d, const char* where) {
+  switch (d) {
+    case Dtype::float32: return TQ_F32;
+    case Dtype::float16: return TQ_F16;
+    case Dtype::bfloat16: return TQ_BF16;
+    default: raise(where, "expected a float32, float16 or bfloat16 array");
+  }
+}
+
+// Per (device, stream) split-KV workspace, grown on demand and zero-filled
+// once (kernels leave its merge counters at zero). Calls on one stream are
+// ordered, so they may share it; other streams get their own.
+std::mutex g_ws_mu;
+std::map<std::pair<int, cudaStream_t>, array> g_ws;
+
+array workspace(size_t bytes, cudaStream_t s) {
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "workspace");
+  std::lock_guard<std::mutex> lock(g_ws_mu);
+  array& ws = g_ws[{dev, s}];
+  if (ws.nbytes() < bytes) {
+    const size_t n = std::max<size_t>(bytes, 1 << 20);
+    ws = array({static_cast<int>(n)}, Dtype::uint8, s);
+    check(tq_workspace_init(ws.data(), ws.nbytes(), s), "workspace");
+  }
+  return ws;
+}
+
+}  // namespace
+
+size_t itemsize(Dtype d) {
+  switch (d) {
+    case Dtype::float32: return 4;
+    case Dtype::float16: return 2;
+    case Dtype::bfloat16: return 2;
+    case Dtype::uint32: return 4;
+    case Dtype::int32: return 4;
+    case Dtype::uint8: return 1;
+  }
+  return 1;
+}
+
+// ---- array -------------------------------------------------------------------
+
+array::array(std::vector<int> shape, Dtype dtype, cudaStream_t s)
+    : shape_(std::move(shape)), dtype_(dtype) {
+  for (int d : shape_)
+    if (d < 0) raise("array", "negative dimension");
+  check_cuda(cudaGetDevice(&device_), "array");
+  const size_t bytes = nbytes();
+  if (bytes == 0) return;
+  void* p = nullptr;
+  check_cuda(cudaMallocAsync(&p, bytes, s), "array (cudaMallocAsync)");
+  ptr_ = p;
+  buf_ = std::shared_ptr<void>(p, [s](void* q) { cudaFreeAsync(q, s); });
+}
+
+array array::zeros(std::vector<int> shape, Dtype dtype, cudaStream_t s) {
+  array a(std::move(shape), dtype, s);
+  if (a.nbytes()) check_cuda(cudaMemsetAsync(a.data(), 0, a.nbytes(), s), "zeros");
+  return a;
+}
+
+array array::from_host(const void* src, std::vector<int> shape, Dtype dtype, cudaStream_t s) {
+  array a(std::move(shape), dtype, s);
+  if (a.nbytes()) {
+    check_cuda(cudaMemcpyAsync(a.data(), src, a.nbytes(), cudaMemcpyHostToDevice, s), "from_host");
+    check_cuda(cudaStreamSynchronize(s), "from_host");
+  }
+  return a;
+}
+
+void array::to_host(void* dst, cudaStream_t s) const {
+  if (!nbytes()) return;
+  check_cuda(cudaMemcpyAsync(dst, ptr_, nbytes(), cudaMemcpyDeviceToHost, s), "to_host");
+  check_cuda(cudaStreamSynchronize(s), "to_host");
+}
+
+size_t array::size() const {
+  size_t n = 1;
+  for (int d : shape_) n *= static_cast<size_t>(d);
+  return n;
+}
+
+array array::reshape(std::vector<int> shape) const {
+  array v = *this;
+  v.shape_ = std::move(shape);
+  if (v.size() != size()) raise("reshape", "element count changes");
+  return v;
+}
+
+// ---- quantizer ---------------------------------------------------------------
+
+std::vector<array> quantize(const array& w, int group_size, int bits, cudaStream_t s,
+                            Dtype scales_dtype) {
+  if (group_size != 64 || bits != 4) raise("quantize", "only group_size=64, bits=4 is implemented");
+  if (w.ndim() < 1) raise("quantize", "need at least one dimension");
+  const int D = w.shape(-1);
+  const long long rows = D ? static_cast<long long>(w.size() / D) : 0;
+  std::vector<int> cs = w.shape(), ss = w.shape();
+  cs.back() = D / 8;
+  ss.back() = D / 64;
+  array codes(cs, Dtype::uint32, s), scales(ss, scales_dtype, s), biases(ss, scales_dtype, s);
+  check(tq_quantize(w.data(), to_c(w.dtype(), "quantize"), rows, D,
+                    static_cast<uint32_t*>(codes.data()), scales.data(), biases.data(),
+                    to_c(scales_dtype, "quantize"), s),
+        "quantize");
+  return {codes, scales, biases};
+}
+
+array dequantize(const array& w, const array& scales, const array& biases, int group_size, int bits,
+                 cudaStream_t s, Dtype out_dtype) {
+  if (group_size != 64 || bits != 4) raise("dequantize", "only group_size=64, bits=4 is implemented");
+  const int D = w.shape(-1) * 8;
+  const long long rows = D ? static_cast<long long>(w.size() * 8 / D) : 0;
+  std::vector<int> os = w.shape();
+  os.back() = D;
+  array out(os, out_dtype, s);
+  check(tq_dequantize(static_cast<const uint32_t*>(w.data()), scales.data(), biases.data(),
+                      to_c(scales.dtype(), "dequantize"), rows, D, out.data(),
+                      to_c(out_dtype, "dequantize"), s),
+        "dequantize");
+  return out;
+}
+
+// ---- decode attention --------------------------------------------------------
+
+namespace {
+
+// (Hkv, N, w) cache slice -> (Hkv, cap, w) with cap = N rounded up to 4 (the
+// library's token capacity must be a multiple of 4 for 16-byte aligned rows).
+array pad_tokens(const array& a, int cap, cudaStream_t s) {
+  const int hkv = a.shape(0), n = a.shape(1), w = a.shape(2);
+  array p = array::zeros({hkv, cap, w}, a.dtype(), s);
+  const size_t row = static_cast<size_t>(w) * itemsize(a.dtype());
+  check_cuda(cudaMemcpy2DAsync(p.data(), cap * row, a.data(), n * row, n * row, hkv,
+                               cudaMemcpyDeviceToDevice, s),
+             "sdpa_int4 (pad)");
+  return p;
+}
+
+array decode(const array& q, const array* c, int batch, int hkv, int D, int n_tokens, int cap,
+             int gqa, float scale, int window, cudaStream_t s, const char* where) {
+  const int H = hkv * gqa;
+  array out({batch, H, D}, q.dtype(), s);
+  const size_t ws_bytes = tq_sdpa_int4_workspace_size(batch, H, hkv, D, n_tokens, window);
+  array ws_arr = ws_bytes ? workspace(ws_bytes, s) : array();
+  void* ws = ws_bytes ? ws_arr.data() : nullptr;
+  const size_t have = ws_bytes ? ws_arr.nbytes() : 0;
+  check(tq_sdpa_int4(q.data(), to_c(q.dtype(), where), static_cast<const uint32_t*>(c[0].data()),
+                     c[1].data(), c[2].data(), static_cast<const uint32_t*>(c[3].data()),
+                     c[4].data(), c[5].data(), to_c(c[1].dtype(), where), gqa, scale, window, batch,
+                     hkv, D, n_tokens, cap, nullptr, out.data(), to_c(q.dtype(), where), ws, have, s),
+        where);
+  return out;
+}
+
+}  // namespace
+
+array sdpa_int4(const array& queries, const array& k_quant, const array& k_scales,
+                const array& k_biases, const array& v_quant, const array& v_scales,
+                const array& v_biases, int gqa_factor, float scale, int sliding_window,
+                cudaStream_t s) {
+  if (queries.ndim() != 2 || k_quant.ndim() != 3)
+    raise("sdpa_int4", "queries must be (H, D) and the cache (Hkv, N, D/8)");
+  const int D = queries.shape(1), hkv = k_quant.shape(0), n = k_quant.shape(1);
+  if (queries.shape(0) != hkv * gqa_factor) raise("sdpa_int4", "H != Hkv * gqa_factor");
+  if (k_quant.shape(2) * 8 != D) raise("sdpa_int4", "k_quant last dim must be head_dim / 8");
+  const array* src[6] = {&k_quant, &k_scales, &k_biases, &v_quant, &v_scales, &v_biases};
+  array padded[6];
+  const int cap = (n + 3) / 4 * 4;
+  for (int i = 0; i < 6; ++i) padded[i] = cap == n ? *src[i] : pad_tokens(*src[i], cap, s);
+  array out = decode(queries, padded, 1, hkv, D, n, cap, gqa_factor, scale, sliding_window, s,
+                     "sdpa_int4");
+  return out.reshape({queries.shape(0), D});
+}
+
+void set_metallib_path(const std::string& path) { tq_set_metallib_path(path.c_str()); }
+
+// ---- KVCache -------------------------------------------------------------------
+
+KVCache::KVCache(int batch, int num_kv_heads, int head_dim, int capacity, Dtype scales_dtype,
+                 cudaStream_t s)
+    : batch_(batch), num_kv_heads_(num_kv_heads), head_dim_(head_dim), capacity_(capacity) {
+  if (capacity % 4) raise("KVCache", "capacity must be a multiple of 4");
+  if (head_dim % 64) raise("KVCache", "head_dim must be a multiple of 64");
+  k_quant = array::zeros({batch, num_kv_heads, capacity, head_dim / 8}, Dtype::uint32, s);
+  v_quant = array::zeros({batch, num_kv_heads, capacity, head_dim / 8}, Dtype::uint32, s);
+  k_scales = array::zeros({batch, num_kv_heads, capacity, head_dim / 64}, scales_dtype, s);
+  k_biases = array::zeros({batch, num_kv_heads, capacity, head_dim / 64}, scales_dtype, s);
+  v_scales = array::zeros({batch, num_kv_heads, capacity, head_dim / 64}, scales_dtype, s);
+  v_biases = array::zeros({batch, num_kv_heads, capacity, head_dim / 64}, scales_dtype, s);
+}
+
+void KVCache::append(const array& k_new, const array& v_new, cudaStream_t s) {
+  if (k_new.ndim() != 3 && k_new.ndim() != 4) raise("KVCache::append", "k_new must be 3-D or 4-D");
+  const int n_new = k_new.shape(-2);
+  if (k_new.shape(-1) != head_dim_ || k_new.size() != v_new.size() ||
+      k_new.size() != static_cast<size_t>(batch_) * num_kv_heads_ * n_new * head_dim_)
+    raise("KVCache::append", "k_new/v_new must be (B, Hkv, n_new, D)");
+  check(tq_quantize_append(k_new.data(), v_new.data(), to_c(k_new.dtype(), "KVCache::append"),
+                           batch_, num_kv_heads_, head_dim_, n_new,
+                           static_cast<uint32_t*>(k_quant.data()), k_scales.data(), k_biases.data(),
+                           static_cast<uint32_t*>(v_quant.data()), v_scales.data(), v_biases.data(),
+                           to_c(k_scales.dtype(), "KVCache::append"), capacity_, length_, nullptr, s),
+        "KVCache::append");
+  length_ += n_new;
+}
+
+array KVCache::sdpa(const array& queries, int gqa_factor, float scale, int sliding_window,
+                    cudaStream_t s) {
+  const bool flat = queries.ndim() == 2;
+  if (flat && batch_ != 1) raise("KVCache::sdpa", "(H, D) queries need batch 1");
+  const array* c[6] = {&k_quant, &k_scales, &k_biases, &v_quant, &v_scales, &v_biases};
+  array cc[6];
+  for (int i = 0; i < 6; ++i) cc[i] = *c[i];
+  array out = decode(queries, cc, batch_, num_kv_heads_, head_dim_, length_, capacity_, gqa_factor,
+                     scale, sliding_window, s, "KVCache::sdpa");
+  return flat ? out.reshape({queries.shape(0), head_dim_}) : out;
+}
+
+// ---- sequence split ---------------------------------------------------------
+
+array sdpa_int4_partial(const array& queries, const KVCache& shard, int n_local, int token_offset,
+                        int n_total, int gqa_factor, float scale, int sliding_window,
+                        cudaStream_t s) {
+  const int B = shard.k_quant.shape(0), hkv = shard.k_quant.shape(1), cap = shard.capacity();
+  const int D = shard.k_quant.shape(3) * 8, H = hkv * gqa_factor;
+  array part({B, H * (D + 2)}, Dtype::float32, s);
+  const size_t ws_bytes = tq_sdpa_int4_workspace_size(B, H, hkv, D, n_local, sliding_window);
+  array ws_arr = ws_bytes ? workspace(ws_bytes, s) : array();
+  void* ws = ws_bytes ? ws_arr.data() : nullptr;
+  const size_t have = ws_bytes ? ws_arr.nbytes() : 0;
+  check(tq_sdpa_int4_partial(queries.data(), to_c(queries.dtype(), "sdpa_int4_partial"),
+                             static_cast<const uint32_t*>(shard.k_quant.data()), shard.k_scales.data(),
+                             shard.k_biases.data(), static_cast<const uint32_t*>(shard.v_quant.data()),
+                             shard.v_scales.data(), shard.v_biases.data(),
+                             to_c(shard.k_scales.dtype(), "sdpa_int4_partial"), gqa_factor, scale,
+                             sliding_window, B, hkv, D, n_local, cap, token_offset, n_total,
+                             static_cast<float*>(part.data()), ws, have, s),
+        "sdpa_int4_partial");
+  return part;
+}
+
+array lse_merge(const array& parts, int num_heads, int head_dim, Dtype out_dtype, cudaStream_t s) {
+  if (parts.ndim() != 3) raise("lse_merge", "parts must be (P, B, H*(D+2))");
+  const int P = parts.shape(0), B = parts.shape(1);
+  array out({B, num_heads, head_dim}, out_dtype, s);
+  check(tq_lse_merge(static_cast<const float*>(parts.data()), P, B, num_heads, head_dim, out.data(),
+                     to_c(out_dtype, "lse_merge"), s),
+        "lse_merge");
+  return out;
+}
+
+}  // namespace turboquant

@@ -131,7 +131,8 @@ def quantize(x: torch.Tensor, group_size: int = 64, bits: int = 4,
     codes = torch.empty(*lead, D // 8, dtype=torch.int32, device=x.device)
     scales = torch.empty(*lead, D // 64, dtype=scales_dtype, device=x.device)
     biases = torch.empty_like(scales)
-    _check(load_library().tq_quantize(_ptr(x.contiguous()), _dt(x), rows, D, _ptr(codes),
+    xc = x.contiguous()  # kept alive until the launch is enqueued
+    _check(load_library().tq_quantize(_ptr(xc), _dt(x), rows, D, _ptr(codes),
                                       _ptr(scales), _ptr(biases), _dt(scales), _stream(s)))
     return codes, scales, biases
 
@@ -200,8 +201,11 @@ def quantize_append(k_new: torch.Tensor, v_new: torch.Tensor, k_quant, k_scales,
         k_new, v_new = k_new.unsqueeze(0), v_new.unsqueeze(0)
     B, Hkv, n_new, D = k_new.shape
     cap = k_quant.shape[-2]
+    # contiguous copies of sliced inputs must stay referenced until the launch
+    # is enqueued: a temporary freed early could hand its memory to the next one
+    kc, vc = k_new.contiguous(), v_new.contiguous()
     _check(load_library().tq_quantize_append(
-        _ptr(k_new.contiguous()), _ptr(v_new.contiguous()), _dt(k_new), B, Hkv, D, n_new,
+        _ptr(kc), _ptr(vc), _dt(k_new), B, Hkv, D, n_new,
         _ptr(k_quant), _ptr(k_scales), _ptr(k_biases), _ptr(v_quant), _ptr(v_scales),
         _ptr(v_biases), _dt(k_scales), cap, int(pos), _ptr(positions), _stream(s)))
 
@@ -257,8 +261,9 @@ def sdpa_int4(queries: torch.Tensor, k_quant: torch.Tensor, k_scales: torch.Tens
     nbytes = sdpa_int4_workspace_size(B, H, Hkv, D, n, sliding_window)
     if ws is None:
         ws = workspace(q.device, nbytes, s)
+    qc = q.contiguous()
     _check(load_library().tq_sdpa_int4(
-        _ptr(q.contiguous()), _dt(q), *[_ptr(c) for c in cache], _dt(cache[1]), int(gqa_factor),
+        _ptr(qc), _dt(q), *[_ptr(c) for c in cache], _dt(cache[1]), int(gqa_factor),
         float(scale), int(sliding_window), B, Hkv, D, n, cap, _ptr(seq_lens), _ptr(out), _dt(out),
         _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
     return out[0] if squeeze else out
@@ -284,8 +289,9 @@ def sdpa_int4_partial(queries: torch.Tensor, k_quant, k_scales, k_biases, v_quan
     nbytes = sdpa_int4_workspace_size(B, H, Hkv, D, nl, sliding_window)
     if ws is None:
         ws = workspace(q.device, nbytes, s)
+    qc = q.contiguous()
     _check(load_library().tq_sdpa_int4_partial(
-        _ptr(q.contiguous()), _dt(q), *[_ptr(c) for c in cache], _dt(cache[1]), int(gqa_factor),
+        _ptr(qc), _dt(q), *[_ptr(c) for c in cache], _dt(cache[1]), int(gqa_factor),
         float(scale), int(sliding_window), B, Hkv, D, nl, cap, int(token_offset), nt,
         _ptr(part_out), _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
     return part_out

@@ -1,0 +1,150 @@
+/*
+ * turboquant.hpp -- C++ host API of libturboquant_b200.so, the B200 backend of
+ * gemma4metal's int4 KV-cache attention path.
+ *
+ * It keeps the names, argument order, defaults and shape conventions of the
+ * reference's lib/turboquant.h (namespace turboquant, lib/turboquant.h:52-209)
+ * and of the MLX calls the engine makes around it (quantize / dequantize,
+ * engine/gemma4_multilayer.cpp:228-229,307-308), so engine code and
+ * tests/test_sdpa_int4.cpp switch backends by swapping the include:
+ *
+ *   mlx::core::array     -> turboquant::array   (device tensor, ref-counted)
+ *   StreamOrDevice s = {} -> cudaStream_t s = nullptr
+ *
+ * Differences from the reference, on purpose:
+ *   - Work is enqueued on `s` immediately (CUDA streams), not built as a lazy
+ *     graph; array::to_host() synchronises the stream.
+ *   - Errors throw std::runtime_error, as the reference's primitives do
+ *     (lib/turboquant.cpp:363-365), with the library's message.
+ *   - Outputs are allocated stream-ordered (cudaMallocAsync) on `s`, as the
+ *     reference allocates outputs inside eval_gpu (lib/turboquant.cpp:372).
+ *     The allocation-free path is the C ABI (turboquant_c.h) and KVCache.
+ *   - Attention accepts fp32, fp16 or bf16 queries and fp16 or fp32
+ *     scales/biases (the reference hard-codes fp32, lib/turboquant.metal:725-732)
+ *     and head_dim 128/256/512 (the reference: 256/512, lib/turboquant.cpp:378).
+ */
+#ifndef TURBOQUANT_HPP
+#define TURBOQUANT_HPP
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#if defined(__GNUC__)
+#define TQ_CXX_API __attribute__((visibility("default")))
+#else
+#define TQ_CXX_API
+#endif
+
+namespace turboquant {
+
+enum class Dtype : int { float32 = 0, float16 = 1, bfloat16 = 2, uint32 = 3, int32 = 4, uint8 = 5 };
+
+TQ_CXX_API size_t itemsize(Dtype d);
+
+// Dense, row-major device tensor (the subset of mlx::core::array the path
+// needs). Copies share storage; reshape() returns a view.
+class TQ_CXX_API array {
+ public:
+  array() = default;
+  // Uninitialised device memory on the current device, allocated on stream s.
+  array(std::vector<int> shape, Dtype dtype, cudaStream_t s = nullptr);
+
+  static array zeros(std::vector<int> shape, Dtype dtype, cudaStream_t s = nullptr);
+  // Copy `size() * itemsize` bytes from host memory (synchronous for the host buffer).
+  static array from_host(const void* src, std::vector<int> shape, Dtype dtype,
+                         cudaStream_t s = nullptr);
+  // Copy to host memory; synchronises s.
+  void to_host(void* dst, cudaStream_t s = nullptr) const;
+  template <typename T>
+  std::vector<T> to_vector(cudaStream_t s = nullptr) const {
+    std::vector<T> v(nbytes() / sizeof(T));
+    to_host(v.data(), s);
+    return v;
+  }
+
+  const std::vector<int>& shape() const { return shape_; }
+  int shape(int dim) const { return shape_.at(dim < 0 ? dim + ndim() : dim); }
+  int ndim() const { return static_cast<int>(shape_.size()); }
+  size_t size() const;
+  size_t nbytes() const { return size() * itemsize(dtype_); }
+  Dtype dtype() const { return dtype_; }
+  void* data() { return ptr_; }
+  const void* data() const { return ptr_; }
+  int device() const { return device_; }
+  bool valid() const { return ptr_ != nullptr || size() == 0; }
+
+  // Same storage, new shape (element count must match).
+  array reshape(std::vector<int> shape) const;
+
+ private:
+  std::shared_ptr<void> buf_;
+  void* ptr_ = nullptr;
+  std::vector<int> shape_;
+  Dtype dtype_ = Dtype::float32;
+  int device_ = 0;
+};
+
+// ---- MLX-compatible quantizer (engine/gemma4_multilayer.cpp:228-229) -------
+// Affine group-64 4-bit: returns {codes uint32 (..., D/8), scales (..., D/64),
+// biases (..., D/64)}; scales/biases fp16 unless scales_dtype says otherwise.
+TQ_CXX_API std::vector<array> quantize(const array& w, int group_size = 64, int bits = 4,
+                            cudaStream_t s = nullptr, Dtype scales_dtype = Dtype::float16);
+// value = scale * code + bias (engine/gemma4_multilayer.cpp:307-308); float32 out.
+TQ_CXX_API array dequantize(const array& w, const array& scales, const array& biases, int group_size = 64,
+                 int bits = 4, cudaStream_t s = nullptr, Dtype out_dtype = Dtype::float32);
+
+// ---- fused int4 decode attention (lib/turboquant.h:196-207) ----------------
+// queries (H, D); k_quant/v_quant (Hkv, N, D/8) uint32; scales/biases
+// (Hkv, N, D/64). Returns (H, D) in the query dtype. Query head h reads KV
+// head h / gqa_factor; sliding_window > 0 masks tokens t with
+// (N-1-t) >= sliding_window. A token count N that is not a multiple of 4 is
+// served through a padded copy of the cache (KVCache avoids it).
+TQ_CXX_API array sdpa_int4(const array& queries, const array& k_quant, const array& k_scales,
+                const array& k_biases, const array& v_quant, const array& v_scales,
+                const array& v_biases, int gqa_factor, float scale = 1.0f,
+                int sliding_window = 0, cudaStream_t s = nullptr);
+
+// No-op (lib/turboquant.h:209): kernels are linked into the library.
+TQ_CXX_API void set_metallib_path(const std::string& path);
+
+// ---- preallocated cache: quantize-on-append + decode without copies ---------
+// Replaces the engine's per-token quantize + concatenate + trim of the whole
+// cache (engine/gemma4_multilayer.cpp:228-249) with in-place appends.
+class TQ_CXX_API KVCache {
+ public:
+  KVCache(int batch, int num_kv_heads, int head_dim, int capacity,
+          Dtype scales_dtype = Dtype::float16, cudaStream_t s = nullptr);
+  // k_new, v_new: (B, Hkv, n_new, D) (or (Hkv, n_new, D) when B = 1), fp32/fp16/bf16,
+  // written at token slots [length, length + n_new).
+  void append(const array& k_new, const array& v_new, cudaStream_t s = nullptr);
+  // Decode attention over the cached tokens: queries (B, H, D) or (H, D).
+  array sdpa(const array& queries, int gqa_factor, float scale = 1.0f, int sliding_window = 0,
+             cudaStream_t s = nullptr);
+  int length() const { return length_; }
+  int capacity() const { return capacity_; }
+  void reset() { length_ = 0; }
+  array k_quant, k_scales, k_biases, v_quant, v_scales, v_biases;
+
+ private:
+  int batch_, num_kv_heads_, head_dim_, capacity_, length_ = 0;
+};
+
+// ---- sequence split across GPUs ----------------------------------------------
+// Partial softmax state of a contiguous token shard [token_offset, +n_local) of a
+// sequence of n_total tokens: (B, H*(D+2)) fp32 = o (H, D) unnormalised, then
+// (m, l) per head (natural-log max, sum of exponentials).
+TQ_CXX_API array sdpa_int4_partial(const array& queries, const KVCache& shard, int n_local, int token_offset,
+                        int n_total, int gqa_factor, float scale = 1.0f, int sliding_window = 0,
+                        cudaStream_t s = nullptr);
+// Log-sum-exp merge of P stacked partial states (P, B, H*(D+2)) -> (B, H, D).
+TQ_CXX_API array lse_merge(const array& parts, int num_heads, int head_dim, Dtype out_dtype = Dtype::float32,
+                cudaStream_t s = nullptr);
+
+}  // namespace turboquant
+
+#endif  // TURBOQUANT_HPP

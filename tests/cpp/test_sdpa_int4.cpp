@@ -1,0 +1,176 @@
+// C++ parity test of the turboquant.hpp API, mirroring the reference's
+// tests/test_sdpa_int4.cpp (same shape nh=16, nkv=16, N=10, hd=256, gqa=1,
+// scale 1, fp32 queries; same flow: quantize K/V, reference = dequantize +
+// SDPA, fused = turboquant::sdpa_int4) with seeded inputs and the task's
+// tolerance (max-abs 2e-3, cosine >= 0.99999 against an fp64 SDPA) instead of
+// the reference's unseeded draw and 0.1 bound (tests/test_sdpa_int4.cpp:20-22,77).
+// Also runs the preallocated-cache path (KVCache append + sdpa, D=128, GQA 2,
+// sliding window) and the sequence-split path (sdpa_int4_partial + lse_merge).
+// Exit code 0 = pass.
+#include <cmath>
+#include <cstdio>
+#include <random>
+#include <vector>
+
+#include "turboquant.hpp"
+
+using turboquant::array;
+using turboquant::Dtype;
+
+namespace {
+
+std::vector<float> normal(size_t n, std::mt19937& rng) {
+  std::normal_distribution<float> nd(0.0f, 1.0f);
+  std::vector<float> v(n);
+  for (auto& x : v) x = nd(rng);
+  return v;
+}
+
+// out[h] = softmax(scale * q_h . k_t) . v_t over visible t (fp64), kv = h / gqa
+std::vector<double> sdpa_ref(const std::vector<float>& q, const std::vector<float>& k,
+                             const std::vector<float>& v, int nh, int nkv, int n, int hd,
+                             float scale, int window) {
+  const int gqa = nh / nkv;
+  std::vector<double> out(static_cast<size_t>(nh) * hd, 0.0);
+  for (int h = 0; h < nh; ++h) {
+    const int kv = h / gqa;
+    std::vector<double> sc(n);
+    double m = -INFINITY;
+    for (int t = 0; t < n; ++t) {
+      if (window > 0 && (n - 1 - t) >= window) { sc[t] = -INFINITY; continue; }
+      double a = 0;
+      for (int d = 0; d < hd; ++d)
+        a += static_cast<double>(q[h * hd + d]) * k[(static_cast<size_t>(kv) * n + t) * hd + d];
+      sc[t] = a * scale;
+      m = std::max(m, sc[t]);
+    }
+    double l = 0;
+    for (int t = 0; t < n; ++t) {
+      const double p = std::isinf(sc[t]) ? 0.0 : std::exp(sc[t] - m);
+      l += p;
+      for (int d = 0; d < hd; ++d) out[h * hd + d] += p * v[(static_cast<size_t>(kv) * n + t) * hd + d];
+    }
+    for (int d = 0; d < hd; ++d) out[h * hd + d] /= l;
+  }
+  return out;
+}
+
+bool compare(const char* name, const std::vector<float>& got, const std::vector<double>& ref) {
+  double max_err = 0, dot = 0, ng = 0, nr = 0, mean = 0;
+  for (size_t i = 0; i < got.size(); ++i) {
+    const double e = std::fabs(got[i] - ref[i]);
+    max_err = std::max(max_err, e);
+    mean += e;
+    dot += got[i] * ref[i];
+    ng += static_cast<double>(got[i]) * got[i];
+    nr += ref[i] * ref[i];
+  }
+  const double cos = dot / std::sqrt(ng * nr);
+  const bool pass = max_err <= 2e-3 && cos >= 0.99999;
+  printf("%-28s max_err=%.3e mean_err=%.3e cos=%.8f %s\n", name, max_err, mean / got.size(), cos,
+         pass ? "PASS" : "FAIL");
+  return pass;
+}
+
+std::vector<float> f16_to_f32(const std::vector<uint16_t>& h) {
+  std::vector<float> f(h.size());
+  for (size_t i = 0; i < h.size(); ++i) {
+    const uint32_t s = (h[i] & 0x8000u) << 16, e = (h[i] >> 10) & 0x1F, m = h[i] & 0x3FF;
+    float v;
+    if (e == 0) v = std::ldexp(static_cast<float>(m), -24);
+    else if (e == 31) v = m ? NAN : INFINITY;
+    else v = std::ldexp(static_cast<float>(m | 0x400), static_cast<int>(e) - 25);
+    f[i] = s ? -v : v;
+  }
+  return f;
+}
+
+}  // namespace
+
+int main() {
+  turboquant::set_metallib_path("unused");
+  bool ok = true;
+
+  {  // the reference test's shape (tests/test_sdpa_int4.cpp:13-16)
+    const int nh = 16, nkv = 16, N = 10, hd = 256, gqa = nh / nkv;
+    const float scale = 1.0f;
+    printf("Testing sdpa_int4: nh=%d nkv=%d N=%d hd=%d gqa=%d\n", nh, nkv, N, hd, gqa);
+    std::mt19937 rng(0);
+    auto Qh = normal(static_cast<size_t>(nh) * hd, rng);
+    auto Kh = normal(static_cast<size_t>(nkv) * N * hd, rng);
+    auto Vh = normal(static_cast<size_t>(nkv) * N * hd, rng);
+    auto Q = array::from_host(Qh.data(), {nh, hd}, Dtype::float32);
+    auto K = array::from_host(Kh.data(), {nkv, N, hd}, Dtype::float32);
+    auto V = array::from_host(Vh.data(), {nkv, N, hd}, Dtype::float32);
+    auto kqv = turboquant::quantize(K, 64, 4);
+    auto vqv = turboquant::quantize(V, 64, 4);
+    auto Kd = turboquant::dequantize(kqv[0], kqv[1], kqv[2], 64, 4).to_vector<float>();
+    auto Vd = turboquant::dequantize(vqv[0], vqv[1], vqv[2], 64, 4).to_vector<float>();
+    auto ref = sdpa_ref(Qh, Kd, Vd, nh, nkv, N, hd, scale, 0);
+    auto fused = turboquant::sdpa_int4(Q, kqv[0], kqv[1], kqv[2], vqv[0], vqv[1], vqv[2], gqa, scale, 0);
+    if (fused.shape(0) != nh || fused.shape(1) != hd) { printf("bad output shape\n"); return 1; }
+    ok &= compare("reference shape (fp32)", fused.to_vector<float>(), ref);
+  }
+
+  {  // preallocated cache, D=128, GQA 2, appends in two chunks, sliding window
+    const int nh = 32, nkv = 16, hd = 128, n0 = 700, n1 = 1, cap = 1024, win = 512;
+    std::mt19937 rng(1);
+    auto Qh = normal(static_cast<size_t>(nh) * hd, rng);
+    auto K0 = normal(static_cast<size_t>(nkv) * n0 * hd, rng), V0 = normal(K0.size(), rng);
+    auto K1 = normal(static_cast<size_t>(nkv) * n1 * hd, rng), V1 = normal(K1.size(), rng);
+    turboquant::KVCache cache(1, nkv, hd, cap);
+    cache.append(array::from_host(K0.data(), {1, nkv, n0, hd}, Dtype::float32),
+                 array::from_host(V0.data(), {1, nkv, n0, hd}, Dtype::float32));
+    cache.append(array::from_host(K1.data(), {1, nkv, n1, hd}, Dtype::float32),
+                 array::from_host(V1.data(), {1, nkv, n1, hd}, Dtype::float32));
+    const int n = cache.length();
+    // dequantized cache rows [0, n) on the host
+    auto kd_all = turboquant::dequantize(cache.k_quant, cache.k_scales, cache.k_biases).to_vector<float>();
+    auto vd_all = turboquant::dequantize(cache.v_quant, cache.v_scales, cache.v_biases).to_vector<float>();
+    std::vector<float> kd(static_cast<size_t>(nkv) * n * hd), vd(kd.size());
+    for (int h = 0; h < nkv; ++h)
+      for (int t = 0; t < n; ++t)
+        for (int d = 0; d < hd; ++d) {
+          kd[(static_cast<size_t>(h) * n + t) * hd + d] = kd_all[(static_cast<size_t>(h) * cap + t) * hd + d];
+          vd[(static_cast<size_t>(h) * n + t) * hd + d] = vd_all[(static_cast<size_t>(h) * cap + t) * hd + d];
+        }
+    auto Q = array::from_host(Qh.data(), {nh, hd}, Dtype::float32);
+    for (int w : {0, win}) {
+      auto ref = sdpa_ref(Qh, kd, vd, nh, nkv, n, hd, 1.0f, w);
+      auto got = cache.sdpa(Q, nh / nkv, 1.0f, w).to_vector<float>();
+      ok &= compare(w ? "KVCache sliding 512" : "KVCache global", got, ref);
+    }
+    // sequence split in 3 shards of one cache
+    const int cuts[4] = {0, 300, 520, n};
+    std::vector<array> parts;
+    for (int i = 0; i < 3; ++i) {
+      turboquant::KVCache shard(1, nkv, hd, 512);
+      std::vector<float> ks(static_cast<size_t>(nkv) * (cuts[i + 1] - cuts[i]) * hd), vs(ks.size());
+      const int m = cuts[i + 1] - cuts[i];
+      for (int h = 0; h < nkv; ++h)
+        for (int t = 0; t < m; ++t)
+          for (int d = 0; d < hd; ++d) {
+            const size_t dst = (static_cast<size_t>(h) * m + t) * hd + d;
+            const bool first = cuts[i] + t < n0;
+            const size_t s1 = (static_cast<size_t>(h) * n1 + (cuts[i] + t - n0)) * hd + d;
+            const size_t s0 = (static_cast<size_t>(h) * n0 + cuts[i] + t) * hd + d;
+            ks[dst] = first ? K0[s0] : K1[s1];
+            vs[dst] = first ? V0[s0] : V1[s1];
+          }
+      shard.append(array::from_host(ks.data(), {1, nkv, m, hd}, Dtype::float32),
+                   array::from_host(vs.data(), {1, nkv, m, hd}, Dtype::float32));
+      parts.push_back(turboquant::sdpa_int4_partial(Q, shard, m, cuts[i], n, nh / nkv, 1.0f, 0));
+    }
+    const int stride = nh * (hd + 2);
+    array stacked({3, 1, stride}, Dtype::float32);
+    for (int i = 0; i < 3; ++i)
+      cudaMemcpy(static_cast<float*>(stacked.data()) + static_cast<size_t>(i) * stride,
+                 parts[i].data(), stride * sizeof(float), cudaMemcpyDeviceToDevice);
+    auto merged = turboquant::lse_merge(stacked, nh, hd, Dtype::float16);
+    auto ref = sdpa_ref(Qh, kd, vd, nh, nkv, n, hd, 1.0f, 0);
+    ok &= compare("3-shard partial + merge", f16_to_f32(merged.to_vector<uint16_t>()), ref);
+  }
+
+  printf("\n%s\n", ok ? "PASS" : "FAIL");
+  return ok ? 0 : 1;
+}

@@ -106,6 +106,22 @@ def test_quantize_append_bitexact_and_in_place():
         assert np.all(got[bb][:, ~w] == 0)  # untouched slots stay as allocated
 
 
+def test_quantize_append_noncontiguous_slices():
+    # token slices of a (B, Hkv, N, D) tensor are not contiguous: the host
+    # wrapper copies them and must keep both copies alive until the launch
+    B, Hkv, D, N = 1, 8, 256, 300
+    L = inputs.make_layer(6, 16, Hkv, D, N)
+    k, v = dev(L["k"]), dev(L["v"])
+    cache = tq.KVCache(B, Hkv, D, 128)
+    cache.append(k[:, :, 100:200], v[:, :, 100:200], pos=0)
+    torch.cuda.synchronize()
+    rk = O.quantize(L["k"][:, :, 100:200])
+    rv = O.quantize(L["v"][:, :, 100:200])
+    assert np.array_equal(host(cache.k_quant)[:, :, :100], rk[0])
+    assert np.array_equal(host(cache.v_quant)[:, :, :100], rv[0])
+    assert np.array_equal(host(cache.v_scales)[:, :, :100].view(np.uint16), rv[1].view(np.uint16))
+
+
 # ------------------------------------------------------------------ decode --
 
 @pytest.fixture(params=["mma", "simt"])

@@ -1,0 +1,651 @@
+// PolarQuant + QJL compressed keys on sm_100a: encode, decode, QJL signs, and
+// compressed-key attention (scores only, or softmax . int4 V) with GQA and
+// split-KV. Reference: lib/turboquant.metal:8-224 (encode, decode, sequential
+// compressed SDPA), :424-499 (compressed scores), :501-704 (packed formats and
+// cos/sin tables), generalised from 16-value blocks / 4 levels to blocks of
+// 2^L values (16..128; 128 = the 7 levels of the task's config 3). QJL
+// (residual sign sketch) follows its paper; the reference has no code for it.
+//
+// Numerics shared with the CPU oracle so that angle indices, radii and QJL
+// sign bits are bit-identical: the polynomial atan2 below, IEEE sqrt and
+// division, explicit fmaf in a fixed order for every quantity that feeds an
+// index or a sign, and cos/sin tables of the codebook entries computed on the
+// host in double and rounded to fp32.
+#include <cmath>
+#include <cstdio>
+
+#include "../../include/turboquant_c.h"
+#include "tq_common.cuh"
+#include "tq_internal.h"
+
+namespace tq {
+namespace {
+
+constexpr int kCB = 16;         // codebook entries per level (4-bit indices)
+constexpr int kMaxLevels = 7;   // blocks of up to 128 values
+
+struct PolarTables {
+  float cb[kMaxLevels][kCB];        // angle codebooks, level 1 first
+  float cs[kMaxLevels][kCB][2];     // (cos, sin) of the entries
+  int n[kMaxLevels];                // entries used per level
+};
+
+__device__ __forceinline__ float polar_atan2(float y, float x) {
+  // odd degree-17 polynomial for atan on [0, 1] (fit: least squares on
+  // Chebyshev nodes, reweighted towards minimax; max error 9.6e-8 rad)
+  const float ax = fabsf(x), ay = fabsf(y);
+  const float mx = fmaxf(ax, ay), mn = fminf(ax, ay);
+  if (mx == 0.0f) return 0.0f;
+  const float t = __fdiv_rn(mn, mx);
+  const float s = __fmul_rn(t, t);
+  float p = 0.0024567244108766317f;
+  p = fmaf(p, s, -0.014401360414922237f);
+  p = fmaf(p, s, 0.03978123515844345f);
+  p = fmaf(p, s, -0.07234859466552734f);
+  p = fmaf(p, s, 0.10498947650194168f);
+  p = fmaf(p, s, -0.14161230623722076f);
+  p = fmaf(p, s, 0.19985906779766083f);
+  p = fmaf(p, s, -0.33332598209381104f);
+  p = fmaf(p, s, 0.9999998807907104f);
+  float a = __fmul_rn(p, t);
+  if (ay > ax) a = __fsub_rn(1.5707963705062866f, a);
+  if (x < 0.0f) a = __fsub_rn(3.1415927410125732f, a);
+  if (y < 0.0f) a = -a;
+  return a;
+}
+
+__device__ __forceinline__ int nearest(float ang, const float* cb, int n) {
+  float best = 1e10f;
+  int id = 0;
+  for (int c = 0; c < n; ++c) {
+    const float d = fabsf(__fsub_rn(ang, cb[c]));
+    if (d < best) {
+      best = d;
+      id = c;
+    }
+  }
+  return id;
+}
+
+__host__ __device__ constexpr int level_off(int block, int L) {
+  int off = 0;
+  for (int l = 1; l < L; ++l) off += block >> l;
+  return off;
+}
+
+// ---- encode: one warp per 128 consecutive values; lane l holds 4 values ------
+// Levels 1 and 2 stay in the lane; level L >= 3 pairs lane l with lane
+// l + 2^(L-3) inside the block (lanes l with l % 2^(L-2) == 0 compute).
+__global__ void __launch_bounds__(128) polar_encode_kernel(const float* __restrict__ y,
+                                                           long long groups, int block,
+                                                           PolarTables T, uint8_t* angles,
+                                                           uint8_t* packed, __half* radii) {
+  __shared__ uint8_t s_idx[4][128];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int levels = 31 - __clz(block);
+  const int lpb = block / 4;            // lanes per block
+  const int ll = lane % lpb;            // lane inside its block
+  const int kb = lane / lpb;            // block inside the 128 values
+  for (long long g = static_cast<long long>(blockIdx.x) * 4 + w; g < groups;
+       g += static_cast<long long>(gridDim.x) * 4) {
+    const float4 v = reinterpret_cast<const float4*>(y + g * 128)[lane];
+    uint8_t* si = s_idx[w] + kb * block;  // this block's angles, level-major
+    // level 1: pairs (v.x, v.y), (v.z, v.w) = level-1 nodes 2ll, 2ll + 1
+    float r1a, r1b;
+    {
+      float a0 = polar_atan2(v.y, v.x);
+      if (a0 < 0.0f) a0 = __fadd_rn(a0, 6.2831854820251465f);
+      float a1 = polar_atan2(v.w, v.z);
+      if (a1 < 0.0f) a1 = __fadd_rn(a1, 6.2831854820251465f);
+      si[2 * ll] = static_cast<uint8_t>(nearest(a0, T.cb[0], T.n[0]));
+      si[2 * ll + 1] = static_cast<uint8_t>(nearest(a1, T.cb[0], T.n[0]));
+      r1a = __fsqrt_rn(fmaf(v.x, v.x, __fmul_rn(v.y, v.y)));
+      r1b = __fsqrt_rn(fmaf(v.z, v.z, __fmul_rn(v.w, v.w)));
+    }
+    // level 2: node ll from (r1a, r1b)
+    float r = r1a;
+    if (levels >= 2) {
+      const float a = polar_atan2(r1b, r1a);
+      si[level_off(block, 2) + ll] = static_cast<uint8_t>(nearest(a, T.cb[1], T.n[1]));
+      r = __fsqrt_rn(fmaf(r1a, r1a, __fmul_rn(r1b, r1b)));
+    }
+    for (int L = 3; L <= levels; ++L) {
+      const int step = 1 << (L - 3);
+      const float other = __shfl_down_sync(0xffffffffu, r, step);
+      if ((ll & ((step << 1) - 1)) == 0) {
+        const float a = polar_atan2(other, r);
+        si[level_off(block, L) + (ll >> (L - 2))] =
+            static_cast<uint8_t>(nearest(a, T.cb[L - 1], T.n[L - 1]));
+        r = __fsqrt_rn(fmaf(r, r, __fmul_rn(other, other)));
+      }
+    }
+    if (ll == 0) radii[g * (128 / block) + kb] = __float2half_rn(r);
+    __syncwarp();
+    const long long blk0 = g * (128 / block);
+    if (angles) {
+      for (int i = lane; i < 128; i += 32) {
+        const int b = i / block, j = i % block;
+        if (j < block - 1) angles[(blk0 + b) * (block - 1) + j] = s_idx[w][b * block + j];
+      }
+    }
+    if (packed) {
+      for (int i = lane; i < 64; i += 32) {
+        const int b = (2 * i) / block, j = (2 * i) % block;  // angles j, j+1 of block b
+        const int lo = s_idx[w][b * block + j];
+        const int hi = (j + 1 < block - 1) ? s_idx[w][b * block + j + 1] : 0;
+        packed[(blk0 + b) * (block / 2) + j / 2] = static_cast<uint8_t>((lo & 15) | ((hi & 15) << 4));
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// Angle index i of a block from the packed bytes (4-bit, low nibble first).
+__device__ __forceinline__ int packed_idx(const uint8_t* pk, int i) {
+  return (pk[i >> 1] >> (4 * (i & 1))) & 15;
+}
+
+// Values 4ll .. 4ll+3 of a block of `block` values: top-down products
+// radius * e_top * ... * e_1 in the same order as the oracle's decode.
+template <typename IdxFn>
+__device__ __forceinline__ float4 decode4(IdxFn idx, float radius, int block, int ll,
+                                          const float (*cs)[kCB][2]) {
+  const int levels = 31 - __clz(block);
+  float x = radius;
+  for (int L = levels; L >= 3; --L) {
+    const int node = ll >> (L - 2);             // this lane's node at level L
+    const int child = (ll >> (L - 3)) & 1;      // which child the lane descends into
+    const int i = idx(level_off(block, L) + node);
+    x = __fmul_rn(x, cs[L - 1][i][child]);
+  }
+  float xa = x, xb = 0.0f;
+  if (levels >= 2) {
+    const int i = idx(level_off(block, 2) + ll);
+    xa = __fmul_rn(x, cs[1][i][0]);
+    xb = __fmul_rn(x, cs[1][i][1]);
+  }
+  const int ia = idx(2 * ll), ib = idx(2 * ll + 1);
+  return make_float4(__fmul_rn(xa, cs[0][ia][0]), __fmul_rn(xa, cs[0][ia][1]),
+                     __fmul_rn(xb, cs[0][ib][0]), __fmul_rn(xb, cs[0][ib][1]));
+}
+
+__global__ void __launch_bounds__(128) polar_decode_kernel(const uint8_t* angles,
+                                                           const uint8_t* packed,
+                                                           const __half* radii, long long groups,
+                                                           int block, PolarTables T, float* y) {
+  __shared__ float s_cs[kMaxLevels][kCB][2];
+  for (int i = threadIdx.x; i < kMaxLevels * kCB * 2; i += blockDim.x)
+    (&s_cs[0][0][0])[i] = (&T.cs[0][0][0])[i];
+  __syncthreads();
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int lpb = block / 4, ll = lane % lpb, kb = lane / lpb;
+  for (long long g = static_cast<long long>(blockIdx.x) * 4 + w; g < groups;
+       g += static_cast<long long>(gridDim.x) * 4) {
+    const long long b = g * (128 / block) + kb;
+    const float rad = __half2float(radii[b]);
+    float4 out;
+    if (angles) {
+      const uint8_t* a = angles + b * (block - 1);
+      out = decode4([&](int i) { return static_cast<int>(a[i]); }, rad, block, ll, s_cs);
+    } else {
+      const uint8_t* pk = packed + b * (block / 2);
+      out = decode4([&](int i) { return packed_idx(pk, i); }, rad, block, ll, s_cs);
+    }
+    reinterpret_cast<float4*>(y + g * 128)[lane] = out;
+  }
+}
+
+// ---- QJL: r = y - yhat, signs of S r (m rows), |r| -------------------------------
+// One CTA per key row; thread i computes (S r)_i as a sequential fmaf sum over
+// j = 0..D-1 (the oracle's order), warp ballots pack the sign bits.
+__global__ void __launch_bounds__(256) qjl_encode_kernel(const float* __restrict__ y,
+                                                         const float* __restrict__ yhat,
+                                                         long long rows, int D,
+                                                         const float* __restrict__ S, int m,
+                                                         uint32_t* signs, __half* rnorm) {
+  extern __shared__ float s_r[];
+  for (long long n = blockIdx.x; n < rows; n += gridDim.x) {
+    for (int j = threadIdx.x; j < D; j += blockDim.x)
+      s_r[j] = __fsub_rn(y[n * D + j], yhat[n * D + j]);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float nn = 0.0f;
+      for (int j = 0; j < D; ++j) nn = fmaf(s_r[j], s_r[j], nn);
+      rnorm[n] = __float2half_rn(__fsqrt_rn(nn));
+    }
+    for (int i0 = 0; i0 < m; i0 += blockDim.x) {
+      const int i = i0 + threadIdx.x;
+      float acc = 0.0f;
+      if (i < m) {
+        const float* Si = S + static_cast<long long>(i) * D;
+        for (int j = 0; j < D; ++j) acc = fmaf(Si[j], s_r[j], acc);
+      }
+      const unsigned bits = __ballot_sync(0xffffffffu, i < m && acc >= 0.0f);
+      if ((threadIdx.x & 31) == 0 && i < m) signs[n * (m / 32) + i / 32] = bits;
+    }
+    __syncthreads();
+  }
+}
+
+// ---- compressed-key attention ----------------------------------------------------
+// grid = (splits, Hkv); 4 warps. Each warp takes keys of its split's range in
+// turn; lane l decodes values 4l..4l+3 of each 128-value group (DPL = D/128
+// groups), forms the partial dot products with the G query heads plus its 8
+// QJL sign terms, a warp sum gives the scores; softmax . int4 V (lane l owns
+// dims 4l..4l+3 of every group) or the scores themselves are the output.
+struct CParams {
+  const void* q;
+  int q_dtype;
+  const uint8_t* packed;  // (Hkv, N, D/block, block/2)
+  const __half* radii;    // (Hkv, N, D/block)
+  const uint32_t* signs;  // (Hkv, N, m/32) or null
+  const __half* rnorm;    // (Hkv, N)
+  const float* S;         // (m, D)
+  int m;
+  const uint32_t* vq;     // (Hkv, N, D/8)
+  int attend;             // 1: softmax . V into out; 0: scores only
+  const void* vs;
+  const void* vb;
+  int sb_f32;
+  int H, Hkv, N, block;
+  float scale;            // natural-log scale of the scores
+  int keys_per_split;
+  float* scores;          // (H, N) when scores-only
+  void* out;              // (H, D)
+  int out_dtype;
+  float* ws;              // split partials: (Hkv, splits, 4 warps, G, D + 2)
+  unsigned* counters;     // Hkv tickets
+  int splits;
+};
+
+template <int D, int G>
+__global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p, const PolarTables T) {
+  constexpr int DPL = D / 128;      // 128-value groups per key
+  __shared__ float s_cs[kMaxLevels][kCB][2];
+  __shared__ float s_sq[G][256];    // S q per head (m <= 256)
+  __shared__ float s_q[G][D];
+  __shared__ int s_last;
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int split = blockIdx.x, kv = blockIdx.y;
+  const int h0 = kv * G;
+  pdl_wait();
+  pdl_trigger();
+  for (int i = tid; i < kMaxLevels * kCB * 2; i += 128) (&s_cs[0][0][0])[i] = (&T.cs[0][0][0])[i];
+  for (int i = tid; i < G * D; i += 128) s_q[i / D][i % D] = load_as_float(p.q, static_cast<long long>(h0) * D + i, p.q_dtype);
+  __syncthreads();
+  const bool qjl = p.signs != nullptr;
+  if (qjl)
+    for (int i = tid; i < G * p.m; i += 128) {
+      const int g = i / p.m, r = i % p.m;
+      float a = 0.0f;
+      for (int j = 0; j < D; ++j) a = fmaf(p.S[static_cast<long long>(r) * D + j], s_q[g][j], a);
+      s_sq[g][r] = a;
+    }
+  __syncthreads();
+  const float qjl_c = 1.2533141373155003f / static_cast<float>(p.m > 0 ? p.m : 1);  // sqrt(pi/2)/m
+
+  // this lane's query values and QJL terms
+  float qv[G][DPL][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int c = 0; c < DPL; ++c)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) qv[g][c][e] = s_q[g][c * 128 + 4 * lane + e];
+  const int block = p.block, lpb = block / 4, ll = lane % lpb, kb = lane / lpb;
+  const int nbk = D / block;  // blocks per key
+
+  float m_run[G], l_run[G], o[G][DPL][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m_run[g] = -INFINITY;
+    l_run[g] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < DPL; ++c)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o[g][c][e] = 0.0f;
+  }
+
+  const int t_begin = split * p.keys_per_split;
+  const int t_end = min(p.N, t_begin + p.keys_per_split);
+  for (int t = t_begin + w; t < t_end; t += 4) {
+    const long long row = static_cast<long long>(kv) * p.N + t;
+    float part[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) part[g] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) {
+      const long long b = row * nbk + c * (128 / block) + kb;
+      const uint8_t* pk = p.packed + b * (block / 2);
+      const float4 kv4 = decode4([&](int i) { return packed_idx(pk, i); },
+                                 __half2float(p.radii[b]), block, ll, s_cs);
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+        part[g] += qv[g][c][0] * kv4.x + qv[g][c][1] * kv4.y + qv[g][c][2] * kv4.z +
+                   qv[g][c][3] * kv4.w;
+    }
+    if (qjl) {
+      // lane l owns sign bits [l*m/32, (l+1)*m/32)
+      const int per = p.m / 32;
+      const uint32_t* sg = p.signs + row * (p.m / 32);
+      const float rn = __half2float(p.rnorm[row]) * qjl_c;
+      for (int i = lane * per; i < (lane + 1) * per; ++i) {
+        const bool bit = (sg[i >> 5] >> (i & 31)) & 1u;
+#pragma unroll
+        for (int g = 0; g < G; ++g) part[g] += rn * (bit ? s_sq[g][i] : -s_sq[g][i]);
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
+      part[g] *= p.scale;
+    }
+    if (!p.attend) {  // scores only
+      if (lane < G) {
+        float v = part[0];
+#pragma unroll
+        for (int g = 1; g < G; ++g) v = (lane == g) ? part[g] : v;
+        p.scores[static_cast<long long>(h0 + lane) * p.N + t] = v;
+      }
+      continue;
+    }
+    // online softmax (natural log) and V accumulation
+    const uint32_t* vw = p.vq + row * (D / 8);
+#pragma unroll
+    for (int c = 0; c < DPL; ++c) {
+      const int d0 = c * 128 + 4 * lane;
+      const uint32_t word = vw[d0 / 8];
+      const int sh = 4 * (d0 % 8);
+      const long long gi = row * (D / 64) + d0 / 64;
+      const float sc = p.sb_f32 ? reinterpret_cast<const float*>(p.vs)[gi]
+                                : __half2float(reinterpret_cast<const __half*>(p.vs)[gi]);
+      const float bi = p.sb_f32 ? reinterpret_cast<const float*>(p.vb)[gi]
+                                : __half2float(reinterpret_cast<const __half*>(p.vb)[gi]);
+      float vv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) vv[e] = fmaf(sc, static_cast<float>((word >> (sh + 4 * e)) & 15u), bi);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        if (c == 0) {
+          const float mn = fmaxf(m_run[g], part[g]);
+          const float a = (m_run[g] == -INFINITY) ? 0.0f : __expf(m_run[g] - mn);
+          const float pe = __expf(part[g] - mn);
+          l_run[g] = l_run[g] * a + pe;
+          m_run[g] = mn;
+#pragma unroll
+          for (int cc = 0; cc < DPL; ++cc)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) o[g][cc][e] *= a;
+          part[g] = pe;  // reuse as this key's weight
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[g][c][e] = fmaf(part[g], vv[e], o[g][c][e]);
+      }
+    }
+  }
+  if (!p.attend) return;
+
+  // ---- per-warp partial (m, l, o) -> workspace; last CTA of the KV head merges
+  float* wsp = p.ws + ((static_cast<long long>(kv) * p.splits + split) * 4 + w) * G * (D + 2);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+#pragma unroll
+    for (int c = 0; c < DPL; ++c)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) wsp[g * (D + 2) + c * 128 + 4 * lane + e] = o[g][c][e];
+    if (lane == 0) {
+      wsp[g * (D + 2) + D] = m_run[g];
+      wsp[g * (D + 2) + D + 1] = l_run[g];
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned prev = atomic_add_acq_rel(&p.counters[kv], 1u);
+    s_last = prev == static_cast<unsigned>(p.splits - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  const int parts = p.splits * 4;
+  const float* base = p.ws + static_cast<long long>(kv) * parts * G * (D + 2);
+  for (int i = tid; i < G * D; i += 128) {
+    const int g = i / D, d = i % D;
+    float M = -INFINITY;
+    for (int s = 0; s < parts; ++s) M = fmaxf(M, __ldcg(base + (s * G + g) * (D + 2) + D));
+    float L = 0.0f, acc = 0.0f;
+    for (int s = 0; s < parts; ++s) {
+      const float* ps = base + (s * G + g) * (D + 2);
+      const float ms = __ldcg(ps + D);
+      const float e = (ms == -INFINITY) ? 0.0f : __expf(ms - M);
+      L = fmaf(e, __ldcg(ps + D + 1), L);
+      acc = fmaf(e, __ldcg(ps + d), acc);
+    }
+    store_from_float(p.out, static_cast<long long>(h0 + g) * D + d, p.out_dtype,
+                     L > 0.0f ? acc / L : 0.0f);
+  }
+  if (tid == 0) p.counters[kv] = 0u;
+}
+
+template <int D>
+void* pick_cattn(int G) {
+  switch (G) {
+    case 1: return reinterpret_cast<void*>(compressed_attn_kernel<D, 1>);
+    case 2: return reinterpret_cast<void*>(compressed_attn_kernel<D, 2>);
+    case 4: return reinterpret_cast<void*>(compressed_attn_kernel<D, 4>);
+    case 8: return reinterpret_cast<void*>(compressed_attn_kernel<D, 8>);
+  }
+  return nullptr;
+}
+
+bool make_tables(const float* codebooks, const int* cb_sizes, int levels, PolarTables* T) {
+  *T = PolarTables{};
+  for (int l = 0; l < levels; ++l) {
+    const int n = cb_sizes ? cb_sizes[l] : kCB;
+    if (n < 1 || n > kCB) return false;
+    T->n[l] = n;
+    for (int c = 0; c < kCB; ++c) {
+      const float th = codebooks[l * kCB + c];
+      T->cb[l][c] = th;
+      T->cs[l][c][0] = static_cast<float>(std::cos(static_cast<double>(th)));
+      T->cs[l][c][1] = static_cast<float>(std::sin(static_cast<double>(th)));
+    }
+  }
+  return true;
+}
+
+int levels_of(int block) {
+  int l = 0;
+  while ((1 << l) < block) ++l;
+  return l;
+}
+
+bool valid_block(int block, int D) {
+  return (block == 16 || block == 32 || block == 64 || block == 128) && D % 128 == 0;
+}
+
+int grid_for(long long groups) {
+  const long long ctas = (groups + 3) / 4;
+  return static_cast<int>(ctas < 4096 ? (ctas > 0 ? ctas : 1) : 4096);
+}
+
+int err(int code, const char* msg) {
+  set_last_error("%s", msg);
+  return code;
+}
+
+int cuda_err(cudaError_t e, const char* where) {
+  set_last_error("%s: %s", where, cudaGetErrorString(e));
+  return TQ_ERR_CUDA;
+}
+
+constexpr int kCSplitsMax = 64;
+
+int csplits(int Hkv, int N) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int target = device_sm_count(dev) * 4;  // 4 CTAs of 128 threads per SM
+  int s = target / (Hkv > 0 ? Hkv : 1);
+  s = s < 1 ? 1 : (s > kCSplitsMax ? kCSplitsMax : s);
+  const int per = (N + s - 1) / (s > 0 ? s : 1);
+  return per > 0 ? (N + per - 1) / per : 1;
+}
+
+}  // namespace
+}  // namespace tq
+
+using namespace tq;
+
+extern "C" {
+
+TQ_API int tq_polar_encode(const float* y, int64_t rows, int head_dim, int block,
+                           const float* codebooks, const int* cb_sizes, uint8_t* angles,
+                           uint8_t* packed, void* radii, void* stream) {
+  if (!valid_block(block, head_dim))
+    return err(TQ_ERR_UNSUPPORTED, "tq_polar_encode: block must be 16/32/64/128 and head_dim a multiple of 128");
+  if (rows < 0 || !y || !codebooks || !radii || (!angles && !packed))
+    return err(TQ_ERR_INVALID, "tq_polar_encode: bad arguments");
+  PolarTables T;
+  if (!make_tables(codebooks, cb_sizes, levels_of(block), &T))
+    return err(TQ_ERR_INVALID, "tq_polar_encode: codebook sizes must be 1..16");
+  const long long groups = rows * (head_dim / 128);
+  if (groups == 0) return TQ_OK;
+  polar_encode_kernel<<<grid_for(groups), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      y, groups, block, T, angles, packed, static_cast<__half*>(radii));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TQ_OK : cuda_err(e, "tq_polar_encode");
+}
+
+TQ_API int tq_polar_decode(const uint8_t* angles, const uint8_t* packed, const void* radii,
+                           int64_t rows, int head_dim, int block, const float* codebooks,
+                           float* y, void* stream) {
+  if (!valid_block(block, head_dim))
+    return err(TQ_ERR_UNSUPPORTED, "tq_polar_decode: block must be 16/32/64/128 and head_dim a multiple of 128");
+  if (rows < 0 || !y || !codebooks || !radii || (!angles == !packed))
+    return err(TQ_ERR_INVALID, "tq_polar_decode: give exactly one of angles / packed");
+  PolarTables T;
+  make_tables(codebooks, nullptr, levels_of(block), &T);
+  const long long groups = rows * (head_dim / 128);
+  if (groups == 0) return TQ_OK;
+  polar_decode_kernel<<<grid_for(groups), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      angles, packed, static_cast<const __half*>(radii), groups, block, T, y);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TQ_OK : cuda_err(e, "tq_polar_decode");
+}
+
+TQ_API int tq_qjl_encode(const float* y, const float* y_hat, int64_t rows, int head_dim,
+                         const float* S, int m, uint32_t* signs, void* rnorm, void* stream) {
+  if (rows < 0 || !y || !y_hat || !S || !signs || !rnorm || head_dim < 1 || head_dim > 1024 ||
+      m < 32 || m % 32 != 0 || m > 256)
+    return err(TQ_ERR_INVALID, "tq_qjl_encode: bad arguments (m a multiple of 32 in [32, 256])");
+  if (rows == 0) return TQ_OK;
+  const int grid = static_cast<int>(rows < 8192 ? rows : 8192);
+  qjl_encode_kernel<<<grid, 256, head_dim * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
+      y, y_hat, rows, head_dim, S, m, signs, static_cast<__half*>(rnorm));
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TQ_OK : cuda_err(e, "tq_qjl_encode");
+}
+
+TQ_API size_t tq_compressed_sdpa_workspace_size(int num_heads, int num_kv_heads, int head_dim,
+                                                int n_keys) {
+  if (num_kv_heads < 1 || num_heads < num_kv_heads || n_keys < 0) return 0;
+  const int G = num_heads / num_kv_heads;
+  const int s = csplits(num_kv_heads, n_keys);
+  return 256 + static_cast<size_t>(num_kv_heads) * s * 4 * G * (head_dim + 2) * sizeof(float);
+}
+
+static int compressed_common(const void* q, tq_dtype q_dtype, const uint8_t* packed,
+                             const void* radii, const uint32_t* signs, const void* rnorm,
+                             const float* S, int m, int num_heads, int num_kv_heads, int head_dim,
+                             int n_keys, int block, const float* codebooks, float scale,
+                             float* scores, const uint32_t* vq, const void* vs, const void* vb,
+                             tq_dtype sb_dtype, void* out, tq_dtype out_dtype, void* workspace,
+                             size_t workspace_bytes, void* stream, const char* fn) {
+  // key and value buffers may be NULL only for an empty context
+  if (!q || !codebooks || (n_keys > 0 && (!packed || !radii || (signs && (!rnorm || !S)))))
+    return err(TQ_ERR_INVALID, "compressed attention: null pointer argument");
+  if (head_dim != 128 && head_dim != 256)
+    return err(TQ_ERR_UNSUPPORTED, "compressed attention: head_dim must be 128 or 256");
+  if (block != 16 && block != 32 && block != 64 && block != 128)
+    return err(TQ_ERR_UNSUPPORTED, "compressed attention: block must be 16, 32, 64 or 128");
+  if (num_kv_heads < 1 || num_heads % num_kv_heads != 0 || n_keys < 0)
+    return err(TQ_ERR_INVALID, "compressed attention: bad head counts");
+  const int G = num_heads / num_kv_heads;
+  if (G != 1 && G != 2 && G != 4 && G != 8)
+    return err(TQ_ERR_UNSUPPORTED, "compressed attention: gqa factor must be 1, 2, 4 or 8");
+  if (signs && (m % 32 != 0 || m < 32 || m > 256))
+    return err(TQ_ERR_INVALID, "compressed attention: m must be a multiple of 32 in [32, 256]");
+  PolarTables T;
+  make_tables(codebooks, nullptr, levels_of(block), &T);
+  CParams p{};
+  p.q = q;
+  p.q_dtype = q_dtype;
+  p.packed = packed;
+  p.radii = static_cast<const __half*>(radii);
+  p.signs = signs;
+  p.rnorm = static_cast<const __half*>(rnorm);
+  p.S = S;
+  p.m = signs ? m : 0;
+  p.vq = vq;
+  p.attend = out != nullptr;
+  p.vs = vs;
+  p.vb = vb;
+  p.sb_f32 = sb_dtype == TQ_F32;
+  p.H = num_heads;
+  p.Hkv = num_kv_heads;
+  p.N = n_keys;
+  p.block = block;
+  p.scale = scale;
+  p.scores = scores;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  const bool attend = out != nullptr;
+  const int splits = attend ? csplits(num_kv_heads, n_keys) : (n_keys + 127) / 128;
+  p.splits = splits > 0 ? splits : 1;
+  p.keys_per_split = (n_keys + p.splits - 1) / p.splits;
+  if (attend) {
+    const size_t need = tq_compressed_sdpa_workspace_size(num_heads, num_kv_heads, head_dim, n_keys);
+    if (!workspace || workspace_bytes < need) {
+      set_last_error("%s: workspace of %zu bytes needed", fn, need);
+      return TQ_ERR_WORKSPACE;
+    }
+    p.counters = static_cast<unsigned*>(workspace);
+    p.ws = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + 256);
+    if (num_kv_heads * sizeof(unsigned) > 256)
+      return err(TQ_ERR_UNSUPPORTED, "compressed attention: at most 64 KV heads");
+  }
+  void* fn_ptr = head_dim == 128 ? pick_cattn<128>(G) : pick_cattn<256>(G);
+  void* args[] = {&p, &T};
+  const cudaError_t e = cudaLaunchKernel(fn_ptr, dim3(p.splits, num_kv_heads), dim3(128), args, 0,
+                                         static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TQ_OK : cuda_err(e, fn);
+}
+
+TQ_API int tq_compressed_score(const void* queries, tq_dtype q_dtype, const uint8_t* packed,
+                               const void* radii, const uint32_t* signs, const void* rnorm,
+                               const float* S, int m, int num_heads, int num_kv_heads,
+                               int head_dim, int n_keys, int block, const float* codebooks,
+                               float scale, float* scores, void* stream) {
+  if (!scores) return err(TQ_ERR_INVALID, "tq_compressed_score: null scores");
+  return compressed_common(queries, q_dtype, packed, radii, signs, rnorm, S, m, num_heads,
+                           num_kv_heads, head_dim, n_keys, block, codebooks, scale, scores,
+                           nullptr, nullptr, nullptr, TQ_F16, nullptr, TQ_F32, nullptr, 0, stream,
+                           "tq_compressed_score");
+}
+
+TQ_API int tq_compressed_sdpa(const void* queries, tq_dtype q_dtype, const uint8_t* packed,
+                              const void* radii, const uint32_t* signs, const void* rnorm,
+                              const float* S, int m, int num_heads, int num_kv_heads,
+                              int head_dim, int n_keys, int block, const float* codebooks,
+                              float scale, const uint32_t* v_quant, const void* v_scales,
+                              const void* v_biases, tq_dtype sb_dtype, void* out,
+                              tq_dtype out_dtype, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  if (!out || (n_keys > 0 && (!v_quant || !v_scales || !v_biases)))
+    return err(TQ_ERR_INVALID, "tq_compressed_sdpa: null V or out");
+  return compressed_common(queries, q_dtype, packed, radii, signs, rnorm, S, m, num_heads,
+                           num_kv_heads, head_dim, n_keys, block, codebooks, scale, nullptr,
+                           v_quant, v_scales, v_biases, sb_dtype, out, out_dtype, workspace,
+                           workspace_bytes, stream, "tq_compressed_sdpa");
+}
+
+}  // extern "C"

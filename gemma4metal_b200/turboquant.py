@@ -68,15 +68,16 @@ def load_library() -> ctypes.CDLL:
 
 
 def _register_extra(L) -> None:
-    """Bind entry points that only some builds export (added incrementally)."""
+    """Bind the PolarQuant / QJL entry points."""
     P, I, I64, F, SZ = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
-    if hasattr(L, "tq_polar_encode"):
-        L.tq_polar_encode.argtypes = [P, I, I64, I, I, P, P, P, P, P, P, P, P, P, P]
-        L.tq_compressed_score.argtypes = [P, I, P, P, P, P, I, I, I, I, I, I, P, P, P, F, P, I, P]
-        L.tq_compressed_sdpa.argtypes = [P, I, P, P, P, P, P, P, P, I, I, I, I, I, I, P, P, P, F,
-                                         I, P, I, P, SZ, P]
-        L.tq_compressed_sdpa_workspace_size.restype = SZ
-        L.tq_compressed_sdpa_workspace_size.argtypes = [I, I, I, I, I]
+    L.tq_polar_encode.argtypes = [P, I64, I, I, P, P, P, P, P, P]
+    L.tq_polar_decode.argtypes = [P, P, P, I64, I, I, P, P, P]
+    L.tq_qjl_encode.argtypes = [P, P, I64, I, P, I, P, P, P]
+    L.tq_compressed_score.argtypes = [P, I, P, P, P, P, P, I, I, I, I, I, I, P, F, P, P]
+    L.tq_compressed_sdpa_workspace_size.restype = SZ
+    L.tq_compressed_sdpa_workspace_size.argtypes = [I, I, I, I]
+    L.tq_compressed_sdpa.argtypes = [P, I, P, P, P, P, P, I, I, I, I, I, I, P, F, P, P, P, I, P, I,
+                                     P, SZ, P]
 
 
 def _check(rc: int) -> None:
@@ -316,3 +317,148 @@ def device_error(s=None) -> int:
     code = ctypes.c_uint32(0)
     _check(load_library().tq_device_error(_stream(s), ctypes.byref(code)))
     return int(code.value)
+
+
+# ------------------------------------------------------ PolarQuant + QJL --
+# The reference's polar_quantize / polar_dequantize / compressed_score /
+# compressed_sdpa (lib/turboquant.h:52-165) over the C ABI, generalised to
+# blocks of 2^L values, plus the QJL residual sketch. Codebooks and the QJL
+# matrix are caller inputs (the reference ships no generator); the helpers
+# below give the build's defaults.
+
+def uniform_codebooks(levels: int, device=None) -> torch.Tensor:
+    """(levels, 16) fp32 bin centres: level 1 on [0, 2*pi), deeper levels on
+    [0, pi/2] (their angles come from non-negative radii)."""
+    import math
+    c = torch.arange(16, dtype=torch.float64) + 0.5
+    rows = [c * (2 * math.pi / 16)] + [c * (math.pi / 2 / 16)] * (levels - 1)
+    return torch.stack(rows).float().to(device or "cuda")
+
+
+def qjl_matrix(m: int, head_dim: int, seed: int, device=None) -> torch.Tensor:
+    """Seeded Gaussian JL matrix S (m, head_dim), entries N(0, 1), drawn on the
+    host with numpy's default_rng(seed) so every process gets the same S."""
+    import numpy as np
+    S = np.random.default_rng(seed).standard_normal((m, head_dim)).astype(np.float32)
+    return torch.from_numpy(S).to(device or "cuda")
+
+
+def _cb_host(codebooks: torch.Tensor) -> torch.Tensor:
+    """(7, 16) fp32 host copy of the codebooks: the C ABI reads them on the
+    host to build the kernels' codebook and cos/sin tables."""
+    cb = torch.zeros(7, 16, dtype=torch.float32)
+    cb[:codebooks.shape[0]] = codebooks.detach().float().cpu()
+    return cb.contiguous()
+
+
+def _host_ptr(t: torch.Tensor):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def polar_quantize(vectors: torch.Tensor, block_size: int, codebooks: torch.Tensor,
+                   cb_sizes=None, precondition: Optional[torch.Tensor] = None, s=None):
+    """PolarQuant encode of the last axis (lib/turboquant.h:52-59): y = x P^T
+    when a preconditioner is given, then per block of block_size values the
+    level-major angle indices. Returns (angles uint8 (..., D/block, block-1),
+    packed uint8 (..., D/block, block/2), radii fp16 (..., D/block))."""
+    y = vectors.float()
+    if precondition is not None:
+        y = y @ precondition.float().t()
+    y = y.contiguous()
+    D = y.shape[-1]
+    rows = y.numel() // D
+    nb = D // block_size
+    lead = tuple(y.shape[:-1])
+    angles = torch.empty(lead + (nb, block_size - 1), dtype=torch.uint8, device=y.device)
+    packed = torch.empty(lead + (nb, block_size // 2), dtype=torch.uint8, device=y.device)
+    radii = torch.empty(lead + (nb,), dtype=torch.float16, device=y.device)
+    cb = _cb_host(codebooks)
+    sizes = None
+    if cb_sizes is not None:
+        import numpy as np
+        sizes = np.ascontiguousarray(np.asarray(cb_sizes, np.int32))
+    _check(load_library().tq_polar_encode(
+        _ptr(y), rows, D, block_size, _host_ptr(cb),
+        sizes.ctypes.data_as(ctypes.c_void_p) if sizes is not None else None,
+        _ptr(angles), _ptr(packed), _ptr(radii), _stream(s)))
+    return angles, packed, radii
+
+
+def polar_dequantize(packed: Optional[torch.Tensor], radii: torch.Tensor, head_dim: int,
+                     block_size: int, codebooks: torch.Tensor, angles: Optional[torch.Tensor] = None,
+                     precondition: Optional[torch.Tensor] = None, s=None) -> torch.Tensor:
+    """Inverse PolarQuant (lib/turboquant.h:61-72,96-106): (..., head_dim) fp32;
+    multiplied by the preconditioner when given (x = y P)."""
+    lead = tuple(radii.shape[:-1])
+    rows = radii.numel() // (head_dim // block_size)
+    y = torch.empty(lead + (head_dim,), dtype=torch.float32, device=radii.device)
+    cb = _cb_host(codebooks)
+    _check(load_library().tq_polar_decode(
+        _ptr(angles) if angles is not None else None, _ptr(packed) if angles is None else None,
+        _ptr(radii), rows, head_dim, block_size, _host_ptr(cb), _ptr(y), _stream(s)))
+    if precondition is not None:
+        y = y @ precondition.float()
+    return y
+
+
+def qjl_encode(y: torch.Tensor, y_hat: torch.Tensor, S: torch.Tensor, s=None):
+    """QJL sketch of the residual r = y - y_hat: (sign bits uint32 (..., m/32)
+    as int32 bit patterns, |r| fp16 (...))."""
+    yc, yh, Sc = y.float().contiguous(), y_hat.float().contiguous(), S.float().contiguous()
+    m, D = Sc.shape
+    rows = yc.numel() // D
+    lead = tuple(yc.shape[:-1])
+    signs = torch.empty(lead + (m // 32,), dtype=torch.int32, device=y.device)
+    rnorm = torch.empty(lead, dtype=torch.float16, device=y.device)
+    _check(load_library().tq_qjl_encode(_ptr(yc), _ptr(yh), rows, D, _ptr(Sc), m, _ptr(signs),
+                                        _ptr(rnorm), _stream(s)))
+    return signs, rnorm
+
+
+def compressed_score(queries: torch.Tensor, packed: torch.Tensor, radii: torch.Tensor,
+                     codebooks: torch.Tensor, block_size: int, scale: float = 1.0,
+                     signs: Optional[torch.Tensor] = None, rnorm: Optional[torch.Tensor] = None,
+                     S: Optional[torch.Tensor] = None, s=None) -> torch.Tensor:
+    """Scores (H, N) of queries (H, D) (preconditioned) against compressed keys
+    packed (Hkv, N, D/block, block/2) (lib/turboquant.h:154-162, with GQA and
+    the optional QJL correction)."""
+    H, D = queries.shape
+    Hkv, N = radii.shape[0], radii.shape[1]
+    scores = torch.empty(H, N, dtype=torch.float32, device=queries.device)
+    qc = queries.contiguous()
+    Sc = S.float().contiguous() if S is not None else None
+    cb = _cb_host(codebooks)
+    _check(load_library().tq_compressed_score(
+        _ptr(qc), _dt(qc), _ptr(packed), _ptr(radii), _ptr(signs), _ptr(rnorm), _ptr(Sc),
+        0 if Sc is None else Sc.shape[0], H, Hkv, D, N, block_size, _host_ptr(cb),
+        float(scale), _ptr(scores), _stream(s)))
+    return scores
+
+
+def compressed_sdpa(queries: torch.Tensor, packed: torch.Tensor, radii: torch.Tensor,
+                    codebooks: torch.Tensor, v_quant: torch.Tensor, v_scales: torch.Tensor,
+                    v_biases: torch.Tensor, block_size: int, scale: float = 0.0884,
+                    signs: Optional[torch.Tensor] = None, rnorm: Optional[torch.Tensor] = None,
+                    S: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                    out: Optional[torch.Tensor] = None, ws: Optional[torch.Tensor] = None,
+                    s=None) -> torch.Tensor:
+    """Compressed-key attention (lib/turboquant.h:129-142): softmax of the
+    compressed scores . int4 V (v_quant (Hkv, N, D/8), scales/biases
+    (Hkv, N, D/64)). Returns (H, D)."""
+    H, D = queries.shape
+    Hkv, N = radii.shape[0], radii.shape[1]
+    od = out_dtype or queries.dtype
+    if out is None:
+        out = torch.empty(H, D, dtype=od, device=queries.device)
+    nbytes = int(load_library().tq_compressed_sdpa_workspace_size(H, Hkv, D, N))
+    if ws is None:
+        ws = workspace(queries.device, nbytes, s)
+    qc = queries.contiguous()
+    Sc = S.float().contiguous() if S is not None else None
+    cb = _cb_host(codebooks)
+    _check(load_library().tq_compressed_sdpa(
+        _ptr(qc), _dt(qc), _ptr(packed), _ptr(radii), _ptr(signs), _ptr(rnorm), _ptr(Sc),
+        0 if Sc is None else Sc.shape[0], H, Hkv, D, N, block_size, _host_ptr(cb),
+        float(scale), _ptr(v_quant), _ptr(v_scales), _ptr(v_biases), _dt(v_scales), _ptr(out),
+        _dt(out), _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
+    return out

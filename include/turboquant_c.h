@@ -173,6 +173,75 @@ TQ_API int tq_sdpa_int4_noalloc(const void* queries, tq_dtype q_dtype, const uin
                                 const int32_t* seq_lens, void* out, tq_dtype out_dtype,
                                 void* stream);
 
+/* ---- PolarQuant + QJL compressed keys ----------------------------------------
+ * Blocks of `block` values (16, 32, 64 or 128; head_dim a multiple of 128) are
+ * encoded as in lib/turboquant.metal:8-98 (polar_fused_quantize), generalised
+ * from 4 levels to log2(block) levels: per level, each pair (a, b) of the
+ * previous level's values gives angle atan2(b, a) (level 1 wrapped to
+ * [0, 2pi)) and radius sqrt(a*a + b*b); the angle is replaced by the index of
+ * the nearest codebook entry (linear scan, first minimum); the last radius is
+ * stored as fp16. Angles are level-major inside a block (level 1's block/2
+ * angles first). codebooks: levels x 16 fp32 (level 1 first); cb_sizes: the
+ * entries used per level (NULL = 16 each). */
+
+/* y: (rows, head_dim) fp32, already multiplied by the preconditioner if one is
+ * used (the reference does y = x P^T before encoding, lib/turboquant.cpp:102).
+ * Outputs (angles or packed may be NULL, not both):
+ *   angles uint8 (rows, head_dim/block, block-1), one byte per angle index;
+ *   packed uint8 (rows, head_dim/block, block/2): 4-bit indices, low nibble
+ *          first (the last nibble of a block is 0);
+ *   radii  fp16 (rows, head_dim/block).
+ * Replaces polar_quantize / polar_quantize_packed (lib/turboquant.h:52-59,80-86). */
+TQ_API int tq_polar_encode(const float* y, int64_t rows, int head_dim, int block,
+                           const float* codebooks, const int* cb_sizes, uint8_t* angles,
+                           uint8_t* packed, void* radii, void* stream);
+
+/* Inverse (lib/turboquant.metal:100-164): y (rows, head_dim) fp32 from exactly
+ * one of angles / packed plus radii. Replaces polar_dequantize_fast and
+ * polar_dequantize_packed_fast (lib/turboquant.h:96-106,144-151); multiply by
+ * the preconditioner afterwards for polar_dequantize (lib/turboquant.cpp:122). */
+TQ_API int tq_polar_decode(const uint8_t* angles, const uint8_t* packed, const void* radii,
+                           int64_t rows, int head_dim, int block, const float* codebooks,
+                           float* y, void* stream);
+
+/* QJL residual sketch (arXiv 2406.03482; the reference has no implementation):
+ * r = y - y_hat; signs uint32 (rows, m/32), bit i = ((S r)_i >= 0); rnorm fp16
+ * (rows) = |r|. S: (m, head_dim) fp32, m a multiple of 32 in [32, 256]. */
+TQ_API int tq_qjl_encode(const float* y, const float* y_hat, int64_t rows, int head_dim,
+                         const float* S, int m, uint32_t* signs, void* rnorm, void* stream);
+
+/* Scores of single queries against compressed keys (replaces compressed_score,
+ * lib/turboquant.h:154-162, lib/turboquant.metal:424-499, with GQA):
+ *   scores[h][n] = scale * ( <q_h, decode(key n of KV head h/G)>
+ *                            + sqrt(pi/2)/m * rnorm * <S q_h, sign bits> )
+ * queries (H, head_dim) in q_dtype (already preconditioned); packed/radii as
+ * from tq_polar_encode for (Hkv, n_keys) key rows; signs/rnorm/S may be NULL
+ * (no QJL term). scores: (H, n_keys) fp32. */
+TQ_API int tq_compressed_score(const void* queries, tq_dtype q_dtype, const uint8_t* packed,
+                               const void* radii, const uint32_t* signs, const void* rnorm,
+                               const float* S, int m, int num_heads, int num_kv_heads,
+                               int head_dim, int n_keys, int block, const float* codebooks,
+                               float scale, float* scores, void* stream);
+
+/* Workspace bytes for tq_compressed_sdpa (zero-filled once before first use,
+ * tq_workspace_init; kernels leave it reusable). */
+TQ_API size_t tq_compressed_sdpa_workspace_size(int num_heads, int num_kv_heads, int head_dim,
+                                                int n_keys);
+
+/* Compressed-key attention (replaces compressed_sdpa, lib/turboquant.h:129-142,
+ * lib/turboquant.metal:166-224): softmax over the scores above, then . V with V
+ * in the int4 cache layout (v_quant (Hkv, n_keys, D/8), scales/biases
+ * (Hkv, n_keys, D/64) in sb_dtype). out (H, head_dim) in out_dtype; an empty
+ * context gives 0. */
+TQ_API int tq_compressed_sdpa(const void* queries, tq_dtype q_dtype, const uint8_t* packed,
+                              const void* radii, const uint32_t* signs, const void* rnorm,
+                              const float* S, int m, int num_heads, int num_kv_heads,
+                              int head_dim, int n_keys, int block, const float* codebooks,
+                              float scale, const uint32_t* v_quant, const void* v_scales,
+                              const void* v_biases, tq_dtype sb_dtype, void* out,
+                              tq_dtype out_dtype, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
 /* Read and clear the device error word that kernels set when a bounded wait
  * gives up (0 = no error). Synchronises `stream`. */
 TQ_API int tq_device_error(void* stream, uint32_t* code);

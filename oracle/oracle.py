@@ -53,15 +53,14 @@ def lib():
 
 
 def _register_polar(L):
-    if not hasattr(L, "tqo_polar_encode"):
-        return
     P, I, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
     L.tqo_atan2.restype = F
     L.tqo_atan2.argtypes = [F, F]
-    L.tqo_polar_encode.argtypes = [P, I64, I, I, P, P, P, P, P, P, P, P]
-    L.tqo_polar_decode.argtypes = [P, P, I64, I, I, P, P, P, P]
-    L.tqo_qjl_encode.argtypes = [P, P, I64, I, I, P, P, P]
-    L.tqo_compressed_score.argtypes = [P, I, I, P, P, P, P, I, I, I, I, I, I, P, P, P, P, F, P]
+    L.tqo_polar_encode.argtypes = [P, I64, I, I, P, P, P, P, P]
+    L.tqo_polar_decode.argtypes = [P, P, P, I64, I, I, P, P]
+    L.tqo_qjl_encode.argtypes = [P, P, I64, I, P, I, P, P]
+    L.tqo_compressed_score.argtypes = [P, I, I, I, I, I, I, P, P, P, P, P, P, I, F, P]
+    L.tqo_compressed_sdpa.argtypes = [P, I, I, I, I, I, I, P, P, P, P, P, P, I, F, P, P, P, I, P]
 
 
 def _ptr(a: np.ndarray):
@@ -284,3 +283,97 @@ def num_threads() -> int:
 
 def set_num_threads(n: int) -> None:
     lib().tqo_set_num_threads(int(n))
+
+
+# ------------------------------------------------------ PolarQuant + QJL --
+# (restated in oracle/tq_oracle_polar.c; lib/turboquant.metal:8-224,424-704)
+
+def atan2(y: float, x: float) -> float:
+    return float(lib().tqo_atan2(float(y), float(x)))
+
+
+def polar_encode(y: np.ndarray, block: int, codebooks: np.ndarray, cb_sizes=None):
+    """y (..., D) f32 -> (angles uint8 (..., D/block, block-1) level-major,
+    packed uint8 (..., D/block, block/2), radii fp16 (..., D/block))."""
+    y = np.ascontiguousarray(y, np.float32)
+    D = y.shape[-1]
+    rows = y.size // D
+    nb = D // block
+    levels = int(np.log2(block))
+    cb = np.zeros((7, 16), np.float32)
+    cb[:codebooks.shape[0]] = codebooks
+    sizes = np.array(cb_sizes if cb_sizes is not None else [16] * 7, np.int32)
+    ang = np.empty(y.shape[:-1] + (nb, block - 1), np.uint8)
+    pk = np.empty(y.shape[:-1] + (nb, block // 2), np.uint8)
+    rad = np.empty(y.shape[:-1] + (nb,), np.float16)
+    lib().tqo_polar_encode(_ptr(y), rows, D, block, _ptr(cb), _ptr(sizes), _ptr(ang), _ptr(pk),
+                           _ptr(rad))
+    assert levels <= 7
+    return ang, pk, rad
+
+
+def polar_decode(packed: np.ndarray, radii: np.ndarray, D: int, block: int,
+                 codebooks: np.ndarray, angles: np.ndarray = None) -> np.ndarray:
+    rows = radii.size // (D // block)
+    cb = np.zeros((7, 16), np.float32)
+    cb[:codebooks.shape[0]] = codebooks
+    out = np.empty(radii.shape[:-1] + (D,), np.float32)
+    a = None if angles is None else np.ascontiguousarray(angles, np.uint8)
+    p = None if angles is not None else np.ascontiguousarray(packed, np.uint8)
+    lib().tqo_polar_decode(_ptr(a) if a is not None else None, _ptr(p) if p is not None else None,
+                           _ptr(np.ascontiguousarray(radii, np.float16)), rows, D, block, _ptr(cb),
+                           _ptr(out))
+    return out
+
+
+def qjl_encode(y: np.ndarray, yhat: np.ndarray, S: np.ndarray):
+    """signs uint32 (..., m/32) with bit i = (S (y - yhat))_i >= 0; |y - yhat| fp16."""
+    y = np.ascontiguousarray(y, np.float32)
+    yhat = np.ascontiguousarray(yhat, np.float32)
+    S = np.ascontiguousarray(S, np.float32)
+    m, D = S.shape
+    rows = y.size // D
+    signs = np.empty(y.shape[:-1] + (m // 32,), np.uint32)
+    rn = np.empty(y.shape[:-1], np.float16)
+    lib().tqo_qjl_encode(_ptr(y), _ptr(yhat), rows, D, _ptr(S), m, _ptr(signs), _ptr(rn))
+    return signs, rn
+
+
+def compressed_score(q, packed, radii, codebooks, block, scale=1.0, signs=None, rnorm=None,
+                     S=None, q_dtype=F32):
+    """q (H, D) preconditioned; keys packed (Hkv, N, D/block, block/2) ->
+    scores (H, N) f32 (fp64 sums)."""
+    q = np.ascontiguousarray(q)
+    H, D = q.shape
+    Hkv, N = radii.shape[0], radii.shape[1]
+    cb = np.zeros((7, 16), np.float32)
+    cb[:codebooks.shape[0]] = codebooks
+    out = np.empty((H, N), np.float32)
+    m = 0 if S is None else S.shape[0]
+    lib().tqo_compressed_score(
+        _ptr(q), q_dtype, H, Hkv, D, N, block, _ptr(np.ascontiguousarray(packed, np.uint8)),
+        _ptr(np.ascontiguousarray(radii, np.float16)), _ptr(cb),
+        _ptr(signs) if signs is not None else None, _ptr(rnorm) if rnorm is not None else None,
+        _ptr(np.ascontiguousarray(S, np.float32)) if S is not None else None, m, float(scale),
+        _ptr(out))
+    return out
+
+
+def compressed_sdpa(q, packed, radii, codebooks, block, vq, vs, vb, scale=1.0, signs=None,
+                    rnorm=None, S=None, q_dtype=F32):
+    q = np.ascontiguousarray(q)
+    H, D = q.shape
+    Hkv, N = radii.shape[0], radii.shape[1]
+    cb = np.zeros((7, 16), np.float32)
+    cb[:codebooks.shape[0]] = codebooks
+    out = np.empty((H, D), np.float32)
+    m = 0 if S is None else S.shape[0]
+    Sc = np.ascontiguousarray(S, np.float32) if S is not None else None
+    lib().tqo_compressed_sdpa(
+        _ptr(q), q_dtype, H, Hkv, D, N, block, _ptr(np.ascontiguousarray(packed, np.uint8)),
+        _ptr(np.ascontiguousarray(radii, np.float16)), _ptr(cb),
+        _ptr(signs) if signs is not None else None, _ptr(rnorm) if rnorm is not None else None,
+        _ptr(Sc) if Sc is not None else None, m, float(scale),
+        _ptr(np.ascontiguousarray(vq)), _ptr(np.ascontiguousarray(vs)),
+        _ptr(np.ascontiguousarray(vb)), 1 if vs.dtype == np.float32 else 0, _ptr(out))
+    return out

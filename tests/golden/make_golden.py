@@ -49,6 +49,25 @@ def make(name, seed, H, Hkv, D, N, window, sb_f16, store_codes):
     return h.hexdigest()
 
 
+def make_polar(name="polar_cfg3_small", seed=11, Hkv=2, N=40, D=128, H=4, block=128, m=256):
+    """PolarQuant + QJL of config-3-shaped keys (7 levels of 16-entry uniform
+    codebooks, Gaussian S from default_rng(seed)): packed indices, radii,
+    sign bits and residual norms the encoders must reproduce."""
+    import math
+    k = inputs.make_layer(seed, H, Hkv, D, N)["k"][0]
+    c = np.arange(16) + 0.5
+    cb = np.stack([c * (2 * math.pi / 16)] + [c * (math.pi / 2 / 16)] * 6).astype(np.float32)
+    _, pk, rad = O.polar_encode(k, block, cb)
+    kh = O.polar_decode(pk, rad, D, block, cb)
+    S = np.random.default_rng(seed).standard_normal((m, D)).astype(np.float32)
+    signs, rn = O.qjl_encode(k, kh, S)
+    np.savez_compressed(os.path.join(HERE, f"{name}.npz"), seed=seed, Hkv=Hkv, N=N, D=D, H=H,
+                        block=block, m=m, packed=pk, radii=rad.view(np.uint16), signs=signs,
+                        rnorm=rn.view(np.uint16))
+    return name
+
+
 if __name__ == "__main__":
     for c in CASES:
         print(c[0], make(*c))
+    print(make_polar())

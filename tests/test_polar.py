@@ -1,0 +1,279 @@
+"""PolarQuant + QJL compressed keys (reference: lib/turboquant.metal:8-224,
+424-704; QJL per arXiv 2406.03482, absent in the reference).
+
+CPU: the oracle's own atan2, encoder/decoder invariants, a float64 numpy
+restatement of the encoder, the QJL estimator's unbiasedness, and the golden
+fixture. GPU: encode/decode/QJL bit-exact against the oracle (indices, radii,
+sign bits), compressed scores within 1e-3 relative of the oracle's fp64
+evaluation, compressed attention within max-abs 2e-3 / cosine 0.99999."""
+import math
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import inputs, oracle as O
+from tests.conftest import parity
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "polar_cfg3_small.npz")
+
+
+def codebooks(levels):
+    c = np.arange(16) + 0.5
+    rows = [c * (2 * math.pi / 16)] + [c * (math.pi / 2 / 16)] * (levels - 1)
+    return np.stack(rows).astype(np.float32)
+
+
+def keys(seed, Hkv, N, D):
+    return inputs.make_layer(seed, 2 * Hkv, Hkv, D, N)["k"][0]  # (Hkv, N, D) RMS-normalised
+
+
+def np_encode(y, block, cb):
+    """float64 numpy restatement of the encoder (indices can differ from the
+    fp32 oracle only when an angle sits within rounding of a bin boundary)."""
+    levels = int(math.log2(block))
+    blocks = y.reshape(-1, block).astype(np.float64)
+    idx = []
+    r = blocks
+    for L in range(1, levels + 1):
+        a, b = r[:, 0::2], r[:, 1::2]
+        ang = np.arctan2(b, a)
+        if L == 1:
+            ang = np.where(ang < 0, ang + 2 * math.pi, ang)
+        d = np.abs(ang[..., None] - cb[L - 1][None, None, :].astype(np.float64))
+        idx.append(np.argmin(d, axis=-1))
+        r = np.hypot(a, b)
+    return np.concatenate(idx, axis=1), r[:, 0]
+
+
+# ------------------------------------------------------------------ CPU --
+
+def test_atan2_accuracy_and_quadrants():
+    rng = np.random.default_rng(0)
+    pts = list(rng.standard_normal((3000, 2))) + [(0, 1), (1, 0), (0, -1), (-1, 0), (1, 1),
+                                                  (-1, -1), (1e-30, 1), (5, -1e-20)]
+    for y, x in pts:
+        assert abs(O.atan2(y, x) - math.atan2(float(np.float32(y)), float(np.float32(x)))) < 5e-7
+    assert O.atan2(0.0, 0.0) == 0.0
+
+
+@pytest.mark.parametrize("block", [16, 128])
+def test_encoder_matches_float64_restatement(block):
+    y = keys(11, 2, 64, 128).reshape(-1, 128)
+    cb = codebooks(int(math.log2(block)))
+    ang, pk, rad = O.polar_encode(y, block, cb)
+    ref_idx, ref_rad = np_encode(y, block, cb)
+    got = ang.reshape(-1, block - 1)
+    mism = np.mean(got != ref_idx)
+    assert mism < 2e-3, mism
+    np.testing.assert_allclose(rad.reshape(-1).astype(np.float64), ref_rad, rtol=1e-3)
+    # packed nibbles carry the same indices
+    flat = pk.reshape(-1, block // 2)
+    nib = np.stack([flat & 15, flat >> 4], -1).reshape(-1, block)[:, :block - 1]
+    assert np.array_equal(nib, got)
+
+
+@pytest.mark.parametrize("block", [16, 128])
+def test_decode_preserves_norm_and_bounds_error(block):
+    y = keys(12, 2, 64, 256).reshape(-1, 256)
+    cb = codebooks(int(math.log2(block)))
+    ang, pk, rad = O.polar_encode(y, block, cb)
+    yh = O.polar_decode(pk, rad, 256, block, cb)
+    yh2 = O.polar_decode(None, rad, 256, block, cb, angles=ang)
+    assert np.array_equal(yh, yh2)
+    nb = yh.reshape(-1, block)
+    np.testing.assert_allclose(np.linalg.norm(nb, axis=1), rad.reshape(-1).astype(np.float32),
+                               rtol=2e-6)
+    rel = np.linalg.norm(yh - y) / np.linalg.norm(y)
+    assert rel < 0.3  # 16-bin angles: a coarse code, exact direction recovery is not expected
+
+
+def test_qjl_estimator_is_unbiased():
+    rng = np.random.default_rng(3)
+    D, m = 128, 256
+    q = rng.standard_normal(D).astype(np.float32)
+    r = rng.standard_normal(D).astype(np.float32) * 0.3
+    est = []
+    for seed in range(200):
+        S = np.random.default_rng(1000 + seed).standard_normal((m, D)).astype(np.float32)
+        signs, rn = O.qjl_encode(r[None], np.zeros((1, D), np.float32), S)
+        bits = np.unpackbits(signs.view(np.uint8), bitorder="little")[:m].astype(np.float64)
+        e = math.sqrt(math.pi / 2) / m * float(rn[0]) * float(((2 * bits - 1) * (S @ q)).sum())
+        est.append(e)
+    true = float(q @ r)
+    sd = np.std(est) / math.sqrt(len(est))
+    assert abs(np.mean(est) - true) < 4 * sd + 1e-3, (np.mean(est), true, sd)
+
+
+def test_compressed_score_matches_decode_dot():
+    Hkv, N, D, H, block, m = 2, 50, 128, 4, 128, 256
+    k = keys(5, Hkv, N, D)
+    cb = codebooks(7)
+    ang, pk, rad = O.polar_encode(k, block, cb)
+    kh = O.polar_decode(pk, rad, D, block, cb)
+    S = np.random.default_rng(11).standard_normal((m, D)).astype(np.float32)
+    signs, rn = O.qjl_encode(k, kh, S)
+    q = np.random.default_rng(6).standard_normal((H, D)).astype(np.float32)
+    got = O.compressed_score(q, pk, rad, cb, block, 0.5, signs, rn, S)
+    bits = np.unpackbits(signs.reshape(Hkv, N, -1).view(np.uint8), axis=-1, bitorder="little")
+    sg = 2.0 * bits[..., :m] - 1.0
+    G = H // Hkv
+    for h in range(H):
+        kv = h // G
+        ref = kh[kv].astype(np.float64) @ q[h]
+        ref += math.sqrt(math.pi / 2) / m * rn[kv].astype(np.float64) * (sg[kv] @ (S.astype(np.float64) @ q[h]))
+        np.testing.assert_allclose(got[h], 0.5 * ref, rtol=1e-5, atol=1e-5)
+
+
+def test_polar_golden_fixture():
+    g = np.load(GOLDEN)
+    Hkv, N, D, H, block, m = (int(g[k]) for k in ("Hkv", "N", "D", "H", "block", "m"))
+    k = keys(int(g["seed"]), Hkv, N, D)
+    cb = codebooks(int(math.log2(block)))
+    ang, pk, rad = O.polar_encode(k, block, cb)
+    assert np.array_equal(pk, g["packed"]) and np.array_equal(rad.view(np.uint16), g["radii"])
+    kh = O.polar_decode(pk, rad, D, block, cb)
+    S = np.random.default_rng(int(g["seed"])).standard_normal((m, D)).astype(np.float32)
+    signs, rn = O.qjl_encode(k, kh, S)
+    assert np.array_equal(signs, g["signs"]) and np.array_equal(rn.view(np.uint16), g["rnorm"])
+
+
+# ------------------------------------------------------------------ GPU --
+
+def _cuda():
+    import gemma4metal_b200.turboquant as tq
+    return tq
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("block,D", [(16, 128), (32, 128), (64, 256), (128, 128), (128, 256)])
+def test_gpu_encode_decode_bitexact(block, D):
+    tq = _cuda()
+    k = keys(21, 4, 333, D)
+    cb = codebooks(int(math.log2(block)))
+    ang, pk, rad = O.polar_encode(k, block, cb)
+    ga, gp, gr = tq.polar_quantize(torch.from_numpy(k).cuda(), block, torch.from_numpy(cb))
+    torch.cuda.synchronize()
+    assert np.array_equal(ga.cpu().numpy(), ang)
+    assert np.array_equal(gp.cpu().numpy(), pk)
+    assert np.array_equal(gr.cpu().numpy().view(np.uint16), rad.view(np.uint16))
+    yh = O.polar_decode(pk, rad, D, block, cb)
+    gy = tq.polar_dequantize(gp, gr, D, block, torch.from_numpy(cb))
+    gy2 = tq.polar_dequantize(None, gr, D, block, torch.from_numpy(cb), angles=ga)
+    assert np.array_equal(gy.cpu().numpy(), yh)
+    assert np.array_equal(gy2.cpu().numpy(), yh)
+
+
+@pytest.mark.gpu
+def test_gpu_reduced_codebooks_and_preconditioner():
+    tq = _cuda()
+    D, block = 128, 16
+    k = keys(22, 2, 100, D)
+    cb = codebooks(4)
+    sizes = [16, 4, 4, 4]
+    P, _ = np.linalg.qr(np.random.default_rng(4).standard_normal((D, D)))
+    P = P.astype(np.float32)
+    y = (torch.from_numpy(k).cuda() @ torch.from_numpy(P).cuda().t()).cpu().numpy()
+    ang, pk, rad = O.polar_encode(y, block, cb, sizes)
+    ga, gp, gr = tq.polar_quantize(torch.from_numpy(k).cuda(), block, torch.from_numpy(cb), sizes,
+                                   precondition=torch.from_numpy(P).cuda())
+    torch.cuda.synchronize()
+    assert np.array_equal(ga.cpu().numpy(), ang) and ang.max() < 16
+    lvl = ga.cpu().numpy().reshape(-1, 15)
+    assert lvl[:, 8:].max() < 4  # levels 2-4 use 4 entries
+    x = tq.polar_dequantize(gp, gr, D, block, torch.from_numpy(cb),
+                            precondition=torch.from_numpy(P).cuda()).cpu().numpy()
+    ref = O.polar_decode(pk, rad, D, block, cb) @ P
+    np.testing.assert_allclose(x, ref, rtol=0, atol=1e-5)
+
+
+@pytest.mark.gpu
+def test_gpu_qjl_bitexact():
+    tq = _cuda()
+    D, m = 128, 256
+    k = keys(23, 4, 257, D)
+    cb = codebooks(7)
+    _, pk, rad = O.polar_encode(k, 128, cb)
+    kh = O.polar_decode(pk, rad, D, 128, cb)
+    S = np.random.default_rng(11).standard_normal((m, D)).astype(np.float32)
+    sg, rn = O.qjl_encode(k, kh, S)
+    gs, gn = tq.qjl_encode(torch.from_numpy(k).cuda(), torch.from_numpy(kh).cuda(),
+                           torch.from_numpy(S).cuda())
+    torch.cuda.synchronize()
+    assert np.array_equal(gs.cpu().numpy().view(np.uint32), sg)
+    assert np.array_equal(gn.cpu().numpy().view(np.uint16), rn.view(np.uint16))
+
+
+def _cfg3(seed, Hkv, N, D, H, block, m, qjl=True):
+    L = inputs.make_layer(seed, H, Hkv, D, N)
+    k, v, q = L["k"][0], L["v"][0], L["q"][0]
+    cb = codebooks(int(math.log2(block)))
+    _, pk, rad = O.polar_encode(k, block, cb)
+    S = signs = rn = None
+    if qjl:
+        kh = O.polar_decode(pk, rad, D, block, cb)
+        S = np.random.default_rng(seed).standard_normal((m, D)).astype(np.float32)
+        signs, rn = O.qjl_encode(k, kh, S)
+    vq, vs, vb = O.quantize(v)
+    return dict(q=q, cb=cb, pk=pk, rad=rad, S=S, signs=signs, rn=rn, vq=vq, vs=vs, vb=vb)
+
+
+def _dev(a):
+    if a is None:
+        return None
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint32:
+        a = a.view(np.int32)
+    return torch.from_numpy(a).cuda()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("Hkv,H,D,N,block,qjl,qdt", [
+    (16, 32, 128, 4096, 128, True, "f16"),   # config 3
+    (16, 32, 128, 4096, 128, False, "f32"),
+    (4, 16, 128, 513, 16, True, "f32"),
+    (2, 16, 256, 300, 64, True, "bf16"),
+    (8, 8, 128, 77, 32, False, "f16"),
+])
+def test_gpu_compressed_score(Hkv, H, D, N, block, qjl, qdt):
+    tq = _cuda()
+    c = _cfg3(11, Hkv, N, D, H, block, 256, qjl)
+    tdt = {"f16": torch.float16, "f32": torch.float32, "bf16": torch.bfloat16}[qdt]
+    qg = torch.from_numpy(c["q"]).to(tdt).cuda()
+    qref = qg.float().cpu().numpy()
+    ref = O.compressed_score(qref, c["pk"], c["rad"], c["cb"], block, 1.0, c["signs"], c["rn"], c["S"])
+    got = tq.compressed_score(qg, _dev(c["pk"]), _dev(c["rad"]), torch.from_numpy(c["cb"]), block, 1.0,
+                              _dev(c["signs"]), _dev(c["rn"]), _dev(c["S"])).cpu().numpy()
+    tol = 1e-3 * (np.abs(ref) + np.sqrt(np.mean(ref ** 2)))
+    assert np.all(np.abs(got - ref) <= tol), float(np.max(np.abs(got - ref) / tol))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("Hkv,H,D,N,block,qjl", [
+    (16, 32, 128, 4096, 128, True),   # config 3
+    (16, 32, 128, 4096, 128, False),
+    (4, 16, 256, 1000, 128, True),
+    (2, 2, 128, 33, 16, True),
+])
+def test_gpu_compressed_sdpa(Hkv, H, D, N, block, qjl):
+    tq = _cuda()
+    c = _cfg3(11, Hkv, N, D, H, block, 256, qjl)
+    qg = torch.from_numpy(c["q"]).half().cuda()
+    ref = O.compressed_sdpa(qg.float().cpu().numpy(), c["pk"], c["rad"], c["cb"], block, c["vq"],
+                            c["vs"], c["vb"], 1.0, c["signs"], c["rn"], c["S"])
+    got = tq.compressed_sdpa(qg, _dev(c["pk"]), _dev(c["rad"]), torch.from_numpy(c["cb"]),
+                             _dev(c["vq"]), _dev(c["vs"]), _dev(c["vb"]), block, 1.0,
+                             _dev(c["signs"]), _dev(c["rn"]), _dev(c["S"]), out_dtype=torch.float32)
+    parity(got.cpu().numpy(), ref)
+
+
+@pytest.mark.gpu
+def test_gpu_compressed_sdpa_empty_is_zero():
+    tq = _cuda()
+    c = _cfg3(11, 2, 4, 128, 4, 128, 256, True)
+    out = tq.compressed_sdpa(torch.zeros(4, 128, dtype=torch.float16, device="cuda"),
+                             _dev(c["pk"][:, :0]), _dev(c["rad"][:, :0]), torch.from_numpy(c["cb"]),
+                             _dev(c["vq"][:, :0]), _dev(c["vs"][:, :0]), _dev(c["vb"][:, :0]), 128,
+                             out_dtype=torch.float32)
+    assert torch.count_nonzero(out).item() == 0

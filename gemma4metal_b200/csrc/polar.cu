@@ -242,7 +242,9 @@ struct CParams {
   const __half* rnorm;    // (Hkv, N)
   const float* S;         // (m, D)
   int m;
-  const uint32_t* vq;     // (Hkv, N, D/8)
+  const uint32_t* vq;     // (Hkv, N, D/8) int4 V, or null when vdense is used
+  const void* vdense;     // (Hkv, N, D) dense V in vdense_dtype (the reference's fp32 values)
+  int vdense_dtype;
   int attend;             // 1: softmax . V into out; 0: scores only
   const void* vs;
   const void* vb;
@@ -351,20 +353,24 @@ __global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p, c
       continue;
     }
     // online softmax (natural log) and V accumulation
-    const uint32_t* vw = p.vq + row * (D / 8);
 #pragma unroll
     for (int c = 0; c < DPL; ++c) {
       const int d0 = c * 128 + 4 * lane;
-      const uint32_t word = vw[d0 / 8];
-      const int sh = 4 * (d0 % 8);
-      const long long gi = row * (D / 64) + d0 / 64;
-      const float sc = p.sb_f32 ? reinterpret_cast<const float*>(p.vs)[gi]
-                                : __half2float(reinterpret_cast<const __half*>(p.vs)[gi]);
-      const float bi = p.sb_f32 ? reinterpret_cast<const float*>(p.vb)[gi]
-                                : __half2float(reinterpret_cast<const __half*>(p.vb)[gi]);
       float vv[4];
+      if (p.vdense) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) vv[e] = fmaf(sc, static_cast<float>((word >> (sh + 4 * e)) & 15u), bi);
+        for (int e = 0; e < 4; ++e) vv[e] = load_as_float(p.vdense, row * D + d0 + e, p.vdense_dtype);
+      } else {
+        const uint32_t word = p.vq[row * (D / 8) + d0 / 8];
+        const int sh = 4 * (d0 % 8);
+        const long long gi = row * (D / 64) + d0 / 64;
+        const float sc = p.sb_f32 ? reinterpret_cast<const float*>(p.vs)[gi]
+                                  : __half2float(reinterpret_cast<const __half*>(p.vs)[gi]);
+        const float bi = p.sb_f32 ? reinterpret_cast<const float*>(p.vb)[gi]
+                                  : __half2float(reinterpret_cast<const __half*>(p.vb)[gi]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) vv[e] = fmaf(sc, static_cast<float>((word >> (sh + 4 * e)) & 15u), bi);
+      }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         if (c == 0) {
@@ -490,6 +496,74 @@ int csplits(int Hkv, int N) {
   return per > 0 ? (N + per - 1) / per : 1;
 }
 
+// ---- the reference's packed format for 16-value blocks (lib/turboquant.metal:501-600)
+// level 1: 8 x 4-bit in one uint32 (low nibble first); levels 2..4: 4, 2, 1 x
+// 2-bit fields in one byte each.
+__global__ void pack_ref_kernel(const uint8_t* angles, long long nblocks, uint32_t* p1, uint8_t* p2,
+                                uint8_t* p3, uint8_t* p4) {
+  for (long long b = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; b < nblocks;
+       b += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const uint8_t* a = angles + b * 15;
+    uint32_t w = 0;
+    for (int j = 0; j < 8; ++j) w |= (static_cast<uint32_t>(a[j]) & 15u) << (4 * j);
+    p1[b] = w;
+    uint32_t x = 0;
+    for (int j = 0; j < 4; ++j) x |= (a[8 + j] & 3u) << (2 * j);
+    p2[b] = static_cast<uint8_t>(x);
+    p3[b] = static_cast<uint8_t>((a[12] & 3u) | ((a[13] & 3u) << 2));
+    p4[b] = static_cast<uint8_t>(a[14] & 3u);
+  }
+}
+
+__global__ void unpack_ref_kernel(const uint32_t* p1, const uint8_t* p2, const uint8_t* p3,
+                                  const uint8_t* p4, long long nblocks, uint8_t* angles) {
+  for (long long b = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; b < nblocks;
+       b += static_cast<long long>(gridDim.x) * blockDim.x) {
+    uint8_t* a = angles + b * 15;
+    for (int j = 0; j < 8; ++j) a[j] = static_cast<uint8_t>((p1[b] >> (4 * j)) & 15u);
+    for (int j = 0; j < 4; ++j) a[8 + j] = static_cast<uint8_t>((p2[b] >> (2 * j)) & 3u);
+    a[12] = static_cast<uint8_t>(p3[b] & 3u);
+    a[13] = static_cast<uint8_t>((p3[b] >> 2) & 3u);
+    a[14] = static_cast<uint8_t>(p4[b] & 3u);
+  }
+}
+
+// level-major angle bytes (block-1 per block) -> 4-bit packed (block/2 per block)
+__global__ void pack4_kernel(const uint8_t* angles, long long nblocks, int block, uint8_t* packed) {
+  const long long total = nblocks * (block / 2);
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long b = i / (block / 2);
+    const int j = static_cast<int>(i % (block / 2)) * 2;
+    const uint8_t* a = angles + b * (block - 1);
+    const int lo = a[j], hi = (j + 1 < block - 1) ? a[j + 1] : 0;
+    packed[i] = static_cast<uint8_t>((lo & 15) | ((hi & 15) << 4));
+  }
+}
+
+// y = x P^T (transpose_p = 0) or y = x P (transpose_p = 1), D x D fp32 P.
+__global__ void __launch_bounds__(256) precondition_kernel(const void* x, int x_dtype, long long rows,
+                                                           int D, const float* P, int transpose_p,
+                                                           float* y) {
+  extern __shared__ float s_x[];  // 8 rows
+  for (long long r0 = static_cast<long long>(blockIdx.x) * 8; r0 < rows;
+       r0 += static_cast<long long>(gridDim.x) * 8) {
+    const int nr = static_cast<int>(rows - r0 < 8 ? rows - r0 : 8);
+    for (int i = threadIdx.x; i < nr * D; i += blockDim.x)
+      s_x[i] = load_as_float(x, r0 * D + i, x_dtype);
+    __syncthreads();
+    for (int i = threadIdx.x; i < nr * D; i += blockDim.x) {
+      const int rr = i / D, c = i % D;
+      float acc = 0.0f;
+      for (int j = 0; j < D; ++j)
+        acc = fmaf(s_x[rr * D + j], transpose_p ? P[static_cast<long long>(j) * D + c]
+                                                : P[static_cast<long long>(c) * D + j], acc);
+      y[(r0 + rr) * D + c] = acc;
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace
 }  // namespace tq
 
@@ -550,7 +624,10 @@ TQ_API size_t tq_compressed_sdpa_workspace_size(int num_heads, int num_kv_heads,
   if (num_kv_heads < 1 || num_heads < num_kv_heads || n_keys < 0) return 0;
   const int G = num_heads / num_kv_heads;
   const int s = csplits(num_kv_heads, n_keys);
-  return 256 + static_cast<size_t>(num_kv_heads) * s * 4 * G * (head_dim + 2) * sizeof(float);
+  // merge counters in the counter region every workspace of this library
+  // starts with (so decode and compressed calls can share one workspace)
+  return kCounterRegionBytes +
+         static_cast<size_t>(num_kv_heads) * s * 4 * G * (head_dim + 2) * sizeof(float);
 }
 
 static int compressed_common(const void* q, tq_dtype q_dtype, const uint8_t* packed,
@@ -559,7 +636,8 @@ static int compressed_common(const void* q, tq_dtype q_dtype, const uint8_t* pac
                              int n_keys, int block, const float* codebooks, float scale,
                              float* scores, const uint32_t* vq, const void* vs, const void* vb,
                              tq_dtype sb_dtype, void* out, tq_dtype out_dtype, void* workspace,
-                             size_t workspace_bytes, void* stream, const char* fn) {
+                             size_t workspace_bytes, void* stream, const char* fn,
+                             const void* vdense = nullptr, tq_dtype vdense_dtype = TQ_F32) {
   // key and value buffers may be NULL only for an empty context
   if (!q || !codebooks || (n_keys > 0 && (!packed || !radii || (signs && (!rnorm || !S)))))
     return err(TQ_ERR_INVALID, "compressed attention: null pointer argument");
@@ -586,6 +664,8 @@ static int compressed_common(const void* q, tq_dtype q_dtype, const uint8_t* pac
   p.S = S;
   p.m = signs ? m : 0;
   p.vq = vq;
+  p.vdense = vdense;
+  p.vdense_dtype = vdense_dtype;
   p.attend = out != nullptr;
   p.vs = vs;
   p.vb = vb;
@@ -609,9 +689,9 @@ static int compressed_common(const void* q, tq_dtype q_dtype, const uint8_t* pac
       return TQ_ERR_WORKSPACE;
     }
     p.counters = static_cast<unsigned*>(workspace);
-    p.ws = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + 256);
-    if (num_kv_heads * sizeof(unsigned) > 256)
-      return err(TQ_ERR_UNSUPPORTED, "compressed attention: at most 64 KV heads");
+    p.ws = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kCounterRegionBytes);
+    if (num_kv_heads * sizeof(unsigned) > kCounterRegionBytes)
+      return err(TQ_ERR_UNSUPPORTED, "compressed attention: too many KV heads");
   }
   void* fn_ptr = head_dim == 128 ? pick_cattn<128>(G) : pick_cattn<256>(G);
   void* args[] = {&p, &T};
@@ -646,6 +726,81 @@ TQ_API int tq_compressed_sdpa(const void* queries, tq_dtype q_dtype, const uint8
                            num_kv_heads, head_dim, n_keys, block, codebooks, scale, nullptr,
                            v_quant, v_scales, v_biases, sb_dtype, out, out_dtype, workspace,
                            workspace_bytes, stream, "tq_compressed_sdpa");
+}
+
+TQ_API int tq_compressed_sdpa_dense_v(const void* queries, tq_dtype q_dtype, const uint8_t* packed,
+                                      const void* radii, const uint32_t* signs, const void* rnorm,
+                                      const float* S, int m, int num_heads, int num_kv_heads,
+                                      int head_dim, int n_keys, int block, const float* codebooks,
+                                      float scale, const void* values, tq_dtype v_dtype, void* out,
+                                      tq_dtype out_dtype, void* workspace, size_t workspace_bytes,
+                                      void* stream) {
+  if (!out || (n_keys > 0 && !values))
+    return err(TQ_ERR_INVALID, "tq_compressed_sdpa_dense_v: null values or out");
+  return compressed_common(queries, q_dtype, packed, radii, signs, rnorm, S, m, num_heads,
+                           num_kv_heads, head_dim, n_keys, block, codebooks, scale, nullptr,
+                           nullptr, nullptr, nullptr, TQ_F16, out, out_dtype, workspace,
+                           workspace_bytes, stream, "tq_compressed_sdpa_dense_v", values, v_dtype);
+}
+
+}  // extern "C"
+
+extern "C" {
+
+TQ_API int tq_polar_pack_ref(const uint8_t* angles, int64_t n_blocks, uint32_t* packed_l1,
+                             uint8_t* packed_l2, uint8_t* packed_l3, uint8_t* packed_l4,
+                             void* stream) {
+  if (n_blocks < 0 || (n_blocks > 0 && (!angles || !packed_l1 || !packed_l2 || !packed_l3 || !packed_l4)))
+    return err(TQ_ERR_INVALID, "tq_polar_pack_ref: bad arguments");
+  if (n_blocks == 0) return TQ_OK;
+  const int grid = static_cast<int>((n_blocks + 255) / 256 < 4096 ? (n_blocks + 255) / 256 : 4096);
+  pack_ref_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(angles, n_blocks, packed_l1,
+                                                                      packed_l2, packed_l3, packed_l4);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TQ_OK : cuda_err(e, "tq_polar_pack_ref");
+}
+
+TQ_API int tq_polar_unpack_ref(const uint32_t* packed_l1, const uint8_t* packed_l2,
+                               const uint8_t* packed_l3, const uint8_t* packed_l4, int64_t n_blocks,
+                               uint8_t* angles, void* stream) {
+  if (n_blocks < 0 || (n_blocks > 0 && (!angles || !packed_l1 || !packed_l2 || !packed_l3 || !packed_l4)))
+    return err(TQ_ERR_INVALID, "tq_polar_unpack_ref: bad arguments");
+  if (n_blocks == 0) return TQ_OK;
+  const int grid = static_cast<int>((n_blocks + 255) / 256 < 4096 ? (n_blocks + 255) / 256 : 4096);
+  unpack_ref_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(packed_l1, packed_l2,
+                                                                        packed_l3, packed_l4, n_blocks,
+                                                                        angles);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TQ_OK : cuda_err(e, "tq_polar_unpack_ref");
+}
+
+}  // extern "C"
+
+extern "C" {
+
+TQ_API int tq_polar_pack4(const uint8_t* angles, int64_t n_blocks, int block, uint8_t* packed,
+                          void* stream) {
+  if (n_blocks < 0 || block < 2 || block > 128 || (n_blocks > 0 && (!angles || !packed)))
+    return err(TQ_ERR_INVALID, "tq_polar_pack4: bad arguments");
+  if (n_blocks == 0) return TQ_OK;
+  const long long total = n_blocks * (block / 2);
+  const int grid = static_cast<int>((total + 255) / 256 < 4096 ? (total + 255) / 256 : 4096);
+  pack4_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(angles, n_blocks, block, packed);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TQ_OK : cuda_err(e, "tq_polar_pack4");
+}
+
+TQ_API int tq_precondition(const void* x, tq_dtype x_dtype, int64_t rows, int head_dim,
+                           const float* P, int transpose_p, float* y, void* stream) {
+  if (rows < 0 || head_dim < 1 || head_dim > 1024 || (rows > 0 && (!x || !P || !y)))
+    return err(TQ_ERR_INVALID, "tq_precondition: bad arguments");
+  if (rows == 0) return TQ_OK;
+  const long long ctas = (rows + 7) / 8;
+  const int grid = static_cast<int>(ctas < 4096 ? ctas : 4096);
+  precondition_kernel<<<grid, 256, 8 * head_dim * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
+      x, x_dtype, rows, head_dim, P, transpose_p, y);
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? TQ_OK : cuda_err(e, "tq_precondition");
 }
 
 }  // extern "C"

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <map>
 #include <mutex>
 #include <stdexcept>
@@ -280,6 +281,243 @@ array lse_merge(const array& parts, int num_heads, int head_dim, Dtype out_dtype
   check(tq_lse_merge(static_cast<const float*>(parts.data()), P, B, num_heads, head_dim, out.data(),
                      to_c(out_dtype, "lse_merge"), s),
         "lse_merge");
+  return out;
+}
+
+// ---- PolarQuant (reference block-16 API) ------------------------------------
+
+namespace {
+
+constexpr int kRefBlock = 16;
+constexpr int kRefLevels = 4;
+
+void require_block16(int block_size, const char* where) {
+  if (block_size != kRefBlock)
+    raise(where, "the reference's per-level API is defined for 16-value blocks");
+}
+
+// (7, 16) host codebook table from four device codebooks; sizes per level
+std::vector<float> host_codebooks(const array* cb[kRefLevels], std::vector<int>* sizes,
+                                  cudaStream_t s) {
+  std::vector<float> t(7 * 16, 0.0f);
+  if (sizes) sizes->assign(kRefLevels, 0);
+  for (int l = 0; l < kRefLevels; ++l) {
+    auto v = cb[l]->to_vector<float>(s);
+    if (v.empty() || v.size() > 16) raise("polar", "codebooks need 1..16 entries");
+    for (size_t c = 0; c < v.size(); ++c) t[l * 16 + c] = v[c];
+    if (sizes) (*sizes)[l] = static_cast<int>(v.size());
+  }
+  return t;
+}
+
+// level-major angle bytes (N_blocks, 15) from / to the per-level arrays
+array join_levels(const array* idx[kRefLevels], long long nblocks, cudaStream_t s) {
+  array a({static_cast<int>(nblocks), kRefBlock - 1}, Dtype::uint8, s);
+  int off = 0;
+  for (int l = 0; l < kRefLevels; ++l) {
+    const int w = kRefBlock >> (l + 1);
+    if (static_cast<long long>(idx[l]->size()) != nblocks * w) raise("polar", "index array size");
+    check_cuda(cudaMemcpy2DAsync(static_cast<uint8_t*>(a.data()) + off, kRefBlock - 1, idx[l]->data(), w, w,
+                                 nblocks, cudaMemcpyDeviceToDevice, s),
+               "polar (join levels)");
+    off += w;
+  }
+  return a;
+}
+
+std::vector<array> split_levels(const array& a, long long nblocks, cudaStream_t s) {
+  std::vector<array> out;
+  int off = 0;
+  for (int l = 0; l < kRefLevels; ++l) {
+    const int w = kRefBlock >> (l + 1);
+    array o({static_cast<int>(nblocks * w)}, Dtype::uint8, s);
+    check_cuda(cudaMemcpy2DAsync(o.data(), w, static_cast<const uint8_t*>(a.data()) + off, kRefBlock - 1, w,
+                                 nblocks, cudaMemcpyDeviceToDevice, s),
+               "polar (split levels)");
+    out.push_back(o);
+    off += w;
+  }
+  return out;
+}
+
+array precondition_apply(const array& x, const array& P, int transpose_p, cudaStream_t s) {
+  const int D = x.shape(-1);
+  if (P.ndim() != 2 || P.shape(0) != D || P.shape(1) != D) raise("polar", "precondition must be (D, D)");
+  const long long rows = static_cast<long long>(x.size() / D);
+  array y(x.shape(), Dtype::float32, s);
+  check(tq_precondition(x.data(), to_c(x.dtype(), "polar"), rows, D, static_cast<const float*>(P.data()),
+                        transpose_p, static_cast<float*>(y.data()), s),
+        "polar (precondition)");
+  return y;
+}
+
+// encode -> level-major angles (N_blocks, 15) + radii
+std::pair<array, array> encode16(const array& vectors, const array& precondition,
+                                 const array* cb[kRefLevels], cudaStream_t s) {
+  if (vectors.ndim() != 2) raise("polar_quantize", "vectors must be (N, D)");
+  const int D = vectors.shape(1);
+  if (D % 128) raise("polar_quantize", "D must be a multiple of 128");
+  array y = precondition_apply(vectors, precondition, 0, s);
+  std::vector<int> sizes;
+  auto t = host_codebooks(cb, &sizes, s);
+  const long long nblocks = static_cast<long long>(vectors.shape(0)) * (D / kRefBlock);
+  array ang({static_cast<int>(nblocks), kRefBlock - 1}, Dtype::uint8, s);
+  array rad({static_cast<int>(nblocks)}, Dtype::float16, s);
+  check(tq_polar_encode(static_cast<const float*>(y.data()), vectors.shape(0), D, kRefBlock, t.data(),
+                        sizes.data(), static_cast<uint8_t*>(ang.data()), nullptr, rad.data(), s),
+        "polar_quantize");
+  return {ang, rad};
+}
+
+array decode16(const array& angles, const array& radii, int D, const std::vector<float>& t,
+               cudaStream_t s) {
+  const long long nblocks = static_cast<long long>(radii.size());
+  const long long rows = nblocks * kRefBlock / D;
+  array y({static_cast<int>(rows), D}, Dtype::float32, s);
+  check(tq_polar_decode(static_cast<const uint8_t*>(angles.data()), nullptr, radii.data(), rows, D,
+                        kRefBlock, t.data(), static_cast<float*>(y.data()), s),
+        "polar_dequantize");
+  return y;
+}
+
+array packed4(const array& angles, cudaStream_t s) {
+  const long long nblocks = angles.shape(0);
+  array pk({static_cast<int>(nblocks), kRefBlock / 2}, Dtype::uint8, s);
+  check(tq_polar_pack4(static_cast<const uint8_t*>(angles.data()), nblocks, kRefBlock,
+                       static_cast<uint8_t*>(pk.data()), s),
+        "polar (pack)");
+  return pk;
+}
+
+array unpack_ref(const array& p1, const array& p2, const array& p3, const array& p4, cudaStream_t s) {
+  const long long nblocks = static_cast<long long>(p1.size());
+  array ang({static_cast<int>(nblocks), kRefBlock - 1}, Dtype::uint8, s);
+  check(tq_polar_unpack_ref(static_cast<const uint32_t*>(p1.data()), static_cast<const uint8_t*>(p2.data()),
+                            static_cast<const uint8_t*>(p3.data()), static_cast<const uint8_t*>(p4.data()),
+                            nblocks, static_cast<uint8_t*>(ang.data()), s),
+        "polar (unpack)");
+  return ang;
+}
+
+}  // namespace
+
+std::vector<array> polar_quantize(const array& vectors, const array& precondition, const array& cb_l1,
+                                  const array& cb_l2, const array& cb_l3, const array& cb_l4,
+                                  int block_size, cudaStream_t s) {
+  require_block16(block_size, "polar_quantize");
+  const array* cb[kRefLevels] = {&cb_l1, &cb_l2, &cb_l3, &cb_l4};
+  auto enc = encode16(vectors, precondition, cb, s);
+  auto out = split_levels(enc.first, enc.first.shape(0), s);
+  out.push_back(enc.second);
+  return out;
+}
+
+array polar_dequantize(const array& i1, const array& i2, const array& i3, const array& i4,
+                       const array& radii, const array& precondition, const array& cb_l1,
+                       const array& cb_l2, const array& cb_l3, const array& cb_l4, int block_size,
+                       cudaStream_t s) {
+  require_block16(block_size, "polar_dequantize");
+  const array* cb[kRefLevels] = {&cb_l1, &cb_l2, &cb_l3, &cb_l4};
+  const array* idx[kRefLevels] = {&i1, &i2, &i3, &i4};
+  const int D = precondition.shape(0);
+  auto t = host_codebooks(cb, nullptr, s);
+  array y = decode16(join_levels(idx, static_cast<long long>(radii.size()), s), radii, D, t, s);
+  return precondition_apply(y, precondition, 1, s);
+}
+
+std::vector<array> polar_quantize_packed(const array& vectors, const array& precondition,
+                                         const array& cb_l1, const array& cb_l2, const array& cb_l3,
+                                         const array& cb_l4, int block_size, cudaStream_t s) {
+  require_block16(block_size, "polar_quantize_packed");
+  const array* cb[kRefLevels] = {&cb_l1, &cb_l2, &cb_l3, &cb_l4};
+  for (int l = 1; l < kRefLevels; ++l)
+    if (cb[l]->size() > 4) raise("polar_quantize_packed", "levels 2-4 are 2-bit: at most 4 codebook entries");
+  auto enc = encode16(vectors, precondition, cb, s);
+  const long long nblocks = enc.first.shape(0);
+  array p1({static_cast<int>(nblocks)}, Dtype::uint32, s), p2({static_cast<int>(nblocks)}, Dtype::uint8, s),
+      p3({static_cast<int>(nblocks)}, Dtype::uint8, s), p4({static_cast<int>(nblocks)}, Dtype::uint8, s);
+  check(tq_polar_pack_ref(static_cast<const uint8_t*>(enc.first.data()), nblocks,
+                          static_cast<uint32_t*>(p1.data()), static_cast<uint8_t*>(p2.data()),
+                          static_cast<uint8_t*>(p3.data()), static_cast<uint8_t*>(p4.data()), s),
+        "polar_quantize_packed");
+  return {p1, p2, p3, p4, enc.second};
+}
+
+array polar_dequantize_packed(const array& p1, const array& p2, const array& p3, const array& p4,
+                              const array& radii, const array& cb_l1, const array& cb_l2,
+                              const array& cb_l3, const array& cb_l4, int D, int block_size,
+                              cudaStream_t s) {
+  require_block16(block_size, "polar_dequantize_packed");
+  const array* cb[kRefLevels] = {&cb_l1, &cb_l2, &cb_l3, &cb_l4};
+  auto t = host_codebooks(cb, nullptr, s);
+  return decode16(unpack_ref(p1, p2, p3, p4, s), radii, D, t, s);
+}
+
+array polar_dequantize_packed_fast(const array& p1, const array& p2, const array& p3, const array& p4,
+                                   const array& radii, const array& cs_l1, const array& cs_l2,
+                                   const array& cs_l3, const array& cs_l4, int D, int block_size,
+                                   cudaStream_t s) {
+  require_block16(block_size, "polar_dequantize_packed_fast");
+  const array* cs[kRefLevels] = {&cs_l1, &cs_l2, &cs_l3, &cs_l4};
+  std::vector<float> t(7 * 16, 0.0f);
+  for (int l = 0; l < kRefLevels; ++l) {
+    auto v = cs[l]->to_vector<float>(s);
+    for (size_t c = 0; c + 1 < v.size() && c / 2 < 16; c += 2)
+      t[l * 16 + c / 2] = static_cast<float>(std::atan2(static_cast<double>(v[c + 1]), static_cast<double>(v[c])));
+  }
+  return decode16(unpack_ref(p1, p2, p3, p4, s), radii, D, t, s);
+}
+
+array polar_dequantize_fast(const array& i1, const array& i2, const array& i3, const array& i4,
+                            const array& radii, const array& cb_l1, const array& cb_l2,
+                            const array& cb_l3, const array& cb_l4, int D, int block_size,
+                            cudaStream_t s) {
+  require_block16(block_size, "polar_dequantize_fast");
+  const array* cb[kRefLevels] = {&cb_l1, &cb_l2, &cb_l3, &cb_l4};
+  const array* idx[kRefLevels] = {&i1, &i2, &i3, &i4};
+  auto t = host_codebooks(cb, nullptr, s);
+  return decode16(join_levels(idx, static_cast<long long>(radii.size()), s), radii, D, t, s);
+}
+
+array compressed_score(const array& queries, const array& i1, const array& i2, const array& i3,
+                       const array& i4, const array& radii, const array& cb_l1, const array& cb_l2,
+                       const array& cb_l3, const array& cb_l4, int N, int block_size, float scale,
+                       cudaStream_t s) {
+  require_block16(block_size, "compressed_score");
+  const array* cb[kRefLevels] = {&cb_l1, &cb_l2, &cb_l3, &cb_l4};
+  const array* idx[kRefLevels] = {&i1, &i2, &i3, &i4};
+  const int Nq = queries.shape(0), D = queries.shape(1);
+  auto t = host_codebooks(cb, nullptr, s);
+  array pk = packed4(join_levels(idx, static_cast<long long>(radii.size()), s), s);
+  array scores({Nq, N}, Dtype::float32, s);
+  check(tq_compressed_score(queries.data(), to_c(queries.dtype(), "compressed_score"),
+                            static_cast<const uint8_t*>(pk.data()), radii.data(), nullptr, nullptr,
+                            nullptr, 0, Nq, Nq, D, N, kRefBlock, t.data(), scale,
+                            static_cast<float*>(scores.data()), s),
+        "compressed_score");
+  return scores;
+}
+
+array compressed_sdpa(const array& queries, const array& i1, const array& i2, const array& i3,
+                      const array& i4, const array& radii, const array& cb_l1, const array& cb_l2,
+                      const array& cb_l3, const array& cb_l4, const array& values, int block_size,
+                      float scale, cudaStream_t s) {
+  require_block16(block_size, "compressed_sdpa");
+  const array* cb[kRefLevels] = {&cb_l1, &cb_l2, &cb_l3, &cb_l4};
+  const array* idx[kRefLevels] = {&i1, &i2, &i3, &i4};
+  const int Nq = queries.shape(0), D = queries.shape(1);
+  const int N = values.shape(0) / (Nq > 0 ? Nq : 1);
+  auto t = host_codebooks(cb, nullptr, s);
+  array pk = packed4(join_levels(idx, static_cast<long long>(radii.size()), s), s);
+  array out({Nq, D}, Dtype::float32, s);
+  const size_t need = tq_compressed_sdpa_workspace_size(Nq, Nq, D, N);
+  array ws = workspace(need, s);
+  check(tq_compressed_sdpa_dense_v(queries.data(), to_c(queries.dtype(), "compressed_sdpa"),
+                                   static_cast<const uint8_t*>(pk.data()), radii.data(), nullptr,
+                                   nullptr, nullptr, 0, Nq, Nq, D, N, kRefBlock, t.data(), scale,
+                                   values.data(), to_c(values.dtype(), "compressed_sdpa"), out.data(),
+                                   TQ_F32, ws.data(), ws.nbytes(), s),
+        "compressed_sdpa");
   return out;
 }
 

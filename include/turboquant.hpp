@@ -145,6 +145,63 @@ TQ_CXX_API array sdpa_int4_partial(const array& queries, const KVCache& shard, i
 TQ_CXX_API array lse_merge(const array& parts, int num_heads, int head_dim, Dtype out_dtype = Dtype::float32,
                 cudaStream_t s = nullptr);
 
+// ---- PolarQuant compressed keys (lib/turboquant.h:52-165) --------------------
+// Same names, arguments and shapes as the reference: 16-value blocks and four
+// level codebooks cb_l1..cb_l4 (fp32 device arrays of <= 16 entries; the packed
+// format's levels 2-4 hold 2-bit indices, so those codebooks need <= 4
+// entries). Indices come back as the reference's per-level uint8 arrays
+// i1 (N*nb*8), i2 (N*nb*4), i3 (N*nb*2), i4 (N*nb); radii fp16 (N*nb).
+// Codebooks are read on the host (the stream is synchronised for it).
+TQ_CXX_API std::vector<array> polar_quantize(const array& vectors, const array& precondition,
+                                             const array& cb_l1, const array& cb_l2,
+                                             const array& cb_l3, const array& cb_l4,
+                                             int block_size = 16, cudaStream_t s = nullptr);
+// (N, D) fp32 = decode(...) . precondition, D = precondition.shape(0).
+TQ_CXX_API array polar_dequantize(const array& indices_l1, const array& indices_l2,
+                                  const array& indices_l3, const array& indices_l4,
+                                  const array& radii, const array& precondition,
+                                  const array& cb_l1, const array& cb_l2, const array& cb_l3,
+                                  const array& cb_l4, int block_size = 16, cudaStream_t s = nullptr);
+// {packed_l1 uint32 (N_blocks), packed_l2/l3/l4 uint8 (N_blocks), radii fp16 (N_blocks)}
+TQ_CXX_API std::vector<array> polar_quantize_packed(const array& vectors, const array& precondition,
+                                                    const array& cb_l1, const array& cb_l2,
+                                                    const array& cb_l3, const array& cb_l4,
+                                                    int block_size = 16, cudaStream_t s = nullptr);
+TQ_CXX_API array polar_dequantize_packed(const array& packed_l1, const array& packed_l2,
+                                         const array& packed_l3, const array& packed_l4,
+                                         const array& radii, const array& cb_l1, const array& cb_l2,
+                                         const array& cb_l3, const array& cb_l4, int D,
+                                         int block_size = 16, cudaStream_t s = nullptr);
+// cs_l*: (entries, 2) fp32 {cos, sin} tables; decoded with the angles
+// atan2(sin, cos) of the table entries.
+TQ_CXX_API array polar_dequantize_packed_fast(const array& packed_l1, const array& packed_l2,
+                                              const array& packed_l3, const array& packed_l4,
+                                              const array& radii, const array& cs_l1,
+                                              const array& cs_l2, const array& cs_l3,
+                                              const array& cs_l4, int D, int block_size = 16,
+                                              cudaStream_t s = nullptr);
+// queries (Nq, D) preconditioned; query i attends to keys [i*N, (i+1)*N) and
+// values (Nq*N, D) fp32 (N = values.shape(0) / Nq). Returns (Nq, D) fp32.
+TQ_CXX_API array compressed_sdpa(const array& queries, const array& indices_l1,
+                                 const array& indices_l2, const array& indices_l3,
+                                 const array& indices_l4, const array& radii, const array& cb_l1,
+                                 const array& cb_l2, const array& cb_l3, const array& cb_l4,
+                                 const array& values, int block_size = 16, float scale = 0.0884f,
+                                 cudaStream_t s = nullptr);
+// Inverse polar only (no preconditioner): (N_blocks * block / D, D) fp32.
+TQ_CXX_API array polar_dequantize_fast(const array& indices_l1, const array& indices_l2,
+                                       const array& indices_l3, const array& indices_l4,
+                                       const array& radii, const array& cb_l1, const array& cb_l2,
+                                       const array& cb_l3, const array& cb_l4, int D,
+                                       int block_size = 16, cudaStream_t s = nullptr);
+// (Nq, N) fp32 scores of query i against keys [i*N, (i+1)*N).
+TQ_CXX_API array compressed_score(const array& queries, const array& indices_l1,
+                                  const array& indices_l2, const array& indices_l3,
+                                  const array& indices_l4, const array& radii, const array& cb_l1,
+                                  const array& cb_l2, const array& cb_l3, const array& cb_l4, int N,
+                                  int block_size = 16, float scale = 0.0884f,
+                                  cudaStream_t s = nullptr);
+
 }  // namespace turboquant
 
 #endif  // TURBOQUANT_HPP

@@ -242,6 +242,41 @@ TQ_API int tq_compressed_sdpa(const void* queries, tq_dtype q_dtype, const uint8
                               tq_dtype out_dtype, void* workspace, size_t workspace_bytes,
                               void* stream);
 
+/* tq_compressed_sdpa with dense values (Hkv, n_keys, head_dim) in v_dtype, as
+ * the reference's compressed_sdpa takes fp32 values (lib/turboquant.h:129-142,
+ * lib/turboquant.metal:166-224; the reference normalises by sum + 1e-8, this
+ * by the exact sum). */
+TQ_API int tq_compressed_sdpa_dense_v(const void* queries, tq_dtype q_dtype, const uint8_t* packed,
+                                      const void* radii, const uint32_t* signs, const void* rnorm,
+                                      const float* S, int m, int num_heads, int num_kv_heads,
+                                      int head_dim, int n_keys, int block, const float* codebooks,
+                                      float scale, const void* values, tq_dtype v_dtype, void* out,
+                                      tq_dtype out_dtype, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+
+/* The reference's packed format for 16-value blocks (polar_quantize_packed,
+ * lib/turboquant.h:75-92, lib/turboquant.metal:501-600): from/to the
+ * level-major angle bytes of tq_polar_encode (15 per block). packed_l1 holds
+ * level 1's 8 4-bit indices per block (low nibble first); packed_l2..l4 hold
+ * levels 2..4 as 2-bit fields (4, 2, 1 per byte), so their indices must be < 4. */
+TQ_API int tq_polar_pack_ref(const uint8_t* angles, int64_t n_blocks, uint32_t* packed_l1,
+                             uint8_t* packed_l2, uint8_t* packed_l3, uint8_t* packed_l4,
+                             void* stream);
+TQ_API int tq_polar_unpack_ref(const uint32_t* packed_l1, const uint8_t* packed_l2,
+                               const uint8_t* packed_l3, const uint8_t* packed_l4, int64_t n_blocks,
+                               uint8_t* angles, void* stream);
+
+/* Level-major angle bytes (n_blocks, block-1) -> 4-bit packed (n_blocks, block/2),
+ * the format the compressed-key attention reads. */
+TQ_API int tq_polar_pack4(const uint8_t* angles, int64_t n_blocks, int block, uint8_t* packed,
+                          void* stream);
+
+/* Preconditioner (lib/turboquant.cpp:102,122): y = x P^T (transpose_p = 0, the
+ * encode side) or y = x P (transpose_p = 1, the decode side); x (rows, head_dim)
+ * in x_dtype, P (head_dim, head_dim) fp32, y fp32. */
+TQ_API int tq_precondition(const void* x, tq_dtype x_dtype, int64_t rows, int head_dim,
+                           const float* P, int transpose_p, float* y, void* stream);
+
 /* Read and clear the device error word that kernels set when a bounded wait
  * gives up (0 = no error). Synchronises `stream`. */
 TQ_API int tq_device_error(void* stream, uint32_t* code);

@@ -22,7 +22,9 @@ def test_library_exports_cpp_api():
     from gemma4metal_b200.turboquant import LIB_PATH
     names = declared_cpp_functions()
     assert {"quantize", "dequantize", "sdpa_int4", "set_metallib_path", "sdpa_int4_partial",
-            "lse_merge"} <= names
+            "lse_merge", "polar_quantize", "polar_dequantize", "polar_quantize_packed",
+            "polar_dequantize_packed", "polar_dequantize_packed_fast", "compressed_sdpa",
+            "polar_dequantize_fast", "compressed_score"} <= names
     out = subprocess.run(["nm", "-DC", "--defined-only", LIB_PATH], capture_output=True, text=True,
                          check=True).stdout
     for n in names:
@@ -39,9 +41,12 @@ def test_cpp_mirror_test_builds():
 
 
 @pytest.mark.gpu
-def test_cpp_mirror_of_reference_test_passes():
+@pytest.mark.parametrize("name", ["test_sdpa_int4", "test_polar"])
+def test_cpp_programs_pass(name):
+    """tests/cpp/test_sdpa_int4.cpp mirrors the reference's tests/test_sdpa_int4.cpp;
+    tests/cpp/test_polar.cpp exercises the reference's PolarQuant entry points."""
     from gemma4metal_b200 import build as b
-    exe = b.cpp_test_binary("test_sdpa_int4")
+    exe = b.cpp_test_binary(name)
     if not os.path.exists(exe):
         b.build_cpp_tests()
     r = subprocess.run([exe], capture_output=True, text=True, timeout=300)

@@ -95,6 +95,8 @@ int visible_max(int n_tokens, int window) {
 }  // namespace
 
 namespace tq {
+uint32_t* device_error_word() { return device_error_ptr(); }
+
 void set_last_error(const char* fmt, ...) {
   char buf[512];
   va_list ap;

@@ -112,6 +112,9 @@ cudaError_t launch_pdl(void (*kernel)(K...), dim3 grid, dim3 block, size_t smem,
 // ("" if it did not); the C ABI appends it to tq_last_error().
 std::string& launch_detail();
 
+// The current device's error word (kernels record bounded-wait timeouts in it).
+uint32_t* device_error_word();
+
 // Set the calling thread's tq_last_error() message (printf-style).
 void set_last_error(const char* fmt, ...);
 

@@ -78,6 +78,10 @@ def _register_extra(L) -> None:
     L.tq_compressed_sdpa_workspace_size.argtypes = [I, I, I, I]
     L.tq_compressed_sdpa.argtypes = [P, I, P, P, P, P, P, I, I, I, I, I, I, P, F, P, P, P, I, P, I,
                                      P, SZ, P]
+    L.tq_sdpa_int4_multi_workspace_size.restype = SZ
+    L.tq_sdpa_int4_multi_workspace_size.argtypes = [I, I, I, I, I]
+    L.tq_sdpa_int4_multi.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, I, I, P, I,
+                                     P, SZ, P]
 
 
 def _check(rc: int) -> None:
@@ -460,5 +464,36 @@ def compressed_sdpa(queries: torch.Tensor, packed: torch.Tensor, radii: torch.Te
         _ptr(qc), _dt(qc), _ptr(packed), _ptr(radii), _ptr(signs), _ptr(rnorm), _ptr(Sc),
         0 if Sc is None else Sc.shape[0], H, Hkv, D, N, block_size, _host_ptr(cb),
         float(scale), _ptr(v_quant), _ptr(v_scales), _ptr(v_biases), _dt(v_scales), _ptr(out),
+        _dt(out), _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
+    return out
+
+
+# ------------------------------------------- many queries per KV head (tcgen05) --
+
+def sdpa_int4_multi(queries: torch.Tensor, k_quant, k_scales, k_biases, v_quant, v_scales,
+                    v_biases, gqa_factor: int, scale: float = 1.0, sliding_window: int = 0, *,
+                    n_tokens: Optional[int] = None, causal: bool = False, pos0: int = 0,
+                    out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                    ws: Optional[torch.Tensor] = None, s=None) -> torch.Tensor:
+    """Attention of n_q queries (n_q, H, D) against one int4 cache (Hkv, cap, D/8)
+    on the tensor cores: batched decode of many sequences over a shared cache
+    (causal=False) or a causal prefill chunk whose query i sits at position
+    pos0 + i (causal=True)."""
+    cache = [k_quant, k_scales, k_biases, v_quant, v_scales, v_biases]
+    if k_quant.dim() == 4:
+        cache = [c[0] for c in cache]
+    nq, H, D = queries.shape
+    Hkv, cap, _ = cache[0].shape
+    n = cap if n_tokens is None else int(n_tokens)
+    od = out_dtype or queries.dtype
+    if out is None:
+        out = torch.empty(nq, H, D, dtype=od, device=queries.device)
+    nbytes = int(load_library().tq_sdpa_int4_multi_workspace_size(nq, H, Hkv, D, n))
+    if ws is None:
+        ws = workspace(queries.device, nbytes, s)
+    qc = queries.contiguous()
+    _check(load_library().tq_sdpa_int4_multi(
+        _ptr(qc), _dt(qc), *[_ptr(c) for c in cache], _dt(cache[1]), int(gqa_factor), float(scale),
+        int(sliding_window), Hkv, D, nq, n, cap, 1 if causal else 0, int(pos0), _ptr(out),
         _dt(out), _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
     return out

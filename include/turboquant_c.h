@@ -173,6 +173,28 @@ TQ_API int tq_sdpa_int4_noalloc(const void* queries, tq_dtype q_dtype, const uin
                                 const int32_t* seq_lens, void* out, tq_dtype out_dtype,
                                 void* stream);
 
+/* ---- many query rows per KV head on the tensor cores (tcgen05 + TMEM) -------
+ * n_q queries (n_q, H, D) against one int4 cache (Hkv, capacity, D/8) holding
+ * n_tokens tokens: the batched decode of many sequences against a shared cache
+ * (causal = 0: every query sees all n_tokens, the sliding window counts back
+ * from the last token) and the prefill chunk (causal = 1: query i sits at
+ * position pos0 + i and sees tokens t <= pos0 + i, and pos0 + i - t < window
+ * when sliding_window > 0). The reference runs both through MLX dequantize +
+ * fast::sdpa with a CPU-built mask (engine/gemma4_multilayer.cpp:307-308,
+ * 347-367,441-464). head_dim 128; queries are used in fp16 (bf16 and fp16
+ * inputs exactly); out (n_q, H, D) in out_dtype. The workspace
+ * (tq_sdpa_int4_multi_workspace_size, zero-filled once) may be NULL when
+ * that size is 0. */
+TQ_API size_t tq_sdpa_int4_multi_workspace_size(int n_q, int num_heads, int num_kv_heads,
+                                                int head_dim, int n_tokens);
+TQ_API int tq_sdpa_int4_multi(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,
+                              const void* k_scales, const void* k_biases, const uint32_t* v_quant,
+                              const void* v_scales, const void* v_biases, tq_dtype sb_dtype,
+                              int gqa_factor, float scale, int sliding_window, int num_kv_heads,
+                              int head_dim, int n_q, int n_tokens, int capacity, int causal,
+                              int pos0, void* out, tq_dtype out_dtype, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
 /* ---- PolarQuant + QJL compressed keys ----------------------------------------
  * Blocks of `block` values (16, 32, 64 or 128; head_dim a multiple of 128) are
  * encoded as in lib/turboquant.metal:8-98 (polar_fused_quantize), generalised

@@ -377,3 +377,29 @@ def compressed_sdpa(q, packed, radii, codebooks, block, vq, vs, vb, scale=1.0, s
         _ptr(np.ascontiguousarray(vq)), _ptr(np.ascontiguousarray(vs)),
         _ptr(np.ascontiguousarray(vb)), 1 if vs.dtype == np.float32 else 0, _ptr(out))
     return out
+
+
+def sdpa_multi_np(q, k, v, scale=1.0, causal=False, pos0=0, window=0, n_tokens=None):
+    """Many queries against one dense K/V (fp64): q (n_q, H, D), k, v (Hkv, N, D).
+    causal: query i at position pos0 + i sees t <= pos0 + i; otherwise every
+    query sits at the last token. window > 0 also masks pos - t >= window (the
+    masks the engine builds for prefill, engine/gemma4_multilayer.cpp:347-367,
+    441-464, and lib/turboquant.metal:779 for decode)."""
+    nq, H, D = q.shape
+    Hkv = k.shape[0]
+    N = k.shape[1] if n_tokens is None else n_tokens
+    G = H // Hkv
+    qq = q.astype(np.float64).reshape(nq, Hkv, G, D) * scale
+    s = np.einsum("qhgd,htd->qhgt", qq, k[:, :N].astype(np.float64))
+    t = np.arange(N)
+    pos = (pos0 + np.arange(nq)) if causal else np.full(nq, N - 1)
+    vis = t[None, :] <= pos[:, None]
+    if window > 0:
+        vis &= (pos[:, None] - t[None, :]) < window
+    s = np.where(vis[:, None, None, :], s, -np.inf)
+    m = s.max(axis=-1, keepdims=True)
+    p = np.where(np.isfinite(s), np.exp(s - np.where(np.isfinite(m), m, 0)), 0.0)
+    l = p.sum(axis=-1, keepdims=True)
+    o = np.einsum("qhgt,htd->qhgd", p, v[:, :N].astype(np.float64))
+    out = np.where(l > 0, o / np.where(l > 0, l, 1), 0.0)
+    return out.reshape(nq, H, D).astype(np.float32)

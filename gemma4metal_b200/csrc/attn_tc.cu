@@ -5,26 +5,32 @@
 // a CPU-built mask (engine/gemma4_multilayer.cpp:307-308,347-367,441-464).
 //
 // CTA = 128 query rows of one KV head (row = (query, GQA head) pair; TMEM lane
-// = row), 4 warps, 2 CTAs per SM. Per 64-token tile of the int4 cache:
-//   1. all threads unpack the K and V codes into shared memory as exact fp16
-//      values 1 + c/64, in the UMMA canonical 128B-swizzled layout (K: K-major
-//      B operand of S = Q K^T; V: MN-major B operand of O = P V), one 8 KB
-//      region per 64-dim scale group; per-token scale/bias terms go to smem;
+// = row), 8 warps, 2 CTAs per SM; the two threads of a row (tid, tid + 128)
+// take the two 32-token halves of each 64-token tile. Per tile of the cache:
+//   1. threads 0..127 unpack the K codes into shared memory as exact fp16
+//      values 1 + c/64 in the UMMA canonical K-major 128B-swizzled layout, one
+//      8 KB region per 64-dim scale group, and the per-token score and value
+//      terms;
 //   2. thread 0 issues tcgen05.mma S'_g = Q_g (1 + C_g/64)^T per scale group g
 //      (fp16 x fp16 -> fp32 in TMEM; exact products), commit -> mbarrier;
-//   3. each thread reads its row of S'_0, S'_1 (tcgen05.ld), forms the scores
+//   3. threads 128..255, once the previous tile's O MMA is done, unpack the V
+//      codes as exact fp16 (c - 8)/64 (MN-major B operand of O = P V) while
+//      the S MMA runs; every thread then loads the next tile's codes into
+//      registers;
+//   4. each thread reads its half row of S'_0, S'_1 (tcgen05.ld) and forms
 //      score = 64 s_0 S'_0 + 64 s_1 S'_1 + (b_0 - 64 s_0) sum q_0 + (b_1 - 64 s_1) sum q_1
 //      (the int4 scale/bias factored out of the dot product, as
-//      lib/turboquant.metal:803 does), masks (causal / window / length),
-//      online softmax in log2 units, writes P'_g = p * s_g(token) as fp16
-//      (K-major A operand) and accumulates the bias term
-//      sum p b + 8 p s - 72 fp16(p s) (exact for the rounded weights);
-//   4. thread 0 issues O'_g += P'_g (1 + C_g/64) per group into TMEM.
-// The running max is only moved (and O rescaled in TMEM) when a row's max
-// grows by more than 8 (log2 units), so most tiles skip the rescale.
-// out = (64 O' + bias term) / l. The 8-element dim order inside each
-// code word follows the unpack (d = 0,4,1,5,2,6,3,7), applied to Q as well and
-// undone when O is written.
+//      lib/turboquant.metal:803 does), masks (causal / window / length) only
+//      on tiles that cross a boundary, exchanges the half-row max with its
+//      partner, and writes P'_g = fp16(p s_g(token)) (K-major A operand) while
+//      accumulating the bias term sum p (b_g + 8 s_g);
+//   5. thread 0 issues O'_g += P'_g (c - 8)/64 per group into TMEM.
+// out_g = (64 O'_g + bias term_g) / l: the weights' fp16 rounding error is
+// multiplied by c - 8 (|c - 8| <= 8), not by the code's full value. The
+// running max is only moved (and O rescaled in TMEM) when a row's max grows
+// by more than 8 (log2 units), so most tiles skip the rescale. The 8-element
+// dim order inside each code word follows the unpack (d = 0,4,1,5,2,6,3,7),
+// applied to Q as well and undone when O is written.
 #include <cuda.h>
 
 #include <cstdint>
@@ -39,7 +45,7 @@ namespace {
 constexpr int kRows = 128;     // query rows per CTA (TMEM lanes)
 constexpr int kTok = 64;       // tokens per tile
 constexpr int kD = 128;        // head_dim (two 64-dim scale groups)
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;  // two threads per row (token halves of each tile)
 constexpr int kTmemCols = 256; // S'_0, S'_1, O'_0, O'_1 (64 fp32 columns each)
 // an MMA group finishes in microseconds; give up (and record the error) after
 // ~10 ms of SM clocks so a wait that cannot complete still ends the kernel
@@ -51,10 +57,14 @@ struct TLayout {
   static constexpr int V = K + 2 * kTok * 128;  // [2][64][128 B]               16 KB
   static constexpr int P = V + 2 * kTok * 128;  // [2][128 rows][128 B]         32 KB
   static constexpr int TS = P + 2 * kRows * 128;  // per token: {A0, A1, B0, B1} (score terms)
-  static constexpr int TV = TS + kTok * 16;        // per token: {vs0, vs1, vbm0, vbm1}
-  static constexpr int BAR = TV + kTok * 16;       // mbarriers: S done, O done
+  static constexpr int TV = TS + kTok * 16;        // per token: {vs0, vs1, vb0 + 8 vs0, vb1 + 8 vs1}
+  static constexpr int MX = TV + kTok * 16;        // per thread: half-row max / epilogue sums
+  static constexpr int BAR = MX + kThreads * 4;    // mbarriers: S done, O done
   static constexpr int TMEM = BAR + 16;            // allocated TMEM base address
   static constexpr int BYTES = TMEM + 16 + 1024;   // + alignment slack
+  // f32 queries: Q = hi + lo, both fp16; the lo part follows (32 KB)
+  static constexpr int QL = (TMEM + 16 + 1023) / 1024 * 1024;
+  static constexpr int BYTES_QLO = QL + 2 * kRows * 128 + 1024;
 };
 
 struct TCParams {
@@ -78,8 +88,7 @@ struct TCParams {
   int splits, tiles_per_split;
   void* out;           // (n_q, H, D)
   int out_dtype;
-  float* ws;           // split partials: (units, splits, 128 rows, D + 2)
-  unsigned* counters;
+  float* ws;           // split partials: (units, splits, D + 2, 128 rows)
   uint32_t* err;
 };
 
@@ -151,6 +160,21 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 consecutive fp32 TMEM columns of this thread's lane
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
@@ -186,10 +210,55 @@ __device__ __forceinline__ uint32_t nib64h(uint32_t x) {
 // dim held by element e (0..7) of a word's unpacked chunk: 0,4,1,5,2,6,3,7
 __device__ __forceinline__ int perm8(int e) { return (e >> 1) + 4 * (e & 1); }
 
-__device__ __forceinline__ float sbload(const void* p, long long i, int f32) {
-  return f32 ? reinterpret_cast<const float*>(p)[i] : __half2float(reinterpret_cast<const __half*>(p)[i]);
+// fp16x2 (1 + c/64) -> (c - 8)/64; exact (both operands and the result are
+// multiples of 2^-6 below 2)
+__device__ __forceinline__ uint32_t center8(uint32_t x) {
+  __half2 h = *reinterpret_cast<const __half2*>(&x);
+  h = __hsub2(h, __floats2half2_rn(1.125f, 1.125f));
+  return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// 8 consecutive elements [i, i + 8) as float; vec: 16-byte aligned base
+__device__ __forceinline__ void load8(const void* p, long long i, int dtype, bool vec, float (&v)[8]) {
+  if (vec && dtype != kF32) {
+    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(p) + i);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      float2 f;
+      if (dtype == kF16) f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
+      else f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
+      v[2 * k] = f.x;
+      v[2 * k + 1] = f.y;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = load_as_float(p, i + k, dtype);
+  }
+}
+
+// 8 consecutive elements [i, i + 8) from float; vec: 16-byte aligned base
+__device__ __forceinline__ void store8(void* p, long long i, int dtype, bool vec, const float (&v)[8]) {
+  if (vec && dtype != kF32) {
+    uint32_t w[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      if (dtype == kF16) {
+        const __half2 h = __floats2half2_rn(v[2 * k], v[2 * k + 1]);
+        w[k] = *reinterpret_cast<const uint32_t*>(&h);
+      } else {
+        const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+        w[k] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+    }
+    *reinterpret_cast<uint4*>(static_cast<unsigned short*>(p) + i) = make_uint4(w[0], w[1], w[2], w[3]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) store_from_float(p, i + k, dtype, v[k]);
+  }
+}
+
+template <bool kQLo>
 __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
@@ -199,11 +268,16 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) 
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + TLayout::TMEM);
   float4* s_ts = reinterpret_cast<float4*>(smem + TLayout::TS);
   float4* s_tv = reinterpret_cast<float4*>(smem + TLayout::TV);
+  float* s_mx = reinterpret_cast<float*>(smem + TLayout::MX);
   const uint32_t sbase = smem_u32(smem);
 
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int rl = tid & (kRows - 1);  // row of the tile (TMEM lane)
+  const int hf = tid >> 7;           // token half of each tile; scale group of O
   const int split = blockIdx.x, mt = blockIdx.y, kv = blockIdx.z;
   const int rows_total = p.n_q * p.G;
+  // the two threads of a row meet on named barrier 1 + warp % 4 (64 threads)
+  auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory"); };
 
   pdl_wait();
   pdl_trigger();
@@ -222,92 +296,159 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) 
   }
 
   // ---- this thread's row: query qi, head h (rows past the end compute on zeros)
-  const int row = mt * kRows + tid;
+  const int row = mt * kRows + rl;
   const bool row_ok = row < rows_total;
   const int qi = row_ok ? row / p.G : 0;
   const int h = kv * p.G + (row_ok ? row % p.G : 0);
   // position of the query: causal rows at pos0 + qi; otherwise every query
   // sits at the end of the shared cache (the window counts back from there)
   const int qpos = p.causal ? p.pos0 + qi : p.n_tokens - 1;
-  // Q row -> smem (fp16, dims permuted inside each 8-dim word like the codes)
-  float qsum0 = 0.0f, qsum1 = 0.0f;
+  // Q row, scale group hf -> smem (fp16, dims permuted inside each 8-dim word
+  // like the codes; f32 queries as fp16 hi + lo); the group's sum goes to the
+  // partner through s_mx
   {
-    const long long qb = (static_cast<long long>(qi) * p.H + h) * kD;
+    const long long qb = (static_cast<long long>(qi) * p.H + h) * kD + hf * 64;
+    const bool qvec = (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0;
+    float qsum = 0.0f;
 #pragma unroll
-    for (int g = 0; g < 2; ++g)
+    for (int ch = 0; ch < 8; ++ch) {
+      float x[8];
+      if (row_ok) {
+        load8(p.q, qb + ch * 8, p.q_dtype, qvec, x);
+      } else {
 #pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {
-        float v[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          v[e] = row_ok ? load_as_float(p.q, qb + g * 64 + ch * 8 + perm8(e), p.q_dtype) : 0.0f;
-        // fp16 copies (exact for fp16 and bf16 inputs in range)
-        __half2 hh[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          hh[e] = __floats2half2_rn(v[2 * e], v[2 * e + 1]);
-          const float2 f = __half22float2(hh[e]);
-          if (g == 0) qsum0 += f.x + f.y; else qsum1 += f.x + f.y;
-        }
-        *reinterpret_cast<uint4*>(smem + TLayout::Q + g * kRows * 128 + sw128(tid, ch)) =
-            *reinterpret_cast<uint4*>(hh);
+        for (int e = 0; e < 8; ++e) x[e] = 0.0f;
       }
+      // fp16 copies (exact for fp16 and bf16 inputs in range)
+      __half2 hh[4], hl[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float xa = x[perm8(2 * e)], xb = x[perm8(2 * e + 1)];
+        hh[e] = __floats2half2_rn(xa, xb);
+        const float2 f = __half22float2(hh[e]);
+        qsum += f.x + f.y;
+        if (kQLo) {
+          hl[e] = __floats2half2_rn(xa - f.x, xb - f.y);
+          const float2 fl = __half22float2(hl[e]);
+          qsum += fl.x + fl.y;
+        }
+      }
+      *reinterpret_cast<uint4*>(smem + TLayout::Q + hf * kRows * 128 + sw128(rl, ch)) =
+          *reinterpret_cast<uint4*>(hh);
+      if (kQLo)
+        *reinterpret_cast<uint4*>(smem + TLayout::QL + hf * kRows * 128 + sw128(rl, ch)) =
+            *reinterpret_cast<uint4*>(hl);
+    }
+    s_mx[tid] = qsum;
   }
   fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  const float qsum0 = s_mx[rl], qsum1 = s_mx[rl + kRows];
   const uint32_t tmem = *s_tmem;
-  const uint32_t t_s0 = tmem, t_s1 = tmem + 64, t_o0 = tmem + 128, t_o1 = tmem + 192;
-  const uint32_t lane_off = static_cast<uint32_t>(warp * 32) << 16;
+  const uint32_t t_s0 = tmem, t_s1 = tmem + 64, t_o0 = tmem + 128;
+  const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
 
-  // ---- token range of this split (tiles of 64 tokens)
-  int n_vis = p.n_tokens;
-  const int t_begin = split * p.tiles_per_split * kTok;
-  const int t_end = min(n_vis, t_begin + p.tiles_per_split * kTok);
+  // ---- token range of this split (tiles of 64 tokens), cut to what the CTA's
+  // rows can see: causal rows end at pos0 + last query, windows start at
+  // (first row's position) - window + 1
+  const int row_last = min(rows_total, (mt + 1) * kRows) - 1;
+  const int qpos_lo = p.causal ? p.pos0 + (mt * kRows) / p.G : p.n_tokens - 1;
+  const int qpos_hi = p.causal ? p.pos0 + row_last / p.G : p.n_tokens - 1;
+  const int n_vis = min(p.n_tokens, qpos_hi + 1);
+  const int t_lo = p.window > 0 ? max(0, qpos_lo - p.window + 1) : 0;
+  const int t_begin = max(split * p.tiles_per_split * kTok, t_lo);
+  const int t_end = min(n_vis, split * p.tiles_per_split * kTok + p.tiles_per_split * kTok);
   const long long tok_base = static_cast<long long>(kv) * p.capacity;
 
   float m_run = -INFINITY, l_run = 0.0f, corr0 = 0.0f, corr1 = 0.0f;
   bool o_init = false;  // TMEM O holds accumulated values
-  uint32_t ph = 0;
+  uint32_t ph_s = 0, ph_o = 0;
 
-  for (int t0 = t_begin; t0 < t_end; t0 += kTok) {
-    // ---- 1. unpack K and V codes of 64 tokens into the canonical layouts ----
-    {
-      const int tok = tid & 63, grp = tid >> 6;
-      const int t = t0 + tok;
-      const bool tv = t < t_end;
-      const long long rowi = tok_base + (tv ? t : t0);
-#pragma unroll
-      for (int kvs = 0; kvs < 2; ++kvs) {
-        const uint32_t* src = (kvs ? p.vq : p.kq) + rowi * (kD / 8) + grp * 8;
-        const uint4 w0 = reinterpret_cast<const uint4*>(src)[0];
-        const uint4 w1 = reinterpret_cast<const uint4*>(src)[1];
-        const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        unsigned char* dst = smem + (kvs ? TLayout::V : TLayout::K) + grp * kTok * 128;
-#pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
-          uint4 o;
-          o.x = nib64h<0>(w[ch]);
-          o.y = nib64h<1>(w[ch]);
-          o.z = nib64h<2>(w[ch]);
-          o.w = nib64h<3>(w[ch]);
-          *reinterpret_cast<uint4*>(dst + sw128(tok, ch)) = o;
-        }
-      }
-      if (tid < kTok) {
-        const long long gi = (tok_base + (tv ? t : t0)) * 2;
-        const float ks0 = sbload(p.ks, gi, p.sb_f32), ks1 = sbload(p.ks, gi + 1, p.sb_f32);
-        const float kb0 = sbload(p.kb, gi, p.sb_f32), kb1 = sbload(p.kb, gi + 1, p.sb_f32);
-        const float vs0 = sbload(p.vs, gi, p.sb_f32), vs1 = sbload(p.vs, gi + 1, p.sb_f32);
-        const float vb0 = sbload(p.vb, gi, p.sb_f32), vb1 = sbload(p.vb, gi + 1, p.sb_f32);
-        const float qs = p.qscale;
-        s_ts[tok] = tv ? make_float4(64.0f * ks0 * qs, 64.0f * ks1 * qs, (kb0 - 64.0f * ks0) * qs,
-                                     (kb1 - 64.0f * ks1) * qs)
-                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        s_tv[tok] = tv ? make_float4(vs0, vs1, vb0, vb1) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  // The next tile's codes and scales are loaded into registers while the
+  // current tile is in the tensor cores and the softmax, then unpacked into
+  // shared memory in the next iteration. Thread item: token ptok, scale
+  // group pgrp, K (pkv 0, threads 0..127) or V (pkv 1); 32 B of codes. The K
+  // threads also take the token's scale and bias pairs (raw bits, converted
+  // at unpack): K's for pgrp 0, V's for pgrp 1, so every per-token term is in
+  // shared memory before the tile's first barrier.
+  const int ptok = tid & 63, pgrp = (tid >> 6) & 1, pkv = tid >> 7;
+  uint4 pf0, pf1;
+  uint32_t pfr[4] = {0u, 0u, 0u, 0u};
+  auto prefetch = [&](int t0) {
+    const int t = t0 + ptok;
+    const long long rowi = tok_base + (t < t_end ? t : t0);
+    const uint4* cp = reinterpret_cast<const uint4*>((pkv ? p.vq : p.kq) + rowi * (kD / 8) + pgrp * 8);
+    pf0 = cp[0];
+    pf1 = cp[1];
+    if (!pkv) {
+      const void* sp = pgrp ? p.vs : p.ks;
+      const void* bp = pgrp ? p.vb : p.kb;
+      if (p.sb_f32) {
+        const uint2 a = reinterpret_cast<const uint2*>(sp)[rowi];
+        const uint2 b = reinterpret_cast<const uint2*>(bp)[rowi];
+        pfr[0] = a.x;
+        pfr[1] = a.y;
+        pfr[2] = b.x;
+        pfr[3] = b.y;
+      } else {
+        pfr[0] = reinterpret_cast<const uint32_t*>(sp)[rowi];
+        pfr[1] = reinterpret_cast<const uint32_t*>(bp)[rowi];
       }
     }
+  };
+  auto unpack = [&](int t0) {
+    const uint32_t w[8] = {pf0.x, pf0.y, pf0.z, pf0.w, pf1.x, pf1.y, pf1.z, pf1.w};
+    unsigned char* dst = smem + (pkv ? TLayout::V : TLayout::K) + pgrp * kTok * 128;
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      uint4 o;
+      o.x = nib64h<0>(w[ch]);
+      o.y = nib64h<1>(w[ch]);
+      o.z = nib64h<2>(w[ch]);
+      o.w = nib64h<3>(w[ch]);
+      if (pkv) {
+        o.x = center8(o.x);
+        o.y = center8(o.y);
+        o.z = center8(o.z);
+        o.w = center8(o.w);
+      }
+      *reinterpret_cast<uint4*>(dst + sw128(ptok, ch)) = o;
+    }
+    if (!pkv) {
+      float s0, s1, b0, b1;
+      if (p.sb_f32) {
+        s0 = __uint_as_float(pfr[0]);
+        s1 = __uint_as_float(pfr[1]);
+        b0 = __uint_as_float(pfr[2]);
+        b1 = __uint_as_float(pfr[3]);
+      } else {
+        const float2 sf = __half22float2(*reinterpret_cast<const __half2*>(&pfr[0]));
+        const float2 bf = __half22float2(*reinterpret_cast<const __half2*>(&pfr[1]));
+        s0 = sf.x;
+        s1 = sf.y;
+        b0 = bf.x;
+        b1 = bf.y;
+      }
+      const bool tv = t0 + ptok < t_end;
+      const float qs = p.qscale;
+      if (!pgrp) {
+        s_ts[ptok] = tv ? make_float4(64.0f * s0 * qs, 64.0f * s1 * qs, (b0 - 64.0f * s0) * qs,
+                                      (b1 - 64.0f * s1) * qs)
+                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      } else {
+        s_tv[ptok] = tv ? make_float4(s0, s1, fmaf(8.0f, s0, b0), fmaf(8.0f, s1, b1))
+                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+    }
+  };
+  if (t_begin < t_end) prefetch(t_begin);
+
+  for (int t0 = t_begin; t0 < t_end; t0 += kTok) {
+    // ---- 1. K codes and the per-token terms -> smem (the previous S MMA
+    // finished before its softmax, the previous softmax before its O MMA)
+    if (!pkv) unpack(t0);
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
@@ -323,36 +464,58 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) 
           const uint64_t a = umma_desc(sbase + TLayout::Q + g * kRows * 128 + ks * 32, 16);
           const uint64_t b = umma_desc(sbase + TLayout::K + g * kTok * 128 + ks * 32, 16);
           umma_f16(g ? t_s1 : t_s0, a, b, idS, ks > 0 ? 1u : 0u);
+          if (kQLo) {
+            const uint64_t al = umma_desc(sbase + TLayout::QL + g * kRows * 128 + ks * 32, 16);
+            umma_f16(g ? t_s1 : t_s0, al, b, idS, 1u);
+          }
         }
       umma_commit(bar_s);
     }
-    mbar_wait_bounded(bar_s, ph, p.err, kWaitBudget);
+    // ---- 3. the previous O MMA (reads V and P) done -> V codes -> smem; next
+    // tile's codes -> registers (V's per-token terms went in with step 1)
+    if (o_init) {
+      mbar_wait_bounded(bar_o, ph_o, p.err, kWaitBudget);
+      tc_fence_after();
+      ph_o ^= 1u;
+    }
+    if (pkv) unpack(t0);
+    if (t0 + kTok < t_end) prefetch(t0 + kTok);
+    mbar_wait_bounded(bar_s, ph_s, p.err, kWaitBudget);
     tc_fence_after();
+    ph_s ^= 1u;
 
-    // ---- 3. scores, online softmax, P' and the bias terms ----------------------
-    const bool need_mask = p.causal || p.window > 0 || t0 + kTok > t_end;
-    float s0[64];
-    float mx = -INFINITY;
+    // ---- 4. scores of this thread's 32 tokens, online softmax, P', bias terms
+    float sc[32];
+    tmem_ld32(t_s0 + lane_off + 32 * hf, sc);
 #pragma unroll
-    for (int c = 0; c < 2; ++c) {
-      float a0[32], a1[32];
-      tmem_ld32(t_s0 + lane_off + 32 * c, a0);
-      tmem_ld32(t_s1 + lane_off + 32 * c, a1);
+    for (int hh = 0; hh < 2; ++hh) {
+      float a1[16];
+      tmem_ld16(t_s1 + lane_off + 32 * hf + 16 * hh, a1);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int i = 32 * c + j;
-        const float4 a = s_ts[i];
-        float v = fmaf(a.x, a0[j], fmaf(a.y, a1[j], fmaf(a.z, qsum0, a.w * qsum1)));
-        if (need_mask) {
-          const int t = t0 + i;
-          const bool vis = t < t_end && t <= qpos && (p.window <= 0 || qpos - t < p.window) && row_ok;
-          v = vis ? v : -INFINITY;
-        }
-        s0[i] = v;
-        mx = fmaxf(mx, v);
+      for (int j = 0; j < 16; ++j) {
+        const float4 a = s_ts[32 * hf + 16 * hh + j];
+        float& x = sc[16 * hh + j];
+        x = fmaf(a.x, x, fmaf(a.y, a1[j], fmaf(a.z, qsum0, a.w * qsum1)));
       }
     }
-    // move the running max only when it grows by more than 8 (2^8 headroom)
+    const bool full = t0 + kTok <= t_end && (!p.causal || t0 + kTok - 1 <= qpos_lo) &&
+                      (p.window <= 0 || qpos_hi - t0 < p.window);
+    if (!full) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int t = t0 + 32 * hf + j;
+        const bool vis = t < t_end && t <= qpos && (p.window <= 0 || qpos - t < p.window);
+        sc[j] = vis ? sc[j] : -INFINITY;
+      }
+    }
+    float mx = sc[0];
+#pragma unroll
+    for (int j = 1; j < 32; ++j) mx = fmaxf(mx, sc[j]);
+    s_mx[tid] = mx;
+    pair_sync();
+    mx = fmaxf(s_mx[rl], s_mx[rl + kRows]);
+    // move the running max only when it grows by more than 8 (2^8 headroom);
+    // both threads of the row take the same decision
     bool rescale = false;
     float alpha = 1.0f;
     if (mx > m_run + 8.0f || (m_run == -INFINITY && mx > -INFINITY)) {
@@ -364,44 +527,40 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) 
       corr0 *= alpha;
       corr1 *= alpha;
     }
+    const float mref = m_run == -INFINITY ? 0.0f : m_run;  // masked scores give exp2(-inf) = 0
     float lsum = 0.0f;
     unsigned char* prow = smem + TLayout::P;
 #pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
+    for (int cc = 0; cc < 4; ++cc) {
+      const int ch = 4 * hf + cc;
       uint32_t w0[4], w1[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int i = ch * 8 + 2 * e;
-        const float pa = (s0[i] == -INFINITY) ? 0.0f : fast_exp2(s0[i] - m_run);
-        const float pb = (s0[i + 1] == -INFINITY) ? 0.0f : fast_exp2(s0[i + 1] - m_run);
+        const int j = 8 * cc + 2 * e;
+        const float pa = fast_exp2(sc[j] - mref), pb = fast_exp2(sc[j + 1] - mref);
         lsum += pa + pb;
-        const float4 va = s_tv[i], vb = s_tv[i + 1];
-        const float wa0 = pa * va.x, wb0 = pb * vb.x, wa1 = pa * va.y, wb1 = pb * vb.y;
-        const __half2 h0 = __floats2half2_rn(wa0, wb0);
-        const __half2 h1 = __floats2half2_rn(wa1, wb1);
-        // bias term with the fp16 weights r the mma sees (out = 64 O' + corr):
-        // corr = sum p b + 8 w - 72 r, which leaves the weights' rounding error
-        // multiplied by (c - 8), |c - 8| <= 8, instead of by c
-        const float2 r0 = __half22float2(h0), r1 = __half22float2(h1);
-        corr0 = fmaf(pa, va.z, fmaf(pb, vb.z, fmaf(8.0f, wa0 + wb0, fmaf(-72.0f, r0.x + r0.y, corr0))));
-        corr1 = fmaf(pa, va.w, fmaf(pb, vb.w, fmaf(8.0f, wa1 + wb1, fmaf(-72.0f, r1.x + r1.y, corr1))));
+        const float4 va = s_tv[32 * hf + j], vb = s_tv[32 * hf + j + 1];
+        const __half2 h0 = __floats2half2_rn(pa * va.x, pb * vb.x);
+        const __half2 h1 = __floats2half2_rn(pa * va.y, pb * vb.y);
+        corr0 = fmaf(pa, va.z, fmaf(pb, vb.z, corr0));
+        corr1 = fmaf(pa, va.w, fmaf(pb, vb.w, corr1));
         w0[e] = *reinterpret_cast<const uint32_t*>(&h0);
         w1[e] = *reinterpret_cast<const uint32_t*>(&h1);
       }
-      *reinterpret_cast<uint4*>(prow + sw128(tid, ch)) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
-      *reinterpret_cast<uint4*>(prow + kRows * 128 + sw128(tid, ch)) =
+      *reinterpret_cast<uint4*>(prow + sw128(rl, ch)) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+      *reinterpret_cast<uint4*>(prow + kRows * 128 + sw128(rl, ch)) =
           make_uint4(w1[0], w1[1], w1[2], w1[3]);
     }
     l_run += lsum;
-    // O *= alpha for the rows whose max moved; tcgen05.ld/st are warp-wide
+    // O_hf *= alpha for the rows whose max moved; tcgen05.ld/st are warp-wide
     // (.sync.aligned), so the whole warp takes the branch with alpha = 1 on
     // the other rows
     if (__any_sync(0xffffffffu, rescale)) {
       const float a = rescale ? alpha : 1.0f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float o[32];
-        const uint32_t ta = t_o0 + lane_off + c * 32;
+        const uint32_t ta = t_o0 + lane_off + 64 * hf + 32 * c;
         tmem_ld32(ta, o);
 #pragma unroll
         for (int i = 0; i < 32; ++i) o[i] *= a;
@@ -413,7 +572,7 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) 
     __syncthreads();
     tc_fence_after();
 
-    // ---- 4. O'_g += P'_g (1 + C_g/64) ---------------------------------------------
+    // ---- 5. O'_g += P'_g (C_g - 8)/64 -------------------------------------------
     if (tid == 0) {
       constexpr uint32_t idO = idesc_f16(true);
 #pragma unroll
@@ -422,44 +581,67 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) 
         for (int ks = 0; ks < 4; ++ks) {
           const uint64_t a = umma_desc(sbase + TLayout::P + g * kRows * 128 + ks * 32, 16);
           const uint64_t b = umma_desc(sbase + TLayout::V + g * kTok * 128 + ks * 16 * 128, 16);
-          umma_f16(g ? t_o1 : t_o0, a, b, idO, (o_init || ks > 0) ? 1u : 0u);
+          umma_f16(t_o0 + 64 * g, a, b, idO, (o_init || ks > 0) ? 1u : 0u);
         }
       umma_commit(bar_o);
     }
     o_init = true;
-    mbar_wait_bounded(bar_o, ph, p.err, kWaitBudget);
+  }
+  if (o_init) {
+    mbar_wait_bounded(bar_o, ph_o, p.err, kWaitBudget);
     tc_fence_after();
-    ph ^= 1u;
   }
 
-  // ---- epilogue: out = (64 O' + corr) / l, 32 TMEM columns at a time ---------------
-  // TMEM column j of group g holds dim g*64 + 8*(j/8) + perm8(j%8)
+  // ---- epilogue: the row's two halves add their l and bias terms; thread hf
+  // writes scale group hf: out = (64 O'_hf + corr_hf) / l
+  __syncthreads();  // s_mx reads of the last tile are done
+  // [3][kThreads] sums in the P region (free after the last O MMA)
+  float* s_red = reinterpret_cast<float*>(smem + TLayout::P);
+  s_red[tid] = l_run;
+  s_red[kThreads + tid] = corr0;
+  s_red[2 * kThreads + tid] = corr1;
+  pair_sync();
+  const int pt = tid ^ kRows;  // partner thread
+  const float l_tot = l_run + s_red[pt];
+  const float corr = (hf ? corr1 : corr0) + s_red[(hf ? 2 : 1) * kThreads + pt];
   const bool direct = p.splits == 1;
   const long long unit = static_cast<long long>(kv) * gridDim.y + mt;
-  float* wsr = p.ws + ((unit * p.splits + split) * kRows + tid) * (kD + 2);
-  const float inv = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+  // split partials, column-major so a warp's 32 rows are one 128 B store:
+  // ws[unit][split][d or m or l][row]
+  float* wsr = p.ws + (unit * p.splits + split) * (kD + 2) * kRows + rl;
+  const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
   const long long ob = (static_cast<long long>(qi) * p.H + h) * kD;
+  const bool ovec = (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0;
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < 2; ++c) {
     float o[32];
     if (o_init) {
-      tmem_ld32(t_o0 + lane_off + c * 32, o);
+      tmem_ld32(t_o0 + lane_off + 64 * hf + 32 * c, o);
     } else {
 #pragma unroll
       for (int i = 0; i < 32; ++i) o[i] = 0.0f;
     }
-    const float corr = (c >> 1) ? corr1 : corr0;
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int j = 32 * c + i;
-      const int d = (j & ~7) + perm8(j & 7);
-      const float v = fmaf(64.0f, o[i], corr);
+    for (int k = 0; k < 4; ++k) {
+      const int d0 = 64 * hf + 32 * c + 8 * k;  // first dim of this 8-column chunk
+      float v[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[perm8(e)] = fmaf(64.0f, o[8 * k + e], corr);
       if (direct) {
-        if (row_ok) store_from_float(p.out, ob + d, p.out_dtype, l_run > 0.0f ? v * inv : 0.0f);
+        if (row_ok) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] *= inv;
+          store8(p.out, ob + d0, p.out_dtype, ovec, v);
+        }
       } else {
-        wsr[d] = v;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) __stcg(wsr + (d0 + e) * kRows, v[e]);
       }
     }
+  }
+  if (!direct && hf == 0) {
+    __stcg(wsr + kD * kRows, l_tot > 0.0f ? m_run : -INFINITY);
+    __stcg(wsr + (kD + 1) * kRows, l_tot);
   }
   tc_fence_before();
   __syncthreads();
@@ -468,47 +650,55 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) 
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
                  : "memory");
   }
-  if (direct) return;
-  // split partial: (o unnormalised, m in log2 units, l), row-major per CTA
-  wsr[kD] = l_run > 0.0f ? m_run : -INFINITY;
-  wsr[kD + 1] = l_run;
-  __syncthreads();
-  __shared__ int s_last;
-  if (tid == 0) {
-    const unsigned prev = atomic_add_acq_rel(&p.counters[unit], 1u);
-    s_last = prev == static_cast<unsigned>(p.splits - 1);
-  }
-  __syncthreads();
-  if (!s_last || !row_ok) {
-    if (s_last && tid == 0) p.counters[unit] = 0u;
-    return;
-  }
-  const float* base = p.ws + (unit * p.splits * kRows + tid) * (kD + 2);
-  const long long sstride = static_cast<long long>(kRows) * (kD + 2);
+}
+
+// Merge of the split partials (log-sum-exp weights), launched after the
+// attention grid with programmatic dependent launch. Grid (D/32, 128/32,
+// units); 256 threads: lane = row of a 32-row block, warp = 4 of the block's
+// 32 dims; the block is transposed through shared memory so the output rows
+// are written 64 B at a time.
+__global__ void __launch_bounds__(256) attn_tc_merge_kernel(const TCParams p, int mtiles) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float tile[32][33];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int db = blockIdx.x * 32, rb = blockIdx.y * 32;
+  const long long unit = blockIdx.z;
+  const int kv = static_cast<int>(unit / mtiles), mt = static_cast<int>(unit % mtiles);
+  const int S = p.splits;
+  const long long sstride = static_cast<long long>(kD + 2) * kRows;
+  const float* base = p.ws + unit * S * sstride + rb + lane;
   float M = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) M = fmaxf(M, __ldcg(base + s * sstride + kD));
-  float L = 0.0f;
-  for (int s = 0; s < p.splits; ++s) {
-    const float ms = __ldcg(base + s * sstride + kD);
+  for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(base + s * sstride + kD * kRows));
+  float L = 0.0f, acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const float* col = base + (db + 4 * warp) * kRows;
+#pragma unroll 4
+  for (int s = 0; s < S; ++s) {
+    const float* ps = base + s * sstride;
+    const float ms = __ldcg(ps + kD * kRows);
+    const float ls = __ldcg(ps + (kD + 1) * kRows);
+    float v[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) v[k] = __ldcg(col + s * sstride + k * kRows);
     const float e = (ms == -INFINITY) ? 0.0f : fast_exp2(ms - M);
-    L = fmaf(e, __ldcg(base + s * sstride + kD + 1), L);
+    L = fmaf(e, ls, L);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] = fmaf(e, v[k], acc[k]);
   }
   const float invL = L > 0.0f ? 1.0f / L : 0.0f;
-#pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    float acc[32];
 #pragma unroll
-    for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
-    for (int s = 0; s < p.splits; ++s) {
-      const float ms = __ldcg(base + s * sstride + kD);
-      const float e = (ms == -INFINITY) ? 0.0f : fast_exp2(ms - M);
+  for (int k = 0; k < 4; ++k) tile[lane][4 * warp + k] = acc[k] * invL;
+  __syncthreads();
+  const int rows_total = p.n_q * p.G;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) acc[i] = fmaf(e, __ldcg(base + s * sstride + 32 * c + i), acc[i]);
+  for (int rr = warp; rr < 32; rr += 8) {
+    const int row = mt * kRows + rb + rr;
+    if (row < rows_total) {
+      const int qi = row / p.G, h = kv * p.G + row % p.G;
+      store_from_float(p.out, (static_cast<long long>(qi) * p.H + h) * kD + db + lane, p.out_dtype,
+                       tile[rr][lane]);
     }
-#pragma unroll
-    for (int i = 0; i < 32; ++i) store_from_float(p.out, ob + 32 * c + i, p.out_dtype, acc[i] * invL);
   }
-  if (tid == 0) p.counters[unit] = 0u;
 }
 
 int tc_splits(int units, int tiles) {
@@ -599,24 +789,35 @@ TQ_API int tq_sdpa_int4_multi(const void* queries, tq_dtype q_dtype, const uint3
       set_last_error("tq_sdpa_int4_multi: workspace of %zu bytes needed", need);
       return TQ_ERR_WORKSPACE;
     }
-    if (units * sizeof(unsigned) > kCounterRegionBytes) return fail(TQ_ERR_UNSUPPORTED, "too many row tiles");
-    p.counters = static_cast<unsigned*>(workspace);
     p.ws = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kCounterRegionBytes);
   }
   int dev = 0;
   cudaGetDevice(&dev);
   static int attr_set[64] = {0};
   if (dev < 64 && !attr_set[dev]) {
-    cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TLayout::BYTES);
+    cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, TLayout::BYTES);
+    cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         TLayout::BYTES_QLO);
     attr_set[dev] = 1;
   }
   p.err = device_error_word();
-  const cudaError_t e = launch_pdl(attn_tc_kernel, dim3(splits, mtiles, num_kv_heads), dim3(kThreads),
-                                   static_cast<size_t>(TLayout::BYTES),
-                                   static_cast<cudaStream_t>(stream), p);
+  const bool qlo = q_dtype == TQ_F32;
+  const cudaError_t e =
+      qlo ? launch_pdl(attn_tc_kernel<true>, dim3(splits, mtiles, num_kv_heads), dim3(kThreads),
+                       static_cast<size_t>(TLayout::BYTES_QLO), static_cast<cudaStream_t>(stream), p)
+          : launch_pdl(attn_tc_kernel<false>, dim3(splits, mtiles, num_kv_heads), dim3(kThreads),
+                       static_cast<size_t>(TLayout::BYTES), static_cast<cudaStream_t>(stream), p);
   if (e != cudaSuccess) {
     set_last_error("tq_sdpa_int4_multi: %s", cudaGetErrorString(e));
     return TQ_ERR_CUDA;
+  }
+  if (splits > 1) {
+    const cudaError_t e2 = launch_pdl(attn_tc_merge_kernel, dim3(kD / 32, kRows / 32, units), dim3(256), 0,
+                                      static_cast<cudaStream_t>(stream), p, mtiles);
+    if (e2 != cudaSuccess) {
+      set_last_error("tq_sdpa_int4_multi (merge): %s", cudaGetErrorString(e2));
+      return TQ_ERR_CUDA;
+    }
   }
   return TQ_OK;
 }

@@ -45,9 +45,17 @@ def run(nq, H, Hkv, N, causal, pos0, window, qdt, odt, seed=7, sb=np.float16):
     (40, 16, 4, 777, True, 737, 128, "f16", "f32"),      # GQA 4, causal + window
     (8, 32, 16, 4096, False, 0, 0, "bf16", "f32"),       # few rows: split over the cache
     (3, 8, 8, 65, True, 62, 0, "f16", "f16"),            # GQA 1, tiny, ragged tile
+    (50, 24, 8, 900, True, 850, 0, "bf16", "f32"),       # GQA 3: a query's heads straddle row tiles
+    (16, 32, 4, 3000, True, 2984, 1000, "bf16", "f32"),  # GQA 8, window cuts into the splits
+    (64, 32, 16, 1000, True, 936, 0, "f32", "f32"),      # f32 queries (fp16 hi + lo on the MMA)
 ])
 def test_multi_parity(nq, H, Hkv, N, causal, pos0, window, qdt, odt):
     out, ref = run(nq, H, Hkv, N, causal, pos0, window, qdt, odt)
+    parity(out, ref)
+
+
+def test_multi_f32_scales():
+    out, ref = run(64, 32, 16, 1500, False, 0, 0, "f32", "f32", sb=np.float32)
     parity(out, ref)
 
 

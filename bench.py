@@ -5,7 +5,8 @@
 
 One step = one decode step of one attention layer: quantize-on-append of the
 new token's K/V into the preallocated int4 cache, then fused decode attention
-over the whole context (H=32, Hkv=16, D=128, batch 1, fp16 Q/out, fp16
+over the whole context, in one launch (`tq_sdpa_int4_append`; `--split-step`
+runs them as two launches) (H=32, Hkv=16, D=128, batch 1, fp16 Q/out, fp16
 scales/biases). Steps rotate over 8 independent layer caches (8 x 75.5 MB,
 larger than the 126 MB L2), so every step streams its cache from HBM. The
 appended slot is rewritten on each rotation, so every step attends over
@@ -52,8 +53,13 @@ def parse():
     ap.add_argument("--context", type=int, default=32768)
     ap.add_argument("--window", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg4"],
+    ap.add_argument("--split-step", action="store_true",
+                    help="cfg1: run the step as two launches (quantize_append, then sdpa_int4) "
+                         "instead of the fused sdpa_int4_append")
+    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg4"],
                     help="cfg1: config 1 decode step (default, weak scaling over GPUs); "
+                         "cfg2: config 2 on the tensor cores (64 x 1 batched decode over a "
+                         "shared 8K cache; 512-query causal prefill chunk); "
                          "cfg4: config 4, one 256K-token sequence split over the GPUs")
     return ap.parse_args()
 
@@ -186,6 +192,11 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     def step(Lr, s, with_append=True):
         c = Lr["cache"]
+        if with_append and not args.split_step:
+            # one launch: the decode kernel quantizes the new token into slot n - 1
+            tq.sdpa_int4_append(Lr["q"], Lr["kn"], Lr["vn"], *c.tensors(), H // HKV, 1.0, window,
+                                s=s, n_tokens=n_ctx, out=Lr["out"], ws=ws)
+            return
         if with_append:
             tq.quantize_append(Lr["kn"], Lr["vn"], *c.tensors(), pos=n_ctx - 1, s=s)
         tq.sdpa_int4(Lr["q"], *c.tensors(), H // HKV, 1.0, window, s=s, n_tokens=n_ctx,
@@ -445,6 +456,278 @@ def run_cfg4(args, rank: int, world: int, local_rank: int):
     return line
 
 
+# ----------------------------------------- config 2: tcgen05 multi-query --
+
+C2_N0, C2_B, C2_CHUNK, C2_LAYERS = 8192, 64, 512, 12
+
+
+def cfg2_flops() -> dict:
+    """Algorithmic FLOPs of one launch (QK^T and PV, 2 flops per MAC each):
+    batched: every query sees all N0 tokens; prefill: query i sees N0 + i + 1."""
+    vis_pre = sum(C2_N0 + i + 1 for i in range(C2_CHUNK))
+    return {"batched": 4.0 * H * D * C2_N0 * C2_B, "prefill": 4.0 * H * D * vis_pre}
+
+
+def run_cfg2(args, rank: int, world: int, local_rank: int):
+    """Config 2 on the tcgen05 kernel, two workloads over C2_LAYERS rotating
+    layer caches (each 8.7K tokens x 16 KV heads, 20 MB; 250 MB in all):
+    batched decode = 64 sequences x 1 query attending over one shared 8K-token
+    int4 cache; prefill chunk = quantize-append of 512 new tokens' K/V, then
+    the 512 causal queries at positions 8192..8703 over 8704 tokens.
+    Q and outputs bf16. Each rank runs its own layers (weak scaling)."""
+    import torch
+    import torch.distributed as dist
+    import gemma4metal_b200.turboquant as tq
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7 + rank)
+    N = C2_N0 + C2_CHUNK
+
+    def rms_norm(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True)) * w
+
+    wq = 1 + 0.1 * torch.randn(D, device=dev, generator=gen)
+    wk = 1 + 0.1 * torch.randn(D, device=dev, generator=gen)
+    layers = []
+    for _ in range(C2_LAYERS):
+        cache = tq.KVCache(1, HKV, D, N, device=dev)
+        k = rms_norm(torch.randn(1, HKV, C2_N0, D, device=dev, generator=gen), wk).half()
+        v = torch.randn(1, HKV, C2_N0, D, device=dev, generator=gen).half()
+        cache.append(k, v, pos=0)
+        kc = rms_norm(torch.randn(1, HKV, C2_CHUNK, D, device=dev, generator=gen), wk).half()
+        vc = torch.randn(1, HKV, C2_CHUNK, D, device=dev, generator=gen).half()
+        qb = rms_norm(torch.randn(C2_B, H, D, device=dev, generator=gen), wq).bfloat16()
+        qp = rms_norm(torch.randn(C2_CHUNK, H, D, device=dev, generator=gen), wq).bfloat16()
+        layers.append(dict(cache=cache, kc=kc, vc=vc, qb=qb, qp=qp,
+                           ob=torch.empty(C2_B, H, D, dtype=torch.bfloat16, device=dev),
+                           op=torch.empty(C2_CHUNK, H, D, dtype=torch.bfloat16, device=dev)))
+    lib = tq.load_library()
+    ws = tq.workspace(dev, max(int(lib.tq_sdpa_int4_multi_workspace_size(C2_B, H, HKV, D, C2_N0)),
+                               int(lib.tq_sdpa_int4_multi_workspace_size(C2_CHUNK, H, HKV, D, N))))
+    stream = torch.cuda.Stream(device=dev)
+
+    def batched(Lr):
+        tq.sdpa_int4_multi(Lr["qb"], *Lr["cache"].tensors(), H // HKV, 1.0, 0, n_tokens=C2_N0,
+                           out=Lr["ob"], ws=ws, s=stream)
+
+    def prefill(Lr, with_append=True):
+        c = Lr["cache"]
+        if with_append:  # rewrites the same 512 slots every rotation
+            tq.quantize_append(Lr["kc"], Lr["vc"], *c.tensors(), pos=C2_N0, s=stream)
+        tq.sdpa_int4_multi(Lr["qp"], *c.tensors(), H // HKV, 1.0, 0, n_tokens=N, causal=True,
+                           pos0=C2_N0, out=Lr["op"], ws=ws, s=stream)
+
+    with torch.cuda.stream(stream):
+        for Lr in layers:
+            prefill(Lr)
+            batched(Lr)
+    torch.cuda.synchronize()
+    CH = 2 * C2_LAYERS
+
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(CH):
+                    fn(layers[i % C2_LAYERS])
+        return g
+
+    graphs = {"batched": capture(batched), "prefill": capture(prefill),
+              "prefill_attn": capture(lambda Lr: prefill(Lr, False))}
+    torch.cuda.synchronize()
+
+    def timed(name, steps, warmup):
+        g = graphs[name]
+        reps = max(1, steps // CH)
+        with torch.cuda.stream(stream):
+            for _ in range(max(1, warmup // CH)):
+                g.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        with torch.cuda.stream(stream):
+            for _ in range(reps):
+                g.replay()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        return reps * CH, e0.elapsed_time(e1)
+
+    clocks = Clocks(local_rank)
+    clocks.start()
+    nb, tb = timed("batched", args.steps, max(args.warmup, CH))
+    npf, tpf = timed("prefill", max(CH, args.steps // 4), max(args.warmup, CH))
+    # kernel times for the roofline: >= 1.5 s of replays each, so the clock
+    # sampler sees the kernels under load
+    soak = {}
+    for name in ("batched", "prefill_attn"):
+        g = graphs[name]
+        k0 = torch.cuda.Event(enable_timing=True)
+        k1 = torch.cuda.Event(enable_timing=True)
+        reps, t_start = 0, time.perf_counter()
+        k0.record(stream)
+        with torch.cuda.stream(stream):
+            while time.perf_counter() - t_start < 1.5 or reps < 8:
+                for _ in range(8):
+                    g.replay()
+                reps += 8
+                if reps % 64 == 0:
+                    stream.synchronize()
+        k1.record(stream)
+        torch.cuda.synchronize()
+        soak[name] = (reps * CH, k0.elapsed_time(k1))
+    clk = clocks.stop()
+    (nkb, tkb), (npa, tpa) = soak["batched"], soak["prefill_attn"]
+
+    # end to end through the public API: queries from pinned host memory in,
+    # outputs back to pinned host memory, every step
+    hq = torch.empty(C2_B, H, D, dtype=torch.bfloat16, pin_memory=True)
+    ho = torch.empty(C2_B, H, D, dtype=torch.bfloat16, pin_memory=True)
+    hq.copy_(layers[0]["qb"].cpu())
+    e2e_steps = max(10, min(args.steps, 1000))
+
+    def e2e_loop(n):
+        with torch.cuda.stream(stream):
+            for i in range(n):
+                Lr = layers[i % C2_LAYERS]
+                Lr["qb"].copy_(hq, non_blocking=True)
+                batched(Lr)
+                ho.copy_(Lr["ob"], non_blocking=True)
+                stream.synchronize()
+
+    e2e_loop(10)
+    torch.cuda.synchronize()
+    ee0 = torch.cuda.Event(enable_timing=True)
+    ee1 = torch.cuda.Event(enable_timing=True)
+    ee0.record(stream)
+    e2e_loop(e2e_steps)
+    ee1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = ee0.elapsed_time(ee1)
+    assert tq.device_error() == 0, "a kernel reported a device error"
+    tt = torch.tensor([tb, tpf, tpa, tkb, e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    tb, tpf, tpa, tkb, e2e_ms = (float(x) for x in tt)
+    del graphs
+    torch.cuda.synchronize()
+    return dict(nb=nb, tb=tb, npf=npf, tpf=tpf, npa=npa, tpa=tpa, nkb=nkb, tkb=tkb, e2e_ms=e2e_ms,
+                e2e_steps=e2e_steps, clocks=clk)
+
+
+def cpu_reference_cfg2(budget_s: float = 15.0, seed: int = 7):
+    """The reference's algorithm for config 2 on the host: MLX-style
+    dequantize of the int4 cache to fp32, then SDPA in fp32 with the causal
+    mask the engine builds (engine/gemma4_multilayer.cpp:307-308,347-367) —
+    numpy matmuls over all host threads. Times one batched-decode step
+    (64 queries x 8K tokens) and the prefill chunk on a bounded sample of
+    its queries; returns queries/s for each."""
+    from oracle import inputs, oracle as O
+    L = inputs.make_layer(seed, H, HKV, D, C2_N0 + C2_CHUNK)
+    kq, ks, kb = O.quantize(L["k"][0])
+    vq, vs, vb = O.quantize(L["v"][0])
+    del L
+    rng = np.random.default_rng(seed)
+    G = H // HKV
+
+    def attend(q, n_tokens, pos):
+        kd = O.dequantize_np(kq, ks, kb)[:, :n_tokens].astype(np.float32)
+        vd = O.dequantize_np(vq, vs, vb)[:, :n_tokens].astype(np.float32)
+        nq = q.shape[0]
+        out = np.empty((nq, H, D), np.float32)
+        t = np.arange(n_tokens)
+        vis = t[None, :] <= pos[:, None]
+        for hk in range(HKV):
+            qh = q[:, hk * G:(hk + 1) * G].reshape(nq * G, D)
+            s = qh @ kd[hk].T
+            s = np.where(np.repeat(vis, G, axis=0), s, -np.inf)
+            s -= s.max(axis=1, keepdims=True)
+            p = np.exp(s)
+            o = (p @ vd[hk]) / p.sum(axis=1, keepdims=True)
+            out[:, hk * G:(hk + 1) * G] = o.reshape(nq, G, D)
+        return out
+
+    qb = rng.standard_normal((C2_B, H, D)).astype(np.float32)
+    attend(qb[:4], C2_N0, np.full(4, C2_N0 - 1))  # untimed warm-up
+    t0 = time.perf_counter()
+    nb = 0
+    while nb == 0 or time.perf_counter() - t0 < budget_s / 2:
+        attend(qb, C2_N0, np.full(C2_B, C2_N0 - 1))
+        nb += 1
+    tb = time.perf_counter() - t0
+    sample = 64  # queries of the 512-query chunk per timed call (positions spread over the chunk)
+    qp = rng.standard_normal((sample, H, D)).astype(np.float32)
+    pos = C2_N0 + np.linspace(0, C2_CHUNK - 1, sample).astype(np.int64)
+    t0 = time.perf_counter()
+    npf = 0
+    while npf == 0 or time.perf_counter() - t0 < budget_s / 2:
+        attend(qp, C2_N0 + C2_CHUNK, pos)
+        npf += 1
+    tp = time.perf_counter() - t0
+    return {"batched_tokens_s": nb * C2_B / tb, "prefill_tokens_s": npf * sample / tp,
+            "cores": os.cpu_count(), "seconds": tb + tp,
+            "sample": f"{nb} batched steps (64 queries x 8192 tokens) and {npf} x {sample} of the "
+                      f"512 prefill queries (positions spread over the chunk), dequantize + fp32 SDPA"}
+
+
+def cfg2_line(args, world, res, cpu):
+    peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json"))) \
+        if os.path.exists(os.path.join(ROOT, "MEASURED_PEAKS.json")) else {}
+    peak = float(peaks.get("bf16_tflops", 1590.0))
+    src = "measured (MEASURED_PEAKS.json bf16_tflops, burst)" if peaks else "fallback"
+    fl = cfg2_flops()
+    us_b = res["tkb"] * 1000.0 / res["nkb"]
+    us_pa = res["tpa"] * 1000.0 / res["npa"]
+    ach_b = fl["batched"] / (us_b * 1e-6) / 1e12
+    ach_p = fl["prefill"] / (us_pa * 1e-6) / 1e12
+    traffic = None
+    path = os.path.join(ROOT, "profiles", "attn_tc_cfg2.md")
+    if os.path.exists(path):
+        m = re.search(r"traffic_bytes_per_launch_batched:\s*([0-9.eE+]+)", open(path).read())
+        traffic = float(m.group(1)) if m else None
+    value = res["nb"] * C2_B * world / (res["tb"] / 1000.0)
+    line = {"metric": "int4-KV decode-attention tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": world, "steps": res["nb"], "warmup": args.warmup,
+            "ms_per_step": res["tb"] / res["nb"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16 (exact int4 codes and bf16-exact Q on the tensor cores), f32 softmax",
+            "data": "synthetic (seeded torch.randn, RMS-normalised Q/K as task configs[0])",
+            "config": {"workload": "cfg2 batched decode: 64 sequences x 1 query over one shared "
+                                   "8192-token int4 cache (tcgen05)",
+                       "batch": C2_B, "heads": H, "kv_heads": HKV, "head_dim": D, "context": C2_N0,
+                       "q_out": "bf16", "layers_rotated": C2_LAYERS,
+                       "l2": f"inputs larger than L2: {C2_LAYERS} rotating 20 MB layer caches",
+                       "parallelism": f"dp{world} (independent layers per GPU)"},
+            "roofline": {"bound": "tensor", "achieved": ach_b, "peak": peak, "unit": "TFLOP/s",
+                         "frac": ach_b / peak, "traffic": traffic,
+                         "kernel": "tq::attn_tc_kernel (tcgen05.mma kind::f16, TMEM) + attn_tc_merge_kernel",
+                         "kernel_us": us_b, "algorithmic_flops_per_launch": fl["batched"],
+                         "peak_source": src},
+            "prefill_chunk": {"workload": "cfg2 prefill: append 512 tokens + 512 causal queries at "
+                                          "8192..8703 (tcgen05)",
+                              "tokens_per_s": res["npf"] * C2_CHUNK * world / (res["tpf"] / 1000.0),
+                              "ms_per_step": res["tpf"] / res["npf"],
+                              "attn_us": us_pa, "attn_tflops": ach_p, "attn_frac": ach_p / peak},
+            "cpu_baseline": None if cpu is None else {
+                "value": cpu["batched_tokens_s"], "unit": "tokens/s", "cores": cpu["cores"],
+                "kind": "port", "sample": cpu["sample"],
+                "prefill_tokens_s": cpu["prefill_tokens_s"]},
+            "e2e": {"value": res["e2e_steps"] * C2_B * world / (res["e2e_ms"] / 1000.0),
+                    "unit": "tokens/s", "h2d_bytes_per_step": C2_B * H * D * 2,
+                    "d2h_bytes_per_step": C2_B * H * D * 2,
+                    "path": "gemma4metal_b200.turboquant.sdpa_int4_multi (ctypes C ABI), batched"},
+            "gpu_launches": 2 * res["nb"],
+            "launches_per_step": "2 (attn_tc_kernel, attn_tc_merge_kernel)",
+            "clocks": res["clocks"]}
+    return line
+
+
 # ----------------------------------------------------------- CPU reference --
 
 def cpu_reference(n_ctx: int, window: int, steps: int, warmup: int, seed: int = 5):
@@ -494,6 +777,23 @@ def main():
                     f"({LAYERS * bps['attn'] / 1e6:.0f} MB > 126 MB L2)",
               "parallelism": f"dp{args.gpus} (independent KV heads/sequences per GPU)"}
 
+    if args.impl == "reference" and args.workload == "cfg2":
+        if rank != 0:
+            return
+        cpu = cpu_reference_cfg2()
+        v = cpu["batched_tokens_s"]
+        line = {"metric": "int4-KV decode-attention tokens/s", "value": v, "unit": "tokens/s",
+                "n_gpus": args.gpus, "steps": 1, "warmup": 0, "ms_per_step": C2_B * 1000.0 / v,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "data": "synthetic (seeded numpy)", "impl": "reference",
+                "config": {"workload": "cfg2 batched decode: 64 sequences x 1 query over one shared "
+                                       "8192-token int4 cache", "batch": C2_B, "heads": H,
+                           "kv_heads": HKV, "head_dim": D, "context": C2_N0},
+                "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cpu["cores"], "kind": "port",
+                                 "sample": cpu["sample"], "prefill_tokens_s": cpu["prefill_tokens_s"]},
+                "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
     if args.impl == "reference":
         if rank != 0:
             return
@@ -527,6 +827,17 @@ def main():
             dist.barrier()
             dist.destroy_process_group()
         return
+    if args.workload == "cfg2":
+        res = run_cfg2(args, rank, world, local_rank)
+        cpu = None
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_reference_cfg2()
+        if rank == 0:
+            print(json.dumps(cfg2_line(args, world, res, cpu)), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     res = run_ours(args, rank, world, local_rank)
     steps_total = args.steps * world
     value = steps_total / (res["t_ms"] / 1000.0)
@@ -556,9 +867,12 @@ def main():
             "e2e": {"value": e2e_value, "unit": "tokens/s",
                     "h2d_bytes_per_step": (H * D + 2 * HKV * D) * 2,
                     "d2h_bytes_per_step": H * D * 2,
-                    "path": "gemma4metal_b200.turboquant.quantize_append + sdpa_int4 (ctypes C ABI)"},
-            "gpu_launches": 2 * args.steps,
-            "launches_per_step": "2 (quantize_rows_kernel for K+V, decode_kernel)", "clocks": res["clocks"],
+                    "path": ("gemma4metal_b200.turboquant.quantize_append + sdpa_int4" if args.split_step
+                             else "gemma4metal_b200.turboquant.sdpa_int4_append") + " (ctypes C ABI)"},
+            "gpu_launches": (2 if args.split_step else 1) * args.steps,
+            "launches_per_step": ("2 (quantize_rows_kernel for K+V, decode_mma_kernel)" if args.split_step
+                                  else "1 (decode_mma_kernel with the new token's quantize-on-append fused)"),
+            "clocks": res["clocks"],
             "hbm_gbs_step": bps["step"] * value / world / 1e9}
     if rank == 0:
         print(json.dumps(line), flush=True)

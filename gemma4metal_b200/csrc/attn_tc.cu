@@ -221,16 +221,7 @@ __device__ __forceinline__ uint32_t center8(uint32_t x) {
 // 8 consecutive elements [i, i + 8) as float; vec: 16-byte aligned base
 __device__ __forceinline__ void load8(const void* p, long long i, int dtype, bool vec, float (&v)[8]) {
   if (vec && dtype != kF32) {
-    const uint4 u = *reinterpret_cast<const uint4*>(static_cast<const unsigned short*>(p) + i);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      float2 f;
-      if (dtype == kF16) f = __half22float2(*reinterpret_cast<const __half2*>(&w[k]));
-      else f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[k]));
-      v[2 * k] = f.x;
-      v[2 * k + 1] = f.y;
-    }
+    load8_aligned(p, i, dtype, v);
   } else {
 #pragma unroll
     for (int k = 0; k < 8; ++k) v[k] = load_as_float(p, i + k, dtype);
@@ -668,11 +659,14 @@ __global__ void __launch_bounds__(256) attn_tc_merge_kernel(const TCParams p, in
   const int S = p.splits;
   const long long sstride = static_cast<long long>(kD + 2) * kRows;
   const float* base = p.ws + unit * S * sstride + rb + lane;
+  // unrolled so the loads of several splits are in flight at once (a
+  // load -> max -> load chain would pay one memory latency per split)
   float M = -INFINITY;
+#pragma unroll 8
   for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(base + s * sstride + kD * kRows));
   float L = 0.0f, acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   const float* col = base + (db + 4 * warp) * kRows;
-#pragma unroll 4
+#pragma unroll 8
   for (int s = 0; s < S; ++s) {
     const float* ps = base + s * sstride;
     const float ms = __ldcg(ps + kD * kRows);

@@ -64,6 +64,10 @@ struct DecodeCommon {
   const void *ks, *kb, *vs, *vb;
   int sb_dtype, gqa, window, B, Hkv, D, n_tokens, capacity;
   float scale;
+  // decode step with quantize-on-append of the new token (nullable)
+  const void* k_new = nullptr;
+  const void* v_new = nullptr;
+  int new_dtype = 0;
 };
 
 int validate_decode(const DecodeCommon& c, const char* fn) {
@@ -251,6 +255,23 @@ static int decode_common(const DecodeCommon& c, const char* fn, const int32_t* s
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
   a.err = device_error_ptr();
+  if (c.k_new) {
+    // the mma kernel quantizes the new token in the same launch; the CUDA-core
+    // kernel gets it from a quantize-on-append launch just before
+    if (pl.variant == tq::kDecodeMma) {
+      a.k_new = c.k_new;
+      a.v_new = c.v_new;
+      a.new_dtype = c.new_dtype;
+    } else {
+      e = tq::launch_quantize_rows(
+          c.k_new, c.new_dtype, static_cast<long long>(c.B) * c.Hkv, c.D, 1, c.Hkv, c.capacity,
+          a.bstride_tok, c.n_tokens - 1, seq_lens, const_cast<uint32_t*>(c.kq),
+          const_cast<void*>(c.ks), const_cast<void*>(c.kb), c.sb_dtype,
+          static_cast<cudaStream_t>(stream), c.v_new, const_cast<uint32_t*>(c.vq),
+          const_cast<void*>(c.vs), const_cast<void*>(c.vb), -1);
+      if (e != cudaSuccess) return cuda_fail(e, fn);
+    }
+  }
   tq::launch_detail().clear();
   e = tq::launch_decode(a, pl, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
@@ -275,6 +296,29 @@ int tq_sdpa_int4(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,
                  capacity, scale};
   return decode_common(c, "tq_sdpa_int4", seq_lens, 0, 0, 0, out, out_dtype, nullptr, workspace,
                        workspace_bytes, stream);
+}
+
+int tq_sdpa_int4_append(const void* queries, tq_dtype q_dtype, const void* k_new,
+                        const void* v_new, tq_dtype new_dtype, uint32_t* k_quant, void* k_scales,
+                        void* k_biases, uint32_t* v_quant, void* v_scales, void* v_biases,
+                        tq_dtype sb_dtype, int gqa_factor, float scale, int sliding_window,
+                        int batch, int num_kv_heads, int head_dim, int n_tokens, int capacity,
+                        const int32_t* seq_lens, void* out, tq_dtype out_dtype, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  t_err.clear();
+  if (!out) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: null out");
+  if (!valid_dtype(out_dtype)) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: bad out_dtype");
+  if (!k_new || !v_new) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: null k_new/v_new");
+  if (!valid_dtype(new_dtype)) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: bad new_dtype");
+  if (!aligned16(k_new) || !aligned16(v_new))
+    return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: k_new/v_new must be 16-byte aligned");
+  if (!seq_lens && n_tokens < 1)
+    return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: n_tokens must include the new token (>= 1)");
+  DecodeCommon c{queries, q_dtype, k_quant, v_quant, k_scales, k_biases, v_scales, v_biases,
+                 sb_dtype, gqa_factor, sliding_window, batch, num_kv_heads, head_dim, n_tokens,
+                 capacity, scale, k_new, v_new, new_dtype};
+  return decode_common(c, "tq_sdpa_int4_append", seq_lens, 0, 0, 0, out, out_dtype, nullptr,
+                       workspace, workspace_bytes, stream);
 }
 
 int tq_sdpa_int4_partial(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,

@@ -21,7 +21,8 @@ struct QuantRows {
   int Hkv, capacity;
   long long bstride_tok;  // tokens between consecutive sequences of the cache
   int pos;
-  const int32_t* positions;  // nullable, per-sequence slot
+  const int32_t* positions;  // nullable, per-sequence slot (+ pos_bias)
+  int pos_bias;
   uint32_t* codes;
   void* scales;
   void* biases;
@@ -32,52 +33,6 @@ struct QuantRows {
   void* scales2;
   void* biases2;
 };
-
-__device__ __forceinline__ void load8(const void* p, long long i, int dtype, float (&v)[8]) {
-  if (dtype == kF16) {
-    const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(p) + i);
-    const __half2* h = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 f = __half22float2(h[k]);
-      v[2 * k] = f.x;
-      v[2 * k + 1] = f.y;
-    }
-  } else if (dtype == kBF16) {
-    const uint4 raw =
-        *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p) + i);
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float2 f = __bfloat1622float2(h[k]);
-      v[2 * k] = f.x;
-      v[2 * k + 1] = f.y;
-    }
-  } else {
-    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
-    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i + 4);
-    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-  }
-}
-
-// Round to the scale/bias storage type, store (if dst), and return the value
-// read back.
-__device__ __forceinline__ float round_store(float v, int dtype, void* dst, long long i,
-                                             bool write) {
-  if (dtype == kF16) {
-    const __half h = __float2half_rn(v);
-    if (write) reinterpret_cast<__half*>(dst)[i] = h;
-    return __half2float(h);
-  }
-  if (dtype == kBF16) {
-    const __nv_bfloat16 h = __float2bfloat16_rn(v);
-    if (write) reinterpret_cast<__nv_bfloat16*>(dst)[i] = h;
-    return __bfloat162float(h);
-  }
-  if (write) reinterpret_cast<float*>(dst)[i] = v;
-  return v;
-}
 
 __global__ void __launch_bounds__(256) quantize_rows_kernel(QuantRows p) {
   pdl_wait();
@@ -99,22 +54,13 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(QuantRows p) {
 
   float v[8];
   if (live) {
-    load8(p.x, r * p.D + w * 8, p.x_dtype, v);
+    load8_aligned(p.x, r * p.D + w * 8, p.x_dtype, v);
   } else {
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = 0.0f;
   }
-  float mn = v[0], mx = v[0];
-#pragma unroll
-  for (int j = 1; j < 8; ++j) {
-    mn = fminf(mn, v[j]);
-    mx = fmaxf(mx, v[j]);
-  }
-#pragma unroll
-  for (int o = 1; o < 8; o <<= 1) {
-    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  }
+  float mn, mx;
+  group_minmax8(v, mn, mx);
   if (!live) return;
 
   // destination slot
@@ -122,7 +68,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(QuantRows p) {
   const long long bh = r / p.n_new;
   const int h = static_cast<int>(bh % p.Hkv);
   const long long b = bh / p.Hkv;
-  const int base = p.positions ? p.positions[b] : p.pos;
+  const int base = p.positions ? p.positions[b] + p.pos_bias : p.pos;
   // a device-provided position outside the cache writes nothing
   if (p.positions && (base < 0 || base + i >= p.capacity)) return;
   const long long tok = b * p.bstride_tok + static_cast<long long>(h) * p.capacity + base + i;
@@ -130,20 +76,8 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(QuantRows p) {
   const int g = w / 8;
   const long long sidx = tok * (p.D / 64) + g;
   const bool leader = (w % 8) == 0;
-  const float scale_f = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
-  const float s = round_store(scale_f, p.sb_dtype, p.scales, sidx, leader);
-  const float bb = round_store(mn, p.sb_dtype, p.biases, sidx, leader);
-
-  uint32_t packed = 0;
-  if (s != 0.0f) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      float c = rintf(__fdiv_rn(__fsub_rn(v[j], bb), s));
-      c = fminf(fmaxf(c, 0.0f), 15.0f);
-      packed |= static_cast<uint32_t>(c) << (4 * j);
-    }
-  }
-  p.codes[tok * words_per_row + w] = packed;
+  p.codes[tok * words_per_row + w] =
+      quantize_word8(v, mn, mx, p.sb_dtype, p.scales, p.biases, sidx, leader);
 }
 
 template <typename OUT>
@@ -173,8 +107,9 @@ cudaError_t launch_quantize_rows(const void* x, int x_dtype, long long rows, int
                                  int Hkv, int capacity, long long bstride_tok, int pos,
                                  const int32_t* positions, uint32_t* codes, void* scales,
                                  void* biases, int sb_dtype, cudaStream_t stream, const void* x2,
-                                 uint32_t* codes2, void* scales2, void* biases2) {
+                                 uint32_t* codes2, void* scales2, void* biases2, int pos_bias) {
   QuantRows p;
+  p.pos_bias = pos_bias;
   p.x2 = x2;
   p.codes2 = codes2;
   p.scales2 = scales2;

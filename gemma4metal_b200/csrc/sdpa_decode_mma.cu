@@ -78,8 +78,9 @@ struct MLayout {
   static constexpr int SBB = TILE * NG * static_cast<int>(sizeof(SB));
   static constexpr int STAGE = (2 * CODE + 4 * SBB + 1023) / 1024 * 1024;
   static constexpr int STAGES = MCfg<D>::STAGES * STAGE;
-  static constexpr int BAR = STAGES;  // full[MCfg<D>::STAGES], empty[MCfg<D>::STAGES], q
-  static constexpr int FLAG = BAR + ((2 * MCfg<D>::STAGES + 1) * 8 + 15) / 16 * 16;
+  // full[MCfg<D>::STAGES], empty[MCfg<D>::STAGES], q, appended token written
+  static constexpr int BAR = STAGES;
+  static constexpr int FLAG = BAR + ((2 * MCfg<D>::STAGES + 2) * 8 + 15) / 16 * 16;
   static constexpr int QB = FLAG + 16;                   // the CTA's G query rows (<= f32)
   static_assert(QB % 16 == 0, "bulk-copy destination must be 16-byte aligned");
   static constexpr int BYTES = QB + G * D * 4 + 1024;    // + alignment slack
@@ -113,6 +114,11 @@ struct MParams {
   int out_dtype;
   float* part_out;
   int splits, chunks_per_split;
+  // fused quantize-on-append (nullable): the step's K/V rows (B, Hkv, D) are
+  // quantized into slot n_local - 1 of each sequence before it is read
+  const void* k_new;
+  const void* v_new;
+  int new_dtype;
   float* ws_o;
   float* ws_ml;
   unsigned* counters;
@@ -258,6 +264,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lyt::BAR);
   uint64_t* empty = full + MCfg<D>::STAGES;
   uint64_t* qbar = empty + MCfg<D>::STAGES;
+  uint64_t* nbar = qbar + 1;  // the appended token is in global memory (fused append)
   int* s_flag = reinterpret_cast<int*>(smem + Lyt::FLAG);
 
   const int tid = threadIdx.x;
@@ -318,6 +325,15 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   range(n_local, t_lo, cb, ce);
   const int ntiles = ce > cb ? (ce - cb + CPT - 1) / CPT : 0;
   const int r_hi = min(t_hi, ce * kChunk);  // tokens at or past r_hi are masked
+  // fused append: the CTA whose chunks hold slot n_local - 1 quantizes the
+  // step's K/V row into it (CTAs of other query-head subsets of the same KV
+  // head write the same bytes); its producer issues the tile holding the
+  // slot only after the writers' release on nbar
+  constexpr int NWW = D / 128;  // writer warps: D/8 words of K and of V, one per lane
+  const int new_slot = n_local - 1;
+  const bool has_new = p.k_new != nullptr && n_local > 0 && new_slot >= cb * kChunk &&
+                       new_slot < ce * kChunk;
+  const int new_tile = has_new ? (new_slot / kChunk - cb) / CPT : -1;
 
   if (tid == 0) {
     for (int s = 0; s < MCfg<D>::STAGES; ++s) {
@@ -325,6 +341,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
       mbar_init(&empty[s], W);
     }
     mbar_init(qbar, 1);
+    mbar_init(nbar, NWW);
     fence_barrier_init();
   }
   __syncthreads();
@@ -351,6 +368,10 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
       uint32_t par = 0;
       for (int i = 0; i < ntiles; ++i) {
         if (i >= MCfg<D>::STAGES) mbar_wait_bounded(&empty[st], par ^ 1u, p.err);
+        if (i == new_tile) {  // the appended token's codes and scales are written
+          mbar_wait_bounded(nbar, 0, p.err);
+          fence_proxy_async_global();
+        }
         const int c0 = cb + i * CPT;
         const int nc = min(CPT, ce - c0);
         const int t0 = c0 * kChunk;
@@ -378,6 +399,28 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   }
 
   // ======================= consumer warps =======================================
+  // fused append: lane = one packed word of the K row (first D/8 writer
+  // threads) or of the V row, quantized exactly as quantize_rows_kernel does
+  if (has_new && warp < NWW) {
+    constexpr int WPR = D / 8;
+    const int wi = warp * 32 + lane;
+    const bool is_v = wi >= WPR;
+    const int w = wi % WPR;
+    float v[8];
+    load8_aligned(is_v ? p.v_new : p.k_new,
+                  (static_cast<long long>(b) * p.Hkv + kv) * D + w * 8, p.new_dtype, v);
+    float mn, mx;
+    group_minmax8(v, mn, mx);
+    const long long tok = tok_base + new_slot;
+    void* sc = const_cast<void*>(is_v ? p.vs : p.ks);
+    void* bi = const_cast<void*>(is_v ? p.vb : p.kb);
+    constexpr int kSb = sizeof(SB) == 4 ? kF32 : kF16;
+    const uint32_t packed = quantize_word8(v, mn, mx, kSb, sc, bi, tok * NG + w / 8, (w % 8) == 0);
+    const_cast<uint32_t*>(is_v ? p.vq : p.kq)[tok * WPR + w] = packed;
+    fence_proxy_async_global();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(nbar);
+  }
   const int r = lane >> 2;  // mma groupID
   const int c = lane & 3;   // mma thread-in-group
 
@@ -1114,6 +1157,9 @@ cudaError_t launch_decode_mma(const DecodeArgs& a, const DecodePlan& pl, cudaStr
   p.part_out = a.part_out;
   p.splits = pl.splits;
   p.chunks_per_split = pl.tiles_per_split;  // the planner's tiles are 64-token chunks here
+  p.k_new = a.k_new;
+  p.v_new = a.v_new;
+  p.new_dtype = a.new_dtype;
   if (pl.splits > 1) {
     unsigned char* ws = static_cast<unsigned char*>(a.workspace);
     p.ws_o = reinterpret_cast<float*>(ws + pl.ws_o_off);

@@ -176,4 +176,101 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 8 consecutive elements [i, i + 8) of a 16-byte aligned row as float.
+__device__ __forceinline__ void load8_aligned(const void* p, long long i, int dtype, float (&v)[8]) {
+  if (dtype == kF16) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const __half*>(p) + i);
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __half22float2(h[k]);
+      v[2 * k] = f.x;
+      v[2 * k + 1] = f.y;
+    }
+  } else if (dtype == kBF16) {
+    const uint4 raw =
+        *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(p) + i);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 f = __bfloat1622float2(h[k]);
+      v[2 * k] = f.x;
+      v[2 * k + 1] = f.y;
+    }
+  } else {
+    const float4 a = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+    const float4 b = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+  }
+}
+
+// Orders this thread's generic-proxy global writes before later async-proxy
+// accesses (TMA / bulk copies) of the same data.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// ---- MLX affine group-64 4-bit quantization (mlx quantize(x, 64, 4)) ----------
+// A lane holds 8 consecutive values of a row (one packed word); the 8 lanes
+// 8k..8k+7 of a warp hold one 64-value group. All arithmetic is IEEE
+// round-to-nearest (explicit __fsub_rn/__fdiv_rn, rintf = ties-to-even), so
+// the codes, scales and biases are bit-identical to the CPU oracle.
+
+// Group min/max over the 8 lanes of the group (warp-collective: all 32 lanes).
+__device__ __forceinline__ void group_minmax8(const float (&v)[8], float& mn, float& mx) {
+  mn = v[0];
+  mx = v[0];
+#pragma unroll
+  for (int j = 1; j < 8; ++j) {
+    mn = fminf(mn, v[j]);
+    mx = fmaxf(mx, v[j]);
+  }
+#pragma unroll
+  for (int o = 1; o < 8; o <<= 1) {
+    mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, o));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
+}
+
+// Round to the scale/bias storage type, store (if write), and return the value
+// read back.
+__device__ __forceinline__ float round_store(float v, int dtype, void* dst, long long i,
+                                             bool write) {
+  if (dtype == kF16) {
+    const __half h = __float2half_rn(v);
+    if (write) reinterpret_cast<__half*>(dst)[i] = h;
+    return __half2float(h);
+  }
+  if (dtype == kBF16) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    if (write) reinterpret_cast<__nv_bfloat16*>(dst)[i] = h;
+    return __bfloat162float(h);
+  }
+  if (write) reinterpret_cast<float*>(dst)[i] = v;
+  return v;
+}
+
+// Scale = (max - min) / 15 and bias = min, rounded to the storage type and
+// written at sidx by the group's leader; returns the packed word of the 8
+// codes round((x - bias) / scale) clamped to 0..15, low nibble first (all
+// zero when the scale is zero).
+__device__ __forceinline__ uint32_t quantize_word8(const float (&v)[8], float mn, float mx,
+                                                   int sb_dtype, void* scales, void* biases,
+                                                   long long sidx, bool leader) {
+  const float scale_f = __fdiv_rn(__fsub_rn(mx, mn), 15.0f);
+  const float s = round_store(scale_f, sb_dtype, scales, sidx, leader);
+  const float bb = round_store(mn, sb_dtype, biases, sidx, leader);
+  uint32_t packed = 0;
+  if (s != 0.0f) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float c = rintf(__fdiv_rn(__fsub_rn(v[j], bb), s));
+      c = fminf(fmaxf(c, 0.0f), 15.0f);
+      packed |= static_cast<uint32_t>(c) << (4 * j);
+    }
+  }
+  return packed;
+}
+
 }  // namespace tq

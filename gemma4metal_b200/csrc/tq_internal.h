@@ -14,7 +14,8 @@ cudaError_t launch_quantize_rows(const void* x, int x_dtype, long long rows, int
                                  const int32_t* positions, uint32_t* codes, void* scales,
                                  void* biases, int sb_dtype, cudaStream_t stream,
                                  const void* x2 = nullptr, uint32_t* codes2 = nullptr,
-                                 void* scales2 = nullptr, void* biases2 = nullptr);
+                                 void* scales2 = nullptr, void* biases2 = nullptr,
+                                 int pos_bias = 0);  // added to positions[b]
 
 cudaError_t launch_dequantize(const uint32_t* codes, const void* scales, const void* biases,
                               int sb_dtype, long long rows, int D, void* out, int out_dtype,
@@ -47,6 +48,11 @@ struct DecodeArgs {
   void* workspace;
   size_t workspace_bytes;
   uint32_t* err;
+  // fused quantize-on-append (mma kernel only; nullable): (B, Hkv, D) rows
+  // written to slot n_local - 1 of each sequence before the attention reads it
+  const void* k_new = nullptr;
+  const void* v_new = nullptr;
+  int new_dtype = 0;
 };
 
 // Decode kernel variants: the CUDA-core kernel (sdpa_decode.cu) and the

@@ -58,6 +58,8 @@ def load_library() -> ctypes.CDLL:
     L.tq_sdpa_int4_workspace_size.argtypes = [I, I, I, I, I, I]
     L.tq_workspace_init.argtypes = [P, SZ, P]
     L.tq_sdpa_int4.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, P, P, I, P, SZ, P]
+    L.tq_sdpa_int4_append.argtypes = [P, I, P, P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I,
+                                      P, P, I, P, SZ, P]
     L.tq_sdpa_int4_partial.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, I, I, P,
                                        P, SZ, P]
     L.tq_lse_merge.argtypes = [P, I, I, I, I, P, I, P]
@@ -271,6 +273,40 @@ def sdpa_int4(queries: torch.Tensor, k_quant: torch.Tensor, k_scales: torch.Tens
         _ptr(qc), _dt(q), *[_ptr(c) for c in cache], _dt(cache[1]), int(gqa_factor),
         float(scale), int(sliding_window), B, Hkv, D, n, cap, _ptr(seq_lens), _ptr(out), _dt(out),
         _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
+    return out[0] if squeeze else out
+
+
+def sdpa_int4_append(queries: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                     k_quant, k_scales, k_biases, v_quant, v_scales, v_biases, gqa_factor: int,
+                     scale: float = 1.0, sliding_window: int = 0, s=None, *, n_tokens: int,
+                     seq_lens: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                     out_dtype: Optional[torch.dtype] = None,
+                     ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One decode step: quantize-on-append of the new token's K/V (B, Hkv, D)
+    (or (B, Hkv, 1, D)) into slot n - 1 of a (B, Hkv, capacity, ...) cache,
+    then fused int4 decode attention over the n tokens (n = n_tokens, or
+    seq_lens[b]); one launch with the tensor-core decode kernel. Same result
+    as quantize_append(pos = n - 1) followed by sdpa_int4."""
+    squeeze = queries.dim() == 2
+    q = queries.unsqueeze(0) if squeeze else queries
+    cache = [k_quant, k_scales, k_biases, v_quant, v_scales, v_biases]
+    if k_quant.dim() == 3:
+        cache = [c.unsqueeze(0) for c in cache]
+    B, H, D = q.shape
+    _, Hkv, cap, _ = cache[0].shape
+    n = int(n_tokens)
+    od = out_dtype or q.dtype
+    if out is None:
+        out = torch.empty(B, H, D, dtype=od, device=q.device)
+    nbytes = sdpa_int4_workspace_size(B, H, Hkv, D, n, sliding_window)
+    if ws is None:
+        ws = workspace(q.device, nbytes, s)
+    # contiguous copies stay referenced until the launch is enqueued
+    qc, kc, vc = q.contiguous(), k_new.contiguous(), v_new.contiguous()
+    _check(load_library().tq_sdpa_int4_append(
+        _ptr(qc), _dt(q), _ptr(kc), _ptr(vc), _dt(kc), *[_ptr(c) for c in cache], _dt(cache[1]),
+        int(gqa_factor), float(scale), int(sliding_window), B, Hkv, D, n, cap, _ptr(seq_lens),
+        _ptr(out), _dt(out), _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
     return out[0] if squeeze else out
 
 

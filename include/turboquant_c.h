@@ -125,6 +125,25 @@ TQ_API int tq_sdpa_int4(const void* queries, tq_dtype q_dtype, const uint32_t* k
                  int n_tokens, int capacity, const int32_t* seq_lens, void* out,
                  tq_dtype out_dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* One decode step of one layer: quantize-on-append of the step's new K/V
+ * row of every sequence into slot n - 1 of the cache (n = seq_lens[b], or
+ * n_tokens), then decode attention over the n tokens. The result, cache
+ * bytes included, equals tq_quantize_append(k_new, v_new, ..., pos = n - 1)
+ * followed by tq_sdpa_int4; the engine runs those as MLX quantize +
+ * concatenate (engine/gemma4_multilayer.cpp:228-236) then
+ * turboquant::sdpa_int4 (lib/turboquant.h:202-207). With the tensor-core
+ * decode kernel (head_dim 128/256) both happen in ONE launch: the CTA that
+ * owns slot n - 1 quantizes the row while its first tiles stream in.
+ *   k_new, v_new: (B, num_kv_heads, head_dim) in new_dtype, 16-byte aligned;
+ *   other arguments as tq_sdpa_int4. */
+TQ_API int tq_sdpa_int4_append(const void* queries, tq_dtype q_dtype, const void* k_new,
+                        const void* v_new, tq_dtype new_dtype, uint32_t* k_quant, void* k_scales,
+                        void* k_biases, uint32_t* v_quant, void* v_scales, void* v_biases,
+                        tq_dtype sb_dtype, int gqa_factor, float scale, int sliding_window,
+                        int batch, int num_kv_heads, int head_dim, int n_tokens, int capacity,
+                        const int32_t* seq_lens, void* out, tq_dtype out_dtype, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
 /* Sequence-split shard of decode attention: this cache holds global token
  * positions [token_offset, token_offset + n_local) of a sequence whose total
  * length is n_total (all sequences of the batch share both). Writes the

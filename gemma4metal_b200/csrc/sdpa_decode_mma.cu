@@ -293,11 +293,26 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     }
   };
 
-  // Before waiting for the preceding kernel, warm L2 with the first tiles of
-  // the range that n_tokens (the largest sequence) gives: a prefetch reads
-  // nothing into this kernel, so data the preceding kernel still writes (the
-  // appended token) is read coherently after pdl_wait.
+  // Before waiting for the preceding kernel: barrier init, tensor-map
+  // prefetch, and L2 warmed with the query rows and the first tiles of the
+  // range that n_tokens (the largest sequence) gives. A prefetch reads
+  // nothing into this kernel, so data a preceding kernel still writes (the
+  // queries, an appended token) is read coherently after pdl_wait.
+  if (tid == 0) {
+    for (int s = 0; s < MCfg<D>::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], W);
+    }
+    mbar_init(qbar, 1);
+    mbar_init(nbar, D / 128);  // one arrival per writer warp of a fused append
+    fence_barrier_init();
+  }
   if (tid == W * 32) {
+    prefetch_tensormap(&tmk);
+    prefetch_tensormap(&tmv);
+    const int qel = p.q_dtype == kF32 ? 4 : 2;
+    prefetch_l2(static_cast<const unsigned char*>(p.q) + (static_cast<long long>(b) * p.H + h0) * D * qel,
+                static_cast<uint32_t>(G * D * qel));
     const int n_pf = max(0, min(p.n_tokens, p.capacity));
     const int n_pf4 = (n_pf + 3) & ~3;  // <= capacity: rows past it are never touched
     int lo, c0, c1;
@@ -316,6 +331,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     }
   }
 
+  __syncthreads();
   pdl_wait();     // inputs of the preceding kernels are visible from here on
   pdl_trigger();  // every CTA of this grid has started: the next may launch
 
@@ -335,22 +351,10 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
                        new_slot < ce * kChunk;
   const int new_tile = has_new ? (new_slot / kChunk - cb) / CPT : -1;
 
-  if (tid == 0) {
-    for (int s = 0; s < MCfg<D>::STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], W);
-    }
-    mbar_init(qbar, 1);
-    mbar_init(nbar, NWW);
-    fence_barrier_init();
-  }
-  __syncthreads();
 
   // ======================= producer warp ========================================
   if (warp == W) {
     if (lane == 0) {
-      prefetch_tensormap(&tmk);
-      prefetch_tensormap(&tmv);
       // the CTA's query rows: one bulk copy, shared through shared memory
       const int qel = p.q_dtype == kF32 ? 4 : 2;
       const uint32_t qbytes = static_cast<uint32_t>(G * D * qel);

@@ -84,16 +84,17 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-// try_wait suspends the warp until the phase completes or the hint (ns)
-// elapses, so a waiting warp does not spin on the issue slots.
+// try_wait blocks for a hardware-chosen interval while the phase is
+// incomplete (no suspend-time hint: the default interval measured faster
+// here than a long hint), so a waiting warp does not spin on the issue slots.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity), "r"(1000000u)
+      : "r"(smem_addr(bar)), "r"(parity)
       : "memory");
   return done != 0;
 }

@@ -105,8 +105,9 @@ def test_decode_step_matches_append_then_decode(H, Hkv, D, N, window, sb, ndt, B
 
 
 def test_decode_step_in_cuda_graph():
-    """The fused step captured once and replayed over a growing context: each
-    replay of a fixed-n graph rewrites the same slot with the same bytes."""
+    """The fused step captured once and replayed: each replay of a fixed-n
+    graph rewrites the same slot with the same bytes and gives the same
+    output."""
     H, Hkv, D, N = 32, 16, 128, 2048
     L = inputs.make_layer(5, H, Hkv, D, N)
     cache = tq.KVCache(1, Hkv, D, N + 4)

@@ -45,27 +45,42 @@ namespace {
 constexpr int kRows = 128;     // query rows per CTA (TMEM lanes)
 constexpr int kTok = 64;       // tokens per tile
 constexpr int kD = 128;        // head_dim (two 64-dim scale groups)
-constexpr int kThreads = 256;  // two threads per row (token halves of each tile)
-constexpr int kTmemCols = 256; // S'_0, S'_1, O'_0, O'_1 (64 fp32 columns each)
+// warp roles: warp 0 issues the MMAs (and owns TMEM); warps 1-2 unpack the
+// codes (one token per thread); warps 3-10 run the softmax, two threads per
+// query row (warp % 4 is the TMEM lane quarter a warp may access, so each
+// quarter has one warp per half). 11 warps = at most 3 per SM sub-partition,
+// which leaves 168 registers per thread. (Four threads per row, 19 warps at
+// 96 registers, measured slower: more per-thread fixed cost per tile.)
+constexpr int kMmaWarp = 0;
+constexpr int kUnpackBase = 1, kUnpackWarps = 2;
+constexpr int kSoftmaxWarps = 8;
+constexpr int kSoftmaxBase = (kUnpackBase + kUnpackWarps) * 32;
+constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
+constexpr int kThreads = kSoftmaxBase + kSoftmaxThreads;  // 352
+constexpr int kTmemCols = 512; // S[0], S[1] (2 groups x 64 tokens each), O (2 groups x 64 dims)
 // an MMA group finishes in microseconds; give up (and record the error) after
 // ~10 ms of SM clocks so a wait that cannot complete still ends the kernel
 constexpr long long kWaitBudget = 20000000LL;
 
 struct TLayout {
-  static constexpr int Q = 0;                   // [2 groups][128 rows][128 B]  32 KB
-  static constexpr int K = Q + 2 * kRows * 128; // [2][64 tokens][128 B]        16 KB
-  static constexpr int V = K + 2 * kTok * 128;  // [2][64][128 B]               16 KB
-  static constexpr int P = V + 2 * kTok * 128;  // [2][128 rows][128 B]         32 KB
-  static constexpr int TS = P + 2 * kRows * 128;  // per token: {A0, A1, B0, B1} (score terms)
-  static constexpr int TV = TS + kTok * 16;        // per token: {vs0, vs1, vb0 + 8 vs0, vb1 + 8 vs1}
-  static constexpr int MX = TV + kTok * 16;        // per thread: half-row max / epilogue sums
-  static constexpr int BAR = MX + kThreads * 4;    // mbarriers: S done, O done
-  static constexpr int TMEM = BAR + 16;            // allocated TMEM base address
-  static constexpr int BYTES = TMEM + 16 + 1024;   // + alignment slack
+  static constexpr int KVB = 2 * 2 * kTok * 128;  // one K/V stage: K [2 groups][64][128 B] + V, 32 KB
+  static constexpr int Q = 0;                     // [2 groups][128 rows][128 B]  32 KB
+  static constexpr int K = Q + 2 * kRows * 128;   // stage b at K + b * KVB
+  static constexpr int V = K + 2 * kTok * 128;    // stage b at V + b * KVB
+  static constexpr int PB = 2 * kRows * 128;      // one P buffer [2 groups][128 rows][128 B], 32 KB
+  static constexpr int P = K + 2 * KVB;           // buffer b at P + b * PB
+  static constexpr int TS = P + 2 * PB;           // [2][64 tokens] {A0, A1, B0, B1} (score terms)
+  static constexpr int TV = TS + 2 * kTok * 16;   // [2][64] {vs0, vs1, vb0 + 8 vs0, vb1 + 8 vs1}
+  static constexpr int MX = TV + 2 * kTok * 16;   // [2 tiles][2 halves][128 rows] maxima (q sums first)
+  static constexpr int RED = MX + 2 * kSoftmaxThreads * 4;  // [3][2][128] epilogue sums
+  static constexpr int BAR = RED + 3 * kSoftmaxThreads * 4; // 12 mbarriers
+  static constexpr int TMEM = BAR + 12 * 8;                 // allocated TMEM base address
+  static constexpr int BYTES = TMEM + 16 + 1024;            // + alignment slack
   // f32 queries: Q = hi + lo, both fp16; the lo part follows (32 KB)
   static constexpr int QL = (TMEM + 16 + 1023) / 1024 * 1024;
   static constexpr int BYTES_QLO = QL + 2 * kRows * 128 + 1024;
 };
+static_assert(TLayout::P % 1024 == 0 && TLayout::K % 1024 == 0, "UMMA operands need 1 KB alignment");
 
 struct TCParams {
   const void* q;       // (n_q, H, D) for prefill; (B, H, D) for batched decode
@@ -160,19 +175,27 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// 16 consecutive fp32 TMEM columns of this thread's lane
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
+// tcgen05.ld of 32 columns without the wait: the registers are valid only
+// after tmem_wait_ld(), and reg_fence() keeps their uses behind it
+__device__ __forceinline__ void tmem_ld32_raw(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
-      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-        "=r"(r[14]), "=r"(r[15])
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t (&r)[N]) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
@@ -211,10 +234,12 @@ __device__ __forceinline__ uint32_t nib64h(uint32_t x) {
 __device__ __forceinline__ int perm8(int e) { return (e >> 1) + 4 * (e & 1); }
 
 // fp16x2 (1 + c/64) -> (c - 8)/64; exact (both operands and the result are
-// multiples of 2^-6 below 2)
+// multiples of 2^-6 below 2). 0x3C80 is fp16 1.125 (a literal: a runtime
+// conversion would cost an XU-pipe instruction per call).
 __device__ __forceinline__ uint32_t center8(uint32_t x) {
+  const uint32_t k = 0x3C803C80u;
   __half2 h = *reinterpret_cast<const __half2*>(&x);
-  h = __hsub2(h, __floats2half2_rn(1.125f, 1.125f));
+  h = __hsub2(h, *reinterpret_cast<const __half2*>(&k));
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
@@ -249,26 +274,36 @@ __device__ __forceinline__ void store8(void* p, long long i, int dtype, bool vec
   }
 }
 
+// shared-memory float4 load kept in program order with the tcgen05 loads (a
+// plain load may be hoisted above them, which costs registers)
+__device__ __forceinline__ float4 lds4(const float4* p) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+  return v;
+}
+
 template <bool kQLo>
-__global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) {
+__global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem = reinterpret_cast<unsigned char*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  uint64_t* bar_s = reinterpret_cast<uint64_t*>(smem + TLayout::BAR);
-  uint64_t* bar_o = bar_s + 1;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TLayout::BAR);
+  // K and V stages have separate lifetimes: K(i) and the score terms are free
+  // once softmax(i) is done (p_full), V(i) and the value terms once PV(i) is
+  uint64_t* k_full = bars;       // [2] unpack warps: K codes + score terms in smem
+  uint64_t* v_full = bars + 2;   // [2] unpack warps: V codes + value terms in smem
+  uint64_t* s_full = bars + 4;   // [2] S MMA done
+  uint64_t* s_free = bars + 6;   // [2] softmax warps have read S
+  uint64_t* p_full = bars + 8;   // [2] P written (and O rescaled): K stage free
+  uint64_t* pv_done = bars + 10; // [2] PV MMA done: P buffer and V stage free
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + TLayout::TMEM);
-  float4* s_ts = reinterpret_cast<float4*>(smem + TLayout::TS);
-  float4* s_tv = reinterpret_cast<float4*>(smem + TLayout::TV);
-  float* s_mx = reinterpret_cast<float*>(smem + TLayout::MX);
   const uint32_t sbase = smem_u32(smem);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int rl = tid & (kRows - 1);  // row of the tile (TMEM lane)
-  const int hf = tid >> 7;           // token half of each tile; scale group of O
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x, mt = blockIdx.y, kv = blockIdx.z;
   const int rows_total = p.n_q * p.G;
-  // the two threads of a row meet on named barrier 1 + warp % 4 (64 threads)
-  auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory"); };
 
   pdl_wait();
   pdl_trigger();
@@ -281,12 +316,39 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) 
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
   if (tid == 0) {
-    mbar_init(bar_s, 1);
-    mbar_init(bar_o, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&k_full[b], kUnpackWarps);
+      mbar_init(&v_full[b], kUnpackWarps);
+      mbar_init(&s_full[b], 1);
+      mbar_init(&s_free[b], kSoftmaxWarps);
+      mbar_init(&p_full[b], kSoftmaxWarps);
+      mbar_init(&pv_done[b], 1);
+    }
     fence_barrier_init();
   }
 
-  // ---- this thread's row: query qi, head h (rows past the end compute on zeros)
+  // ---- token range of this split (tiles of 64 tokens), cut to what the CTA's
+  // rows can see: causal rows end at pos0 + last query, windows start at
+  // (first row's position) - window + 1
+  const int row_last = min(rows_total, (mt + 1) * kRows) - 1;
+  const int qpos_lo = p.causal ? p.pos0 + (mt * kRows) / p.G : p.n_tokens - 1;
+  const int qpos_hi = p.causal ? p.pos0 + row_last / p.G : p.n_tokens - 1;
+  const int n_vis = min(p.n_tokens, qpos_hi + 1);
+  const int t_lo = p.window > 0 ? max(0, qpos_lo - p.window + 1) : 0;
+  const int t_begin = max(split * p.tiles_per_split * kTok, t_lo);
+  const int t_end = min(n_vis, split * p.tiles_per_split * kTok + p.tiles_per_split * kTok);
+  const int n_tiles = t_end > t_begin ? (t_end - t_begin + kTok - 1) / kTok : 0;
+  const long long tok_base = static_cast<long long>(kv) * p.capacity;
+
+  // ---- softmax threads: (token half hf, row rl); warp % 4 is the TMEM lane
+  // quarter a warp may access
+  const int sid = tid - kSoftmaxBase;
+  const bool is_softmax = sid >= 0;
+  const int rl = 32 * (warp & 3) + lane;
+  const int hf = is_softmax ? sid / kRows : 0;
+  // exchange slot of (half, row): the partner of slot x is x ^ kRows (a
+  // warp's threads need not have sid == row: warp % 4 fixes the rows)
+  const int xs = hf * kRows + rl;
   const int row = mt * kRows + rl;
   const bool row_ok = row < rows_total;
   const int qi = row_ok ? row / p.G : 0;
@@ -294,10 +356,11 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) 
   // position of the query: causal rows at pos0 + qi; otherwise every query
   // sits at the end of the shared cache (the window counts back from there)
   const int qpos = p.causal ? p.pos0 + qi : p.n_tokens - 1;
-  // Q row, scale group hf -> smem (fp16, dims permuted inside each 8-dim word
-  // like the codes; f32 queries as fp16 hi + lo); the group's sum goes to the
-  // partner through s_mx
-  {
+  float* s_mx = reinterpret_cast<float*>(smem + TLayout::MX);  // [2 tiles][256]
+  if (is_softmax) {
+    // Q row, scale group hf -> smem (fp16, dims permuted inside each 8-dim
+    // word like the codes; f32 queries as fp16 hi + lo); the group's sum goes
+    // to the partner through s_mx
     const long long qb = (static_cast<long long>(qi) * p.H + h) * kD + hf * 64;
     const bool qvec = (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0;
     float qsum = 0.0f;
@@ -330,313 +393,342 @@ __global__ void __launch_bounds__(kThreads, 2) attn_tc_kernel(const TCParams p) 
         *reinterpret_cast<uint4*>(smem + TLayout::QL + hf * kRows * 128 + sw128(rl, ch)) =
             *reinterpret_cast<uint4*>(hl);
     }
-    s_mx[tid] = qsum;
+    s_mx[xs] = qsum;
+    fence_async_smem();
   }
-  fence_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const float qsum0 = s_mx[rl], qsum1 = s_mx[rl + kRows];
   const uint32_t tmem = *s_tmem;
-  const uint32_t t_s0 = tmem, t_s1 = tmem + 64, t_o0 = tmem + 128;
-  const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+  // TMEM columns: S[b] at 128 b (group g at + 64 g), O at 256 (group g at + 64 g)
+  const uint32_t t_o = tmem + 256;
 
-  // ---- token range of this split (tiles of 64 tokens), cut to what the CTA's
-  // rows can see: causal rows end at pos0 + last query, windows start at
-  // (first row's position) - window + 1
-  const int row_last = min(rows_total, (mt + 1) * kRows) - 1;
-  const int qpos_lo = p.causal ? p.pos0 + (mt * kRows) / p.G : p.n_tokens - 1;
-  const int qpos_hi = p.causal ? p.pos0 + row_last / p.G : p.n_tokens - 1;
-  const int n_vis = min(p.n_tokens, qpos_hi + 1);
-  const int t_lo = p.window > 0 ? max(0, qpos_lo - p.window + 1) : 0;
-  const int t_begin = max(split * p.tiles_per_split * kTok, t_lo);
-  const int t_end = min(n_vis, split * p.tiles_per_split * kTok + p.tiles_per_split * kTok);
-  const long long tok_base = static_cast<long long>(kv) * p.capacity;
-
-  float m_run = -INFINITY, l_run = 0.0f, corr0 = 0.0f, corr1 = 0.0f;
-  bool o_init = false;  // TMEM O holds accumulated values
-  uint32_t ph_s = 0, ph_o = 0;
-
-  // The next tile's codes and scales are loaded into registers while the
-  // current tile is in the tensor cores and the softmax, then unpacked into
-  // shared memory in the next iteration. Thread item: token ptok, scale
-  // group pgrp, K (pkv 0, threads 0..127) or V (pkv 1); 32 B of codes. The K
-  // threads also take the token's scale and bias pairs (raw bits, converted
-  // at unpack): K's for pgrp 0, V's for pgrp 1, so every per-token term is in
-  // shared memory before the tile's first barrier.
-  const int ptok = tid & 63, pgrp = (tid >> 6) & 1, pkv = tid >> 7;
-  uint4 pf0, pf1;
-  uint32_t pfr[4] = {0u, 0u, 0u, 0u};
-  auto prefetch = [&](int t0) {
-    const int t = t0 + ptok;
-    const long long rowi = tok_base + (t < t_end ? t : t0);
-    const uint4* cp = reinterpret_cast<const uint4*>((pkv ? p.vq : p.kq) + rowi * (kD / 8) + pgrp * 8);
-    pf0 = cp[0];
-    pf1 = cp[1];
-    if (!pkv) {
-      const void* sp = pgrp ? p.vs : p.ks;
-      const void* bp = pgrp ? p.vb : p.kb;
-      if (p.sb_f32) {
-        const uint2 a = reinterpret_cast<const uint2*>(sp)[rowi];
-        const uint2 b = reinterpret_cast<const uint2*>(bp)[rowi];
-        pfr[0] = a.x;
-        pfr[1] = a.y;
-        pfr[2] = b.x;
-        pfr[3] = b.y;
-      } else {
-        pfr[0] = reinterpret_cast<const uint32_t*>(sp)[rowi];
-        pfr[1] = reinterpret_cast<const uint32_t*>(bp)[rowi];
-      }
-    }
-  };
-  auto unpack = [&](int t0) {
-    const uint32_t w[8] = {pf0.x, pf0.y, pf0.z, pf0.w, pf1.x, pf1.y, pf1.z, pf1.w};
-    unsigned char* dst = smem + (pkv ? TLayout::V : TLayout::K) + pgrp * kTok * 128;
-#pragma unroll
-    for (int ch = 0; ch < 8; ++ch) {
-      uint4 o;
-      o.x = nib64h<0>(w[ch]);
-      o.y = nib64h<1>(w[ch]);
-      o.z = nib64h<2>(w[ch]);
-      o.w = nib64h<3>(w[ch]);
-      if (pkv) {
-        o.x = center8(o.x);
-        o.y = center8(o.y);
-        o.z = center8(o.z);
-        o.w = center8(o.w);
-      }
-      *reinterpret_cast<uint4*>(dst + sw128(ptok, ch)) = o;
-    }
-    if (!pkv) {
-      float s0, s1, b0, b1;
-      if (p.sb_f32) {
-        s0 = __uint_as_float(pfr[0]);
-        s1 = __uint_as_float(pfr[1]);
-        b0 = __uint_as_float(pfr[2]);
-        b1 = __uint_as_float(pfr[3]);
-      } else {
-        const float2 sf = __half22float2(*reinterpret_cast<const __half2*>(&pfr[0]));
-        const float2 bf = __half22float2(*reinterpret_cast<const __half2*>(&pfr[1]));
-        s0 = sf.x;
-        s1 = sf.y;
-        b0 = bf.x;
-        b1 = bf.y;
-      }
-      const bool tv = t0 + ptok < t_end;
-      const float qs = p.qscale;
-      if (!pgrp) {
-        s_ts[ptok] = tv ? make_float4(64.0f * s0 * qs, 64.0f * s1 * qs, (b0 - 64.0f * s0) * qs,
-                                      (b1 - 64.0f * s1) * qs)
-                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      } else {
-        s_tv[ptok] = tv ? make_float4(s0, s1, fmaf(8.0f, s0, b0), fmaf(8.0f, s1, b1))
-                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      }
-    }
-  };
-  if (t_begin < t_end) prefetch(t_begin);
-
-  for (int t0 = t_begin; t0 < t_end; t0 += kTok) {
-    // ---- 1. K codes and the per-token terms -> smem (the previous S MMA
-    // finished before its softmax, the previous softmax before its O MMA)
-    if (!pkv) unpack(t0);
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-
-    // ---- 2. S'_g = Q_g (1 + C_g/64)^T ------------------------------------------
-    if (tid == 0) {
+  // ======================= MMA warp (one thread issues) =========================
+  // S(i) is issued before PV(i-1), so the tensor pipe works on the next tile's
+  // scores while the softmax warps still finish the current one.
+  if (warp == kMmaWarp) {
+    if (lane == 0) {
       constexpr uint32_t idS = idesc_f16(false);
-#pragma unroll
-      for (int g = 0; g < 2; ++g)
-#pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint64_t a = umma_desc(sbase + TLayout::Q + g * kRows * 128 + ks * 32, 16);
-          const uint64_t b = umma_desc(sbase + TLayout::K + g * kTok * 128 + ks * 32, 16);
-          umma_f16(g ? t_s1 : t_s0, a, b, idS, ks > 0 ? 1u : 0u);
-          if (kQLo) {
-            const uint64_t al = umma_desc(sbase + TLayout::QL + g * kRows * 128 + ks * 32, 16);
-            umma_f16(g ? t_s1 : t_s0, al, b, idS, 1u);
-          }
-        }
-      umma_commit(bar_s);
-    }
-    // ---- 3. the previous O MMA (reads V and P) done -> V codes -> smem; next
-    // tile's codes -> registers (V's per-token terms went in with step 1)
-    if (o_init) {
-      mbar_wait_bounded(bar_o, ph_o, p.err, kWaitBudget);
-      tc_fence_after();
-      ph_o ^= 1u;
-    }
-    if (pkv) unpack(t0);
-    if (t0 + kTok < t_end) prefetch(t0 + kTok);
-    mbar_wait_bounded(bar_s, ph_s, p.err, kWaitBudget);
-    tc_fence_after();
-    ph_s ^= 1u;
-
-    // ---- 4. scores of this thread's 32 tokens, online softmax, P', bias terms
-    float sc[32];
-    tmem_ld32(t_s0 + lane_off + 32 * hf, sc);
-#pragma unroll
-    for (int hh = 0; hh < 2; ++hh) {
-      float a1[16];
-      tmem_ld16(t_s1 + lane_off + 32 * hf + 16 * hh, a1);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const float4 a = s_ts[32 * hf + 16 * hh + j];
-        float& x = sc[16 * hh + j];
-        x = fmaf(a.x, x, fmaf(a.y, a1[j], fmaf(a.z, qsum0, a.w * qsum1)));
-      }
-    }
-    const bool full = t0 + kTok <= t_end && (!p.causal || t0 + kTok - 1 <= qpos_lo) &&
-                      (p.window <= 0 || qpos_hi - t0 < p.window);
-    if (!full) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int t = t0 + 32 * hf + j;
-        const bool vis = t < t_end && t <= qpos && (p.window <= 0 || qpos - t < p.window);
-        sc[j] = vis ? sc[j] : -INFINITY;
-      }
-    }
-    float mx = sc[0];
-#pragma unroll
-    for (int j = 1; j < 32; ++j) mx = fmaxf(mx, sc[j]);
-    s_mx[tid] = mx;
-    pair_sync();
-    mx = fmaxf(s_mx[rl], s_mx[rl + kRows]);
-    // move the running max only when it grows by more than 8 (2^8 headroom);
-    // both threads of the row take the same decision
-    bool rescale = false;
-    float alpha = 1.0f;
-    if (mx > m_run + 8.0f || (m_run == -INFINITY && mx > -INFINITY)) {
-      const float m_new = fmaxf(mx, m_run);
-      alpha = (m_run == -INFINITY) ? 0.0f : fast_exp2(m_run - m_new);
-      rescale = o_init && m_run != -INFINITY;
-      m_run = m_new;
-      l_run *= alpha;
-      corr0 *= alpha;
-      corr1 *= alpha;
-    }
-    const float mref = m_run == -INFINITY ? 0.0f : m_run;  // masked scores give exp2(-inf) = 0
-    float lsum = 0.0f;
-    unsigned char* prow = smem + TLayout::P;
-#pragma unroll
-    for (int cc = 0; cc < 4; ++cc) {
-      const int ch = 4 * hf + cc;
-      uint32_t w0[4], w1[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int j = 8 * cc + 2 * e;
-        const float pa = fast_exp2(sc[j] - mref), pb = fast_exp2(sc[j + 1] - mref);
-        lsum += pa + pb;
-        const float4 va = s_tv[32 * hf + j], vb = s_tv[32 * hf + j + 1];
-        const __half2 h0 = __floats2half2_rn(pa * va.x, pb * vb.x);
-        const __half2 h1 = __floats2half2_rn(pa * va.y, pb * vb.y);
-        corr0 = fmaf(pa, va.z, fmaf(pb, vb.z, corr0));
-        corr1 = fmaf(pa, va.w, fmaf(pb, vb.w, corr1));
-        w0[e] = *reinterpret_cast<const uint32_t*>(&h0);
-        w1[e] = *reinterpret_cast<const uint32_t*>(&h1);
-      }
-      *reinterpret_cast<uint4*>(prow + sw128(rl, ch)) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
-      *reinterpret_cast<uint4*>(prow + kRows * 128 + sw128(rl, ch)) =
-          make_uint4(w1[0], w1[1], w1[2], w1[3]);
-    }
-    l_run += lsum;
-    // O_hf *= alpha for the rows whose max moved; tcgen05.ld/st are warp-wide
-    // (.sync.aligned), so the whole warp takes the branch with alpha = 1 on
-    // the other rows
-    if (__any_sync(0xffffffffu, rescale)) {
-      const float a = rescale ? alpha : 1.0f;
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        float o[32];
-        const uint32_t ta = t_o0 + lane_off + 64 * hf + 32 * c;
-        tmem_ld32(ta, o);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] *= a;
-        tmem_st32(ta, o);
-      }
-    }
-    fence_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-
-    // ---- 5. O'_g += P'_g (C_g - 8)/64 -------------------------------------------
-    if (tid == 0) {
       constexpr uint32_t idO = idesc_f16(true);
+      auto issue_pv = [&](int i) {
+        const int b = i & 1;
+        const uint32_t use = static_cast<uint32_t>(i >> 1);
+        mbar_wait_bounded(&v_full[b], use & 1u, p.err, kWaitBudget);
+        mbar_wait_bounded(&p_full[b], use & 1u, p.err, kWaitBudget);
+        tc_fence_after();
 #pragma unroll
-      for (int g = 0; g < 2; ++g)
+        for (int g = 0; g < 2; ++g)
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          const uint64_t a = umma_desc(sbase + TLayout::P + g * kRows * 128 + ks * 32, 16);
-          const uint64_t b = umma_desc(sbase + TLayout::V + g * kTok * 128 + ks * 16 * 128, 16);
-          umma_f16(t_o0 + 64 * g, a, b, idO, (o_init || ks > 0) ? 1u : 0u);
-        }
-      umma_commit(bar_o);
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t a = umma_desc(sbase + TLayout::P + b * TLayout::PB + g * kRows * 128 + ks * 32, 16);
+            const uint64_t v = umma_desc(sbase + TLayout::V + b * TLayout::KVB + g * kTok * 128 + ks * 16 * 128, 16);
+            umma_f16(t_o + 64 * g, a, v, idO, (i > 0 || ks > 0) ? 1u : 0u);
+          }
+        umma_commit(&pv_done[b]);
+      };
+      for (int i = 0; i < n_tiles; ++i) {
+        const int b = i & 1;
+        const uint32_t use = static_cast<uint32_t>(i >> 1);
+        mbar_wait_bounded(&k_full[b], use & 1u, p.err, kWaitBudget);
+        if (i >= 2) mbar_wait_bounded(&s_free[b], (use - 1) & 1u, p.err, kWaitBudget);
+        tc_fence_after();
+        const uint32_t t_s = tmem + 128 * b;
+#pragma unroll
+        for (int g = 0; g < 2; ++g)
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t kd = umma_desc(sbase + TLayout::K + b * TLayout::KVB + g * kTok * 128 + ks * 32, 16);
+            const uint64_t a = umma_desc(sbase + TLayout::Q + g * kRows * 128 + ks * 32, 16);
+            umma_f16(t_s + 64 * g, a, kd, idS, ks > 0 ? 1u : 0u);
+            if (kQLo) {
+              const uint64_t al = umma_desc(sbase + TLayout::QL + g * kRows * 128 + ks * 32, 16);
+              umma_f16(t_s + 64 * g, al, kd, idS, 1u);
+            }
+          }
+        umma_commit(&s_full[b]);
+        if (i >= 1) issue_pv(i - 1);
+      }
+      if (n_tiles > 0) issue_pv(n_tiles - 1);
     }
-    o_init = true;
-  }
-  if (o_init) {
-    mbar_wait_bounded(bar_o, ph_o, p.err, kWaitBudget);
-    tc_fence_after();
   }
 
-  // ---- epilogue: the row's two halves add their l and bias terms; thread hf
-  // writes scale group hf: out = (64 O'_hf + corr_hf) / l
-  __syncthreads();  // s_mx reads of the last tile are done
-  // [3][kThreads] sums in the P region (free after the last O MMA)
-  float* s_red = reinterpret_cast<float*>(smem + TLayout::P);
-  s_red[tid] = l_run;
-  s_red[kThreads + tid] = corr0;
-  s_red[2 * kThreads + tid] = corr1;
-  pair_sync();
-  const int pt = tid ^ kRows;  // partner thread
-  const float l_tot = l_run + s_red[pt];
-  const float corr = (hf ? corr1 : corr0) + s_red[(hf ? 2 : 1) * kThreads + pt];
-  const bool direct = p.splits == 1;
-  const long long unit = static_cast<long long>(kv) * gridDim.y + mt;
-  // split partials, column-major so a warp's 32 rows are one 128 B store:
-  // ws[unit][split][d or m or l][row]
-  float* wsr = p.ws + (unit * p.splits + split) * (kD + 2) * kRows + rl;
-  const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
-  const long long ob = (static_cast<long long>(qi) * p.H + h) * kD;
-  const bool ovec = (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0;
-#pragma unroll 1
-  for (int c = 0; c < 2; ++c) {
-    float o[32];
-    if (o_init) {
-      tmem_ld32(t_o0 + lane_off + 64 * hf + 32 * c, o);
-    } else {
+  // ======================= unpack warps =========================================
+  // Thread = token ptok: 64 B of K codes and 64 B of V codes per tile (both
+  // scale groups), the next tile's held in registers while this one is
+  // unpacked; K as exact fp16 1 + c/64 (K-major), V as exact fp16 (c - 8)/64
+  // (MN-major), both 128B-swizzled; the token's score and value terms.
+  if (warp >= kUnpackBase && warp < kUnpackBase + kUnpackWarps) {
+    const int ptok = tid - kUnpackBase * 32;
+    uint4 kf[4], vf[4];
+    uint32_t sr[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};  // ks, kb, vs, vb (raw: 1 or 2 words each)
+    int tcur = t_end;  // the tile held in registers
+    auto prefetch = [&](int t0) {
+      const int t = t0 + ptok;
+      const long long rowi = tok_base + (t < t_end ? t : t0);
+      const uint4* kp = reinterpret_cast<const uint4*>(p.kq + rowi * (kD / 8));
+      const uint4* vp = reinterpret_cast<const uint4*>(p.vq + rowi * (kD / 8));
 #pragma unroll
-      for (int i = 0; i < 32; ++i) o[i] = 0.0f;
-    }
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int d0 = 64 * hf + 32 * c + 8 * k;  // first dim of this 8-column chunk
-      float v[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) v[perm8(e)] = fmaf(64.0f, o[8 * k + e], corr);
-      if (direct) {
-        if (row_ok) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) v[e] *= inv;
-          store8(p.out, ob + d0, p.out_dtype, ovec, v);
+      for (int k = 0; k < 4; ++k) {
+        kf[k] = kp[k];
+        vf[k] = vp[k];
+      }
+      auto load_pair = [&](const void* src, int k) {
+        if (p.sb_f32) {
+          const uint2 a = reinterpret_cast<const uint2*>(src)[rowi];
+          sr[2 * k] = a.x;
+          sr[2 * k + 1] = a.y;
+        } else {
+          sr[2 * k] = reinterpret_cast<const uint32_t*>(src)[rowi];
         }
+      };
+      load_pair(p.ks, 0);
+      load_pair(p.kb, 1);
+      load_pair(p.vs, 2);
+      load_pair(p.vb, 3);
+      tcur = t0;
+    };
+    // the scale-group pair of a raw f16x2 or f32 pair
+    auto pair = [&](int k) {
+      if (p.sb_f32) return make_float2(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1]));
+      return __half22float2(*reinterpret_cast<const __half2*>(&sr[2 * k]));
+    };
+    auto unpack_codes = [&](uint4 c0, uint4 c1, unsigned char* dst, bool centre) {
+      const uint32_t w[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        uint4 o;
+        o.x = nib64h<0>(w[ch]);
+        o.y = nib64h<1>(w[ch]);
+        o.z = nib64h<2>(w[ch]);
+        o.w = nib64h<3>(w[ch]);
+        if (centre) {
+          o.x = center8(o.x);
+          o.y = center8(o.y);
+          o.z = center8(o.z);
+          o.w = center8(o.w);
+        }
+        *reinterpret_cast<uint4*>(dst + sw128(ptok, ch)) = o;
+      }
+    };
+    if (n_tiles > 0) prefetch(t_begin);
+    for (int i = 0; i < n_tiles; ++i) {
+      const int b = i & 1;
+      const uint32_t use = static_cast<uint32_t>(i >> 1);
+      const int t0 = tcur;
+      unsigned char* stage = smem + b * TLayout::KVB;
+      const bool tv = t0 + ptok < t_end;
+      const float2 ks = pair(0), kb = pair(1), vs = pair(2), vb = pair(3);
+      // K(i) and the score terms: the stage is free once softmax(i-2) is done
+      if (i >= 2) mbar_wait_bounded(&p_full[b], (use - 1) & 1u, p.err, kWaitBudget);
+#pragma unroll
+      for (int g = 0; g < 2; ++g)
+        unpack_codes(kf[2 * g], kf[2 * g + 1], stage + TLayout::K + g * kTok * 128, false);
+      const float qs = p.qscale;
+      float4* ts = reinterpret_cast<float4*>(smem + TLayout::TS + b * kTok * 16);
+      ts[ptok] = tv ? make_float4(64.0f * ks.x * qs, 64.0f * ks.y * qs, (kb.x - 64.0f * ks.x) * qs,
+                                  (kb.y - 64.0f * ks.y) * qs)
+                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&k_full[b]);
+      // V(i) and the value terms: free once PV(i-2) is done
+      if (i >= 2) mbar_wait_bounded(&pv_done[b], (use - 1) & 1u, p.err, kWaitBudget);
+#pragma unroll
+      for (int g = 0; g < 2; ++g)
+        unpack_codes(vf[2 * g], vf[2 * g + 1], stage + TLayout::V + g * kTok * 128, true);
+      float4* tvv = reinterpret_cast<float4*>(smem + TLayout::TV + b * kTok * 16);
+      tvv[ptok] = tv ? make_float4(vs.x, vs.y, fmaf(8.0f, vs.x, vb.x), fmaf(8.0f, vs.y, vb.y))
+                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      if (i + 1 < n_tiles) prefetch(t0 + kTok);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&v_full[b]);
+    }
+  }
+
+  // ======================= softmax warps ========================================
+  if (is_softmax) {
+    const float qsum0 = s_mx[rl], qsum1 = s_mx[rl + kRows];
+    const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    // the two threads of a row meet on named barrier 1 + warp % 4 (64 threads)
+    auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory"); };
+    float m_run = -INFINITY, l_run = 0.0f, corr0 = 0.0f, corr1 = 0.0f;
+    pair_sync();  // both halves have read the q sums before s_mx is reused
+    for (int i = 0; i < n_tiles; ++i) {
+      const int b = i & 1;
+      const uint32_t use = static_cast<uint32_t>(i >> 1);
+      const int t0 = t_begin + i * kTok;
+      const float4* s_ts = reinterpret_cast<const float4*>(smem + TLayout::TS + b * kTok * 16);
+      const float4* s_tv = reinterpret_cast<const float4*>(smem + TLayout::TV + b * kTok * 16);
+      mbar_wait_bounded(&s_full[b], use & 1u, p.err, kWaitBudget);
+      mbar_wait_bounded(&k_full[b], use & 1u, p.err, kWaitBudget);  // score terms (done: S(i) needed them)
+      tc_fence_after();
+      // scores of this thread's 32 tokens (both scale groups' S' halves)
+      // scores relative to the running max (the previous tile's; 0 before
+      // any): sc = score - mref, the subtraction folded into the FMA chain
+      const float mref = m_run == -INFINITY ? 0.0f : m_run;
+      float sc[32];
+      {
+        uint32_t r0[32], r1[32];
+        tmem_ld32_raw(tmem + 128 * b + lane_off + 32 * hf, r0);
+        tmem_ld32_raw(tmem + 128 * b + 64 + lane_off + 32 * hf, r1);
+        tmem_wait_ld();
+        reg_fence(r0);
+        reg_fence(r1);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[b]);  // S[b] may take tile i + 2
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float4 a = lds4(&s_ts[32 * hf + j]);
+          sc[j] = fmaf(a.x, __uint_as_float(r0[j]),
+                       fmaf(a.y, __uint_as_float(r1[j]), fmaf(a.z, qsum0, fmaf(a.w, qsum1, -mref))));
+        }
+      }
+      const bool full = t0 + kTok <= t_end && (!p.causal || t0 + kTok - 1 <= qpos_lo) &&
+                        (p.window <= 0 || qpos_hi - t0 < p.window);
+      if (!full) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int t = t0 + 32 * hf + j;
+          const bool vis = t < t_end && t <= qpos && (p.window <= 0 || qpos - t < p.window);
+          sc[j] = vis ? sc[j] : -INFINITY;
+        }
+      }
+      float mx = sc[0];
+#pragma unroll
+      for (int j = 1; j < 32; ++j) mx = fmaxf(mx, sc[j]);
+      float* mxb = s_mx + b * kSoftmaxThreads;  // by tile parity: a partner may lag one tile
+      mxb[xs] = mx;
+      pair_sync();
+      mx = fmaxf(mxb[rl], mxb[rl + kRows]);
+      // move the running max only when it grows by more than 8 (2^8 headroom;
+      // mx is relative to mref); both threads of the row take the same
+      // decision, and then shift their scores to the new max
+      bool rescale = false;
+      float alpha = 1.0f;
+      if (mx > 8.0f || (m_run == -INFINITY && mx > -INFINITY)) {
+        const float m_new = fmaxf(mx + mref, m_run);
+        alpha = (m_run == -INFINITY) ? 0.0f : fast_exp2(m_run - m_new);
+        rescale = i > 0 && m_run != -INFINITY;
+        const float delta = m_new - mref;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sc[j] -= delta;
+        m_run = m_new;
+        l_run *= alpha;
+        corr0 *= alpha;
+        corr1 *= alpha;
+      }
+      // O_hf *= alpha once PV(i-1) is done; tcgen05.ld/st are warp-wide, so the
+      // whole warp takes the branch with alpha = 1 on the other rows
+      if (__any_sync(0xffffffffu, rescale)) {
+        const int pb = (i - 1) & 1;
+        mbar_wait_bounded(&pv_done[pb], static_cast<uint32_t>((i - 1) >> 1) & 1u, p.err, kWaitBudget);
+        tc_fence_after();
+        const float a = rescale ? alpha : 1.0f;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float o[32];
+          const uint32_t ta = t_o + lane_off + 64 * hf + 32 * c;
+          tmem_ld32(ta, o);
+#pragma unroll
+          for (int k = 0; k < 32; ++k) o[k] *= a;
+          tmem_st32(ta, o);
+        }
+      }
+      // P[b] is free once PV(i-2) is done; the value terms of tile i are in
+      if (i >= 2) mbar_wait_bounded(&pv_done[b], (use - 1) & 1u, p.err, kWaitBudget);
+      mbar_wait_bounded(&v_full[b], use & 1u, p.err, kWaitBudget);
+      float lsum = 0.0f;  // masked scores give exp2(-inf) = 0
+      unsigned char* prow = smem + TLayout::P + b * TLayout::PB;
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        const int ch = 4 * hf + cc;
+        uint32_t w0[4], w1[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int j = 8 * cc + 2 * e;
+          const float pa = fast_exp2(sc[j]), pb2 = fast_exp2(sc[j + 1]);
+          lsum += pa + pb2;
+          const float4 va = lds4(&s_tv[32 * hf + j]), vb = lds4(&s_tv[32 * hf + j + 1]);
+          const __half2 h0 = __floats2half2_rn(pa * va.x, pb2 * vb.x);
+          const __half2 h1 = __floats2half2_rn(pa * va.y, pb2 * vb.y);
+          corr0 = fmaf(pa, va.z, fmaf(pb2, vb.z, corr0));
+          corr1 = fmaf(pa, va.w, fmaf(pb2, vb.w, corr1));
+          w0[e] = *reinterpret_cast<const uint32_t*>(&h0);
+          w1[e] = *reinterpret_cast<const uint32_t*>(&h1);
+        }
+        *reinterpret_cast<uint4*>(prow + sw128(rl, ch)) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+        *reinterpret_cast<uint4*>(prow + kRows * 128 + sw128(rl, ch)) =
+            make_uint4(w1[0], w1[1], w1[2], w1[3]);
+      }
+      l_run += lsum;
+      fence_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[b]);
+    }
+
+    // ---- epilogue: the row's two halves add their l and bias terms; thread hf
+    // writes scale group hf: out = (64 O'_hf + corr_hf) / l
+    const bool o_init = n_tiles > 0;
+    if (o_init) {
+      const int lb = (n_tiles - 1) & 1;
+      mbar_wait_bounded(&pv_done[lb], static_cast<uint32_t>((n_tiles - 1) >> 1) & 1u, p.err,
+                        kWaitBudget);
+      tc_fence_after();
+    }
+    float* s_red = reinterpret_cast<float*>(smem + TLayout::RED);  // [3][256]
+    s_red[xs] = l_run;
+    s_red[kSoftmaxThreads + xs] = corr0;
+    s_red[2 * kSoftmaxThreads + xs] = corr1;
+    pair_sync();
+    const int pt = xs ^ kRows;  // partner's slot
+    const float l_tot = l_run + s_red[pt];
+    const float corr = (hf ? corr1 : corr0) + s_red[(hf ? 2 : 1) * kSoftmaxThreads + pt];
+    const bool direct = p.splits == 1;
+    const long long unit = static_cast<long long>(kv) * gridDim.y + mt;
+    // split partials, column-major so a warp's 32 rows are one 128 B store:
+    // ws[unit][split][d or m or l][row]
+    float* wsr = p.ws + (unit * p.splits + split) * (kD + 2) * kRows + rl;
+    const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
+    const long long ob = (static_cast<long long>(qi) * p.H + h) * kD;
+    const bool ovec = (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0;
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      float o[32];
+      if (o_init) {
+        tmem_ld32(t_o + lane_off + 64 * hf + 32 * c, o);
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) __stcg(wsr + (d0 + e) * kRows, v[e]);
+        for (int k = 0; k < 32; ++k) o[k] = 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int d0 = 64 * hf + 32 * c + 8 * k;  // first dim of this 8-column chunk
+        float v[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[perm8(e)] = fmaf(64.0f, o[8 * k + e], corr);
+        if (direct) {
+          if (row_ok) {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) v[e] *= inv;
+            store8(p.out, ob + d0, p.out_dtype, ovec, v);
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) __stcg(wsr + (d0 + e) * kRows, v[e]);
+        }
       }
     }
-  }
-  if (!direct && hf == 0) {
-    __stcg(wsr + kD * kRows, l_tot > 0.0f ? m_run : -INFINITY);
-    __stcg(wsr + (kD + 1) * kRows, l_tot);
+    if (!direct && hf == 0) {
+      __stcg(wsr + kD * kRows, l_tot > 0.0f ? m_run : -INFINITY);
+      __stcg(wsr + (kD + 1) * kRows, l_tot);
+    }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols)
                  : "memory");
@@ -698,7 +790,7 @@ __global__ void __launch_bounds__(256) attn_tc_merge_kernel(const TCParams p, in
 int tc_splits(int units, int tiles) {
   int dev = 0;
   cudaGetDevice(&dev);
-  const int target = device_sm_count(dev) * 2;
+  const int target = device_sm_count(dev);  // one CTA per SM (512 TMEM columns, 170 KB smem)
   int s = target / (units > 0 ? units : 1);
   if (s < 1) s = 1;
   if (s > tiles) s = tiles > 0 ? tiles : 1;

@@ -84,6 +84,11 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
+// Plain arrival (release at CTA scope) on a shared-memory mbarrier.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // try_wait blocks for a hardware-chosen interval while the phase is
 // incomplete (no suspend-time hint: the default interval measured faster
 // here than a long hint), so a waiting warp does not spin on the issue slots.

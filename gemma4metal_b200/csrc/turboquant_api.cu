@@ -251,6 +251,70 @@ array KVCache::sdpa(const array& queries, int gqa_factor, float scale, int slidi
   return flat ? out.reshape({queries.shape(0), head_dim_}) : out;
 }
 
+array KVCache::decode_step(const array& queries, const array& k_new, const array& v_new,
+                           int gqa_factor, float scale, int sliding_window, cudaStream_t s) {
+  const char* where = "KVCache::decode_step";
+  const bool flat = queries.ndim() == 2;
+  if (flat && batch_ != 1) raise(where, "(H, D) queries need batch 1");
+  if (length_ >= capacity_) raise(where, "cache is full");
+  if (k_new.size() != static_cast<size_t>(batch_) * num_kv_heads_ * head_dim_ ||
+      v_new.size() != k_new.size() || k_new.shape(-1) != head_dim_)
+    raise(where, "k_new/v_new must be (B, Hkv, D) or (B, Hkv, 1, D)");
+  const int H = num_kv_heads_ * gqa_factor;
+  array out = flat ? array({1, H, head_dim_}, queries.dtype(), s) : array(queries.shape(), queries.dtype(), s);
+  const int n = length_ + 1;
+  const size_t ws_bytes = tq_sdpa_int4_workspace_size(batch_, H, num_kv_heads_, head_dim_, n, sliding_window);
+  array ws_arr = ws_bytes ? workspace(ws_bytes, s) : array();
+  check(tq_sdpa_int4_append(queries.data(), to_c(queries.dtype(), where), k_new.data(), v_new.data(),
+                            to_c(k_new.dtype(), where), static_cast<uint32_t*>(k_quant.data()),
+                            k_scales.data(), k_biases.data(), static_cast<uint32_t*>(v_quant.data()),
+                            v_scales.data(), v_biases.data(), to_c(k_scales.dtype(), where),
+                            gqa_factor, scale, sliding_window, batch_, num_kv_heads_, head_dim_, n,
+                            capacity_, nullptr, out.data(), to_c(queries.dtype(), where),
+                            ws_bytes ? ws_arr.data() : nullptr, ws_bytes ? ws_arr.nbytes() : 0, s),
+        where);
+  length_ = n;
+  return flat ? out.reshape({queries.shape(0), head_dim_}) : out;
+}
+
+namespace {
+array multi(const KVCache& c, const array& queries, int n_tokens, int gqa, float scale, int window,
+            bool causal, int pos0, Dtype out_dtype, cudaStream_t s, const char* where) {
+  if (queries.ndim() != 3) raise(where, "queries must be (n, H, D)");
+  if (c.k_quant.shape(0) != 1) raise(where, "needs a batch-1 cache");
+  const int nq = queries.shape(0), H = queries.shape(1), D = queries.shape(2);
+  const int hkv = c.k_quant.shape(1);
+  if (H != hkv * gqa || D != c.k_quant.shape(3) * 8) raise(where, "query shape does not match the cache");
+  array out({nq, H, D}, out_dtype, s);
+  const size_t ws_bytes = tq_sdpa_int4_multi_workspace_size(nq, H, hkv, D, n_tokens);
+  array ws_arr = ws_bytes ? workspace(ws_bytes, s) : array();
+  check(tq_sdpa_int4_multi(queries.data(), to_c(queries.dtype(), where),
+                           static_cast<const uint32_t*>(c.k_quant.data()), c.k_scales.data(),
+                           c.k_biases.data(), static_cast<const uint32_t*>(c.v_quant.data()),
+                           c.v_scales.data(), c.v_biases.data(), to_c(c.k_scales.dtype(), where), gqa,
+                           scale, window, hkv, D, nq, n_tokens, c.capacity(), causal ? 1 : 0, pos0,
+                           out.data(), to_c(out_dtype, where), ws_bytes ? ws_arr.data() : nullptr,
+                           ws_bytes ? ws_arr.nbytes() : 0, s),
+        where);
+  return out;
+}
+}  // namespace
+
+array KVCache::prefill_chunk(const array& queries, const array& k_chunk, const array& v_chunk,
+                             int gqa_factor, float scale, int sliding_window, Dtype out_dtype,
+                             cudaStream_t s) {
+  const int pos0 = length_;
+  append(k_chunk, v_chunk, s);
+  return multi(*this, queries, length_, gqa_factor, scale, sliding_window, true, pos0, out_dtype, s,
+               "KVCache::prefill_chunk");
+}
+
+array KVCache::sdpa_multi(const array& queries, int gqa_factor, float scale, int sliding_window,
+                          Dtype out_dtype, cudaStream_t s) {
+  return multi(*this, queries, length_, gqa_factor, scale, sliding_window, false, 0, out_dtype, s,
+               "KVCache::sdpa_multi");
+}
+
 // ---- sequence split ---------------------------------------------------------
 
 array sdpa_int4_partial(const array& queries, const KVCache& shard, int n_local, int token_offset,

@@ -5,32 +5,33 @@
 // a CPU-built mask (engine/gemma4_multilayer.cpp:307-308,347-367,441-464).
 //
 // CTA = 128 query rows of one KV head (row = (query, GQA head) pair; TMEM lane
-// = row), 8 warps, 2 CTAs per SM; the two threads of a row (tid, tid + 128)
-// take the two 32-token halves of each 64-token tile. Per tile of the cache:
-//   1. threads 0..127 unpack the K codes into shared memory as exact fp16
-//      values 1 + c/64 in the UMMA canonical K-major 128B-swizzled layout, one
-//      8 KB region per 64-dim scale group, and the per-token score and value
-//      terms;
-//   2. thread 0 issues tcgen05.mma S'_g = Q_g (1 + C_g/64)^T per scale group g
-//      (fp16 x fp16 -> fp32 in TMEM; exact products), commit -> mbarrier;
-//   3. threads 128..255, once the previous tile's O MMA is done, unpack the V
-//      codes as exact fp16 (c - 8)/64 (MN-major B operand of O = P V) while
-//      the S MMA runs; every thread then loads the next tile's codes into
-//      registers;
-//   4. each thread reads its half row of S'_0, S'_1 (tcgen05.ld) and forms
-//      score = 64 s_0 S'_0 + 64 s_1 S'_1 + (b_0 - 64 s_0) sum q_0 + (b_1 - 64 s_1) sum q_1
-//      (the int4 scale/bias factored out of the dot product, as
-//      lib/turboquant.metal:803 does), masks (causal / window / length) only
-//      on tiles that cross a boundary, exchanges the half-row max with its
-//      partner, and writes P'_g = fp16(p s_g(token)) (K-major A operand) while
-//      accumulating the bias term sum p (b_g + 8 s_g);
-//   5. thread 0 issues O'_g += P'_g (c - 8)/64 per group into TMEM.
+// = row), one CTA per SM, warp-specialized, tiles of 64 tokens:
+//   * unpack warps (2, one token per thread) turn the int4 codes into exact
+//     fp16 in shared memory: K as 1 + c/64 (UMMA canonical K-major, 128B
+//     swizzle, one 8 KB region per 64-dim scale group), V as (c - 8)/64
+//     (MN-major); per-token score terms and value terms go beside them. K and
+//     V have two stages each, with separate lifetimes (K(i) is free once the
+//     softmax of tile i is done, V(i) once PV(i) is), and the next tile's
+//     codes wait in registers.
+//   * the MMA warp (one thread) issues S'_g = Q_g K_g'^T for tile i into one of
+//     two TMEM S buffers, then PV for tile i-1 into the TMEM O accumulator,
+//     committing each group to an mbarrier -- the tensor pipe works on the
+//     next tile's scores while the softmax finishes the current one.
+//   * softmax warps (8, two threads per row on the two 32-token halves of a
+//     tile) read S' (tcgen05.ld) and form
+//       score = 64 s_0 S'_0 + 64 s_1 S'_1 + (b_0 - 64 s_0) sum q_0 + (b_1 - 64 s_1) sum q_1 - m
+//     (the int4 scale/bias factored out of the dot product, as
+//     lib/turboquant.metal:803 does; the running max m folded into the FMA
+//     chain), mask only tiles that cross a boundary, exchange the half-row
+//     max, and write P'_g = fp16(p s_g(token)) (K-major A operand) while
+//     accumulating the bias term sum p (b_g + 8 s_g) in fp32.
 // out_g = (64 O'_g + bias term_g) / l: the weights' fp16 rounding error is
 // multiplied by c - 8 (|c - 8| <= 8), not by the code's full value. The
-// running max is only moved (and O rescaled in TMEM) when a row's max grows
-// by more than 8 (log2 units), so most tiles skip the rescale. The 8-element
-// dim order inside each code word follows the unpack (d = 0,4,1,5,2,6,3,7),
-// applied to Q as well and undone when O is written.
+// running max moves (and O is rescaled in TMEM) only when a row's max grows by
+// more than 8 in log2 units. The 8-element dim order inside each code word
+// follows the unpack (d = 0,4,1,5,2,6,3,7), applied to Q as well and undone
+// when O is written. Splits over the cache (when row tiles alone leave SMs
+// idle) write column-major partials merged by attn_tc_merge_kernel.
 #include <cuda.h>
 
 #include <cstdint>

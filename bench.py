@@ -53,6 +53,9 @@ def parse():
     ap.add_argument("--context", type=int, default=32768)
     ap.add_argument("--window", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="cfg4 with N>1: partial states exchanged and merged by one kernel over "
+                         "NVLink peer memory (peer) or NCCL all-gather + merge kernel (nccl)")
     ap.add_argument("--split-step", action="store_true",
                     help="cfg1: run the step as two launches (quantize_append, then sdpa_int4) "
                          "instead of the fused sdpa_int4_append")
@@ -328,7 +331,8 @@ def run_cfg4(args, rank: int, world: int, local_rank: int):
     """Config 4: one decode step of a 262144-token global-attention layer
     (H=32, Hkv=8, D=256) whose int4 cache is split by sequence over the GPUs.
     Step = append the new token on the last rank + partial decode on every
-    rank + NCCL all-gather of the fp32 (o, m, l) states + LSE merge, captured
+    rank + exchange of the fp32 (o, m, l) states + LSE merge (one peer-memory
+    kernel, or NCCL all-gather + merge kernel with --exchange nccl), captured
     in CUDA graphs. Layers rotate so every step streams its shard from HBM."""
     import math
 
@@ -373,6 +377,7 @@ def run_cfg4(args, rank: int, world: int, local_rank: int):
     n_local = layers[0]["sc"].n_local
     last = rank == world - 1
     ws = tq.workspace(dev, tq.sdpa_int4_workspace_size(1, C4_H, C4_HKV, C4_D, n_local + 1, 0))
+    peer = seqsplit.PeerExchange(1, C4_H, C4_D, device=dev) if world > 1 and args.exchange == "peer" else None
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(device=dev)
 
@@ -383,6 +388,9 @@ def run_cfg4(args, rank: int, world: int, local_rank: int):
         nl = n_local + (1 if last else 0)
         tq.sdpa_int4_partial(Lr["q"], *sc.cache.tensors(), C4_H // C4_HKV, 1.0, 0, n_local=nl,
                              token_offset=sc.t0, n_total=C4_N, part_out=Lr["part"], ws=ws, s=stream)
+        if peer is not None:
+            peer.merge(Lr["part"], out=Lr["out"], s=stream)
+            return
         if world > 1:
             dist.all_gather_into_tensor(Lr["parts"], Lr["part"])
         else:
@@ -440,6 +448,8 @@ def run_cfg4(args, rank: int, world: int, local_rank: int):
     assert tq.device_error() == 0, "a kernel reported a device error"
     del graph
     torch.cuda.synchronize()
+    if peer is not None:
+        peer.close()
     value = steps / (t_ms / 1000.0)
     total_bytes = C4_N * C4_HKV * 2 * (C4_D // 2 + 4 * (C4_D // 64))
     line = {"metric": "int4-KV decode-attention tokens/s", "value": value, "unit": "tokens/s",
@@ -448,7 +458,9 @@ def run_cfg4(args, rank: int, world: int, local_rank: int):
             "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded torch.randn, RMS-normalised Q/K as task configs[0])",
             "config": {"workload": "cfg4 decode step: 262144-token global layer split by sequence, "
-                                   "append + partial decode + NCCL all-gather + LSE merge",
+                                   "append + partial decode + " +
+                                   ("peer-memory exchange + merge (one kernel)" if peer is not None
+                                    else "NCCL all-gather + LSE merge"),
                        "batch": 1, "heads": C4_H, "kv_heads": C4_HKV, "head_dim": C4_D,
                        "context": C4_N, "layers_rotated": layers_n,
                        "l2": f"inputs larger than L2: {layers_n} rotating shards of {shard_bytes / 1e6:.0f} MB",

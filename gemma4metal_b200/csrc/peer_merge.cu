@@ -1,0 +1,262 @@
+// Sequence-split merge over peer memory (NVLink / NVSwitch P2P stores), in
+// place of an NCCL all-gather of the per-GPU partial states followed by the
+// merge kernel: one launch pushes this rank's partial (B, H*(D+2)) fp32 into
+// every rank's exchange buffer, raises a per-rank flag there, waits for all
+// ranks' flags of this step and merges the states it received -- the same
+// log-sum-exp merge as lse_merge.cu (the reference merges simdgroup states the
+// same way, lib/turboquant.metal:838-888).
+//
+// Exchange buffer of one rank (allocated here, shared through CUDA IPC):
+//   header: [0] this rank's step counter, [32 * (1 + k)] flag of rank k (its
+//           last pushed step; one 128 B line per rank), [32 * 65] grid counter
+//   data:   [2 step parities][world][B * H * (D + 2)] fp32
+// Flags only grow and the ranks advance in lockstep (a rank's step e + 1
+// needs every rank's push of e + 1, which follows that rank's merge of e), so
+// a rank is at most one step ahead and the parity slots never collide. Every
+// wait is bounded; on timeout the kernel records kErrPeerTimeout in the device
+// error word and returns.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+
+#include "../../include/turboquant_c.h"
+#include "tq_common.cuh"
+#include "tq_internal.h"
+
+namespace tq {
+namespace {
+
+constexpr int kHeaderWords = 32 * 66;  // step counter, 64 flags (128 B apart), grid counter
+constexpr int kGridCounter = 32 * 65;
+__device__ __forceinline__ int flag_word(int k) { return 32 * (1 + k); }
+constexpr int kMaxWorld = 64;
+constexpr int kPeerThreads = 256;
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct PeerParams {
+  const float* part;      // this rank's partial state (B, H*(D+2))
+  void* const* bufs;      // device array: exchange buffer of every rank (own at [rank])
+  int world, rank;
+  int B, H, D;
+  void* out;
+  int out_dtype;
+  long long budget;       // SM clocks a wait may take
+  uint32_t* err;
+};
+
+__global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerParams p) {
+  __shared__ uint32_t s_step;
+  __shared__ float s_w[kMaxWorld];
+  __shared__ float s_L;
+  uint32_t* own = static_cast<uint32_t*>(p.bufs[p.rank]);
+  if (threadIdx.x == 0) s_step = *reinterpret_cast<volatile uint32_t*>(own) + 1u;
+  __syncthreads();
+  const uint32_t step = s_step;
+  const long long blk = static_cast<long long>(p.B) * p.H * (p.D + 2);  // floats per state
+  const int par = static_cast<int>(step & 1u);
+
+  // ---- push: CTA j copies the state into rank j's slot [par][rank]
+  for (int j = blockIdx.x; j < p.world; j += gridDim.x) {
+    float* dst = reinterpret_cast<float*>(static_cast<uint32_t*>(p.bufs[j]) + kHeaderWords) +
+                 (static_cast<long long>(par) * p.world + p.rank) * blk;
+    if ((blk & 3) == 0) {
+      const float4* s4 = reinterpret_cast<const float4*>(p.part);
+      float4* d4 = reinterpret_cast<float4*>(dst);
+      for (long long i = threadIdx.x; i < blk / 4; i += kPeerThreads) d4[i] = s4[i];
+    } else {
+      for (long long i = threadIdx.x; i < blk; i += kPeerThreads) dst[i] = p.part[i];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) st_release_sys(static_cast<uint32_t*>(p.bufs[j]) + flag_word(p.rank), step);
+  }
+
+  // ---- wait for every rank's state of this step (bounded)
+  if (threadIdx.x < p.world) {
+    const uint32_t* flag = own + flag_word(threadIdx.x);
+    const long long t0 = clock64();
+    while (static_cast<int>(ld_acquire_sys(flag) - step) < 0) {
+      if (clock64() - t0 > p.budget) {
+        atomicOr(p.err, kErrPeerTimeout);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- merge: CTA c takes (sequence, head) items c, c + grid, ...
+  const float* data = reinterpret_cast<const float*>(own + kHeaderWords) +
+                      static_cast<long long>(par) * p.world * blk;
+  const long long hd = static_cast<long long>(p.H) * p.D;
+  for (int item = blockIdx.x; item < p.B * p.H; item += gridDim.x) {
+    const int b = item / p.H, h = item % p.H;
+    const float* base = data + static_cast<long long>(b) * p.H * (p.D + 2);
+    if (threadIdx.x == 0) {
+      float M = -INFINITY;
+      for (int k = 0; k < p.world; ++k) M = fmaxf(M, __ldcg(base + k * blk + hd + 2 * h));
+      float L = 0.0f;
+      for (int k = 0; k < p.world; ++k) {
+        const float m = __ldcg(base + k * blk + hd + 2 * h);
+        const float l = __ldcg(base + k * blk + hd + 2 * h + 1);
+        const float w = (M == -INFINITY || m == -INFINITY) ? 0.0f : __expf(m - M);
+        s_w[k] = w;
+        L += w * l;
+      }
+      s_L = L;
+    }
+    __syncthreads();
+    const float L = s_L;
+    for (int d = threadIdx.x; d < p.D; d += kPeerThreads) {
+      float acc = 0.0f;
+      for (int k = 0; k < p.world; ++k) acc += s_w[k] * __ldcg(base + k * blk + static_cast<long long>(h) * p.D + d);
+      store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * p.D + d, p.out_dtype,
+                       L > 0.0f ? acc / L : 0.0f);
+    }
+    __syncthreads();
+  }
+
+  // ---- the last CTA to finish advances this rank's step counter (every CTA
+  // read it at its start, before any CTA could finish)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned done = atomicAdd(own + kGridCounter, 1u);
+    if (done == gridDim.x - 1) {
+      own[kGridCounter] = 0u;
+      *reinterpret_cast<volatile uint32_t*>(own) = step;
+    }
+  }
+}
+
+size_t state_floats(int world, int B, int H, int D) {
+  return 2ull * world * B * H * (D + 2);
+}
+
+}  // namespace
+}  // namespace tq
+
+using namespace tq;
+
+extern "C" {
+
+TQ_API size_t tq_peer_buffer_bytes(int world, int batch, int num_heads, int head_dim) {
+  if (world < 1 || world > kMaxWorld || batch < 1 || num_heads < 1 || head_dim < 1) return 0;
+  return kHeaderWords * sizeof(uint32_t) + state_floats(world, batch, num_heads, head_dim) * sizeof(float);
+}
+
+TQ_API int tq_peer_buffer_alloc(size_t bytes, void** buf) {
+  if (!buf || bytes == 0) {
+    set_last_error("tq_peer_buffer_alloc: bad arguments");
+    return TQ_ERR_INVALID;
+  }
+  cudaError_t e = cudaMalloc(buf, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*buf, 0, bytes);
+  if (e != cudaSuccess) {
+    set_last_error("tq_peer_buffer_alloc: %s", cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  return TQ_OK;
+}
+
+TQ_API int tq_peer_buffer_free(void* buf) {
+  const cudaError_t e = cudaFree(buf);
+  if (e != cudaSuccess) {
+    set_last_error("tq_peer_buffer_free: %s", cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  return TQ_OK;
+}
+
+TQ_API int tq_ipc_handle(void* buf, void* handle) {
+  if (!buf || !handle) {
+    set_last_error("tq_ipc_handle: null pointer");
+    return TQ_ERR_INVALID;
+  }
+  cudaIpcMemHandle_t h;
+  const cudaError_t e = cudaIpcGetMemHandle(&h, buf);
+  if (e != cudaSuccess) {
+    set_last_error("tq_ipc_handle: %s", cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  static_assert(sizeof(h) == TQ_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(handle, &h, sizeof(h));
+  return TQ_OK;
+}
+
+TQ_API int tq_ipc_open(const void* handle, void** peer_buf) {
+  if (!handle || !peer_buf) {
+    set_last_error("tq_ipc_open: null pointer");
+    return TQ_ERR_INVALID;
+  }
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(peer_buf, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    set_last_error("tq_ipc_open: %s", cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  return TQ_OK;
+}
+
+TQ_API int tq_ipc_close(void* peer_buf) {
+  const cudaError_t e = cudaIpcCloseMemHandle(peer_buf);
+  if (e != cudaSuccess) {
+    set_last_error("tq_ipc_close: %s", cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  return TQ_OK;
+}
+
+TQ_API int tq_peer_merge(const float* part, void* const* peer_bufs, int world, int rank,
+                         int batch, int num_heads, int head_dim, void* out, tq_dtype out_dtype,
+                         int timeout_us, void* stream) {
+  if (!part || !peer_bufs || !out) {
+    set_last_error("tq_peer_merge: null pointer");
+    return TQ_ERR_INVALID;
+  }
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || batch < 1 || num_heads < 1 ||
+      head_dim < 1 || timeout_us < 1) {
+    set_last_error("tq_peer_merge: bad sizes");
+    return TQ_ERR_INVALID;
+  }
+  if (reinterpret_cast<uintptr_t>(part) & 15u) {
+    set_last_error("tq_peer_merge: part must be 16-byte aligned");
+    return TQ_ERR_INVALID;
+  }
+  int dev = 0, khz = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev);
+  PeerParams p{};
+  p.part = part;
+  p.bufs = peer_bufs;
+  p.world = world;
+  p.rank = rank;
+  p.B = batch;
+  p.H = num_heads;
+  p.D = head_dim;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.budget = static_cast<long long>(timeout_us) * (khz > 0 ? khz : 2000000) / 1000;
+  p.err = device_error_word();
+  int grid = batch * num_heads;
+  if (grid < world) grid = world;
+  if (grid > 148) grid = 148;
+  peer_merge_kernel<<<grid, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_last_error("tq_peer_merge: %s", cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  return TQ_OK;
+}
+
+}  // extern "C"

@@ -12,7 +12,7 @@ namespace tq {
 enum Dtype : int { kF32 = 0, kF16 = 1, kBF16 = 2 };
 
 // Error codes written to the device error word (see tq_device_error).
-enum DeviceError : uint32_t { kErrNone = 0, kErrBarrierTimeout = 1u };
+enum DeviceError : uint32_t { kErrNone = 0, kErrBarrierTimeout = 1u, kErrPeerTimeout = 2u };
 
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;

@@ -15,8 +15,14 @@ turboquant::sdpa_int4 once per layer, engine/gemma4_multilayer.cpp:280-282):
   query heads; no exchange is needed unless the caller wants the full output,
   which one all-gather of (H/P, D) per rank provides.
 
-Remote partials land in this GPU's memory (the all-gather's output buffer)
-before the merge kernel reads them; no kernel reads peer memory.
+Two exchanges of the partial states: NCCL (`all_gather_into_tensor` into this
+GPU's memory, then the merge kernel) or `PeerExchange`, which does the
+exchange and the merge in one kernel of this library: every rank stores its
+state into every rank's exchange buffer over NVLink (CUDA IPC mappings, plain
+P2P stores), raises a step flag there and merges what it received once all
+flags of the step are up (waits bounded; a missing rank shows up as
+TQ_DEVICE_ERR_PEER_TIMEOUT in tq_device_error). Kernels only ever read their
+own GPU's memory.
 """
 from __future__ import annotations
 
@@ -72,6 +78,77 @@ def _all_gather(part: torch.Tensor, world: int, group) -> torch.Tensor:
     return parts
 
 
+class PeerExchange:
+    """Exchange buffers of one sequence-split group for `tq_peer_merge`.
+
+    Collective: every rank of `group` constructs it (it allocates this rank's
+    buffer, all-gathers the CUDA IPC handles as objects and maps the others'
+    buffers) and calls `merge` once per step in the same order; `close` is
+    collective too. State layout: that of `tq_sdpa_int4_partial`."""
+
+    def __init__(self, batch: int, num_heads: int, head_dim: int, group=None, device=None,
+                 timeout_us: int = 5_000_000):
+        import ctypes
+        self.group = group
+        self.world, self.rank = _world_rank(group)
+        self.B, self.H, self.D = batch, num_heads, head_dim
+        self.timeout_us = int(timeout_us)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        lib = tq.load_library()
+        nbytes = int(lib.tq_peer_buffer_bytes(self.world, batch, num_heads, head_dim))
+        if nbytes == 0:
+            raise ValueError("bad peer exchange sizes")
+        buf = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            tq._check(lib.tq_peer_buffer_alloc(nbytes, ctypes.byref(buf)))
+            self._own = buf.value
+            handle = (ctypes.c_ubyte * 64)()
+            tq._check(lib.tq_ipc_handle(self._own, handle))
+            handles = [None] * self.world
+            if self.world > 1:
+                dist.all_gather_object(handles, bytes(handle), group=group)
+            else:
+                handles[0] = bytes(handle)
+            self._opened = []
+            ptrs = []
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(self._own)
+                    continue
+                p = ctypes.c_void_p()
+                h = (ctypes.c_ubyte * 64).from_buffer_copy(handles[r])
+                tq._check(lib.tq_ipc_open(h, ctypes.byref(p)))
+                self._opened.append(p.value)
+                ptrs.append(p.value)
+            self.bufs = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        if self.world > 1:
+            dist.barrier(group=group)  # every buffer is mapped before any rank pushes
+
+    def merge(self, part: torch.Tensor, out: Optional[torch.Tensor] = None,
+              out_dtype: torch.dtype = torch.float32, s=None) -> torch.Tensor:
+        """Push this rank's state (B, H*(D+2)) fp32, wait for the others',
+        return the merged (B, H, D)."""
+        if out is None:
+            out = torch.empty(self.B, self.H, self.D, dtype=out_dtype, device=self.device)
+        pc = part.contiguous()
+        tq._check(tq.load_library().tq_peer_merge(
+            tq._ptr(pc), self.bufs.data_ptr(), self.world, self.rank, self.B, self.H, self.D,
+            tq._ptr(out), tq._dt(out), self.timeout_us, tq._stream(s)))
+        return out
+
+    def close(self) -> None:
+        lib = tq.load_library()
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no rank still stores into a buffer being released
+        for p in self._opened:
+            tq._check(lib.tq_ipc_close(p))
+        self._opened = []
+        if self._own:
+            tq._check(lib.tq_peer_buffer_free(self._own))
+            self._own = None
+
+
 def _cuda_partial(queries, cache, n_local, token_offset, n_total, gqa, scale, window):
     return tq.sdpa_int4_partial(queries, *cache, gqa, scale, window, n_local=n_local,
                                 token_offset=token_offset, n_total=n_total)
@@ -85,19 +162,24 @@ def seqsplit_decode(queries: torch.Tensor, cache, n_local: int, token_offset: in
                     gqa_factor: int, scale: float = 1.0, sliding_window: int = 0, *,
                     group=None, out_dtype: Optional[torch.dtype] = None,
                     partial_fn: Optional[Callable] = None,
-                    merge_fn: Optional[Callable] = None) -> torch.Tensor:
+                    merge_fn: Optional[Callable] = None,
+                    exchange: Optional[PeerExchange] = None) -> torch.Tensor:
     """Decode attention of a sequence split across the ranks of `group`.
 
     queries (B, H, D) (the same on every rank); cache = this rank's shard
     (k_quant, k_scales, k_biases, v_quant, v_scales, v_biases) holding global
     tokens [token_offset, token_offset + n_local) of a sequence of n_total.
     Returns (B, H, D) on every rank. partial_fn / merge_fn default to the CUDA
-    kernels; tests substitute CPU implementations to check the host logic."""
+    kernels; tests substitute CPU implementations to check the host logic.
+    With `exchange` the states move over peer memory and the merge happens in
+    the same kernel (`PeerExchange.merge`) instead of all-gather + merge."""
     world, _ = _world_rank(group)
     B, H, D = queries.shape
     part = (partial_fn or _cuda_partial)(queries, cache, n_local, token_offset, n_total,
                                          gqa_factor, scale, sliding_window)
     part = part.reshape(B, H * (D + 2))
+    if exchange is not None:
+        return exchange.merge(part, out_dtype=out_dtype or queries.dtype)
     parts = _all_gather(part, world, group)
     return (merge_fn or _cuda_merge)(parts, H, D, out_dtype or queries.dtype)
 
@@ -135,7 +217,8 @@ class SeqSplitCache:
         self.n_total += k_new.shape[2]
 
     def decode(self, queries: torch.Tensor, gqa_factor: int, scale: float = 1.0,
-               sliding_window: int = 0, out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+               sliding_window: int = 0, out_dtype: Optional[torch.dtype] = None,
+               exchange: Optional[PeerExchange] = None) -> torch.Tensor:
         return seqsplit_decode(queries, self.cache.tensors(), self.n_local, self.t0, self.n_total,
                                gqa_factor, scale, sliding_window, group=self.group,
-                               out_dtype=out_dtype)
+                               out_dtype=out_dtype, exchange=exchange)

@@ -58,6 +58,14 @@ def load_library() -> ctypes.CDLL:
     L.tq_sdpa_int4_workspace_size.argtypes = [I, I, I, I, I, I]
     L.tq_workspace_init.argtypes = [P, SZ, P]
     L.tq_sdpa_int4.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, P, P, I, P, SZ, P]
+    L.tq_peer_buffer_bytes.restype = SZ
+    L.tq_peer_buffer_bytes.argtypes = [I, I, I, I]
+    L.tq_peer_buffer_alloc.argtypes = [SZ, ctypes.POINTER(ctypes.c_void_p)]
+    L.tq_peer_buffer_free.argtypes = [P]
+    L.tq_ipc_handle.argtypes = [P, P]
+    L.tq_ipc_open.argtypes = [P, ctypes.POINTER(ctypes.c_void_p)]
+    L.tq_ipc_close.argtypes = [P]
+    L.tq_peer_merge.argtypes = [P, P, I, I, I, I, I, P, I, I, P]
     L.tq_sdpa_int4_append.argtypes = [P, I, P, P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I,
                                       P, P, I, P, SZ, P]
     L.tq_sdpa_int4_partial.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, I, I, P,

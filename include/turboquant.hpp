@@ -125,6 +125,22 @@ class TQ_CXX_API KVCache {
   // Decode attention over the cached tokens: queries (B, H, D) or (H, D).
   array sdpa(const array& queries, int gqa_factor, float scale = 1.0f, int sliding_window = 0,
              cudaStream_t s = nullptr);
+  // One decode step: append the step's K/V row (B, Hkv, D) or (B, Hkv, 1, D)
+  // and attend over the cache including it -- one launch with the tensor-core
+  // decode kernel; same result as append() followed by sdpa().
+  array decode_step(const array& queries, const array& k_new, const array& v_new, int gqa_factor,
+                    float scale = 1.0f, int sliding_window = 0, cudaStream_t s = nullptr);
+  // Prefill chunk (batch 1): append n new tokens' K/V (Hkv, n, D), then causal
+  // attention of their queries (n, H, D) -- query i at position length + i --
+  // on the tensor cores (tcgen05). Returns (n, H, D) in out_dtype.
+  array prefill_chunk(const array& queries, const array& k_chunk, const array& v_chunk,
+                      int gqa_factor, float scale = 1.0f, int sliding_window = 0,
+                      Dtype out_dtype = Dtype::bfloat16, cudaStream_t s = nullptr);
+  // Batched decode over this (batch 1) cache shared by n sequences: queries
+  // (n, H, D), each at the last position; tensor cores. Returns (n, H, D).
+  array sdpa_multi(const array& queries, int gqa_factor, float scale = 1.0f,
+                   int sliding_window = 0, Dtype out_dtype = Dtype::bfloat16,
+                   cudaStream_t s = nullptr);
   int length() const { return length_; }
   int capacity() const { return capacity_; }
   void reset() { length_ = 0; }

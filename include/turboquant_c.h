@@ -161,6 +161,33 @@ TQ_API int tq_sdpa_int4_partial(const void* queries, tq_dtype q_dtype, const uin
                          int token_offset, int n_total, float* part_out, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* ---- sequence split over peer memory (CUDA IPC + NVLink P2P stores) ------
+ * In place of an all-gather + tq_lse_merge: every rank of a sequence split
+ * allocates one exchange buffer (tq_peer_buffer_bytes / _alloc, zeroed),
+ * shares it with tq_ipc_handle (TQ_IPC_HANDLE_BYTES opaque bytes, exchanged
+ * by the caller, e.g. an all-gather of objects) and opens the others' with
+ * tq_ipc_open. tq_peer_merge then, in one launch, stores this rank's partial
+ * state (the layout of tq_sdpa_int4_partial's part_out) into every rank's
+ * buffer, raises a per-rank step flag there, waits for all ranks' flags of the
+ * step and writes the merged (B, H, D) output. peer_bufs is a DEVICE array of
+ * the world's buffer pointers (this rank's own at [rank]). Every rank calls it
+ * once per step, in the same order; a rank that does not arrive within
+ * timeout_us makes the others record TQ_DEVICE_ERR_PEER_TIMEOUT in the device
+ * error word (tq_device_error) and return. No counterpart in the reference
+ * (it is single-device). */
+#define TQ_IPC_HANDLE_BYTES 64
+#define TQ_DEVICE_ERR_BARRIER_TIMEOUT 1u
+#define TQ_DEVICE_ERR_PEER_TIMEOUT 2u
+TQ_API size_t tq_peer_buffer_bytes(int world, int batch, int num_heads, int head_dim);
+TQ_API int tq_peer_buffer_alloc(size_t bytes, void** buf);
+TQ_API int tq_peer_buffer_free(void* buf);
+TQ_API int tq_ipc_handle(void* buf, void* handle);
+TQ_API int tq_ipc_open(const void* handle, void** peer_buf);
+TQ_API int tq_ipc_close(void* peer_buf);
+TQ_API int tq_peer_merge(const float* part, void* const* peer_bufs, int world, int rank,
+                         int batch, int num_heads, int head_dim, void* out, tq_dtype out_dtype,
+                         int timeout_us, void* stream);
+
 /* Log-sum-exp merge of n_parts partial states (e.g. one per GPU after an
  * all-gather). parts: n_parts blocks of (H*(D+2)) floats per batch entry,
  * laid out [part][batch][H*(D+2)]; out: (B, H, D) in out_dtype.

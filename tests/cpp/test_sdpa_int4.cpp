@@ -5,7 +5,9 @@
 // tolerance (max-abs 2e-3, cosine >= 0.99999 against an fp64 SDPA) instead of
 // the reference's unseeded draw and 0.1 bound (tests/test_sdpa_int4.cpp:20-22,77).
 // Also runs the preallocated-cache path (KVCache append + sdpa, D=128, GQA 2,
-// sliding window) and the sequence-split path (sdpa_int4_partial + lse_merge).
+// sliding window), the sequence-split path (sdpa_int4_partial + lse_merge),
+// the one-launch decode step (KVCache::decode_step == append + sdpa, bit for
+// bit) and the tensor-core paths (KVCache::sdpa_multi, prefill_chunk).
 // Exit code 0 = pass.
 #include <cmath>
 #include <cstdio>
@@ -169,6 +171,80 @@ int main() {
     auto merged = turboquant::lse_merge(stacked, nh, hd, Dtype::float16);
     auto ref = sdpa_ref(Qh, kd, vd, nh, nkv, n, hd, 1.0f, 0);
     ok &= compare("3-shard partial + merge", f16_to_f32(merged.to_vector<uint16_t>()), ref);
+  }
+
+  {  // decode_step (fused append + decode), prefill_chunk and sdpa_multi (tcgen05)
+    const int nh = 32, nkv = 16, hd = 128, n0 = 1000, cap = 1100, nc = 40;
+    std::mt19937 rng(2);
+    auto K0 = normal(static_cast<size_t>(nkv) * n0 * hd, rng), V0 = normal(K0.size(), rng);
+    auto Kn = normal(static_cast<size_t>(nkv) * hd, rng), Vn = normal(Kn.size(), rng);
+    auto Qh = normal(static_cast<size_t>(nh) * hd, rng);
+    auto Q = array::from_host(Qh.data(), {nh, hd}, Dtype::float32);
+    auto fill = [&](turboquant::KVCache& c) {
+      c.append(array::from_host(K0.data(), {1, nkv, n0, hd}, Dtype::float32),
+               array::from_host(V0.data(), {1, nkv, n0, hd}, Dtype::float32));
+    };
+    // rows [0, n) of a cache, dequantized on the host, (nkv, n, hd)
+    auto deq = [&](turboquant::KVCache& c, int n, std::vector<float>& kd, std::vector<float>& vd) {
+      auto ka = turboquant::dequantize(c.k_quant, c.k_scales, c.k_biases).to_vector<float>();
+      auto va = turboquant::dequantize(c.v_quant, c.v_scales, c.v_biases).to_vector<float>();
+      kd.assign(static_cast<size_t>(nkv) * n * hd, 0.0f);
+      vd.assign(kd.size(), 0.0f);
+      for (int h = 0; h < nkv; ++h)
+        for (int t = 0; t < n; ++t)
+          for (int d = 0; d < hd; ++d) {
+            kd[(static_cast<size_t>(h) * n + t) * hd + d] = ka[(static_cast<size_t>(h) * cap + t) * hd + d];
+            vd[(static_cast<size_t>(h) * n + t) * hd + d] = va[(static_cast<size_t>(h) * cap + t) * hd + d];
+          }
+    };
+    turboquant::KVCache a(1, nkv, hd, cap), b(1, nkv, hd, cap);
+    fill(a);
+    fill(b);
+    auto kn = array::from_host(Kn.data(), {1, nkv, hd}, Dtype::float32);
+    auto vn = array::from_host(Vn.data(), {1, nkv, hd}, Dtype::float32);
+    auto fused = a.decode_step(Q, kn, vn, nh / nkv).to_vector<float>();
+    b.append(kn.reshape({1, nkv, 1, hd}), vn.reshape({1, nkv, 1, hd}));
+    auto split = b.sdpa(Q, nh / nkv).to_vector<float>();
+    const bool same = fused == split && a.length() == b.length();
+    printf("%-28s %s\n", "decode_step == append+sdpa", same ? "PASS" : "FAIL");
+    ok &= same;
+    std::vector<float> kd, vd;
+    deq(a, n0 + 1, kd, vd);
+    ok &= compare("decode_step vs fp64", fused, sdpa_ref(Qh, kd, vd, nh, nkv, n0 + 1, hd, 1.0f, 0));
+
+    // batched decode: 8 queries against the shared cache a (n0 + 1 tokens)
+    const int nb = 8;
+    auto Qb = normal(static_cast<size_t>(nb) * nh * hd, rng);
+    auto mb = a.sdpa_multi(array::from_host(Qb.data(), {nb, nh, hd}, Dtype::float32), nh / nkv, 1.0f,
+                           0, Dtype::float32).to_vector<float>();
+    for (int i : {0, 5}) {
+      std::vector<float> qi(Qb.begin() + static_cast<size_t>(i) * nh * hd,
+                            Qb.begin() + static_cast<size_t>(i + 1) * nh * hd);
+      std::vector<float> gi(mb.begin() + static_cast<size_t>(i) * nh * hd,
+                            mb.begin() + static_cast<size_t>(i + 1) * nh * hd);
+      ok &= compare(i ? "sdpa_multi query 5" : "sdpa_multi query 0", gi,
+                    sdpa_ref(qi, kd, vd, nh, nkv, n0 + 1, hd, 1.0f, 0));
+    }
+
+    // prefill chunk of nc tokens at positions n0 + 1 .. n0 + nc on cache a
+    auto Kc = normal(static_cast<size_t>(nkv) * nc * hd, rng), Vc = normal(Kc.size(), rng);
+    auto Qc = normal(static_cast<size_t>(nc) * nh * hd, rng);
+    const int base = a.length();
+    auto pc = a.prefill_chunk(array::from_host(Qc.data(), {nc, nh, hd}, Dtype::float32),
+                              array::from_host(Kc.data(), {1, nkv, nc, hd}, Dtype::float32),
+                              array::from_host(Vc.data(), {1, nkv, nc, hd}, Dtype::float32),
+                              nh / nkv, 1.0f, 0, Dtype::float32).to_vector<float>();
+    for (int i : {0, 17, nc - 1}) {
+      const int n = base + i + 1;  // query i sees tokens [0, base + i]
+      deq(a, n, kd, vd);
+      std::vector<float> qi(Qc.begin() + static_cast<size_t>(i) * nh * hd,
+                            Qc.begin() + static_cast<size_t>(i + 1) * nh * hd);
+      std::vector<float> gi(pc.begin() + static_cast<size_t>(i) * nh * hd,
+                            pc.begin() + static_cast<size_t>(i + 1) * nh * hd);
+      char name[64];
+      snprintf(name, sizeof(name), "prefill_chunk query %d", i);
+      ok &= compare(name, gi, sdpa_ref(qi, kd, vd, nh, nkv, n, hd, 1.0f, 0));
+    }
   }
 
   printf("\n%s\n", ok ? "PASS" : "FAIL");

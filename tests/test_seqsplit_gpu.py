@@ -74,3 +74,123 @@ def test_seqsplit_two_gpus_nccl():
     for rank, rr in res.items():
         for err, cos in rr:
             assert err <= 2e-3 and cos >= 0.99999, (rank, err, cos)
+
+
+def _peer_worker(rank, world, port, q, mode):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    import gemma4metal_b200.turboquant as tq
+    from gemma4metal_b200 import seqsplit
+    from oracle import inputs, oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ex = None
+    try:
+        H, Hkv, D, N = 32, 8, 256, 3000
+        L = inputs.make_layer(17, H, Hkv, D, N)
+        sc = seqsplit.SeqSplitCache(N, Hkv, D, device=f"cuda:{rank}")
+        sc.load_prefix(torch.from_numpy(L["k"]).cuda(), torch.from_numpy(L["v"]).cuda())
+        q16 = torch.from_numpy(L["q"]).half().cuda()
+        # kernels load on first launch; a warm-up step keeps the ranks' first
+        # peer step within the wait bound
+        sc.decode(q16, H // Hkv, 1.0, 0, out_dtype=torch.float32)
+        torch.cuda.synchronize()
+        ex = seqsplit.PeerExchange(1, H, D, device=f"cuda:{rank}",
+                                   timeout_us=5_000_000 if mode == "parity" else 200_000)
+        if mode == "parity":
+            res, codes = [], []
+            # several steps: the exchange alternates its two slots and step flags
+            for step in range(5):
+                kn = torch.from_numpy(L["k_new"]).cuda() * (1 + 0.1 * step)
+                vn = torch.from_numpy(L["v_new"]).cuda() * (1 - 0.1 * step)
+                sc.append(kn, vn)
+                peer = sc.decode(q16, H // Hkv, 1.0, 0, out_dtype=torch.float32, exchange=ex)
+                nccl = sc.decode(q16, H // Hkv, 1.0, 0, out_dtype=torch.float32)
+                torch.cuda.synchronize()
+                res.append(float((peer - nccl).abs().max()))
+                codes.append(tq.device_error())
+            assert codes == [0] * 5, codes
+            # the last step against the oracle's unsplit dequantize + SDPA
+            ks = [L["k"]] + [L["k_new"] * (1 + 0.1 * s) for s in range(5)]
+            vs = [L["v"]] + [L["v_new"] * (1 - 0.1 * s) for s in range(5)]
+            kq, kss, kb = O.quantize(np.concatenate(ks, 2))
+            vq, vss, vb = O.quantize(np.concatenate(vs, 2))
+            ref = O.sdpa_int4(L["q"].astype(np.float16), kq, kss, kb, vq, vss, vb, f64=True)
+            got = peer.cpu().numpy()
+            err = float(np.max(np.abs(got - ref)))
+            cos = float(got.ravel() @ ref.ravel() / (np.linalg.norm(got) * np.linalg.norm(ref)))
+            q.put((rank, (max(res), err, cos)))
+        else:  # rank 1 misses one step: rank 0's merge must time out, record it, return
+            part_q = q16
+            if rank == 0:
+                sc.decode(part_q, H // Hkv, 1.0, 0, out_dtype=torch.float32, exchange=ex)
+                torch.cuda.synchronize()
+                code = tq.device_error()
+            else:
+                code = -1
+            dist.barrier()
+            q.put((rank, code))
+    finally:
+        if ex is not None:
+            ex.close()
+        dist.destroy_process_group()
+
+
+def _run_two(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, q, mode)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        assert p.exitcode == 0
+    return dict(q.get(timeout=10) for _ in range(2))
+
+
+def test_peer_exchange_two_gpus():
+    """State exchange + merge over NVLink P2P stores (one kernel) equals the
+    NCCL all-gather + merge path step after step, and the oracle."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    for rank, (diff, err, cos) in _run_two("parity").items():
+        assert diff <= 1e-5, (rank, diff)
+        assert err <= 2e-3 and cos >= 0.99999, (rank, err, cos)
+
+
+def test_peer_exchange_missing_rank_times_out():
+    """A rank that skips a step (host-side failure, no GPU fault): the other
+    rank's merge gives up after its bound and reports the peer timeout in the
+    device error word instead of hanging."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    res = _run_two("timeout")
+    assert res[0] == 2  # TQ_DEVICE_ERR_PEER_TIMEOUT
+
+
+def test_peer_exchange_single_gpu_equals_merge():
+    """World of one (no process group): the exchange kernel pushes to its own
+    buffer and merges one state -- the same as lse_merge of that state."""
+    import gemma4metal_b200.turboquant as tq
+    from gemma4metal_b200 import seqsplit
+    torch.manual_seed(3)
+    B, H, D = 2, 16, 128
+    part = torch.randn(B, H * (D + 2), device="cuda")
+    part.view(B, H * (D + 2))[:, H * D:].view(B, H, 2)[..., 1].abs_()  # l >= 0
+    ex = seqsplit.PeerExchange(B, H, D)
+    try:
+        for _ in range(3):  # several steps (slot parity, step counter)
+            got = ex.merge(part)
+        ref = tq.lse_merge(part[None], H, D)
+        torch.cuda.synchronize()
+        assert tq.device_error() == 0
+        assert torch.allclose(got, ref, rtol=1e-6, atol=1e-6)
+    finally:
+        ex.close()

@@ -68,6 +68,7 @@ struct DecodeCommon {
   const void* k_new = nullptr;
   const void* v_new = nullptr;
   int new_dtype = 0;
+  int new_slot = -1;
 };
 
 int validate_decode(const DecodeCommon& c, const char* fn) {
@@ -262,11 +263,13 @@ static int decode_common(const DecodeCommon& c, const char* fn, const int32_t* s
       a.k_new = c.k_new;
       a.v_new = c.v_new;
       a.new_dtype = c.new_dtype;
+      a.new_slot = c.new_slot;
     } else {
+      const bool at_slot = c.new_slot >= 0;
       e = tq::launch_quantize_rows(
           c.k_new, c.new_dtype, static_cast<long long>(c.B) * c.Hkv, c.D, 1, c.Hkv, c.capacity,
-          a.bstride_tok, c.n_tokens - 1, seq_lens, const_cast<uint32_t*>(c.kq),
-          const_cast<void*>(c.ks), const_cast<void*>(c.kb), c.sb_dtype,
+          a.bstride_tok, at_slot ? c.new_slot : c.n_tokens - 1, at_slot ? nullptr : seq_lens,
+          const_cast<uint32_t*>(c.kq), const_cast<void*>(c.ks), const_cast<void*>(c.kb), c.sb_dtype,
           static_cast<cudaStream_t>(stream), c.v_new, const_cast<uint32_t*>(c.vq),
           const_cast<void*>(c.vs), const_cast<void*>(c.vb), -1);
       if (e != cudaSuccess) return cuda_fail(e, fn);
@@ -298,13 +301,13 @@ int tq_sdpa_int4(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,
                        workspace_bytes, stream);
 }
 
-int tq_sdpa_int4_append(const void* queries, tq_dtype q_dtype, const void* k_new,
-                        const void* v_new, tq_dtype new_dtype, uint32_t* k_quant, void* k_scales,
-                        void* k_biases, uint32_t* v_quant, void* v_scales, void* v_biases,
-                        tq_dtype sb_dtype, int gqa_factor, float scale, int sliding_window,
-                        int batch, int num_kv_heads, int head_dim, int n_tokens, int capacity,
-                        const int32_t* seq_lens, void* out, tq_dtype out_dtype, void* workspace,
-                        size_t workspace_bytes, void* stream) {
+static int append_common(const void* queries, tq_dtype q_dtype, const void* k_new,
+                         const void* v_new, tq_dtype new_dtype, uint32_t* k_quant, void* k_scales,
+                         void* k_biases, uint32_t* v_quant, void* v_scales, void* v_biases,
+                         tq_dtype sb_dtype, int gqa_factor, float scale, int sliding_window,
+                         int batch, int num_kv_heads, int head_dim, int n_tokens, int capacity,
+                         const int32_t* seq_lens, int slot, void* out, tq_dtype out_dtype,
+                         void* workspace, size_t workspace_bytes, void* stream) {
   t_err.clear();
   if (!out) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: null out");
   if (!valid_dtype(out_dtype)) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: bad out_dtype");
@@ -314,10 +317,39 @@ int tq_sdpa_int4_append(const void* queries, tq_dtype q_dtype, const void* k_new
     return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: k_new/v_new must be 16-byte aligned");
   if (!seq_lens && n_tokens < 1)
     return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: n_tokens must include the new token (>= 1)");
+  if (slot >= 0 && (seq_lens || slot >= n_tokens))
+    return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append_at: slot must be < n_tokens (and no seq_lens)");
   DecodeCommon c{queries, q_dtype, k_quant, v_quant, k_scales, k_biases, v_scales, v_biases,
                  sb_dtype, gqa_factor, sliding_window, batch, num_kv_heads, head_dim, n_tokens,
-                 capacity, scale, k_new, v_new, new_dtype};
+                 capacity, scale, k_new, v_new, new_dtype, slot};
   return decode_common(c, "tq_sdpa_int4_append", seq_lens, 0, 0, 0, out, out_dtype, nullptr,
+                       workspace, workspace_bytes, stream);
+}
+
+int tq_sdpa_int4_append(const void* queries, tq_dtype q_dtype, const void* k_new,
+                        const void* v_new, tq_dtype new_dtype, uint32_t* k_quant, void* k_scales,
+                        void* k_biases, uint32_t* v_quant, void* v_scales, void* v_biases,
+                        tq_dtype sb_dtype, int gqa_factor, float scale, int sliding_window,
+                        int batch, int num_kv_heads, int head_dim, int n_tokens, int capacity,
+                        const int32_t* seq_lens, void* out, tq_dtype out_dtype, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  return append_common(queries, q_dtype, k_new, v_new, new_dtype, k_quant, k_scales, k_biases,
+                       v_quant, v_scales, v_biases, sb_dtype, gqa_factor, scale, sliding_window,
+                       batch, num_kv_heads, head_dim, n_tokens, capacity, seq_lens, -1, out,
+                       out_dtype, workspace, workspace_bytes, stream);
+}
+
+int tq_sdpa_int4_append_at(const void* queries, tq_dtype q_dtype, const void* k_new,
+                           const void* v_new, tq_dtype new_dtype, uint32_t* k_quant,
+                           void* k_scales, void* k_biases, uint32_t* v_quant, void* v_scales,
+                           void* v_biases, tq_dtype sb_dtype, int gqa_factor, float scale,
+                           int batch, int num_kv_heads, int head_dim, int n_tokens, int capacity,
+                           int slot, void* out, tq_dtype out_dtype, void* workspace,
+                           size_t workspace_bytes, void* stream) {
+  if (slot < 0) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append_at: slot must be >= 0");
+  return append_common(queries, q_dtype, k_new, v_new, new_dtype, k_quant, k_scales, k_biases,
+                       v_quant, v_scales, v_biases, sb_dtype, gqa_factor, scale, 0, batch,
+                       num_kv_heads, head_dim, n_tokens, capacity, nullptr, slot, out, out_dtype,
                        workspace, workspace_bytes, stream);
 }
 

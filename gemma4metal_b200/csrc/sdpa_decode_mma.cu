@@ -119,6 +119,7 @@ struct MParams {
   const void* k_new;
   const void* v_new;
   int new_dtype;
+  int new_slot;  // < 0: n_local - 1 (the end of each sequence); else this slot (ring caches)
   float* ws_o;
   float* ws_ml;
   unsigned* counters;
@@ -343,9 +344,9 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   // head write the same bytes); its producer issues the tile holding the
   // slot only after the writers' release on nbar
   constexpr int NWW = D / 128;  // writer warps: D/8 words of K and of V, one per lane
-  const int new_slot = n_local - 1;
-  const bool has_new = p.k_new != nullptr && n_local > 0 && new_slot >= cb * kChunk &&
-                       new_slot < ce * kChunk;
+  const int new_slot = p.new_slot >= 0 ? p.new_slot : n_local - 1;
+  const bool has_new = p.k_new != nullptr && n_local > 0 && new_slot < n_local &&
+                       new_slot >= cb * kChunk && new_slot < ce * kChunk;
   const int new_tile = has_new ? (new_slot / kChunk - cb) / CPT : -1;
 
 
@@ -1161,6 +1162,7 @@ cudaError_t launch_decode_mma(const DecodeArgs& a, const DecodePlan& pl, cudaStr
   p.k_new = a.k_new;
   p.v_new = a.v_new;
   p.new_dtype = a.new_dtype;
+  p.new_slot = a.new_slot;
   if (pl.splits > 1) {
     unsigned char* ws = static_cast<unsigned char*>(a.workspace);
     p.ws_o = reinterpret_cast<float*>(ws + pl.ws_o_off);

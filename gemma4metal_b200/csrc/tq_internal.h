@@ -53,6 +53,7 @@ struct DecodeArgs {
   const void* k_new = nullptr;
   const void* v_new = nullptr;
   int new_dtype = 0;
+  int new_slot = -1;  // < 0: n_local - 1
 };
 
 // Decode kernel variants: the CUDA-core kernel (sdpa_decode.cu) and the

@@ -66,6 +66,8 @@ def load_library() -> ctypes.CDLL:
     L.tq_ipc_open.argtypes = [P, ctypes.POINTER(ctypes.c_void_p)]
     L.tq_ipc_close.argtypes = [P]
     L.tq_peer_merge.argtypes = [P, P, I, I, I, I, I, P, I, I, P]
+    L.tq_sdpa_int4_append_at.argtypes = [P, I, P, P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I,
+                                         I, P, I, P, SZ, P]
     L.tq_sdpa_int4_append.argtypes = [P, I, P, P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I,
                                       P, P, I, P, SZ, P]
     L.tq_sdpa_int4_partial.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, I, I, P,
@@ -205,6 +207,87 @@ class KVCache:
         quantize_append(k_new, v_new, *self.tensors(), pos=p, positions=positions, s=s)
         if positions is None:
             self.length = max(self.length, p + n_new)
+
+
+class RingKVCache(KVCache):
+    """int4 KV cache of a sliding-window layer as a ring of `window` slots
+    (batch 1): token t lives in slot t % window, so the cache holds exactly
+    the last `window` tokens -- the set the window rule (N-1-t) < W keeps
+    (lib/turboquant.metal:779) -- with no copy. The reference keeps the same
+    set by concatenating every new token onto the cache and slicing the
+    oldest off the front (engine/gemma4_multilayer.cpp:228-249). Attention
+    does not depend on the tokens' order, so decode runs over the filled
+    slots unmasked."""
+
+    def __init__(self, num_kv_heads: int, head_dim: int, window: int, device=None,
+                 scales_dtype: torch.dtype = torch.float16):
+        super().__init__(1, num_kv_heads, head_dim, window, device=device, scales_dtype=scales_dtype)
+        self.window = window
+        self.total = 0  # tokens appended so far (the layer's position)
+
+    @property
+    def n_valid(self) -> int:
+        return min(self.total, self.window)
+
+    def append(self, k_new: torch.Tensor, v_new: torch.Tensor, s=None) -> None:  # type: ignore[override]
+        """Append (1, Hkv, n, D) tokens at the ring positions (wrapping)."""
+        if k_new.dim() == 3:
+            k_new, v_new = k_new.unsqueeze(0), v_new.unsqueeze(0)
+        n = k_new.shape[2]
+        if n > self.window:  # only the last `window` tokens can survive
+            k_new, v_new = k_new[:, :, n - self.window:], v_new[:, :, n - self.window:]
+            self.total += n - self.window
+            n = self.window
+        slot = self.total % self.window
+        first = min(n, self.window - slot)
+        quantize_append(k_new[:, :, :first], v_new[:, :, :first], *self.tensors(), pos=slot, s=s)
+        if n > first:
+            quantize_append(k_new[:, :, first:], v_new[:, :, first:], *self.tensors(), pos=0, s=s)
+        self.total += n
+        self.length = self.n_valid
+
+    def decode(self, queries: torch.Tensor, gqa_factor: int, scale: float = 1.0, *,
+               out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+               ws: Optional[torch.Tensor] = None, s=None) -> torch.Tensor:
+        """Decode attention over the window (the ring's filled slots)."""
+        return sdpa_int4(queries, *self.tensors(), gqa_factor, scale, 0, s, n_tokens=self.n_valid,
+                         out=out, out_dtype=out_dtype, ws=ws)
+
+    def decode_step(self, queries: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+                    gqa_factor: int, scale: float = 1.0, *, out: Optional[torch.Tensor] = None,
+                    out_dtype: Optional[torch.dtype] = None, ws: Optional[torch.Tensor] = None,
+                    s=None) -> torch.Tensor:
+        """One decode step in one launch: the new token's K/V (1, Hkv, D) go to
+        slot total % window inside the decode kernel, then attention over the
+        window."""
+        squeeze = queries.dim() == 2
+        q = queries.unsqueeze(0) if squeeze else queries
+        B, H, D = q.shape
+        slot = self.total % self.window
+        n = min(self.total + 1, self.window)
+        od = out_dtype or q.dtype
+        if out is None:
+            out = torch.empty(B, H, D, dtype=od, device=q.device)
+        nbytes = sdpa_int4_workspace_size(B, H, self.num_kv_heads, D, n, 0)
+        if ws is None:
+            ws = workspace(q.device, nbytes, s)
+        qc, kc, vc = q.contiguous(), k_new.contiguous(), v_new.contiguous()
+        _check(load_library().tq_sdpa_int4_append_at(
+            _ptr(qc), _dt(q), _ptr(kc), _ptr(vc), _dt(kc), *[_ptr(c) for c in self.tensors()],
+            _dt(self.k_scales), int(gqa_factor), float(scale), B, self.num_kv_heads, D, n,
+            self.capacity, slot, _ptr(out), _dt(out), _ptr(ws), 0 if ws is None else ws.numel(),
+            _stream(s)))
+        self.total += 1
+        self.length = self.n_valid
+        return out[0] if squeeze else out
+
+    def chronological(self):
+        """The six cache arrays cut to the valid tokens, oldest first (the
+        reference's layout, (1, Hkv, n, ...)), as new tensors."""
+        n = self.n_valid
+        start = self.total % self.window if self.total > self.window else 0
+        idx = (torch.arange(n, device=self.k_quant.device) + start) % self.window
+        return tuple(t.index_select(2, idx) for t in self.tensors())
 
 
 def quantize_append(k_new: torch.Tensor, v_new: torch.Tensor, k_quant, k_scales, k_biases,

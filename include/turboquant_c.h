@@ -144,6 +144,22 @@ TQ_API int tq_sdpa_int4_append(const void* queries, tq_dtype q_dtype, const void
                         const int32_t* seq_lens, void* out, tq_dtype out_dtype, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* The same step for a ring cache (a sliding-window layer whose capacity is
+ * its window): the new row goes to `slot` (its position modulo the capacity)
+ * and attention runs over slots [0, n_tokens) unmasked -- a ring of the last
+ * W tokens holds exactly the tokens the window rule (N-1-t) < W keeps
+ * (lib/turboquant.metal:779), and attention does not depend on their order.
+ * Replaces the engine's quantize + concatenate + front trim of sliding
+ * layers (engine/gemma4_multilayer.cpp:228-249). batch 1 or a slot shared by
+ * every sequence; slot < n_tokens <= capacity. */
+TQ_API int tq_sdpa_int4_append_at(const void* queries, tq_dtype q_dtype, const void* k_new,
+                           const void* v_new, tq_dtype new_dtype, uint32_t* k_quant,
+                           void* k_scales, void* k_biases, uint32_t* v_quant, void* v_scales,
+                           void* v_biases, tq_dtype sb_dtype, int gqa_factor, float scale,
+                           int batch, int num_kv_heads, int head_dim, int n_tokens, int capacity,
+                           int slot, void* out, tq_dtype out_dtype, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* Sequence-split shard of decode attention: this cache holds global token
  * positions [token_offset, token_offset + n_local) of a sequence whose total
  * length is n_total (all sequences of the batch share both). Writes the

@@ -909,4 +909,34 @@ TQ_API int tq_sdpa_int4_multi(const void* queries, tq_dtype q_dtype, const uint3
   return TQ_OK;
 }
 
+// The two config-2 cases under their own names (the multi-query kernel serves
+// both): batched decode of n_seq single queries over one shared cache, and a
+// causal prefill chunk of n_q queries whose first sits at position pos0.
+TQ_API int tq_sdpa_int4_batched(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,
+                                const void* k_scales, const void* k_biases,
+                                const uint32_t* v_quant, const void* v_scales,
+                                const void* v_biases, tq_dtype sb_dtype, int gqa_factor,
+                                float scale, int sliding_window, int num_kv_heads, int head_dim,
+                                int n_seq, int n_tokens, int capacity, void* out,
+                                tq_dtype out_dtype, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  return tq_sdpa_int4_multi(queries, q_dtype, k_quant, k_scales, k_biases, v_quant, v_scales,
+                            v_biases, sb_dtype, gqa_factor, scale, sliding_window, num_kv_heads,
+                            head_dim, n_seq, n_tokens, capacity, 0, 0, out, out_dtype, workspace,
+                            workspace_bytes, stream);
+}
+
+TQ_API int tq_sdpa_int4_prefill(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,
+                                const void* k_scales, const void* k_biases,
+                                const uint32_t* v_quant, const void* v_scales,
+                                const void* v_biases, tq_dtype sb_dtype, int gqa_factor,
+                                float scale, int sliding_window, int num_kv_heads, int head_dim,
+                                int n_q, int pos0, int capacity, void* out, tq_dtype out_dtype,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  return tq_sdpa_int4_multi(queries, q_dtype, k_quant, k_scales, k_biases, v_quant, v_scales,
+                            v_biases, sb_dtype, gqa_factor, scale, sliding_window, num_kv_heads,
+                            head_dim, n_q, pos0 + n_q, capacity, 1, pos0, out, out_dtype, workspace,
+                            workspace_bytes, stream);
+}
+
 }  // extern "C"

@@ -171,8 +171,8 @@ array pad_tokens(const array& a, int cap, cudaStream_t s) {
   return p;
 }
 
-array decode(const array& q, const array* c, int batch, int hkv, int D, int n_tokens, int cap,
-             int gqa, float scale, int window, cudaStream_t s, const char* where) {
+array decode_impl(const array& q, const array* c, int batch, int hkv, int D, int n_tokens, int cap,
+                  int gqa, float scale, int window, cudaStream_t s, const char* where) {
   const int H = hkv * gqa;
   array out({batch, H, D}, q.dtype(), s);
   const size_t ws_bytes = tq_sdpa_int4_workspace_size(batch, H, hkv, D, n_tokens, window);
@@ -202,8 +202,8 @@ array sdpa_int4(const array& queries, const array& k_quant, const array& k_scale
   array padded[6];
   const int cap = (n + 3) / 4 * 4;
   for (int i = 0; i < 6; ++i) padded[i] = cap == n ? *src[i] : pad_tokens(*src[i], cap, s);
-  array out = decode(queries, padded, 1, hkv, D, n, cap, gqa_factor, scale, sliding_window, s,
-                     "sdpa_int4");
+  array out = decode_impl(queries, padded, 1, hkv, D, n, cap, gqa_factor, scale, sliding_window, s,
+                          "sdpa_int4");
   return out.reshape({queries.shape(0), D});
 }
 
@@ -246,8 +246,8 @@ array KVCache::sdpa(const array& queries, int gqa_factor, float scale, int slidi
   const array* c[6] = {&k_quant, &k_scales, &k_biases, &v_quant, &v_scales, &v_biases};
   array cc[6];
   for (int i = 0; i < 6; ++i) cc[i] = *c[i];
-  array out = decode(queries, cc, batch_, num_kv_heads_, head_dim_, length_, capacity_, gqa_factor,
-                     scale, sliding_window, s, "KVCache::sdpa");
+  array out = decode_impl(queries, cc, batch_, num_kv_heads_, head_dim_, length_, capacity_,
+                          gqa_factor, scale, sliding_window, s, "KVCache::sdpa");
   return flat ? out.reshape({queries.shape(0), head_dim_}) : out;
 }
 
@@ -313,6 +313,86 @@ array KVCache::sdpa_multi(const array& queries, int gqa_factor, float scale, int
                           Dtype out_dtype, cudaStream_t s) {
   return multi(*this, queries, length_, gqa_factor, scale, sliding_window, false, 0, out_dtype, s,
                "KVCache::sdpa_multi");
+}
+
+// ---- RingKVCache ---------------------------------------------------------------
+
+RingKVCache::RingKVCache(int num_kv_heads, int head_dim, int window, Dtype scales_dtype,
+                         cudaStream_t s)
+    : cache(1, num_kv_heads, head_dim, window, scales_dtype, s), window_(window) {}
+
+void RingKVCache::append(const array& k_new, const array& v_new, cudaStream_t s) {
+  const char* where = "RingKVCache::append";
+  if (k_new.ndim() != 3 && k_new.ndim() != 4) raise(where, "k_new must be 3-D or 4-D");
+  const int hkv = cache.k_quant.shape(1), D = cache.k_quant.shape(3) * 8;
+  const int n = k_new.shape(-2);
+  if (k_new.shape(-1) != D || k_new.size() != static_cast<size_t>(hkv) * n * D ||
+      v_new.size() != k_new.size())
+    raise(where, "k_new/v_new must be (1, Hkv, n, D)");
+  const size_t isz = itemsize(k_new.dtype());
+  const size_t row = static_cast<size_t>(D) * isz;  // bytes per (head, token)
+  // only the last `window` tokens can survive
+  const int skip = n > window_ ? n - window_ : 0;
+  total_ += skip;
+  int done = skip;
+  while (done < n) {
+    const int slot = static_cast<int>(total_ % window_);
+    const int m = std::min(n - done, window_ - slot);
+    // tokens [done, done + m) of every head -> a contiguous (1, Hkv, m, D) copy
+    array kc({1, hkv, m, D}, k_new.dtype(), s), vc({1, hkv, m, D}, v_new.dtype(), s);
+    for (const auto& [dst, src] : {std::pair<array*, const array*>{&kc, &k_new}, {&vc, &v_new}})
+      check_cuda(cudaMemcpy2DAsync(dst->data(), m * row,
+                                   static_cast<const char*>(src->data()) + done * row, n * row,
+                                   m * row, hkv, cudaMemcpyDeviceToDevice, s),
+                 where);
+    check(tq_quantize_append(kc.data(), vc.data(), to_c(k_new.dtype(), where), 1, hkv, D, m,
+                             static_cast<uint32_t*>(cache.k_quant.data()), cache.k_scales.data(),
+                             cache.k_biases.data(), static_cast<uint32_t*>(cache.v_quant.data()),
+                             cache.v_scales.data(), cache.v_biases.data(),
+                             to_c(cache.k_scales.dtype(), where), window_, slot, nullptr, s),
+          where);
+    total_ += m;
+    done += m;
+  }
+}
+
+array RingKVCache::decode(const array& queries, int gqa_factor, float scale, cudaStream_t s) {
+  const bool flat = queries.ndim() == 2;
+  const array* c[6] = {&cache.k_quant, &cache.k_scales, &cache.k_biases,
+                       &cache.v_quant, &cache.v_scales, &cache.v_biases};
+  array cc[6];
+  for (int i = 0; i < 6; ++i) cc[i] = *c[i];
+  const int D = cache.k_quant.shape(3) * 8;
+  array out = decode_impl(queries, cc, 1, cache.k_quant.shape(1), D, n_valid(), window_,
+                          gqa_factor, scale, 0, s, "RingKVCache::decode");
+  return flat ? out.reshape({queries.shape(0), D}) : out;
+}
+
+array RingKVCache::decode_step(const array& queries, const array& k_new, const array& v_new,
+                               int gqa_factor, float scale, cudaStream_t s) {
+  const char* where = "RingKVCache::decode_step";
+  const bool flat = queries.ndim() == 2;
+  const int hkv = cache.k_quant.shape(1), D = cache.k_quant.shape(3) * 8;
+  if (k_new.size() != static_cast<size_t>(hkv) * D || v_new.size() != k_new.size())
+    raise(where, "k_new/v_new must be (1, Hkv, D)");
+  const int H = hkv * gqa_factor;
+  const int slot = static_cast<int>(total_ % window_);
+  const int n = total_ + 1 < window_ ? static_cast<int>(total_ + 1) : window_;
+  array out({1, H, D}, queries.dtype(), s);
+  const size_t ws_bytes = tq_sdpa_int4_workspace_size(1, H, hkv, D, n, 0);
+  array ws_arr = ws_bytes ? workspace(ws_bytes, s) : array();
+  check(tq_sdpa_int4_append_at(queries.data(), to_c(queries.dtype(), where), k_new.data(),
+                               v_new.data(), to_c(k_new.dtype(), where),
+                               static_cast<uint32_t*>(cache.k_quant.data()), cache.k_scales.data(),
+                               cache.k_biases.data(), static_cast<uint32_t*>(cache.v_quant.data()),
+                               cache.v_scales.data(), cache.v_biases.data(),
+                               to_c(cache.k_scales.dtype(), where), gqa_factor, scale, 1, hkv, D,
+                               n, window_, slot, out.data(), to_c(queries.dtype(), where),
+                               ws_bytes ? ws_arr.data() : nullptr, ws_bytes ? ws_arr.nbytes() : 0,
+                               s),
+        where);
+  total_ += 1;
+  return flat ? out.reshape({queries.shape(0), D}) : out;
 }
 
 // ---- sequence split ---------------------------------------------------------

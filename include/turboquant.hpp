@@ -150,6 +150,30 @@ class TQ_CXX_API KVCache {
   int batch_, num_kv_heads_, head_dim_, capacity_, length_ = 0;
 };
 
+// ---- sliding-window layer as a ring of `window` slots (batch 1) ---------------
+// Token t lives in slot t % window, so the cache holds exactly the last
+// `window` tokens -- the set the window rule keeps -- with no copy (the
+// engine concatenates and trims the front, engine/gemma4_multilayer.cpp:228-249).
+// Attention is order-independent: decode runs over the filled slots unmasked.
+class TQ_CXX_API RingKVCache {
+ public:
+  RingKVCache(int num_kv_heads, int head_dim, int window, Dtype scales_dtype = Dtype::float16,
+              cudaStream_t s = nullptr);
+  // k_new, v_new: (1, Hkv, n, D) or (Hkv, n, D); wraps; only the last `window` survive.
+  void append(const array& k_new, const array& v_new, cudaStream_t s = nullptr);
+  array decode(const array& queries, int gqa_factor, float scale = 1.0f, cudaStream_t s = nullptr);
+  // One launch: the step's K/V (1, Hkv, D) go to slot total % window, then attention.
+  array decode_step(const array& queries, const array& k_new, const array& v_new, int gqa_factor,
+                    float scale = 1.0f, cudaStream_t s = nullptr);
+  int n_valid() const { return total_ < window_ ? static_cast<int>(total_) : window_; }
+  long long total() const { return total_; }
+  KVCache cache;
+
+ private:
+  int window_;
+  long long total_ = 0;
+};
+
 // ---- sequence split across GPUs ----------------------------------------------
 // Partial softmax state of a contiguous token shard [token_offset, +n_local) of a
 // sequence of n_total tokens: (B, H*(D+2)) fp32 = o (H, D) unnormalised, then

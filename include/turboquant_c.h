@@ -257,6 +257,29 @@ TQ_API int tq_sdpa_int4_multi(const void* queries, tq_dtype q_dtype, const uint3
                               int pos0, void* out, tq_dtype out_dtype, void* workspace,
                               size_t workspace_bytes, void* stream);
 
+/* Config 2's two cases by name (same kernel as tq_sdpa_int4_multi):
+ *   tq_sdpa_int4_batched: n_seq sequences x 1 query each over one shared
+ *     cache of n_tokens tokens (every query at the last position);
+ *   tq_sdpa_int4_prefill: causal chunk of n_q queries at positions
+ *     pos0 .. pos0 + n_q - 1 whose K/V are already in the cache (slots up to
+ *     pos0 + n_q - 1); query i sees tokens t <= pos0 + i (and the window).
+ * Workspace: tq_sdpa_int4_multi_workspace_size(n, ..., n_tokens). */
+TQ_API int tq_sdpa_int4_batched(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,
+                                const void* k_scales, const void* k_biases,
+                                const uint32_t* v_quant, const void* v_scales,
+                                const void* v_biases, tq_dtype sb_dtype, int gqa_factor,
+                                float scale, int sliding_window, int num_kv_heads, int head_dim,
+                                int n_seq, int n_tokens, int capacity, void* out,
+                                tq_dtype out_dtype, void* workspace, size_t workspace_bytes,
+                                void* stream);
+TQ_API int tq_sdpa_int4_prefill(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,
+                                const void* k_scales, const void* k_biases,
+                                const uint32_t* v_quant, const void* v_scales,
+                                const void* v_biases, tq_dtype sb_dtype, int gqa_factor,
+                                float scale, int sliding_window, int num_kv_heads, int head_dim,
+                                int n_q, int pos0, int capacity, void* out, tq_dtype out_dtype,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- PolarQuant + QJL compressed keys ----------------------------------------
  * Blocks of `block` values (16, 32, 64 or 128; head_dim a multiple of 128) are
  * encoded as in lib/turboquant.metal:8-98 (polar_fused_quantize), generalised

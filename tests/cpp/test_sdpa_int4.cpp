@@ -247,6 +247,50 @@ int main() {
     }
   }
 
+  {  // RingKVCache (sliding layer): == window over a linear cache; fused step == append + decode
+    const int nh = 32, nkv = 16, hd = 128, W = 512, n = 1500;
+    std::mt19937 rng(4);
+    auto K = normal(static_cast<size_t>(nkv) * n * hd, rng), V = normal(K.size(), rng);
+    auto Qh = normal(static_cast<size_t>(nh) * hd, rng);
+    auto Q = array::from_host(Qh.data(), {nh, hd}, Dtype::float32);
+    turboquant::RingKVCache ring(nkv, hd, W), ring2(nkv, hd, W);
+    turboquant::KVCache lin(1, nkv, hd, 1504);
+    auto Ka = array::from_host(K.data(), {1, nkv, n, hd}, Dtype::float32);
+    auto Va = array::from_host(V.data(), {1, nkv, n, hd}, Dtype::float32);
+    ring.append(Ka, Va);
+    lin.append(Ka, Va);
+    auto a = ring.decode(Q, nh / nkv).to_vector<float>();
+    auto b = lin.sdpa(Q, nh / nkv, 1.0f, W).to_vector<float>();
+    double md = 0;
+    for (size_t i = 0; i < a.size(); ++i) md = std::max(md, static_cast<double>(std::fabs(a[i] - b[i])));
+    const bool same_window = md <= 2e-5 && ring.n_valid() == W && ring.total() == n;
+    printf("%-28s max_diff=%.3e %s\n", "RingKVCache == window", md, same_window ? "PASS" : "FAIL");
+    ok &= same_window;
+    // fused ring step vs append + decode, across the wrap
+    std::vector<float> kt(static_cast<size_t>(nkv) * hd), vt(kt.size());
+    ring2.append(array::from_host(K.data(), {1, nkv, 300, hd}, Dtype::float32).reshape({1, nkv, 300, hd}),
+                 array::from_host(V.data(), {1, nkv, 300, hd}, Dtype::float32));
+    turboquant::RingKVCache ring3(nkv, hd, W);
+    ring3.append(array::from_host(K.data(), {1, nkv, 300, hd}, Dtype::float32),
+                 array::from_host(V.data(), {1, nkv, 300, hd}, Dtype::float32));
+    bool steps_equal = true;
+    for (int t = 0; t < 400; ++t) {
+      for (int h = 0; h < nkv; ++h)
+        for (int d = 0; d < hd; ++d) {
+          kt[static_cast<size_t>(h) * hd + d] = static_cast<float>(std::sin(0.01 * (t + 1) * (h + 1) + d));
+          vt[static_cast<size_t>(h) * hd + d] = static_cast<float>(std::cos(0.02 * (t + 1) + h - d));
+        }
+      auto kn = array::from_host(kt.data(), {1, nkv, hd}, Dtype::float32);
+      auto vn = array::from_host(vt.data(), {1, nkv, hd}, Dtype::float32);
+      auto f = ring2.decode_step(Q, kn, vn, nh / nkv).to_vector<float>();
+      ring3.append(kn.reshape({1, nkv, 1, hd}), vn.reshape({1, nkv, 1, hd}));
+      auto g = ring3.decode(Q, nh / nkv).to_vector<float>();
+      steps_equal &= f == g;
+    }
+    printf("%-28s %s\n", "RingKVCache decode_step", steps_equal ? "PASS" : "FAIL");
+    ok &= steps_equal;
+  }
+
   printf("\n%s\n", ok ? "PASS" : "FAIL");
   return ok ? 0 : 1;
 }

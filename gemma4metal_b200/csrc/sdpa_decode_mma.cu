@@ -230,10 +230,21 @@ __device__ __forceinline__ float wsum(float v) {
 }
 
 // Token order of a warp's 16-token block: A-operand row r of the K-side mma
-// and V-side contraction index k < 8 both stand for token sigma(r) (bits 1
-// and 2 swapped); with the 64B/128B TMA swizzle this makes the K-side 8-byte
-// row reads and the ldmatrix reads bank-conflict free. sigma is an involution.
-__device__ __forceinline__ int sigma8(int r) { return (r & 1) | ((r & 2) << 1) | ((r & 4) >> 1); }
+// and V-side contraction index k < 8 both stand for token sigma(r) (any
+// permutation works for the math, both sides use the same one). It is chosen
+// so the K-side 8-byte row reads are bank-conflict free: a half-warp (rows
+// 4p..4p+3, 4 lanes each) reads 16-byte chunk (word chunk) ^ swizzle(row), so
+// the four rows' swizzle values must differ in their chunk-pair bits --
+//   D = 128 (SWIZZLE_64B, 64-byte rows, swizzle (row >> 1) & 3): bits 1 and 2
+//   swapped; D = 256 (SWIZZLE_128B, 128-byte rows, swizzle row & 7): a 3-bit
+//   rotation, so rows 0..3 map to 0,2,4,6 and rows 4..7 to 1,3,5,7.
+// The ldmatrix reads (8 rows of one chunk) are conflict free for any
+// permutation.
+template <int D>
+__device__ __forceinline__ int sigma8(int r) {
+  if constexpr (D == 128) return (r & 1) | ((r & 2) << 1) | ((r & 4) >> 1);
+  return ((r << 1) & 6) | (r >> 2);
+}
 
 template <int D, int G, typename SB, bool QSPLIT>
 __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
@@ -487,7 +498,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   // plus 16*bt rows
   const int wt0 = warp * 16 * TB;
   constexpr int BROW = 16 * Lyt::ROWB;  // bytes of 16 code rows
-  const int sr = sigma8(r);
+  const int sr = sigma8<D>(r);
   int trow[NTK];              // tile rows of the item tokens (block 0)
 #pragma unroll
   for (int f = 0; f < NTK; ++f) trow[f] = wt0 + sr + 8 * (G <= 2 ? (c & 1) : f);
@@ -504,7 +515,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     const int mi = lane >> 3, mrow = lane & 7;
 #pragma unroll
     for (int q2 = 0; q2 < NCH / 2; ++q2)
-      voff[q2] = swz<D>(wt0 + 8 * (mi & 1) + sigma8(mrow), 2 * q2 + (mi >> 1));
+      voff[q2] = swz<D>(wt0 + 8 * (mi & 1) + sigma8<D>(mrow), 2 * q2 + (mi >> 1));
   }
 
   // O[dim][col] accumulators: chunk kk (32 dims), sub-tile s2; rows r / r+8 =

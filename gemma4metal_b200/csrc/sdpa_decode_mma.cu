@@ -1,19 +1,21 @@
 // Tensor-core (warp-level mma.sync m16n8k16, f16 x f16 -> f32) split-KV decode
 // attention straight from the int4 KV cache. Same contract and partial/merge
 // format as decode_kernel in sdpa_decode.cu; this variant exists because the
-// CUDA-core kernel is instruction-bound at GQA >= 2, and a
-// single mma consumes 128 (K side) or 256 (V side) 4-bit codes per warp
-// instruction.
+// CUDA-core kernel is instruction-bound at GQA >= 2 (about 2.6 instructions
+// per 4-bit code; 54 us at 32K tokens against 20 us here), and a single mma
+// consumes 128 (K side) or 256 (V side) 4-bit codes per warp instruction.
 //
 // Data path per CTA (grid = splits x KV-head groups x batch):
 //   * producer warp: 2-D TMA tensor copies of the K and V code tiles
 //     (64 tokens x D/2 bytes, 64B/128B-swizzled so the K-side row reads and
 //     the transposed ldmatrix reads below are bank-conflict free) + 1-D bulk
-//     copies of the fp16 scales/biases, into a 5-stage full/empty mbarrier
-//     ring (64-token boxes; a CTA's token range is a whole number of boxes);
+//     copies of the fp16 scales/biases, into a full/empty mbarrier ring of 3
+//     (D=128) or 5 (D=256) stages (64-token boxes; a CTA's token range is a
+//     whole number of boxes);
 //   * 4 consumer warps, 32 (D=128) or 16 (D=256) tokens of every tile each
 //     (as independent 16-token blocks), each warp with its own online-softmax
-//     state (no CTA barrier in the main loop), 2 CTAs per SM:
+//     state (no CTA barrier in the main loop), 3 (D=128) or 2 (D=256) CTAs
+//     per SM:
 //       K side:  S[token][col] = sum_d (1 + c[token][d]/64) * q[col][d] as
 //                mma(A = codes, rows = tokens; B = q). The codes become exact
 //                fp16 values 1 + c/64 with one LOP3 (and at most one shift)
@@ -33,6 +35,12 @@
 //   * the warp states are LSE-merged in shared memory; the CTA writes its
 //     split partial and the last CTA of the KV head merges all splits with an
 //     online LSE merge, 8 splits' loads in flight per thread.
+//   * launch: programmatic dependent launch; barrier init, tensor-map and L2
+//     prefetches (queries, the CTA's first tiles) run before the dependency
+//     wait; a fused quantize-on-append (tq_sdpa_int4_append) has consumer
+//     warp 0 (and 1 at D=256) write the step's K/V row while the first tiles
+//     stream in, and the producer issues the tile holding it only after that
+//     write is fenced.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -53,8 +61,8 @@ constexpr int kChunk = 64;  // tokens per TMA box; splits are whole chunks
 
 // Per head_dim: W consumer warps (+ one TMA producer warp), each taking TB
 // independent 16-token blocks of every tile (two interleaved dependency
-// chains at D=128); a stage of W*TB*16 tokens (18 KB at D=128 and at D=256),
-// 2 CTAs per SM.
+// chains at D=128); a stage of W*TB*16 tokens (18 KB at D=128 and at D=256);
+// 3 CTAs per SM at D=128, 2 at D=256 (registers).
 template <int D>
 struct MCfg {
   static constexpr int W = 4;

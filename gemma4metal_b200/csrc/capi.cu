@@ -100,6 +100,12 @@ int visible_max(int n_tokens, int window) {
 }  // namespace
 
 namespace tq {
+
+bool& pdl_launches() {
+  static thread_local bool on = true;
+  return on;
+}
+
 uint32_t* device_error_word() { return device_error_ptr(); }
 
 void set_last_error(const char* fmt, ...) {

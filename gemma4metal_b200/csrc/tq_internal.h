@@ -96,9 +96,16 @@ cudaError_t launch_lse_merge(const float* parts, int n_parts, int B, int H, int 
 
 int device_sm_count(int device);
 
+// Whether launch_pdl sets programmatic stream serialization on this thread
+// (true by default). A host decode step turns it off while it captures its
+// graph, where the kernel follows a host-to-device copy: there is no
+// preceding kernel whose tail a launch could overlap.
+bool& pdl_launches();
+
 // Launch `kernel` with programmatic stream serialization, so it may start
 // while the preceding kernel of the stream finishes (the kernel must call
-// pdl_wait() before it touches global memory).
+// pdl_wait() before it touches global memory; without the attribute that
+// wait returns at once).
 template <typename... K, typename... A>
 cudaError_t launch_pdl(void (*kernel)(K...), dim3 grid, dim3 block, size_t smem,
                        cudaStream_t stream, A&&... args) {
@@ -111,7 +118,7 @@ cudaError_t launch_pdl(void (*kernel)(K...), dim3 grid, dim3 block, size_t smem,
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_launches() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
 }
 

@@ -90,6 +90,14 @@ def _register_extra(L) -> None:
     L.tq_compressed_sdpa_workspace_size.argtypes = [I, I, I, I]
     L.tq_compressed_sdpa.argtypes = [P, I, P, P, P, P, P, I, I, I, I, I, I, P, F, P, P, P, I, P, I,
                                      P, SZ, P]
+    L.tq_decode_step_create.argtypes = [I, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I,
+                                        ctypes.POINTER(ctypes.c_void_p)]
+    L.tq_decode_step_buffers.argtypes = [P, ctypes.POINTER(ctypes.c_void_p),
+                                         ctypes.POINTER(ctypes.c_void_p),
+                                         ctypes.POINTER(ctypes.c_void_p),
+                                         ctypes.POINTER(ctypes.c_void_p)]
+    L.tq_decode_step_run.argtypes = [P, P, P, P, ctypes.POINTER(ctypes.c_int32), P]
+    L.tq_decode_step_destroy.argtypes = [P]
     L.tq_sdpa_int4_multi_workspace_size.restype = SZ
     L.tq_sdpa_int4_multi_workspace_size.argtypes = [I, I, I, I, I]
     L.tq_sdpa_int4_multi.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, I, I, P, I,
@@ -399,6 +407,113 @@ def sdpa_int4_append(queries: torch.Tensor, k_new: torch.Tensor, v_new: torch.Te
         int(gqa_factor), float(scale), int(sliding_window), B, Hkv, D, n, cap, _ptr(seq_lens),
         _ptr(out), _dt(out), _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
     return out[0] if squeeze else out
+
+
+class HostDecodeStep:
+    """One decode step of one layer from host memory in one call
+    (tq_decode_step_*): the host's query and new K/V row go up, the new row is
+    quantized into slot n - 1 of `cache` inside the decode kernel, and the
+    output comes back to the host -- one CUDA graph launch (H2D copy, fused
+    step kernel, D2H copy) and one synchronisation per step. The reference's
+    engine makes the same per-token call against unified memory
+    (engine/gemma4_multilayer.cpp:222-236).
+
+    Staging buffers (pinned host tensors) are `queries` (B, H, D), `k_new` and
+    `v_new` (B, Hkv, D) and `out` (B, H, D): write inputs there and pass
+    nothing to run() to skip the host copies, or pass host tensors/arrays."""
+
+    def __init__(self, cache: KVCache, num_heads: int, scale: float = 1.0,
+                 sliding_window: int = 0, q_dtype: torch.dtype = torch.float16,
+                 new_dtype: torch.dtype = torch.float16,
+                 out_dtype: Optional[torch.dtype] = None):
+        if isinstance(cache, RingKVCache):
+            raise ValueError("a ring cache appends at slot total % window: use RingKVCache.decode_step")
+        if num_heads % cache.num_kv_heads:
+            raise ValueError("num_heads must be a multiple of the cache's kv heads")
+        L = load_library()
+        self._L = L
+        self.cache = cache  # the step holds the cache's device pointers
+        self.batch, self.num_heads = cache.batch, num_heads
+        od = out_dtype or q_dtype
+        handle = ctypes.c_void_p()
+        _check(L.tq_decode_step_create(
+            _DT[q_dtype], _DT[new_dtype], *[_ptr(t) for t in cache.tensors()], _dt(cache.k_scales),
+            num_heads // cache.num_kv_heads, float(scale), int(sliding_window), cache.batch,
+            cache.num_kv_heads, cache.head_dim, cache.capacity, _DT[od], ctypes.byref(handle)))
+        self._h = handle
+        ptrs = [ctypes.c_void_p() for _ in range(4)]
+        _check(L.tq_decode_step_buffers(handle, *[ctypes.byref(x) for x in ptrs]))
+        B, H, Hkv, D = cache.batch, num_heads, cache.num_kv_heads, cache.head_dim
+
+        def pinned(ptr, shape, dt):
+            n = 1
+            for x in shape:
+                n *= x
+            nbytes = n * torch.empty((), dtype=dt).element_size()
+            raw = (ctypes.c_char * nbytes).from_address(ptr.value)
+            return torch.frombuffer(raw, dtype=torch.uint8).view(dt).view(shape)
+
+        self.queries = pinned(ptrs[0], (B, H, D), q_dtype)
+        self.k_new = pinned(ptrs[1], (B, Hkv, D), new_dtype)
+        self.v_new = pinned(ptrs[2], (B, Hkv, D), new_dtype)
+        self.out = pinned(ptrs[3], (B, H, D), od)
+        self._n = (ctypes.c_int32 * B)()
+        self._like = (self.queries, self.k_new, self.v_new, self.out)
+        self._seen = [None] * 4
+        self._seen_ptr = [0] * 4
+
+    def _host_ptr(self, x, slot: int):
+        """Host address of x, checked against staging buffer `slot` (a torch
+        tensor already checked in this slot, at the same address, is not
+        checked again)."""
+        if x is None:
+            return None
+        like = self._like[slot]
+        if isinstance(x, torch.Tensor):
+            p = x.data_ptr()
+            if x is self._seen[slot] and p == self._seen_ptr[slot]:
+                return p
+            if x.is_cuda or x.dtype != like.dtype or x.numel() != like.numel() or not x.is_contiguous():
+                raise ValueError(f"expected a contiguous host tensor of {like.numel()} {like.dtype}")
+            self._seen[slot], self._seen_ptr[slot] = x, p
+            return p
+        import numpy as np  # numpy arrays of the same element size and count
+        if not isinstance(x, np.ndarray) or not x.flags["C_CONTIGUOUS"] or \
+                x.size != like.numel() or x.itemsize != like.element_size():
+            raise ValueError(f"expected a C-contiguous array of {like.numel()} {like.dtype}")
+        return x.ctypes.data
+
+    def run(self, n_tokens, queries=None, k_new=None, v_new=None, out=None):
+        """One step: n_tokens (int, or one per sequence) counts the tokens
+        including the new one. Returns `out` (default: the staging tensor,
+        overwritten by the next step)."""
+        if isinstance(n_tokens, int):
+            for b in range(self.batch):
+                self._n[b] = n_tokens
+            n_max = n_tokens
+        else:
+            if len(n_tokens) != self.batch:
+                raise ValueError("n_tokens needs one entry per sequence")
+            for b, n in enumerate(n_tokens):
+                self._n[b] = int(n)
+            n_max = max(int(n) for n in n_tokens)
+        _check(self._L.tq_decode_step_run(
+            self._h, self._host_ptr(queries, 0), self._host_ptr(k_new, 1),
+            self._host_ptr(v_new, 2), self._n, self._host_ptr(out, 3)))
+        if n_max > self.cache.length:
+            self.cache.length = n_max
+        return self.out if out is None else out
+
+    def close(self) -> None:
+        if self._h:
+            _check(self._L.tq_decode_step_destroy(self._h))
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def sdpa_int4_partial(queries: torch.Tensor, k_quant, k_scales, k_biases, v_quant, v_scales,

@@ -384,6 +384,40 @@ TQ_API int tq_polar_pack4(const uint8_t* angles, int64_t n_blocks, int block, ui
 TQ_API int tq_precondition(const void* x, tq_dtype x_dtype, int64_t rows, int head_dim,
                            const float* P, int transpose_p, float* y, void* stream);
 
+/* ---- one decode step from host memory -------------------------------------
+ * The per-token call of a decoding loop with host buffers on both sides, as
+ * the reference's engine makes it against unified memory
+ * (engine/gemma4_multilayer.cpp:222-236: quantize the new K/V row, append it,
+ * sdpa_int4 over the cache, read the output). A step object binds one layer's
+ * cache (B, Hkv, capacity, ...) and owns mapped pinned staging, a device copy
+ * of the inputs, a workspace, a stream and a CUDA graph of two kernels:
+ *   gather [queries | k_new | v_new | n_tokens] from the mapped staging
+ *   -> tq_sdpa_int4_append (programmatic dependent launch) writing the output
+ *      into the mapped output staging,
+ * captured on the first run and again whenever the decode plan for the
+ * longest sequence changes (about every splits x 64 tokens). Unlike the rest
+ * of this ABI it allocates (at create, and the workspace on a re-plan).
+ *
+ * tq_decode_step_run: n_tokens[b] (host, batch entries) counts sequence b's
+ * tokens including the new one (1 <= n <= capacity); the new row goes to slot
+ * n - 1. queries (B, H, D) in q_dtype, k_new/v_new (B, Hkv, D) in new_dtype and
+ * out (B, H, D) in out_dtype are HOST pointers; each may be the staging buffer
+ * tq_decode_step_buffers returns (no host copy then) and out may be NULL (the
+ * result stays in the staging buffer). The call returns once the output is on
+ * the host. Not thread-safe per object; objects on one device may run from
+ * different threads. tq_decode_step_destroy releases everything (NULL: no-op). */
+typedef struct tq_decode_step tq_decode_step;
+TQ_API int tq_decode_step_create(tq_dtype q_dtype, tq_dtype new_dtype, uint32_t* k_quant,
+                                 void* k_scales, void* k_biases, uint32_t* v_quant, void* v_scales,
+                                 void* v_biases, tq_dtype sb_dtype, int gqa_factor, float scale,
+                                 int sliding_window, int batch, int num_kv_heads, int head_dim,
+                                 int capacity, tq_dtype out_dtype, tq_decode_step** step);
+TQ_API int tq_decode_step_buffers(tq_decode_step* step, void** queries, void** k_new,
+                                  void** v_new, void** out);
+TQ_API int tq_decode_step_run(tq_decode_step* step, const void* queries, const void* k_new,
+                              const void* v_new, const int32_t* n_tokens, void* out);
+TQ_API int tq_decode_step_destroy(tq_decode_step* step);
+
 /* Read and clear the device error word that kernels set when a bounded wait
  * gives up (0 = no error). Synchronises `stream`. */
 TQ_API int tq_device_error(void* stream, uint32_t* code);

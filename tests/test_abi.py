@@ -89,3 +89,31 @@ def test_cpp_header_compiles():
     r = subprocess.run(["g++", "-std=c++17", "-fsyntax-only", "-I" + INC,
                         "-I/usr/local/cuda/include", src], capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+def test_decode_step_host_validation():
+    """tq_decode_step_* reject bad arguments before touching the GPU."""
+    from gemma4metal_b200.turboquant import load_library
+    L = load_library()
+    fake = ctypes.c_void_p(0x1000)
+    h = ctypes.c_void_p()
+    # head_dim 96 unsupported
+    rc = L.tq_decode_step_create(1, 1, fake, fake, fake, fake, fake, fake, 1, 2, 1.0, 0, 1, 16,
+                                 96, 64, 1, ctypes.byref(h))
+    assert rc == 2 and b"head_dim" in L.tq_last_error() and not h.value
+    # capacity not a multiple of 4
+    rc = L.tq_decode_step_create(1, 1, fake, fake, fake, fake, fake, fake, 1, 2, 1.0, 0, 1, 16,
+                                 128, 62, 1, ctypes.byref(h))
+    assert rc == 1 and b"sizes" in L.tq_last_error()
+    # null cache pointer, bad scale dtype
+    rc = L.tq_decode_step_create(1, 1, None, fake, fake, fake, fake, fake, 1, 2, 1.0, 0, 1, 16,
+                                 128, 64, 1, ctypes.byref(h))
+    assert rc == 1 and b"null" in L.tq_last_error()
+    rc = L.tq_decode_step_create(1, 1, fake, fake, fake, fake, fake, fake, 2, 2, 1.0, 0, 1, 16,
+                                 128, 64, 1, ctypes.byref(h))
+    assert rc == 1 and b"dtype" in L.tq_last_error()
+    # null step object
+    n = (ctypes.c_int32 * 1)(5)
+    assert L.tq_decode_step_run(None, None, None, None, n, None) == 1
+    assert L.tq_decode_step_buffers(None, None, None, None, None) == 1
+    assert L.tq_decode_step_destroy(None) == 0

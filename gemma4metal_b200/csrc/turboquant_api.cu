@@ -368,6 +368,48 @@ array RingKVCache::decode(const array& queries, int gqa_factor, float scale, cud
   return flat ? out.reshape({queries.shape(0), D}) : out;
 }
 
+HostDecodeStep::HostDecodeStep(KVCache& cache, int num_heads, float scale, int sliding_window,
+                               Dtype q_dtype, Dtype new_dtype, Dtype out_dtype)
+    : cache_(&cache), n_(cache.batch_) {
+  const char* where = "HostDecodeStep";
+  if (num_heads < 1 || num_heads % cache.num_kv_heads_) raise(where, "num_heads must be a multiple of the kv heads");
+  check(tq_decode_step_create(to_c(q_dtype, where), to_c(new_dtype, where),
+                              static_cast<uint32_t*>(cache.k_quant.data()), cache.k_scales.data(),
+                              cache.k_biases.data(), static_cast<uint32_t*>(cache.v_quant.data()),
+                              cache.v_scales.data(), cache.v_biases.data(),
+                              to_c(cache.k_scales.dtype(), where), num_heads / cache.num_kv_heads_,
+                              scale, sliding_window, cache.batch_, cache.num_kv_heads_,
+                              cache.head_dim_, cache.capacity_, to_c(out_dtype, where), &step_),
+        where);
+}
+
+HostDecodeStep::~HostDecodeStep() { tq_decode_step_destroy(step_); }
+
+void HostDecodeStep::run(const void* queries, const void* k_new, const void* v_new, void* out,
+                         const int32_t* n_tokens) {
+  const char* where = "HostDecodeStep::run";
+  int n_max = 0;
+  for (int b = 0; b < cache_->batch_; ++b) {
+    n_[b] = n_tokens ? n_tokens[b] : cache_->length_ + 1;
+    if (n_[b] > n_max) n_max = n_[b];
+  }
+  check(tq_decode_step_run(step_, queries, k_new, v_new, n_.data(), out), where);
+  if (n_max > cache_->length_) cache_->length_ = n_max;
+}
+
+namespace {
+void* step_buffer(tq_decode_step* s, int which) {
+  void* p[4] = {nullptr, nullptr, nullptr, nullptr};
+  check(tq_decode_step_buffers(s, &p[0], &p[1], &p[2], &p[3]), "HostDecodeStep");
+  return p[which];
+}
+}  // namespace
+
+void* HostDecodeStep::queries() const { return step_buffer(step_, 0); }
+void* HostDecodeStep::k_new() const { return step_buffer(step_, 1); }
+void* HostDecodeStep::v_new() const { return step_buffer(step_, 2); }
+void* HostDecodeStep::out() const { return step_buffer(step_, 3); }
+
 array RingKVCache::decode_step(const array& queries, const array& k_new, const array& v_new,
                                int gqa_factor, float scale, cudaStream_t s) {
   const char* where = "RingKVCache::decode_step";

@@ -40,6 +40,8 @@
 #define TQ_CXX_API
 #endif
 
+struct tq_decode_step;  // turboquant_c.h
+
 namespace turboquant {
 
 enum class Dtype : int { float32 = 0, float16 = 1, bfloat16 = 2, uint32 = 3, int32 = 4, uint8 = 5 };
@@ -147,7 +149,39 @@ class TQ_CXX_API KVCache {
   array k_quant, k_scales, k_biases, v_quant, v_scales, v_biases;
 
  private:
+  friend class HostDecodeStep;
   int batch_, num_kv_heads_, head_dim_, capacity_, length_ = 0;
+};
+
+// ---- one decode step from host memory (tq_decode_step_*) ---------------------
+// The engine's per-token call (engine/gemma4_multilayer.cpp:222-236) with the
+// query, the new K/V row and the output in host memory: one CUDA graph launch
+// (gather kernel + fused append/decode kernel writing the output into mapped
+// host memory) and one synchronisation per run(). Binds `cache` (which must
+// outlive the step) and advances its length.
+class TQ_CXX_API HostDecodeStep {
+ public:
+  HostDecodeStep(KVCache& cache, int num_heads, float scale = 1.0f, int sliding_window = 0,
+                 Dtype q_dtype = Dtype::float16, Dtype new_dtype = Dtype::float16,
+                 Dtype out_dtype = Dtype::float16);
+  ~HostDecodeStep();
+  HostDecodeStep(const HostDecodeStep&) = delete;
+  HostDecodeStep& operator=(const HostDecodeStep&) = delete;
+  // queries (B, H, D), k_new/v_new (B, Hkv, D), out (B, H, D): host pointers
+  // (or the staging buffers below; out may be nullptr). n_tokens: per-sequence
+  // token counts including the new token (nullptr: cache length + 1 for all).
+  void run(const void* queries, const void* k_new, const void* v_new, void* out,
+           const int32_t* n_tokens = nullptr);
+  // Pinned staging buffers: inputs written here need no host copy in run().
+  void* queries() const;
+  void* k_new() const;
+  void* v_new() const;
+  void* out() const;
+
+ private:
+  KVCache* cache_;
+  tq_decode_step* step_ = nullptr;
+  std::vector<int32_t> n_;
 };
 
 // ---- sliding-window layer as a ring of `window` slots (batch 1) ---------------

@@ -11,6 +11,7 @@
 // Exit code 0 = pass.
 #include <cmath>
 #include <cstdio>
+#include <cstring>
 #include <random>
 #include <vector>
 
@@ -245,6 +246,42 @@ int main() {
       snprintf(name, sizeof(name), "prefill_chunk query %d", i);
       ok &= compare(name, gi, sdpa_ref(qi, kd, vd, nh, nkv, n, hd, 1.0f, 0));
     }
+  }
+
+  {  // HostDecodeStep (host buffers, one graph per step) == KVCache::decode_step, step by step
+    const int nh = 32, nkv = 16, hd = 128, n0 = 700, cap = 800;
+    std::mt19937 rng(3);
+    auto K0 = normal(static_cast<size_t>(nkv) * n0 * hd, rng), V0 = normal(K0.size(), rng);
+    turboquant::KVCache a(1, nkv, hd, cap), b(1, nkv, hd, cap);
+    for (auto* c : {&a, &b})
+      c->append(array::from_host(K0.data(), {1, nkv, n0, hd}, Dtype::float32),
+                array::from_host(V0.data(), {1, nkv, n0, hd}, Dtype::float32));
+    turboquant::HostDecodeStep step(a, nh, 1.0f, 0, Dtype::float32, Dtype::float32, Dtype::float32);
+    bool same = true;
+    std::vector<float> out(static_cast<size_t>(nh) * hd);
+    for (int t = 0; t < 5; ++t) {
+      auto q = normal(static_cast<size_t>(nh) * hd, rng);
+      auto kn = normal(static_cast<size_t>(nkv) * hd, rng), vn = normal(kn.size(), rng);
+      if (t % 2) {  // through the staging buffers
+        memcpy(step.queries(), q.data(), q.size() * sizeof(float));
+        memcpy(step.k_new(), kn.data(), kn.size() * sizeof(float));
+        memcpy(step.v_new(), vn.data(), vn.size() * sizeof(float));
+        step.run(step.queries(), step.k_new(), step.v_new(), out.data());
+      } else {
+        step.run(q.data(), kn.data(), vn.data(), out.data());
+      }
+      auto want = b.decode_step(array::from_host(q.data(), {1, nh, hd}, Dtype::float32),
+                                array::from_host(kn.data(), {1, nkv, hd}, Dtype::float32),
+                                array::from_host(vn.data(), {1, nkv, hd}, Dtype::float32), nh / nkv)
+                      .to_vector<float>();
+      same &= want == out;
+    }
+    same &= a.length() == n0 + 5 && b.length() == n0 + 5;
+    auto ka = a.k_quant.to_vector<uint32_t>(), kb = b.k_quant.to_vector<uint32_t>();
+    auto va = a.v_scales.to_vector<uint16_t>(), vb = b.v_scales.to_vector<uint16_t>();
+    same &= ka == kb && va == vb;
+    printf("%-28s %s\n", "HostDecodeStep == decode_step", same ? "PASS" : "FAIL");
+    ok &= same;
   }
 
   {  // RingKVCache (sliding layer): == window over a linear cache; fused step == append + decode

@@ -32,9 +32,12 @@
 //                transposed by ldmatrix.trans, B = w hi/lo); the constant part
 //                is removed with corr = sum_t p*(b - 64*s) at the end:
 //                out = 64*O + corr.
+//   * the query rows are loaded by the consumer threads (plain 16-byte loads
+//     into shared memory), so the producer's first TMA issues do not queue
+//     behind them;
 //   * the warp states are LSE-merged in shared memory; the CTA writes its
 //     split partial and the last CTA of the KV head merges all splits with an
-//     online LSE merge, 8 splits' loads in flight per thread.
+//     online LSE merge, 16 (G <= 2) or 8 splits' loads in flight per thread.
 //   * launch: programmatic dependent launch; barrier init, tensor-map and L2
 //     prefetches (queries, the CTA's first tiles) run before the dependency
 //     wait; a fused quantize-on-append (tq_sdpa_int4_append) has consumer
@@ -88,9 +91,9 @@ struct MLayout {
   static constexpr int STAGES = MCfg<D>::STAGES * STAGE;
   // full[MCfg<D>::STAGES], empty[MCfg<D>::STAGES], q, appended token written
   static constexpr int BAR = STAGES;
-  static constexpr int FLAG = BAR + ((2 * MCfg<D>::STAGES + 2) * 8 + 15) / 16 * 16;
+  static constexpr int FLAG = BAR + ((2 * MCfg<D>::STAGES + 1) * 8 + 15) / 16 * 16;
   static constexpr int QB = FLAG + 16;                   // the CTA's G query rows (<= f32)
-  static_assert(QB % 16 == 0, "bulk-copy destination must be 16-byte aligned");
+  static_assert(QB % 16 == 0, "the query rows are stored as 16-byte words");
   static constexpr int BYTES = QB + G * D * 4 + 1024;    // + alignment slack
   // end-of-range combine: per warp m, l, corr[NG], o[D] for G heads
   static constexpr int WST = G * (2 + NG + D);
@@ -280,8 +283,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Lyt::BAR);
   uint64_t* empty = full + MCfg<D>::STAGES;
-  uint64_t* qbar = empty + MCfg<D>::STAGES;
-  uint64_t* nbar = qbar + 1;  // the appended token is in global memory (fused append)
+  uint64_t* nbar = empty + MCfg<D>::STAGES;  // the appended token is in global memory (fused append)
   int* s_flag = reinterpret_cast<int*>(smem + Lyt::FLAG);
 
   const int tid = threadIdx.x;
@@ -320,7 +322,6 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], W);
     }
-    mbar_init(qbar, 1);
     mbar_init(nbar, D / 128);  // one arrival per writer warp of a fused append
     fence_barrier_init();
   }
@@ -372,13 +373,6 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   // ======================= producer warp ========================================
   if (warp == W) {
     if (lane == 0) {
-      // the CTA's query rows: one bulk copy, shared through shared memory
-      const int qel = p.q_dtype == kF32 ? 4 : 2;
-      const uint32_t qbytes = static_cast<uint32_t>(G * D * qel);
-      mbar_arrive_expect_tx(qbar, qbytes);
-      bulk_g2s(smem + Lyt::QB,
-               static_cast<const unsigned char*>(p.q) + (static_cast<long long>(b) * p.H + h0) * D * qel,
-               qbytes, qbar, policy_evict_last());
       const uint64_t pol = policy_evict_first();
       const int t_hi4 = (t_hi + 3) & ~3;
       const SB* ksb = reinterpret_cast<const SB*>(p.ks) + tok_base * NG;
@@ -420,6 +414,17 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   }
 
   // ======================= consumer warps =======================================
+  // the CTA's query rows (0.5-8 KB) into shared memory by the consumer
+  // threads' own loads: the producer's first TMA issues are not queued
+  // behind a copy of them
+  {
+    const int qel = p.q_dtype == kF32 ? 4 : 2;
+    const int qwords = G * D * qel / 16;
+    const uint4* qsrc = reinterpret_cast<const uint4*>(
+        static_cast<const unsigned char*>(p.q) + (static_cast<long long>(b) * p.H + h0) * D * qel);
+    uint4* qdst = reinterpret_cast<uint4*>(smem + Lyt::QB);
+    for (int i = tid; i < qwords; i += W * 32) qdst[i] = qsrc[i];
+  }
   // fused append: lane = one packed word of the K row (first D/8 writer
   // threads) or of the V row, quantized exactly as quantize_rows_kernel does
   if (has_new && warp < NWW) {
@@ -453,7 +458,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   uint32_t qb[NG][4][2];
   uint32_t qb_lo[QSPLIT ? NG : 1][4][2];
   float qs_col[NG];  // sum of q_hb over each group (identical in the 4 lanes of row r)
-  mbar_wait_bounded(qbar, 0, p.err);
+  consumers_sync<W>();  // the query rows are in shared memory
   {
     const int hb = r / P;
     const int phib = r % P;
@@ -945,12 +950,15 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   if (s_flag[0] == 0) return;
 
   // float4 items (head, 4 dims); the splits of an item are spread over R
-  // thread subsets, each running an online log-sum-exp merge with 8 splits'
-  // (m, l, o) loads in flight per step, then the R states are combined.
+  // thread subsets, each running an online log-sum-exp merge with kML splits'
+  // (m, l, o) loads in flight per step (16 at G <= 2: one round of L2 loads
+  // for up to 32 splits; 8 above, where 16 would spill), then the R states
+  // are combined.
   const int S_ = p.splits;
   const long long base = unit * S_ * G;
   constexpr int NI = G * D / 4;
   constexpr int R = NI >= NTH ? 1 : NTH / NI;
+  constexpr int kML = G <= 2 ? 16 : 8;
   float2* mst = reinterpret_cast<float2*>(smem);           // [R][NI] (M, L)
   float4* ost = reinterpret_cast<float4*>(smem + R * NI * 8);  // [R][NI] o
   for (int it = tid; it < NI * R; it += NTH) {
@@ -960,11 +968,11 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     const float* mw = p.ws_ml + (base + g) * 2;
     float M = -INFINITY, L = 0.0f;
     float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int s0 = sub; s0 < S_; s0 += 8 * R) {
-      float2 ml[8];
-      float4 v[8];
+    for (int s0 = sub; s0 < S_; s0 += kML * R) {
+      float2 ml[kML];
+      float4 v[kML];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < kML; ++j) {
         const int s = s0 + j * R;
         if (s < S_) {
           ml[j] = __ldcg(reinterpret_cast<const float2*>(mw + static_cast<long long>(s) * G * 2));
@@ -976,7 +984,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
       }
       float mb = M;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) mb = fmaxf(mb, ml[j].x);
+      for (int j = 0; j < kML; ++j) mb = fmaxf(mb, ml[j].x);
       const float sc = M == -INFINITY ? 0.0f : fast_exp2(M - mb);
       L *= sc;
       a.x *= sc;
@@ -984,7 +992,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
       a.z *= sc;
       a.w *= sc;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < kML; ++j) {
         const float e = ml[j].x == -INFINITY ? 0.0f : fast_exp2(ml[j].x - mb);
         L = fmaf(e, ml[j].y, L);
         a.x = fmaf(e, v[j].x, a.x);

@@ -6,13 +6,13 @@
 //
 // CTA = 128 query rows of one KV head (row = (query, GQA head) pair; TMEM lane
 // = row), one CTA per SM, warp-specialized, tiles of 64 tokens:
-//   * unpack warps (2, one token per thread) turn the int4 codes into exact
-//     fp16 in shared memory: K as 1 + c/64 (UMMA canonical K-major, 128B
-//     swizzle, one 8 KB region per 64-dim scale group), V as (c - 8)/64
-//     (MN-major); per-token score terms and value terms go beside them. K and
-//     V have two stages each, with separate lifetimes (K(i) is free once the
-//     softmax of tile i is done, V(i) once PV(i) is), and the next tile's
-//     codes wait in registers.
+//   * unpack warps (2 for K, 2 for V, one token per thread) turn the int4
+//     codes into exact fp16 in shared memory: K as 1 + c/64 (UMMA canonical
+//     K-major, 128B swizzle, one 8 KB region per 64-dim scale group), V as
+//     (c - 8)/64 (MN-major); per-token score terms and value terms go beside
+//     them. K and V have two stages each, with separate lifetimes (K(i) is
+//     free once the softmax of tile i is done, V(i) once PV(i) is), each
+//     paced by its own warps, and the next tile's codes wait in registers.
 //   * the MMA warp (one thread) issues S'_g = Q_g K_g'^T for tile i into one of
 //     two TMEM S buffers, then PV for tile i-1 into the TMEM O accumulator,
 //     committing each group to an mbarrier -- the tensor pipe works on the
@@ -46,18 +46,23 @@ namespace {
 constexpr int kRows = 128;     // query rows per CTA (TMEM lanes)
 constexpr int kTok = 64;       // tokens per tile
 constexpr int kD = 128;        // head_dim (two 64-dim scale groups)
-// warp roles: warp 0 issues the MMAs (and owns TMEM); warps 1-2 unpack the
-// codes (one token per thread); warps 3-10 run the softmax, two threads per
-// query row (warp % 4 is the TMEM lane quarter a warp may access, so each
-// quarter has one warp per half). 11 warps = at most 3 per SM sub-partition,
-// which leaves 168 registers per thread. (Four threads per row, 19 warps at
-// 96 registers, measured slower: more per-thread fixed cost per tile.)
+// warp roles: warp 0 issues the MMAs (and owns TMEM); warps 1-2 unpack the K
+// codes and warps 3-4 the V codes (one token per thread); warps 5-12 run the
+// softmax, two threads per query row (warp % 4 is the TMEM lane quarter a
+// warp may access, so each quarter has one warp per half). A warp runs on
+// sub-partition warp % 4, so every sub-partition holds two softmax warps and
+// one unpack warp: with two unpack warps (K and V work each), the softmax
+// warps sharing their sub-partitions finished each tile 20% after the others
+// and set the tile period (prefill 251 -> 232 us with four). 13 warps = 4 on
+// one sub-partition, which caps registers at 128 per thread. (Four threads
+// per row, 19 warps at 96 registers, measured slower: more per-thread fixed
+// cost per tile.)
 constexpr int kMmaWarp = 0;
-constexpr int kUnpackBase = 1, kUnpackWarps = 2;
+constexpr int kUnpackBase = 1, kUnpackWarps = 4;
 constexpr int kSoftmaxWarps = 8;
 constexpr int kSoftmaxBase = (kUnpackBase + kUnpackWarps) * 32;
 constexpr int kSoftmaxThreads = kSoftmaxWarps * 32;
-constexpr int kThreads = kSoftmaxBase + kSoftmaxThreads;  // 352
+constexpr int kThreads = kSoftmaxBase + kSoftmaxThreads;  // 416
 constexpr int kTmemCols = 512; // S[0], S[1] (2 groups x 64 tokens each), O (2 groups x 64 dims)
 // an MMA group finishes in microseconds; give up (and record the error) after
 // ~10 ms of SM clocks so a wait that cannot complete still ends the kernel
@@ -318,8 +323,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
   }
   if (tid == 0) {
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&k_full[b], kUnpackWarps);
-      mbar_init(&v_full[b], kUnpackWarps);
+      mbar_init(&k_full[b], kUnpackWarps / 2);
+      mbar_init(&v_full[b], kUnpackWarps / 2);
       mbar_init(&s_full[b], 1);
       mbar_init(&s_free[b], kSoftmaxWarps);
       mbar_init(&p_full[b], kSoftmaxWarps);
@@ -459,20 +464,18 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
   // unpacked; K as exact fp16 1 + c/64 (K-major), V as exact fp16 (c - 8)/64
   // (MN-major), both 128B-swizzled; the token's score and value terms.
   if (warp >= kUnpackBase && warp < kUnpackBase + kUnpackWarps) {
-    const int ptok = tid - kUnpackBase * 32;
-    uint4 kf[4], vf[4];
-    uint32_t sr[8] = {0u, 0u, 0u, 0u, 0u, 0u, 0u, 0u};  // ks, kb, vs, vb (raw: 1 or 2 words each)
+    // warps 1-2 unpack K (paced by the softmax), warps 3-4 V (paced by PV)
+    const bool vside = warp >= kUnpackBase + kUnpackWarps / 2;
+    const int ptok = tid - (kUnpackBase + (vside ? kUnpackWarps / 2 : 0)) * 32;
+    uint4 cf[4];
+    uint32_t sr[4] = {0u, 0u, 0u, 0u};  // scale, bias (raw: 1 or 2 words each)
     int tcur = t_end;  // the tile held in registers
     auto prefetch = [&](int t0) {
       const int t = t0 + ptok;
       const long long rowi = tok_base + (t < t_end ? t : t0);
-      const uint4* kp = reinterpret_cast<const uint4*>(p.kq + rowi * (kD / 8));
-      const uint4* vp = reinterpret_cast<const uint4*>(p.vq + rowi * (kD / 8));
+      const uint4* cp = reinterpret_cast<const uint4*>((vside ? p.vq : p.kq) + rowi * (kD / 8));
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        kf[k] = kp[k];
-        vf[k] = vp[k];
-      }
+      for (int k = 0; k < 4; ++k) cf[k] = cp[k];
       auto load_pair = [&](const void* src, int k) {
         if (p.sb_f32) {
           const uint2 a = reinterpret_cast<const uint2*>(src)[rowi];
@@ -482,13 +485,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
           sr[2 * k] = reinterpret_cast<const uint32_t*>(src)[rowi];
         }
       };
-      load_pair(p.ks, 0);
-      load_pair(p.kb, 1);
-      load_pair(p.vs, 2);
-      load_pair(p.vb, 3);
+      load_pair(vside ? p.vs : p.ks, 0);
+      load_pair(vside ? p.vb : p.kb, 1);
       tcur = t0;
     };
-    // the scale-group pair of a raw f16x2 or f32 pair
     auto pair = [&](int k) {
       if (p.sb_f32) return make_float2(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1]));
       return __half22float2(*reinterpret_cast<const __half2*>(&sr[2 * k]));
@@ -518,32 +518,35 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
       const int t0 = tcur;
       unsigned char* stage = smem + b * TLayout::KVB;
       const bool tv = t0 + ptok < t_end;
-      const float2 ks = pair(0), kb = pair(1), vs = pair(2), vb = pair(3);
-      // K(i) and the score terms: the stage is free once softmax(i-2) is done
-      if (i >= 2) mbar_wait_bounded(&p_full[b], (use - 1) & 1u, p.err, kWaitBudget);
-#pragma unroll
-      for (int g = 0; g < 2; ++g)
-        unpack_codes(kf[2 * g], kf[2 * g + 1], stage + TLayout::K + g * kTok * 128, false);
-      const float qs = p.qscale;
-      float4* ts = reinterpret_cast<float4*>(smem + TLayout::TS + b * kTok * 16);
-      ts[ptok] = tv ? make_float4(64.0f * ks.x * qs, 64.0f * ks.y * qs, (kb.x - 64.0f * ks.x) * qs,
-                                  (kb.y - 64.0f * ks.y) * qs)
-                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&k_full[b]);
-      // V(i) and the value terms: free once PV(i-2) is done
-      if (i >= 2) mbar_wait_bounded(&pv_done[b], (use - 1) & 1u, p.err, kWaitBudget);
-#pragma unroll
-      for (int g = 0; g < 2; ++g)
-        unpack_codes(vf[2 * g], vf[2 * g + 1], stage + TLayout::V + g * kTok * 128, true);
-      float4* tvv = reinterpret_cast<float4*>(smem + TLayout::TV + b * kTok * 16);
-      tvv[ptok] = tv ? make_float4(vs.x, vs.y, fmaf(8.0f, vs.x, vb.x), fmaf(8.0f, vs.y, vb.y))
-                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-      if (i + 1 < n_tiles) prefetch(t0 + kTok);
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&v_full[b]);
+      const float2 sc2 = pair(0), bc2 = pair(1);
+      const uint4 c0 = cf[0], c1 = cf[1], c2 = cf[2], c3 = cf[3];
+      if (!vside) {
+        // K(i) and the score terms: the stage is free once softmax(i-2) is done
+        if (i >= 2) mbar_wait_bounded(&p_full[b], (use - 1) & 1u, p.err, kWaitBudget);
+        if (i + 1 < n_tiles) prefetch(t0 + kTok);
+        unpack_codes(c0, c1, stage + TLayout::K, false);
+        unpack_codes(c2, c3, stage + TLayout::K + kTok * 128, false);
+        const float qs = p.qscale;
+        float4* ts = reinterpret_cast<float4*>(smem + TLayout::TS + b * kTok * 16);
+        ts[ptok] = tv ? make_float4(64.0f * sc2.x * qs, 64.0f * sc2.y * qs, (bc2.x - 64.0f * sc2.x) * qs,
+                                    (bc2.y - 64.0f * sc2.y) * qs)
+                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&k_full[b]);
+      } else {
+        // V(i) and the value terms: free once PV(i-2) is done
+        if (i >= 2) mbar_wait_bounded(&pv_done[b], (use - 1) & 1u, p.err, kWaitBudget);
+        if (i + 1 < n_tiles) prefetch(t0 + kTok);
+        unpack_codes(c0, c1, stage + TLayout::V, true);
+        unpack_codes(c2, c3, stage + TLayout::V + kTok * 128, true);
+        float4* tvv = reinterpret_cast<float4*>(smem + TLayout::TV + b * kTok * 16);
+        tvv[ptok] = tv ? make_float4(sc2.x, sc2.y, fmaf(8.0f, sc2.x, bc2.x), fmaf(8.0f, sc2.y, bc2.y))
+                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&v_full[b]);
+      }
     }
   }
 

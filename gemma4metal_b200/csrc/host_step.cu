@@ -91,8 +91,9 @@ void release(tq_decode_step* s) {
   delete s;
 }
 
-// Capture the three nodes for a step whose longest sequence has n tokens and
-// install them as the executable graph (update in place when one exists).
+// Capture the step's two kernels (gather, fused append + decode) for a step
+// whose longest sequence has n tokens and install them as the executable
+// graph (update in place when one exists).
 int capture(tq_decode_step* s, int n, const tq::DecodePlan& pl) {
   if (pl.ws_bytes > s->ws_bytes) {
     if (s->ws) cudaFree(s->ws);

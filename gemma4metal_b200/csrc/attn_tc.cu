@@ -370,15 +370,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
     const long long qb = (static_cast<long long>(qi) * p.H + h) * kD + hf * 64;
     const bool qvec = (reinterpret_cast<uintptr_t>(p.q) & 15u) == 0;
     float qsum = 0.0f;
+    // all eight 8-dim chunks are loaded before any is converted and stored,
+    // so their global-memory latencies overlap
+    float qx[8][8];
 #pragma unroll
     for (int ch = 0; ch < 8; ++ch) {
-      float x[8];
       if (row_ok) {
-        load8(p.q, qb + ch * 8, p.q_dtype, qvec, x);
+        load8(p.q, qb + ch * 8, p.q_dtype, qvec, qx[ch]);
       } else {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) x[e] = 0.0f;
+        for (int e = 0; e < 8; ++e) qx[ch][e] = 0.0f;
       }
+    }
+#pragma unroll
+    for (int ch = 0; ch < 8; ++ch) {
+      const float* x = qx[ch];
       // fp16 copies (exact for fp16 and bf16 inputs in range)
       __half2 hh[4], hl[4];
 #pragma unroll
@@ -402,6 +408,36 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
     s_mx[xs] = qsum;
     fence_async_smem();
   }
+  // ---- unpack warps' state: warps 1-2 unpack K (paced by the softmax), warps
+  // 3-4 V (paced by PV), thread = token ptok; the codes and scales of the tile
+  // being unpacked next wait in registers. The first tile's are requested
+  // before the set-up barrier, while the softmax warps stage the queries.
+  const bool is_unpack = warp >= kUnpackBase && warp < kUnpackBase + kUnpackWarps;
+  const bool vside = warp >= kUnpackBase + kUnpackWarps / 2;
+  const int ptok = tid - (kUnpackBase + (vside ? kUnpackWarps / 2 : 0)) * 32;
+  uint4 cf[4];
+  uint32_t sr[4] = {0u, 0u, 0u, 0u};  // scale, bias (raw: 1 or 2 words each)
+  int tcur = t_end;  // the tile held in registers
+  auto prefetch = [&](int t0) {
+    const int t = t0 + ptok;
+    const long long rowi = tok_base + (t < t_end ? t : t0);
+    const uint4* cp = reinterpret_cast<const uint4*>((vside ? p.vq : p.kq) + rowi * (kD / 8));
+#pragma unroll
+    for (int k = 0; k < 4; ++k) cf[k] = cp[k];
+    auto load_pair = [&](const void* src, int k) {
+      if (p.sb_f32) {
+        const uint2 a = reinterpret_cast<const uint2*>(src)[rowi];
+        sr[2 * k] = a.x;
+        sr[2 * k + 1] = a.y;
+      } else {
+        sr[2 * k] = reinterpret_cast<const uint32_t*>(src)[rowi];
+      }
+    };
+    load_pair(vside ? p.vs : p.ks, 0);
+    load_pair(vside ? p.vb : p.kb, 1);
+    tcur = t0;
+  };
+  if (is_unpack && n_tiles > 0) prefetch(t_begin);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -459,36 +495,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
   }
 
   // ======================= unpack warps =========================================
-  // Thread = token ptok: 64 B of K codes and 64 B of V codes per tile (both
-  // scale groups), the next tile's held in registers while this one is
-  // unpacked; K as exact fp16 1 + c/64 (K-major), V as exact fp16 (c - 8)/64
-  // (MN-major), both 128B-swizzled; the token's score and value terms.
-  if (warp >= kUnpackBase && warp < kUnpackBase + kUnpackWarps) {
-    // warps 1-2 unpack K (paced by the softmax), warps 3-4 V (paced by PV)
-    const bool vside = warp >= kUnpackBase + kUnpackWarps / 2;
-    const int ptok = tid - (kUnpackBase + (vside ? kUnpackWarps / 2 : 0)) * 32;
-    uint4 cf[4];
-    uint32_t sr[4] = {0u, 0u, 0u, 0u};  // scale, bias (raw: 1 or 2 words each)
-    int tcur = t_end;  // the tile held in registers
-    auto prefetch = [&](int t0) {
-      const int t = t0 + ptok;
-      const long long rowi = tok_base + (t < t_end ? t : t0);
-      const uint4* cp = reinterpret_cast<const uint4*>((vside ? p.vq : p.kq) + rowi * (kD / 8));
-#pragma unroll
-      for (int k = 0; k < 4; ++k) cf[k] = cp[k];
-      auto load_pair = [&](const void* src, int k) {
-        if (p.sb_f32) {
-          const uint2 a = reinterpret_cast<const uint2*>(src)[rowi];
-          sr[2 * k] = a.x;
-          sr[2 * k + 1] = a.y;
-        } else {
-          sr[2 * k] = reinterpret_cast<const uint32_t*>(src)[rowi];
-        }
-      };
-      load_pair(vside ? p.vs : p.ks, 0);
-      load_pair(vside ? p.vb : p.kb, 1);
-      tcur = t0;
-    };
+  // Thread = token ptok: 64 B of K (warps 1-2) or V (warps 3-4) codes per
+  // tile (both scale groups), the next tile's held in registers while this
+  // one is unpacked; K as exact fp16 1 + c/64 (K-major), V as exact fp16
+  // (c - 8)/64 (MN-major), both 128B-swizzled; the token's score or value
+  // terms.
+  if (is_unpack) {
     auto pair = [&](int k) {
       if (p.sb_f32) return make_float2(__uint_as_float(sr[2 * k]), __uint_as_float(sr[2 * k + 1]));
       return __half22float2(*reinterpret_cast<const __half2*>(&sr[2 * k]));
@@ -511,7 +523,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
         *reinterpret_cast<uint4*>(dst + sw128(ptok, ch)) = o;
       }
     };
-    if (n_tiles > 0) prefetch(t_begin);
     for (int i = 0; i < n_tiles; ++i) {
       const int b = i & 1;
       const uint32_t use = static_cast<uint32_t>(i >> 1);

@@ -766,25 +766,55 @@ __global__ void __launch_bounds__(256) attn_tc_merge_kernel(const TCParams p, in
   const int S = p.splits;
   const long long sstride = static_cast<long long>(kD + 2) * kRows;
   const float* base = p.ws + unit * S * sstride + rb + lane;
-  // unrolled so the loads of several splits are in flight at once (a
-  // load -> max -> load chain would pay one memory latency per split)
-  float M = -INFINITY;
-#pragma unroll 8
-  for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(base + s * sstride + kD * kRows));
+  // Up to kOne splits: every split's (m, l, o) is loaded in one round (one
+  // L2 latency), then merged from registers; the batched case's 9 splits
+  // took 7.1 us of merge with the max loaded first and the rest after it,
+  // 3.2 us this way. More splits: the max first, then the rest, both
+  // loops unrolled so several splits' loads are in flight.
   float L = 0.0f, acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
   const float* col = base + (db + 4 * warp) * kRows;
+  constexpr int kOne = 16;
+  if (S <= kOne) {
+    float ms[kOne], ls[kOne], v[kOne][4];
+#pragma unroll
+    for (int s = 0; s < kOne; ++s) {
+      if (s < S) {
+        const float* ps = base + s * sstride;
+        ms[s] = __ldcg(ps + kD * kRows);
+        ls[s] = __ldcg(ps + (kD + 1) * kRows);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[s][k] = __ldcg(col + s * sstride + k * kRows);
+      }
+    }
+    float M = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < kOne; ++s) if (s < S) M = fmaxf(M, ms[s]);
+#pragma unroll
+    for (int s = 0; s < kOne; ++s) {
+      if (s < S) {
+        const float e = (ms[s] == -INFINITY) ? 0.0f : fast_exp2(ms[s] - M);
+        L = fmaf(e, ls[s], L);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc[k] = fmaf(e, v[s][k], acc[k]);
+      }
+    }
+  } else {
+    float M = -INFINITY;
 #pragma unroll 8
-  for (int s = 0; s < S; ++s) {
-    const float* ps = base + s * sstride;
-    const float ms = __ldcg(ps + kD * kRows);
-    const float ls = __ldcg(ps + (kD + 1) * kRows);
-    float v[4];
+    for (int s = 0; s < S; ++s) M = fmaxf(M, __ldcg(base + s * sstride + kD * kRows));
+#pragma unroll 8
+    for (int s = 0; s < S; ++s) {
+      const float* ps = base + s * sstride;
+      const float ms = __ldcg(ps + kD * kRows);
+      const float ls = __ldcg(ps + (kD + 1) * kRows);
+      float v[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) v[k] = __ldcg(col + s * sstride + k * kRows);
-    const float e = (ms == -INFINITY) ? 0.0f : fast_exp2(ms - M);
-    L = fmaf(e, ls, L);
+      for (int k = 0; k < 4; ++k) v[k] = __ldcg(col + s * sstride + k * kRows);
+      const float e = (ms == -INFINITY) ? 0.0f : fast_exp2(ms - M);
+      L = fmaf(e, ls, L);
 #pragma unroll
-    for (int k = 0; k < 4; ++k) acc[k] = fmaf(e, v[k], acc[k]);
+      for (int k = 0; k < 4; ++k) acc[k] = fmaf(e, v[k], acc[k]);
+    }
   }
   const float invL = L > 0.0f ? 1.0f / L : 0.0f;
 #pragma unroll

@@ -48,6 +48,7 @@ def run(nq, H, Hkv, N, causal, pos0, window, qdt, odt, seed=7, sb=np.float16):
     (50, 24, 8, 900, True, 850, 0, "bf16", "f32"),       # GQA 3: a query's heads straddle row tiles
     (16, 32, 4, 3000, True, 2984, 1000, "bf16", "f32"),  # GQA 8, window cuts into the splits
     (64, 32, 16, 1000, True, 936, 0, "f32", "f32"),      # f32 queries (fp16 hi + lo on the MMA)
+    (4, 8, 1, 8192, False, 0, 0, "bf16", "f32"),         # one row tile: 64 splits, two-round merge
 ])
 def test_multi_parity(nq, H, Hkv, N, causal, pos0, window, qdt, odt):
     out, ref = run(nq, H, Hkv, N, causal, pos0, window, qdt, odt)

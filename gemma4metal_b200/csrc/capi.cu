@@ -69,6 +69,7 @@ struct DecodeCommon {
   const void* v_new = nullptr;
   int new_dtype = 0;
   int new_slot = -1;
+  const int32_t* new_slots = nullptr;  // device, one slot per sequence (overrides new_slot)
 };
 
 int validate_decode(const DecodeCommon& c, const char* fn) {
@@ -270,14 +271,18 @@ static int decode_common(const DecodeCommon& c, const char* fn, const int32_t* s
       a.v_new = c.v_new;
       a.new_dtype = c.new_dtype;
       a.new_slot = c.new_slot;
+      a.new_slots = c.new_slots;
     } else {
+      // slot: per-sequence device slots, else the given slot, else n - 1
+      // (seq_lens[b] - 1 per sequence)
       const bool at_slot = c.new_slot >= 0;
+      const int32_t* positions = c.new_slots ? c.new_slots : at_slot ? nullptr : seq_lens;
       e = tq::launch_quantize_rows(
           c.k_new, c.new_dtype, static_cast<long long>(c.B) * c.Hkv, c.D, 1, c.Hkv, c.capacity,
-          a.bstride_tok, at_slot ? c.new_slot : c.n_tokens - 1, at_slot ? nullptr : seq_lens,
+          a.bstride_tok, at_slot ? c.new_slot : c.n_tokens - 1, positions,
           const_cast<uint32_t*>(c.kq), const_cast<void*>(c.ks), const_cast<void*>(c.kb), c.sb_dtype,
           static_cast<cudaStream_t>(stream), c.v_new, const_cast<uint32_t*>(c.vq),
-          const_cast<void*>(c.vs), const_cast<void*>(c.vb), -1);
+          const_cast<void*>(c.vs), const_cast<void*>(c.vb), c.new_slots ? 0 : -1);
       if (e != cudaSuccess) return cuda_fail(e, fn);
     }
   }
@@ -312,8 +317,9 @@ static int append_common(const void* queries, tq_dtype q_dtype, const void* k_ne
                          void* k_biases, uint32_t* v_quant, void* v_scales, void* v_biases,
                          tq_dtype sb_dtype, int gqa_factor, float scale, int sliding_window,
                          int batch, int num_kv_heads, int head_dim, int n_tokens, int capacity,
-                         const int32_t* seq_lens, int slot, void* out, tq_dtype out_dtype,
-                         void* workspace, size_t workspace_bytes, void* stream) {
+                         const int32_t* seq_lens, int slot, const int32_t* slots, void* out,
+                         tq_dtype out_dtype, void* workspace, size_t workspace_bytes,
+                         void* stream) {
   t_err.clear();
   if (!out) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: null out");
   if (!valid_dtype(out_dtype)) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append: bad out_dtype");
@@ -327,7 +333,7 @@ static int append_common(const void* queries, tq_dtype q_dtype, const void* k_ne
     return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append_at: slot must be < n_tokens (and no seq_lens)");
   DecodeCommon c{queries, q_dtype, k_quant, v_quant, k_scales, k_biases, v_scales, v_biases,
                  sb_dtype, gqa_factor, sliding_window, batch, num_kv_heads, head_dim, n_tokens,
-                 capacity, scale, k_new, v_new, new_dtype, slot};
+                 capacity, scale, k_new, v_new, new_dtype, slot, slots};
   return decode_common(c, "tq_sdpa_int4_append", seq_lens, 0, 0, 0, out, out_dtype, nullptr,
                        workspace, workspace_bytes, stream);
 }
@@ -341,8 +347,23 @@ int tq_sdpa_int4_append(const void* queries, tq_dtype q_dtype, const void* k_new
                         size_t workspace_bytes, void* stream) {
   return append_common(queries, q_dtype, k_new, v_new, new_dtype, k_quant, k_scales, k_biases,
                        v_quant, v_scales, v_biases, sb_dtype, gqa_factor, scale, sliding_window,
-                       batch, num_kv_heads, head_dim, n_tokens, capacity, seq_lens, -1, out,
-                       out_dtype, workspace, workspace_bytes, stream);
+                       batch, num_kv_heads, head_dim, n_tokens, capacity, seq_lens, -1, nullptr,
+                       out, out_dtype, workspace, workspace_bytes, stream);
+}
+
+int tq_sdpa_int4_append_slots(const void* queries, tq_dtype q_dtype, const void* k_new,
+                              const void* v_new, tq_dtype new_dtype, uint32_t* k_quant,
+                              void* k_scales, void* k_biases, uint32_t* v_quant, void* v_scales,
+                              void* v_biases, tq_dtype sb_dtype, int gqa_factor, float scale,
+                              int sliding_window, int batch, int num_kv_heads, int head_dim,
+                              int n_tokens, int capacity, const int32_t* seq_lens,
+                              const int32_t* slots, void* out, tq_dtype out_dtype,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  if (!slots) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append_slots: null slots");
+  return append_common(queries, q_dtype, k_new, v_new, new_dtype, k_quant, k_scales, k_biases,
+                       v_quant, v_scales, v_biases, sb_dtype, gqa_factor, scale, sliding_window,
+                       batch, num_kv_heads, head_dim, n_tokens, capacity, seq_lens, -1, slots,
+                       out, out_dtype, workspace, workspace_bytes, stream);
 }
 
 int tq_sdpa_int4_append_at(const void* queries, tq_dtype q_dtype, const void* k_new,
@@ -355,8 +376,8 @@ int tq_sdpa_int4_append_at(const void* queries, tq_dtype q_dtype, const void* k_
   if (slot < 0) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_append_at: slot must be >= 0");
   return append_common(queries, q_dtype, k_new, v_new, new_dtype, k_quant, k_scales, k_biases,
                        v_quant, v_scales, v_biases, sb_dtype, gqa_factor, scale, 0, batch,
-                       num_kv_heads, head_dim, n_tokens, capacity, nullptr, slot, out, out_dtype,
-                       workspace, workspace_bytes, stream);
+                       num_kv_heads, head_dim, n_tokens, capacity, nullptr, slot, nullptr, out,
+                       out_dtype, workspace, workspace_bytes, stream);
 }
 
 int tq_sdpa_int4_partial(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,

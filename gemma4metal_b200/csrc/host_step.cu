@@ -6,18 +6,19 @@
 // kernel). Here the step is a CUDA graph of two kernels captured once per
 // decode plan:
 //
-//   gather: one CTA reads [queries | k_new | v_new | seq_lens] from mapped
-//           pinned host memory into a device buffer
+//   gather: one CTA reads [queries | k_new | v_new | seq_lens | slots] from
+//           mapped pinned host memory into a device buffer
 //   -> tq_sdpa_int4_append (quantize-on-append fused into the decode kernel),
 //      a programmatic dependent launch: its prologue (barrier init, L2
 //      prefetch of its first tiles) overlaps the gather; it writes the output
 //      straight into mapped pinned host memory
 //
 // so the host pays one graph launch and one stream synchronisation per step,
-// and no copy-engine node sits on the path. The per-sequence lengths travel
-// with the inputs (seq_lens), so one graph serves every length whose decode
-// plan (splits x tiles per split) is the same; a new plan re-captures and
-// updates the executable graph in place.
+// and no copy-engine node sits on the path. The per-sequence lengths and the
+// slots the new rows go to travel with the inputs (n - 1 for a growing cache,
+// position mod window for a ring), so one graph serves every length whose
+// decode plan (splits x tiles per split) is the same; a new plan re-captures
+// and updates the executable graph in place.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -39,9 +40,9 @@ struct tq_decode_step {
   void *vs, *vb;
   int gqa, window, B, Hkv, D, capacity;
   float scale;
-  // staging: [q | k_new | v_new | seq_lens] in mapped pinned host memory and
-  // its device copy; the output in mapped pinned host memory
-  size_t q_bytes, kv_bytes, in_bytes, out_bytes;
+  // staging: [q | k_new | v_new | seq_lens | slots] in mapped pinned host
+  // memory and its device copy; the output in mapped pinned host memory
+  size_t q_bytes, kv_bytes, len_bytes, in_bytes, out_bytes;
   unsigned char* h_in = nullptr;
   const uint4* h_in_dev = nullptr;  // h_in as the device sees it
   unsigned char* d_in = nullptr;
@@ -110,16 +111,18 @@ int capture(tq_decode_step* s, int n, const tq::DecodePlan& pl) {
   const bool pdl = tq::pdl_launches();
   tq::pdl_launches() = true;  // the decode kernel follows the gather kernel
   const int32_t* seq = reinterpret_cast<const int32_t*>(s->d_in + s->q_bytes + 2 * s->kv_bytes);
+  const int32_t* slots = reinterpret_cast<const int32_t*>(s->d_in + s->q_bytes + 2 * s->kv_bytes +
+                                                          s->len_bytes);
   step_gather_kernel<<<1, kGatherThreads, 0, s->stream>>>(
       s->h_in_dev, reinterpret_cast<uint4*>(s->d_in), static_cast<int>(s->in_bytes / 16));
   e = cudaGetLastError();
   int rc = TQ_OK;
   if (e == cudaSuccess)
-    rc = tq_sdpa_int4_append(s->d_in, s->q_dtype, s->d_in + s->q_bytes,
-                             s->d_in + s->q_bytes + s->kv_bytes, s->new_dtype, s->kq, s->ks, s->kb,
-                             s->vq, s->vs, s->vb, s->sb_dtype, s->gqa, s->scale, s->window, s->B,
-                             s->Hkv, s->D, n, s->capacity, seq, s->h_out_dev, s->out_dtype, s->ws,
-                             s->ws_bytes, s->stream);
+    rc = tq_sdpa_int4_append_slots(s->d_in, s->q_dtype, s->d_in + s->q_bytes,
+                                   s->d_in + s->q_bytes + s->kv_bytes, s->new_dtype, s->kq, s->ks,
+                                   s->kb, s->vq, s->vs, s->vb, s->sb_dtype, s->gqa, s->scale,
+                                   s->window, s->B, s->Hkv, s->D, n, s->capacity, seq, slots,
+                                   s->h_out_dev, s->out_dtype, s->ws, s->ws_bytes, s->stream);
   tq::pdl_launches() = pdl;
   const cudaError_t e3 = cudaStreamEndCapture(s->stream, &graph);
   if (e != cudaSuccess || e3 != cudaSuccess || rc != TQ_OK) {
@@ -194,7 +197,8 @@ TQ_API int tq_decode_step_create(tq_dtype q_dtype, tq_dtype new_dtype, uint32_t*
   auto r16 = [](size_t x) { return (x + 15) & ~static_cast<size_t>(15); };
   s->q_bytes = r16(batch * H * head_dim * dtype_bytes(q_dtype));
   s->kv_bytes = r16(static_cast<size_t>(batch) * num_kv_heads * head_dim * dtype_bytes(new_dtype));
-  s->in_bytes = s->q_bytes + 2 * s->kv_bytes + r16(batch * sizeof(int32_t));
+  s->len_bytes = r16(batch * sizeof(int32_t));
+  s->in_bytes = s->q_bytes + 2 * s->kv_bytes + 2 * s->len_bytes;
   s->out_bytes = batch * H * head_dim * dtype_bytes(out_dtype);
   cudaError_t e = cudaGetDevice(&s->device);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
@@ -224,16 +228,25 @@ TQ_API int tq_decode_step_buffers(tq_decode_step* step, void** queries, void** k
   return TQ_OK;
 }
 
-TQ_API int tq_decode_step_run(tq_decode_step* step, const void* queries, const void* k_new,
-                              const void* v_new, const int32_t* n_tokens, void* out) {
-  if (!step) return fail_step(TQ_ERR_INVALID, "tq_decode_step_run: null step");
-  tq_decode_step* s = step;
+}  // extern "C"
+
+namespace {
+
+// One step: slots == nullptr writes each new row at slot n_tokens[b] - 1.
+int run_step(tq_decode_step* s, const void* queries, const void* k_new, const void* v_new,
+             const int32_t* n_tokens, const int32_t* slots, void* out) {
+  if (!s) return fail_step(TQ_ERR_INVALID, "tq_decode_step_run: null step");
   if (!n_tokens) return fail_step(TQ_ERR_INVALID, "tq_decode_step_run: null n_tokens");
   int n_max = 0;
   for (int b = 0; b < s->B; ++b) {
     if (n_tokens[b] < 1 || n_tokens[b] > s->capacity) {
       tq::set_last_error("tq_decode_step_run: n_tokens[%d] = %d outside [1, capacity %d]", b,
                          n_tokens[b], s->capacity);
+      return TQ_ERR_INVALID;
+    }
+    if (slots && (slots[b] < 0 || slots[b] >= n_tokens[b])) {
+      tq::set_last_error("tq_decode_step_run_at: slots[%d] = %d outside [0, n_tokens %d)", b,
+                         slots[b], n_tokens[b]);
       return TQ_ERR_INVALID;
     }
     n_max = std::max(n_max, n_tokens[b]);
@@ -252,7 +265,12 @@ TQ_API int tq_decode_step_run(tq_decode_step* step, const void* queries, const v
   if (k_new && k_new != hq + s->q_bytes) memcpy(hq + s->q_bytes, k_new, kn);
   if (v_new && v_new != hq + s->q_bytes + s->kv_bytes)
     memcpy(hq + s->q_bytes + s->kv_bytes, v_new, kn);
-  memcpy(hq + s->q_bytes + 2 * s->kv_bytes, n_tokens, s->B * sizeof(int32_t));
+  int32_t* h_len = reinterpret_cast<int32_t*>(hq + s->q_bytes + 2 * s->kv_bytes);
+  int32_t* h_slot = reinterpret_cast<int32_t*>(hq + s->q_bytes + 2 * s->kv_bytes + s->len_bytes);
+  for (int b = 0; b < s->B; ++b) {
+    h_len[b] = n_tokens[b];
+    h_slot[b] = slots ? slots[b] : n_tokens[b] - 1;
+  }
 
   const int vis = s->window > 0 ? std::min(n_max, s->window) : n_max;
   const tq::DecodePlan pl = tq::plan_decode(s->device, s->B, s->Hkv * s->gqa, s->Hkv, s->D, vis,
@@ -275,6 +293,22 @@ TQ_API int tq_decode_step_run(tq_decode_step* step, const void* queries, const v
   if (rc != TQ_OK) return rc;
   if (out && out != s->h_out) memcpy(out, s->h_out, s->out_bytes);
   return TQ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+TQ_API int tq_decode_step_run(tq_decode_step* step, const void* queries, const void* k_new,
+                              const void* v_new, const int32_t* n_tokens, void* out) {
+  return run_step(step, queries, k_new, v_new, n_tokens, nullptr, out);
+}
+
+TQ_API int tq_decode_step_run_at(tq_decode_step* step, const void* queries, const void* k_new,
+                                 const void* v_new, const int32_t* n_tokens,
+                                 const int32_t* slots, void* out) {
+  if (!slots) return fail_step(TQ_ERR_INVALID, "tq_decode_step_run_at: null slots");
+  return run_step(step, queries, k_new, v_new, n_tokens, slots, out);
 }
 
 TQ_API int tq_decode_step_destroy(tq_decode_step* step) {

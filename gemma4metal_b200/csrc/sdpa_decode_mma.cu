@@ -131,6 +131,7 @@ struct MParams {
   const void* v_new;
   int new_dtype;
   int new_slot;  // < 0: n_local - 1 (the end of each sequence); else this slot (ring caches)
+  const int32_t* new_slots;  // nullable: sequence b's slot in device memory (overrides new_slot)
   float* ws_o;
   float* ws_ml;
   unsigned* counters;
@@ -364,7 +365,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   // head write the same bytes); its producer issues the tile holding the
   // slot only after the writers' release on nbar
   constexpr int NWW = D / 128;  // writer warps: D/8 words of K and of V, one per lane
-  const int new_slot = p.new_slot >= 0 ? p.new_slot : n_local - 1;
+  const int new_slot = p.new_slots ? p.new_slots[b] : p.new_slot >= 0 ? p.new_slot : n_local - 1;
   const bool has_new = p.k_new != nullptr && n_local > 0 && new_slot < n_local &&
                        new_slot >= cb * kChunk && new_slot < ce * kChunk;
   const int new_tile = has_new ? (new_slot / kChunk - cb) / CPT : -1;
@@ -1190,6 +1191,7 @@ cudaError_t launch_decode_mma(const DecodeArgs& a, const DecodePlan& pl, cudaStr
   p.v_new = a.v_new;
   p.new_dtype = a.new_dtype;
   p.new_slot = a.new_slot;
+  p.new_slots = a.new_slots;
   if (pl.splits > 1) {
     unsigned char* ws = static_cast<unsigned char*>(a.workspace);
     p.ws_o = reinterpret_cast<float*>(ws + pl.ws_o_off);

@@ -54,6 +54,7 @@ struct DecodeArgs {
   const void* v_new = nullptr;
   int new_dtype = 0;
   int new_slot = -1;  // < 0: n_local - 1
+  const int32_t* new_slots = nullptr;  // device, one slot per sequence (overrides new_slot)
 };
 
 // Decode kernel variants: the CUDA-core kernel (sdpa_decode.cu) and the

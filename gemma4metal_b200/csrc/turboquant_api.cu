@@ -383,11 +383,35 @@ HostDecodeStep::HostDecodeStep(KVCache& cache, int num_heads, float scale, int s
         where);
 }
 
+HostDecodeStep::HostDecodeStep(RingKVCache& ring, int num_heads, float scale, Dtype q_dtype,
+                               Dtype new_dtype, Dtype out_dtype)
+    : HostDecodeStep(ring.cache, num_heads, scale, 0, q_dtype, new_dtype, out_dtype) {
+  ring_ = &ring;
+}
+
 HostDecodeStep::~HostDecodeStep() { tq_decode_step_destroy(step_); }
+
+void HostDecodeStep::run_at(const void* queries, const void* k_new, const void* v_new, void* out,
+                            const int32_t* n_tokens, const int32_t* slots) {
+  const char* where = "HostDecodeStep::run_at";
+  check(tq_decode_step_run_at(step_, queries, k_new, v_new, n_tokens, slots, out), where);
+  int n_max = 0;
+  for (int b = 0; b < cache_->batch_; ++b) n_max = n_tokens[b] > n_max ? n_tokens[b] : n_max;
+  if (n_max > cache_->length_) cache_->length_ = n_max;
+}
 
 void HostDecodeStep::run(const void* queries, const void* k_new, const void* v_new, void* out,
                          const int32_t* n_tokens) {
   const char* where = "HostDecodeStep::run";
+  if (ring_ && !n_tokens) {
+    const int32_t n = static_cast<int32_t>(ring_->total_ + 1 < ring_->window_ ? ring_->total_ + 1
+                                                                              : ring_->window_);
+    const int32_t slot = static_cast<int32_t>(ring_->total_ % ring_->window_);
+    check(tq_decode_step_run_at(step_, queries, k_new, v_new, &n, &slot, out), where);
+    ++ring_->total_;
+    cache_->length_ = ring_->n_valid();
+    return;
+  }
   int n_max = 0;
   for (int b = 0; b < cache_->batch_; ++b) {
     n_[b] = n_tokens ? n_tokens[b] : cache_->length_ + 1;

@@ -97,6 +97,10 @@ def _register_extra(L) -> None:
                                          ctypes.POINTER(ctypes.c_void_p),
                                          ctypes.POINTER(ctypes.c_void_p)]
     L.tq_decode_step_run.argtypes = [P, P, P, P, ctypes.POINTER(ctypes.c_int32), P]
+    L.tq_decode_step_run_at.argtypes = [P, P, P, P, ctypes.POINTER(ctypes.c_int32),
+                                        ctypes.POINTER(ctypes.c_int32), P]
+    L.tq_sdpa_int4_append_slots.argtypes = [P, I, P, P, I, P, P, P, P, P, P, I, I, F, I, I, I, I,
+                                            I, I, P, P, P, I, P, SZ, P]
     L.tq_decode_step_destroy.argtypes = [P]
     L.tq_sdpa_int4_multi_workspace_size.restype = SZ
     L.tq_sdpa_int4_multi_workspace_size.argtypes = [I, I, I, I, I]
@@ -380,12 +384,15 @@ def sdpa_int4_append(queries: torch.Tensor, k_new: torch.Tensor, v_new: torch.Te
                      scale: float = 1.0, sliding_window: int = 0, s=None, *, n_tokens: int,
                      seq_lens: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
                      out_dtype: Optional[torch.dtype] = None,
-                     ws: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     ws: Optional[torch.Tensor] = None,
+                     slots: Optional[torch.Tensor] = None) -> torch.Tensor:
     """One decode step: quantize-on-append of the new token's K/V (B, Hkv, D)
     (or (B, Hkv, 1, D)) into slot n - 1 of a (B, Hkv, capacity, ...) cache,
     then fused int4 decode attention over the n tokens (n = n_tokens, or
     seq_lens[b]); one launch with the tensor-core decode kernel. Same result
-    as quantize_append(pos = n - 1) followed by sdpa_int4."""
+    as quantize_append(pos = n - 1) followed by sdpa_int4. slots (device
+    int32, one per sequence) puts sequence b's new row at slots[b] instead
+    (tq_sdpa_int4_append_slots: ring caches at different positions)."""
     squeeze = queries.dim() == 2
     q = queries.unsqueeze(0) if squeeze else queries
     cache = [k_quant, k_scales, k_biases, v_quant, v_scales, v_biases]
@@ -402,6 +409,12 @@ def sdpa_int4_append(queries: torch.Tensor, k_new: torch.Tensor, v_new: torch.Te
         ws = workspace(q.device, nbytes, s)
     # contiguous copies stay referenced until the launch is enqueued
     qc, kc, vc = q.contiguous(), k_new.contiguous(), v_new.contiguous()
+    if slots is not None:
+        _check(load_library().tq_sdpa_int4_append_slots(
+            _ptr(qc), _dt(q), _ptr(kc), _ptr(vc), _dt(kc), *[_ptr(c) for c in cache], _dt(cache[1]),
+            int(gqa_factor), float(scale), int(sliding_window), B, Hkv, D, n, cap, _ptr(seq_lens),
+            _ptr(slots), _ptr(out), _dt(out), _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
+        return out[0] if squeeze else out
     _check(load_library().tq_sdpa_int4_append(
         _ptr(qc), _dt(q), _ptr(kc), _ptr(vc), _dt(kc), *[_ptr(c) for c in cache], _dt(cache[1]),
         int(gqa_factor), float(scale), int(sliding_window), B, Hkv, D, n, cap, _ptr(seq_lens),
@@ -420,14 +433,17 @@ class HostDecodeStep:
 
     Staging buffers (pinned host tensors) are `queries` (B, H, D), `k_new` and
     `v_new` (B, Hkv, D) and `out` (B, H, D): write inputs there and pass
-    nothing to run() to skip the host copies, or pass host tensors/arrays."""
+    nothing to run() to skip the host copies, or pass host tensors/arrays.
+    A RingKVCache (sliding layer) works too: each run() writes the next
+    token at slot total % window and attends over the window."""
 
     def __init__(self, cache: KVCache, num_heads: int, scale: float = 1.0,
                  sliding_window: int = 0, q_dtype: torch.dtype = torch.float16,
                  new_dtype: torch.dtype = torch.float16,
                  out_dtype: Optional[torch.dtype] = None):
-        if isinstance(cache, RingKVCache):
-            raise ValueError("a ring cache appends at slot total % window: use RingKVCache.decode_step")
+        self.ring = isinstance(cache, RingKVCache)
+        if self.ring and sliding_window:
+            raise ValueError("a ring cache holds exactly its window: pass sliding_window=0")
         if num_heads % cache.num_kv_heads:
             raise ValueError("num_heads must be a multiple of the cache's kv heads")
         L = load_library()
@@ -458,6 +474,7 @@ class HostDecodeStep:
         self.v_new = pinned(ptrs[2], (B, Hkv, D), new_dtype)
         self.out = pinned(ptrs[3], (B, H, D), od)
         self._n = (ctypes.c_int32 * B)()
+        self._slots = (ctypes.c_int32 * B)()
         self._like = (self.queries, self.k_new, self.v_new, self.out)
         self._seen = [None] * 4
         self._seen_ptr = [0] * 4
@@ -483,10 +500,19 @@ class HostDecodeStep:
             raise ValueError(f"expected a C-contiguous array of {like.numel()} {like.dtype}")
         return x.ctypes.data
 
-    def run(self, n_tokens, queries=None, k_new=None, v_new=None, out=None):
+    def run(self, n_tokens=None, queries=None, k_new=None, v_new=None, out=None, slots=None):
         """One step: n_tokens (int, or one per sequence) counts the tokens
-        including the new one. Returns `out` (default: the staging tensor,
-        overwritten by the next step)."""
+        including the new one (default: the cache's length + 1; for a ring
+        cache min(total + 1, window)); slots (one per sequence) says where the
+        new rows go (default: n - 1; for a ring cache total % window).
+        Returns `out` (default: the staging tensor, overwritten by the next
+        step)."""
+        c = self.cache
+        ring_step = self.ring and n_tokens is None and slots is None
+        if ring_step:
+            n_tokens, slots = min(c.total + 1, c.window), c.total % c.window
+        elif n_tokens is None:
+            n_tokens = c.length + 1
         if isinstance(n_tokens, int):
             for b in range(self.batch):
                 self._n[b] = n_tokens
@@ -497,11 +523,22 @@ class HostDecodeStep:
             for b, n in enumerate(n_tokens):
                 self._n[b] = int(n)
             n_max = max(int(n) for n in n_tokens)
-        _check(self._L.tq_decode_step_run(
-            self._h, self._host_ptr(queries, 0), self._host_ptr(k_new, 1),
-            self._host_ptr(v_new, 2), self._n, self._host_ptr(out, 3)))
-        if n_max > self.cache.length:
-            self.cache.length = n_max
+        args = (self._h, self._host_ptr(queries, 0), self._host_ptr(k_new, 1),
+                self._host_ptr(v_new, 2), self._n)
+        if slots is None:
+            _check(self._L.tq_decode_step_run(*args, self._host_ptr(out, 3)))
+        else:
+            sl = [slots] * self.batch if isinstance(slots, int) else list(slots)
+            if len(sl) != self.batch:
+                raise ValueError("slots needs one entry per sequence")
+            for b, x in enumerate(sl):
+                self._slots[b] = int(x)
+            _check(self._L.tq_decode_step_run_at(*args, self._slots, self._host_ptr(out, 3)))
+        if ring_step:
+            c.total += 1
+            c.length = c.n_valid
+        elif n_max > c.length:
+            c.length = n_max
         return self.out if out is None else out
 
     def close(self) -> None:

@@ -153,6 +153,8 @@ class TQ_CXX_API KVCache {
   int batch_, num_kv_heads_, head_dim_, capacity_, length_ = 0;
 };
 
+class RingKVCache;
+
 // ---- one decode step from host memory (tq_decode_step_*) ---------------------
 // The engine's per-token call (engine/gemma4_multilayer.cpp:222-236) with the
 // query, the new K/V row and the output in host memory: one CUDA graph launch
@@ -164,6 +166,11 @@ class TQ_CXX_API HostDecodeStep {
   HostDecodeStep(KVCache& cache, int num_heads, float scale = 1.0f, int sliding_window = 0,
                  Dtype q_dtype = Dtype::float16, Dtype new_dtype = Dtype::float16,
                  Dtype out_dtype = Dtype::float16);
+  // A sliding layer's ring: run() writes the next token at slot total % window
+  // and attends over the window, advancing the ring's position.
+  HostDecodeStep(RingKVCache& ring, int num_heads, float scale = 1.0f,
+                 Dtype q_dtype = Dtype::float16, Dtype new_dtype = Dtype::float16,
+                 Dtype out_dtype = Dtype::float16);
   ~HostDecodeStep();
   HostDecodeStep(const HostDecodeStep&) = delete;
   HostDecodeStep& operator=(const HostDecodeStep&) = delete;
@@ -172,6 +179,9 @@ class TQ_CXX_API HostDecodeStep {
   // token counts including the new token (nullptr: cache length + 1 for all).
   void run(const void* queries, const void* k_new, const void* v_new, void* out,
            const int32_t* n_tokens = nullptr);
+  // Explicit slot of each sequence's new row (0 <= slots[b] < n_tokens[b]).
+  void run_at(const void* queries, const void* k_new, const void* v_new, void* out,
+              const int32_t* n_tokens, const int32_t* slots);
   // Pinned staging buffers: inputs written here need no host copy in run().
   void* queries() const;
   void* k_new() const;
@@ -180,6 +190,7 @@ class TQ_CXX_API HostDecodeStep {
 
  private:
   KVCache* cache_;
+  RingKVCache* ring_ = nullptr;
   tq_decode_step* step_ = nullptr;
   std::vector<int32_t> n_;
 };
@@ -204,6 +215,7 @@ class TQ_CXX_API RingKVCache {
   KVCache cache;
 
  private:
+  friend class HostDecodeStep;
   int window_;
   long long total_ = 0;
 };

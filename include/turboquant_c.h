@@ -160,6 +160,24 @@ TQ_API int tq_sdpa_int4_append_at(const void* queries, tq_dtype q_dtype, const v
                            int slot, void* out, tq_dtype out_dtype, void* workspace,
                            size_t workspace_bytes, void* stream);
 
+/* The same step with one slot per sequence, read from device memory: slots[b]
+ * (int32, device) is where sequence b's new row goes, and attention runs
+ * over its seq_lens[b] tokens (seq_lens may be NULL: n_tokens for every
+ * sequence) with the sliding window as in tq_sdpa_int4_append (0 for a ring
+ * cache). A batch of ring-cache sequences at different positions, or a step
+ * whose slots are only known on the device (a captured graph replayed every
+ * token). Each slot must lie in [0, its sequence's token count); a slot
+ * outside it writes nothing. */
+TQ_API int tq_sdpa_int4_append_slots(const void* queries, tq_dtype q_dtype, const void* k_new,
+                                     const void* v_new, tq_dtype new_dtype, uint32_t* k_quant,
+                                     void* k_scales, void* k_biases, uint32_t* v_quant,
+                                     void* v_scales, void* v_biases, tq_dtype sb_dtype,
+                                     int gqa_factor, float scale, int sliding_window, int batch,
+                                     int num_kv_heads, int head_dim, int n_tokens, int capacity,
+                                     const int32_t* seq_lens, const int32_t* slots, void* out,
+                                     tq_dtype out_dtype, void* workspace, size_t workspace_bytes,
+                                     void* stream);
+
 /* Sequence-split shard of decode attention: this cache holds global token
  * positions [token_offset, token_offset + n_local) of a sequence whose total
  * length is n_total (all sequences of the batch share both). Writes the
@@ -391,7 +409,7 @@ TQ_API int tq_precondition(const void* x, tq_dtype x_dtype, int64_t rows, int he
  * sdpa_int4 over the cache, read the output). A step object binds one layer's
  * cache (B, Hkv, capacity, ...) and owns mapped pinned staging, a device copy
  * of the inputs, a workspace, a stream and a CUDA graph of two kernels:
- *   gather [queries | k_new | v_new | n_tokens] from the mapped staging
+ *   gather [queries | k_new | v_new | n_tokens | slots] from the mapped staging
  *   -> tq_sdpa_int4_append (programmatic dependent launch) writing the output
  *      into the mapped output staging,
  * captured on the first run and again whenever the decode plan for the
@@ -405,7 +423,11 @@ TQ_API int tq_precondition(const void* x, tq_dtype x_dtype, int64_t rows, int he
  * tq_decode_step_buffers returns (no host copy then) and out may be NULL (the
  * result stays in the staging buffer). The call returns once the output is on
  * the host. Not thread-safe per object; objects on one device may run from
- * different threads. tq_decode_step_destroy releases everything (NULL: no-op). */
+ * different threads. tq_decode_step_destroy releases everything (NULL: no-op).
+ * tq_decode_step_run_at takes the slot of each new row (host, batch entries,
+ * 0 <= slots[b] < n_tokens[b]): a ring cache of a sliding layer (create with
+ * sliding_window 0 and capacity = the window) passes n = min(t + 1, W) and
+ * slot = t mod W for its t-th token. */
 typedef struct tq_decode_step tq_decode_step;
 TQ_API int tq_decode_step_create(tq_dtype q_dtype, tq_dtype new_dtype, uint32_t* k_quant,
                                  void* k_scales, void* k_biases, uint32_t* v_quant, void* v_scales,
@@ -416,6 +438,9 @@ TQ_API int tq_decode_step_buffers(tq_decode_step* step, void** queries, void** k
                                   void** v_new, void** out);
 TQ_API int tq_decode_step_run(tq_decode_step* step, const void* queries, const void* k_new,
                               const void* v_new, const int32_t* n_tokens, void* out);
+TQ_API int tq_decode_step_run_at(tq_decode_step* step, const void* queries, const void* k_new,
+                                 const void* v_new, const int32_t* n_tokens,
+                                 const int32_t* slots, void* out);
 TQ_API int tq_decode_step_destroy(tq_decode_step* step);
 
 /* Read and clear the device error word that kernels set when a bounded wait

@@ -326,6 +326,30 @@ int main() {
     }
     printf("%-28s %s\n", "RingKVCache decode_step", steps_equal ? "PASS" : "FAIL");
     ok &= steps_equal;
+    // host-buffer ring step (HostDecodeStep over a ring) == RingKVCache::decode_step
+    turboquant::RingKVCache ring4(nkv, hd, W), ring5(nkv, hd, W);
+    for (auto* r : {&ring4, &ring5})
+      r->append(array::from_host(K.data(), {1, nkv, 500, hd}, Dtype::float32),
+                array::from_host(V.data(), {1, nkv, 500, hd}, Dtype::float32));
+    turboquant::HostDecodeStep hstep(ring4, nh, 1.0f, Dtype::float32, Dtype::float32,
+                                     Dtype::float32);
+    bool host_ring = true;
+    std::vector<float> hout(static_cast<size_t>(nh) * hd);
+    for (int t = 0; t < 20; ++t) {  // crosses the wrap at 512
+      for (int h = 0; h < nkv; ++h)
+        for (int d = 0; d < hd; ++d) {
+          kt[static_cast<size_t>(h) * hd + d] = static_cast<float>(std::sin(0.03 * (t + 1) * (h + 2) + d));
+          vt[static_cast<size_t>(h) * hd + d] = static_cast<float>(std::cos(0.05 * (t + 1) - h + d));
+        }
+      hstep.run(Qh.data(), kt.data(), vt.data(), hout.data());
+      auto g = ring5.decode_step(Q, array::from_host(kt.data(), {1, nkv, hd}, Dtype::float32),
+                                 array::from_host(vt.data(), {1, nkv, hd}, Dtype::float32), nh / nkv)
+                   .to_vector<float>();
+      host_ring &= g == hout;
+    }
+    host_ring &= ring4.total() == ring5.total() && ring4.n_valid() == W;
+    printf("%-28s %s\n", "HostDecodeStep over a ring", host_ring ? "PASS" : "FAIL");
+    ok &= host_ring;
   }
 
   printf("\n%s\n", ok ? "PASS" : "FAIL");

@@ -130,3 +130,42 @@ def test_decode_step_in_cuda_graph():
     torch.cuda.synchronize()
     assert torch.equal(out, first)
     assert tq.device_error() == 0
+
+
+def test_decode_step_per_sequence_slots(variant):
+    """tq_sdpa_int4_append_slots: sequence b's new row goes to slots[b] (a
+    device array) and attention runs over its seq_lens[b] tokens; the cache
+    bytes and the output equal quantize-on-append at those positions followed
+    by the decode, bit for bit."""
+    H, Hkv, D, B = 16, 8, 128, 3
+    lens = [700, 129, 64]
+    slots = [699, 5, 63]  # the end of a sequence, a ring slot behind it, a chunk edge
+    N = max(lens)
+    L = inputs.make_layer(23, H, Hkv, D, N, batch=B)
+    cap = (N + 3) // 4 * 4
+    k = np.zeros((B, Hkv, cap, D), np.float32)
+    v = np.zeros_like(k)
+    k[:, :, :N] = L["k"]
+    v[:, :, :N] = L["v"]
+    cache = [*O.quantize(k, np.float16), *O.quantize(v, np.float16)]
+    fused = [dev(a) for a in cache]
+    split = [dev(a) for a in cache]
+    rng = np.random.default_rng(9)
+    k_new = torch.from_numpy(rng.standard_normal((B, Hkv, D)).astype(np.float32)).half().cuda()
+    v_new = torch.from_numpy(rng.standard_normal((B, Hkv, D)).astype(np.float32)).half().cuda()
+    q = torch.from_numpy(L["q"]).half().cuda()
+    sl = dev(np.asarray(lens, np.int32))
+    sp = dev(np.asarray(slots, np.int32))
+    out_f = tq.sdpa_int4_append(q, k_new, v_new, *fused, H // Hkv, 1.0, 0, n_tokens=N,
+                                seq_lens=sl, slots=sp, out_dtype=torch.float32)
+    tq.quantize_append(k_new[:, :, None], v_new[:, :, None], *split, pos=0, positions=sp)
+    out_s = tq.sdpa_int4(q, *split, H // Hkv, 1.0, 0, n_tokens=N, seq_lens=sl,
+                         out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert tq.device_error() == 0
+    for a, b in zip(fused, split):
+        assert torch.equal(a, b), "cache bytes differ from quantize-on-append at the slots"
+    assert torch.equal(out_f, out_s), "output differs from append + decode"
+    hc = [host(a) for a in fused]
+    ref = O.sdpa_int4(q.float().cpu().numpy(), *hc, n_tokens=lens, f64=True)
+    parity(host(out_f), ref)

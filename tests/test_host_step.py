@@ -45,19 +45,22 @@ def device_step(cache, q, kn, vn, H, n, window, out_dtype, seq_lens=None):
                                out_dtype=out_dtype)
 
 
+F16, F32 = torch.float16, torch.float32
 CASES = [
-    # B, H, Hkv, D, cap, n0, steps, window, q dtype, out dtype
-    (1, 32, 16, 128, 4096, 1700, 40, 0, torch.float16, torch.float16),   # crosses a plan edge
-    (1, 32, 16, 128, 2048, 900, 6, 512, torch.float16, torch.float32),   # sliding window
-    (3, 16, 8, 128, 1024, 600, 5, 0, torch.bfloat16, torch.bfloat16),   # per-sequence lengths
-    (1, 32, 8, 256, 3072, 2000, 5, 0, torch.float16, torch.float16),     # D = 256
+    # B, H, Hkv, D, cap, n0, steps, window, q dtype, out dtype, scale/bias dtype
+    (1, 32, 16, 128, 4096, 1700, 40, 0, F16, F16, F16),             # crosses a plan edge
+    (1, 32, 16, 128, 2048, 900, 6, 512, F16, F32, F16),             # sliding window
+    (3, 16, 8, 128, 1024, 600, 5, 0, torch.bfloat16, torch.bfloat16, F16),  # per-sequence lengths
+    (1, 32, 8, 256, 3072, 2000, 5, 0, F16, F16, F16),               # D = 256
+    (1, 32, 16, 128, 2048, 700, 4, 0, F16, F16, F32),               # f32 scales and biases
+    (1, 16, 4, 512, 2048, 900, 3, 0, F16, F16, F16),                # D = 512: quantize + CUDA-core decode
 ]
 
 
-@pytest.mark.parametrize("B,H,Hkv,D,cap,n0,steps,window,qdt,odt", CASES)
-def test_host_step_matches_device_step(B, H, Hkv, D, cap, n0, steps, window, qdt, odt):
+@pytest.mark.parametrize("B,H,Hkv,D,cap,n0,steps,window,qdt,odt,sdt", CASES)
+def test_host_step_matches_device_step(B, H, Hkv, D, cap, n0, steps, window, qdt, odt, sdt):
     rng = np.random.default_rng(n0 + D)
-    ca, cb = make_cache(B, Hkv, D, cap, n0, seed=D + B)
+    ca, cb = make_cache(B, Hkv, D, cap, n0, seed=D + B, sdt=sdt)
     step = tq.HostDecodeStep(ca, H, 1.0, window, q_dtype=qdt, new_dtype=torch.float16,
                              out_dtype=odt)
     lens0 = [n0 - 7 * b for b in range(B)]
@@ -120,3 +123,41 @@ def test_host_step_rejects_bad_lengths():
         step.run(3, np.zeros((1, 32, 64), np.float16))  # wrong element count
     step.close()
     step.close()  # idempotent
+
+
+def test_host_step_ring_cache_matches_device_step():
+    """A sliding layer's ring cache: each run() writes slot total % W and
+    attends over the window; outputs and cache bytes equal
+    RingKVCache.decode_step (tq_sdpa_int4_append_at) step by step, across the
+    ring's wrap and the decode plans of growing windows."""
+    H, Hkv, D, W, n0, steps = 32, 16, 128, 256, 200, 90
+    L = inputs.make_layer(17, H, Hkv, D, n0)
+    ra = tq.RingKVCache(Hkv, D, W)
+    rb = tq.RingKVCache(Hkv, D, W)
+    for r in (ra, rb):
+        r.append(torch.from_numpy(L["k"]).cuda(), torch.from_numpy(L["v"]).cuda())
+    step = tq.HostDecodeStep(ra, H)
+    rng = np.random.default_rng(3)
+    for i in range(steps):
+        q = torch.from_numpy(rng.standard_normal((1, H, D)).astype(np.float32)).half()
+        kn = torch.from_numpy(rng.standard_normal((1, Hkv, D)).astype(np.float32)).half()
+        vn = torch.from_numpy(rng.standard_normal((1, Hkv, D)).astype(np.float32)).half()
+        got = step.run(None, q, kn, vn).clone()
+        want = rb.decode_step(q.cuda(), kn.cuda(), vn.cuda(), H // Hkv)
+        torch.cuda.synchronize()
+        assert torch.equal(got, want.cpu()), f"step {i}: output differs from the device ring step"
+    assert ra.total == rb.total == n0 + steps and ra.n_valid == W
+    for x, y in zip(ra.tensors(), rb.tensors()):
+        assert torch.equal(x, y), "ring bytes differ from the device ring step"
+    assert tq.device_error() == 0
+    step.close()
+
+
+def test_host_step_rejects_bad_slots():
+    cache = tq.RingKVCache(16, 128, 64)
+    step = tq.HostDecodeStep(cache, 32)
+    with pytest.raises(RuntimeError, match="slots"):
+        step.run(10, slots=10)  # slot must be < n_tokens
+    with pytest.raises(RuntimeError, match="slots"):
+        step.run(10, slots=-1)
+    step.close()

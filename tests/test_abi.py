@@ -115,5 +115,13 @@ def test_decode_step_host_validation():
     # null step object
     n = (ctypes.c_int32 * 1)(5)
     assert L.tq_decode_step_run(None, None, None, None, n, None) == 1
+    slot = (ctypes.c_int32 * 1)(4)
+    assert L.tq_decode_step_run_at(None, None, None, None, n, slot, None) == 1
+    assert L.tq_decode_step_run_at(None, None, None, None, n, None, None) == 1
+    # the per-sequence-slot step needs its slot array
+    rc = L.tq_sdpa_int4_append_slots(fake, 1, fake, fake, 1, fake, fake, fake, fake, fake, fake,
+                                     1, 2, 1.0, 0, 1, 16, 128, 10, 12, None, None, fake, 1, None,
+                                     0, None)
+    assert rc == 1 and b"slots" in L.tq_last_error()
     assert L.tq_decode_step_buffers(None, None, None, None, None) == 1
     assert L.tq_decode_step_destroy(None) == 0

@@ -53,6 +53,10 @@ struct tq_decode_step {
   // the captured step and the plan it was captured for
   cudaGraphExec_t exec = nullptr;
   int plan_splits = -1, plan_tps = -1, plan_variant = -1;
+  // the last decode plan and the visible-tile count it was made for: the plan
+  // depends on the lengths only through that count
+  tq::DecodePlan last_plan{};
+  int last_tiles = -1;
 };
 
 namespace {
@@ -273,8 +277,15 @@ int run_step(tq_decode_step* s, const void* queries, const void* k_new, const vo
   }
 
   const int vis = s->window > 0 ? std::min(n_max, s->window) : n_max;
-  const tq::DecodePlan pl = tq::plan_decode(s->device, s->B, s->Hkv * s->gqa, s->Hkv, s->D, vis,
-                                            s->window > 0, s->q_dtype != TQ_F16);
+  const int tiles = s->last_tiles >= 0
+                        ? (vis + s->last_plan.tokens_per_tile - 1) / s->last_plan.tokens_per_tile
+                        : -1;
+  if (tiles < 0 || tiles != s->last_tiles) {
+    s->last_plan = tq::plan_decode(s->device, s->B, s->Hkv * s->gqa, s->Hkv, s->D, vis,
+                                   s->window > 0, s->q_dtype != TQ_F16);
+    s->last_tiles = (vis + s->last_plan.tokens_per_tile - 1) / s->last_plan.tokens_per_tile;
+  }
+  const tq::DecodePlan& pl = s->last_plan;
   if (pl.splits < 0) {
     if (dev != s->device) cudaSetDevice(dev);
     return fail_step(TQ_ERR_UNSUPPORTED, "tq_decode_step_run: batch * kv_heads too large");

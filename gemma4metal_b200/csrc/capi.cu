@@ -195,6 +195,8 @@ int tq_quantize_append(const void* k_new, const void* v_new, tq_dtype in_dtype, 
 size_t tq_sdpa_int4_workspace_size(int batch, int num_heads, int num_kv_heads, int head_dim,
                                    int n_tokens, int sliding_window) {
   if (batch < 1 || num_kv_heads < 1 || num_heads < num_kv_heads || n_tokens < 0) return 0;
+  // the planner divides by head_dim: sizes no decode call accepts get 0
+  if (head_dim != 128 && head_dim != 256 && head_dim != 512) return 0;
   int dev = 0;
   cudaGetDevice(&dev);
   tq::DecodePlan pl = tq::plan_decode(dev, batch, num_heads, num_kv_heads, head_dim,

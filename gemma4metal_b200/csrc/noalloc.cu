@@ -9,7 +9,10 @@
 // This entry point serves them with a scratch area that lives in the library
 // itself: a fixed-size __device__ array that every GPU which loads the
 // library holds until the process exits. Nothing here calls cudaMalloc,
-// cudaFree or any allocating routine.
+// cudaFree or any allocating routine. With lazy module loading the driver
+// places the array on a device when its address is first looked up, which is
+// the first call on that device; callers that reserve all device memory up
+// front make that first call before reserving.
 #include <cstdio>
 #include <mutex>
 #include <unordered_map>
@@ -69,6 +72,21 @@ extern "C" TQ_API int tq_sdpa_int4_noalloc(const void* queries, tq_dtype q_dtype
                                            int head_dim, int n_tokens, int capacity,
                                            const int32_t* seq_lens, void* out,
                                            tq_dtype out_dtype, void* stream) {
+  // The shape checks come before the scratch is sized: sizing plans the
+  // split, and the plan is only defined for shapes the decode accepts.
+  if (head_dim != 128 && head_dim != 256 && head_dim != 512) {
+    tq::set_last_error("tq_sdpa_int4_noalloc: head_dim %d not supported (128, 256, 512)", head_dim);
+    return TQ_ERR_UNSUPPORTED;
+  }
+  if (gqa_factor != 1 && gqa_factor != 2 && gqa_factor != 4 && gqa_factor != 8) {
+    tq::set_last_error("tq_sdpa_int4_noalloc: gqa_factor %d not in {1,2,4,8}", gqa_factor);
+    return TQ_ERR_UNSUPPORTED;
+  }
+  if (batch < 1 || num_kv_heads < 1 || n_tokens < 0 || sliding_window < 0) {
+    tq::set_last_error("tq_sdpa_int4_noalloc: need batch >= 1, num_kv_heads >= 1, n_tokens >= 0 "
+                       "and sliding_window >= 0");
+    return TQ_ERR_INVALID;
+  }
   const size_t need = tq_sdpa_int4_workspace_size(batch, num_kv_heads * gqa_factor, num_kv_heads,
                                                   head_dim, n_tokens, sliding_window);
   if (need > kNoAllocScratchBytes) {

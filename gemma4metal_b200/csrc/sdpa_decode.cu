@@ -624,6 +624,10 @@ int choose_decode_variant(int D, int G) {
 DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_max, bool windowed,
                        bool qsplit) {
   DecodePlan pl{};
+  if ((D != 128 && D != 256 && D != 512) || Hkv < 1 || H < Hkv || B < 1) {
+    pl.splits = -1;  // not a decode shape (callers validate first; nothing below may divide by 0)
+    return pl;
+  }
   const int G = H / Hkv;
   pl.variant = choose_decode_variant(D, G);
   pl.gsub = std::min(G, pl.variant == kDecodeMma ? 8 : max_gsub(D));

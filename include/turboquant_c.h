@@ -240,6 +240,12 @@ TQ_API int tq_lse_merge(const float* parts, int n_parts, int batch, int num_head
  * rejected with TQ_ERR_WORKSPACE.
  * The first call on each device looks up the array's device address
  * (cudaGetSymbolAddress); make that first call outside any stream capture.
+ * With lazy module loading (the CUDA 12 default) that lookup is also when
+ * the driver places the 2 MiB array on the device, so a caller that reserves
+ * all remaining device memory up front should make one call whose sizes
+ * need scratch (any context longer than one split) before reserving; later
+ * calls allocate nothing. Shapes are checked before the scratch is sized: an unsupported
+ * head_dim or gqa_factor returns TQ_ERR_UNSUPPORTED.
  * All calls on a device share the array: calls that overlap on the GPU
  * (different streams, or concurrent graphs) race and must be serialised.
  * No counterpart in the reference (its outputs and temporaries come from

@@ -125,3 +125,27 @@ def test_decode_step_host_validation():
     assert rc == 1 and b"slots" in L.tq_last_error()
     assert L.tq_decode_step_buffers(None, None, None, None, None) == 1
     assert L.tq_decode_step_destroy(None) == 0
+
+
+def test_noalloc_and_workspace_size_reject_unsupported_head_dim():
+    """head_dim 0 or far above 512 must come back as an error code, not reach
+    the split planner (which divides by head_dim)."""
+    from gemma4metal_b200.turboquant import load_library
+    L = load_library()
+    P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    L.tq_sdpa_int4_noalloc.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, P, P, I,
+                                       P]
+    L.tq_sdpa_int4_workspace_size.restype = ctypes.c_size_t
+    L.tq_sdpa_int4_workspace_size.argtypes = [I, I, I, I, I, I]
+    fake = P(0x1000)  # never dereferenced: validation fails first
+    for hd in (0, 96, 16384):
+        assert L.tq_sdpa_int4_workspace_size(1, 32, 16, hd, 1024, 0) == 0
+        rc = L.tq_sdpa_int4_noalloc(fake, 1, fake, fake, fake, fake, fake, fake, 1, 2, 1.0, 0, 1,
+                                    16, hd, 1024, 1024, None, fake, 1, None)
+        assert rc == 2 and b"head_dim" in L.tq_last_error(), (hd, rc)
+    rc = L.tq_sdpa_int4_noalloc(fake, 1, fake, fake, fake, fake, fake, fake, 1, 3, 1.0, 0, 1, 16,
+                                128, 1024, 1024, None, fake, 1, None)
+    assert rc == 2 and b"gqa" in L.tq_last_error()
+    rc = L.tq_sdpa_int4_noalloc(fake, 1, fake, fake, fake, fake, fake, fake, 1, 2, 1.0, 0, 0, 16,
+                                128, 1024, 1024, None, fake, 1, None)
+    assert rc == 1

@@ -1,7 +1,9 @@
 """tq_sdpa_int4_noalloc: the decode entry point for callers that cannot
 allocate device memory (its split-KV scratch is an array built into the
-library). Checked against tq_sdpa_int4 with a caller workspace, through the
-C ABI, on consecutive calls that reuse the shared scratch.
+library). Checked through the C ABI against the CPU oracle (dequantize +
+fp64 SDPA) and against tq_sdpa_int4 with a caller workspace, on consecutive
+calls that reuse the shared scratch; a call after the first one must leave
+the free device memory unchanged.
 
 This file sorts last so that a run stopping at the first failure has run
 every other test first."""
@@ -35,10 +37,11 @@ def _case(seed, H, Hkv, D, N):
     v = np.zeros_like(k)
     k[:, :, :N] = L["k"]
     v[:, :, :N] = L["v"]
+    host = (*O.quantize(k), *O.quantize(v))
     dev = [torch.from_numpy(np.ascontiguousarray(a.view(np.int32) if a.dtype == np.uint32 else a)).cuda()
-           for a in (*O.quantize(k), *O.quantize(v))]
+           for a in host]
     q = torch.from_numpy(L["q"]).half().cuda()
-    return q, dev, cap
+    return q, dev, host, cap
 
 
 def _noalloc(L, q, c, G, window, Hkv, D, N, cap, out, stream):
@@ -49,20 +52,46 @@ def _noalloc(L, q, c, G, window, Hkv, D, N, cap, out, stream):
 
 
 @pytest.mark.parametrize("window", [0, 1024])
-def test_noalloc_matches_workspace_entry_point_twice(window):
+def test_noalloc_matches_oracle_twice(window):
     tq, L = _lib()
     stream = torch.cuda.current_stream().cuda_stream
     # two calls in a row with different sizes: the second reuses the scratch
     # (and its counters) left by the first
     for seed, (H, Hkv, D, N) in [(31, (32, 16, 128, 8192)), (32, (16, 4, 256, 3001))]:
-        q, c, cap = _case(seed, H, Hkv, D, N)
+        q, c, h, cap = _case(seed, H, Hkv, D, N)
         out = torch.empty(1, H, D, dtype=torch.float16, device="cuda")
         rc = _noalloc(L, q, c, H // Hkv, window, Hkv, D, N, cap, out, stream)
         assert rc == 0, L.tq_last_error()
-        ref = tq.sdpa_int4(q, *c, H // Hkv, 1.0, window, n_tokens=N)
         torch.cuda.synchronize()
         assert tq.device_error() == 0
-        parity(out.float().cpu().numpy(), ref.float().cpu().numpy())
+        got = out.float().cpu().numpy()
+        ref = O.sdpa_int4(q.float().cpu().numpy(), *h, scale=1.0, window=window, n_tokens=[N],
+                          f64=True)
+        parity(got, ref)
+        # and it agrees with the entry point that takes a caller workspace
+        ws_out = tq.sdpa_int4(q, *c, H // Hkv, 1.0, window, n_tokens=N)
+        parity(got, ws_out.float().cpu().numpy())
+
+
+def test_noalloc_later_calls_allocate_nothing():
+    """The first call on a device may make the driver place the built-in
+    array there; every later call must leave the free device memory as it
+    found it."""
+    tq, L = _lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    H, Hkv, D, N = 32, 16, 128, 8192
+    q, c, h, cap = _case(33, H, Hkv, D, N)
+    out = torch.empty(1, H, D, dtype=torch.float16, device="cuda")
+    assert _noalloc(L, q, c, H // Hkv, 0, Hkv, D, N, cap, out, stream) == 0, L.tq_last_error()
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        assert _noalloc(L, q, c, H // Hkv, 0, Hkv, D, N, cap, out, stream) == 0, L.tq_last_error()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0, (free0, free1)
+    ref = O.sdpa_int4(q.float().cpu().numpy(), *h, scale=1.0, n_tokens=[N], f64=True)
+    parity(out.float().cpu().numpy(), ref)
 
 
 def test_noalloc_rejects_sizes_beyond_the_scratch():

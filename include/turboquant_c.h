@@ -449,6 +449,16 @@ TQ_API int tq_decode_step_run_at(tq_decode_step* step, const void* queries, cons
                                  const int32_t* slots, void* out);
 TQ_API int tq_decode_step_destroy(tq_decode_step* step);
 
+/* ---- measurement ------------------------------------------------------------
+ * Read-only HBM stream over [src, src + bytes) by `ctas` CTAs, each taking one
+ * contiguous range: mode 0 with 1-D bulk copies into a shared-memory ring (the
+ * decode kernels' load path), mode 1 with 16-byte non-caching loads. The XOR of
+ * the data is XOR-accumulated into sink[cta] (ctas words). The practical
+ * ceiling the decode kernels' GB/s are compared with (a copy's figure counts a
+ * write per read). No counterpart in the reference. */
+TQ_API int tq_read_probe(const void* src, size_t bytes, int ctas, int mode, uint32_t* sink,
+                         void* stream);
+
 /* Read and clear the device error word that kernels set when a bounded wait
  * gives up (0 = no error). Synchronises `stream`. */
 TQ_API int tq_device_error(void* stream, uint32_t* code);

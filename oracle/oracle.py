@@ -108,6 +108,60 @@ def quantize_np(x: np.ndarray, sb_dtype=np.float16):
             b_st.reshape(*lead, D // 64))
 
 
+def quantize_signed_edge_np(x: np.ndarray, sb_dtype=np.float16):
+    """A cache of the kind MLX's affine quantizer is published to write
+    (ml-explore/mlx `quantize(x, 64, 4)`, unpinned: the reference clones it at
+    HEAD and no reference test fixes its outputs). Per group of 64:
+    delta = (max - min)/15; the edge is the extreme of larger magnitude
+    (min if |min| > |max|, else max) and the scale carries its sign
+    (+delta for the min edge, -delta for the max edge); q0 = round(edge/scale);
+    when q0 != 0 the scale becomes edge/q0 (so that 0.0 is exactly
+    representable) and the bias is the edge, otherwise the bias is 0. Codes
+    round((x - bias)/scale) clamped to 0..15. Arithmetic in fp32, scale and
+    bias rounded to `sb_dtype` before the codes are taken (what a reader of
+    the cache sees). So half of the groups carry NEGATIVE scales and a bias
+    at the group MAXIMUM -- the cases this repo's own quantizer never
+    writes. Same return layout as quantize_np."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    *lead, D = x.shape
+    assert D % 64 == 0
+    g = x.reshape(-1, D // 64, 64)
+    mn = g.min(axis=-1)
+    mx = g.max(axis=-1)
+    delta = np.maximum((mx - mn) / np.float32(15.0), np.float32(1e-7)).astype(np.float32)
+    use_min = np.abs(mn) > np.abs(mx)
+    scale = np.where(use_min, delta, -delta).astype(np.float32)
+    edge = np.where(use_min, mn, mx).astype(np.float32)
+    q0 = np.rint(edge / scale)
+    with np.errstate(divide="ignore", invalid="ignore"):
+        scale = np.where(q0 != 0, edge / np.where(q0 != 0, q0, 1), scale).astype(np.float32)
+    bias = np.where(q0 != 0, edge, 0.0).astype(np.float32)
+    s_st = scale.astype(sb_dtype)
+    b_st = bias.astype(sb_dtype)
+    s = s_st.astype(np.float32)[..., None]
+    b = b_st.astype(np.float32)[..., None]
+    c = np.clip(np.rint((g - b) / s), 0.0, 15.0).astype(np.uint32).reshape(-1, D // 8, 8)
+    shifts = (4 * np.arange(8, dtype=np.uint32))
+    words = np.bitwise_or.reduce(c << shifts, axis=-1).astype(np.uint32)
+    return (words.reshape(*lead, D // 8), s_st.reshape(*lead, D // 64),
+            b_st.reshape(*lead, D // 64))
+
+
+def random_affine_cache(rng, lead, D: int, sb_dtype=np.float16, s_lo=0.02, s_hi=0.5,
+                        b_sigma=1.0):
+    """Arbitrary affine parameters: uniform random codes, scales of random
+    sign with log-uniform magnitude in [s_lo, s_hi], biases N(0, b_sigma^2)
+    unrelated to the codes (no group minimum or maximum). Returns
+    (codes uint32 (*lead, D/8), scales, biases (*lead, D/64))."""
+    lead = tuple(lead)
+    codes = rng.integers(0, 1 << 32, size=lead + (D // 8,), dtype=np.uint64).astype(np.uint32)
+    mag = np.exp(rng.uniform(np.log(s_lo), np.log(s_hi), size=lead + (D // 64,)))
+    sign = np.where(rng.random(lead + (D // 64,)) < 0.5, -1.0, 1.0)
+    scales = (sign * mag).astype(sb_dtype)
+    biases = (rng.standard_normal(lead + (D // 64,)) * b_sigma).astype(sb_dtype)
+    return codes, scales, biases
+
+
 def unpack_np(codes: np.ndarray) -> np.ndarray:
     """uint32 words -> uint8 nibbles, element 8w+j at bits 4j..4j+3."""
     shifts = (4 * np.arange(8, dtype=np.uint32))
@@ -376,6 +430,39 @@ def compressed_sdpa(q, packed, radii, codebooks, block, vq, vs, vb, scale=1.0, s
         _ptr(Sc) if Sc is not None else None, m, float(scale),
         _ptr(np.ascontiguousarray(vq)), _ptr(np.ascontiguousarray(vs)),
         _ptr(np.ascontiguousarray(vb)), 1 if vs.dtype == np.float32 else 0, _ptr(out))
+    return out
+
+
+def sdpa_multi_f64(q, k, v, scale=1.0, causal=False, pos0=0, window=0, n_tokens=None,
+                   rows=64):
+    """sdpa_multi_np with BLAS matrix products, `rows` queries at a time (for
+    config-2 sizes: 512 queries x 32 heads x 8.7K tokens). Same masks and
+    fp64 arithmetic: q (n_q, H, D), k, v (Hkv, N, D) dense."""
+    nq, H, D = q.shape
+    Hkv = k.shape[0]
+    N = k.shape[1] if n_tokens is None else n_tokens
+    G = H // Hkv
+    out = np.zeros((nq, H, D), np.float32)
+    t = np.arange(N)
+    for hk in range(Hkv):
+        kk = k[hk, :N].astype(np.float64)
+        vv = v[hk, :N].astype(np.float64)
+        for r0 in range(0, nq, rows):
+            r1 = min(nq, r0 + rows)
+            qq = q[r0:r1, hk * G:(hk + 1) * G].astype(np.float64).reshape(-1, D) * scale
+            s = qq @ kk.T                                    # ((r1-r0)*G, N)
+            pos = (pos0 + np.arange(r0, r1)) if causal else np.full(r1 - r0, N - 1)
+            vis = t[None, :] <= pos[:, None]
+            if window > 0:
+                vis &= (pos[:, None] - t[None, :]) < window
+            vis = np.repeat(vis, G, axis=0)
+            s = np.where(vis, s, -np.inf)
+            m = s.max(axis=1, keepdims=True)
+            p = np.where(vis, np.exp(s - np.where(np.isfinite(m), m, 0.0)), 0.0)
+            l = p.sum(axis=1, keepdims=True)
+            o = (p @ vv) / np.where(l > 0, l, 1.0)
+            o = np.where(l > 0, o, 0.0)
+            out[r0:r1, hk * G:(hk + 1) * G] = o.reshape(r1 - r0, G, D).astype(np.float32)
     return out
 
 

@@ -1,21 +1,28 @@
-"""Benchmark of the int4 KV-cache decode-attention path (task config 1 @ 32K).
+"""Benchmark of the int4 KV-cache decode-attention path (task configs 0-4).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--context 32768] [--window 0]
+                    [--workload all|cfg0|cfg1|cfg2|cfg3|cfg4|probe]
+                    [--context 32768] [--window 0] [--exchange peer|nccl]
 
-One step = one decode step of one attention layer: quantize-on-append of the
-new token's K/V into the preallocated int4 cache, then fused decode attention
-over the whole context, in one launch (`tq_sdpa_int4_append`; `--split-step`
-runs them as two launches) (H=32, Hkv=16, D=128, batch 1, fp16 Q/out, fp16
-scales/biases). Steps rotate over 8 independent layer caches (8 x 75.5 MB,
-larger than the 126 MB L2), so every step streams its cache from HBM. The
-appended slot is rewritten on each rotation, so every step attends over
-exactly `--context` tokens.
-
-The metric is decode-attention tokens/s (steps/s x batch), whole job: with
-N GPUs (torchrun, one process per GPU) every rank serves its own layer caches
-(weak scaling: independent KV heads / sequences per GPU, no data-path
+Headline (top-level keys): config 1 at 32K tokens. One step = one decode step
+of one attention layer: quantize-on-append of the new token's K/V into the
+preallocated int4 cache, then fused decode attention over the whole context,
+in one launch (`tq_sdpa_int4_append`; `--split-step` runs them as two
+launches) (H=32, Hkv=16, D=128, batch 1, fp16 Q/out, fp16 scales/biases).
+Steps rotate over 8 independent layer caches (8 x 75.5 MB, larger than the
+126 MB L2), so every step streams its cache from HBM; the appended slot is
+rewritten on each rotation, so every step attends over exactly `--context`
+tokens. The timed region is one CUDA graph of exactly `--steps` steps.
+With N GPUs (torchrun, one process per GPU) every rank serves its own layer
+caches (weak scaling: independent KV heads / sequences per GPU, no data-path
 collective); value = total steps / max-over-ranks time.
+
+Nested under "configs" (default `--workload all`): config 0 (one layer, 1024
+tokens), config 2 (tcgen05: 64 x 1 batched decode over a shared 8K cache and
+the 512-query prefill chunk), config 3 (PolarQuant + QJL compressed keys) and
+a read-only HBM probe on one GPU; config 4 (one 262144-token sequence split
+over all N GPUs, peer-memory exchange + merge, strong scaling) at every N,
+with its time split and its merged output checked against the C oracle.
 
 `--impl reference` times the reference's algorithm on the host CPU instead
 (the CPU oracle in oracle/: quantize the new token, concatenate it onto the
@@ -59,11 +66,14 @@ def parse():
     ap.add_argument("--split-step", action="store_true",
                     help="cfg1: run the step as two launches (quantize_append, then sdpa_int4) "
                          "instead of the fused sdpa_int4_append")
-    ap.add_argument("--workload", default="cfg1", choices=["cfg1", "cfg2", "cfg4"],
-                    help="cfg1: config 1 decode step (default, weak scaling over GPUs); "
-                         "cfg2: config 2 on the tensor cores (64 x 1 batched decode over a "
-                         "shared 8K cache; 512-query causal prefill chunk); "
-                         "cfg4: config 4, one 256K-token sequence split over the GPUs")
+    ap.add_argument("--workload", default="all",
+                    choices=["all", "cfg0", "cfg1", "cfg2", "cfg3", "cfg4", "probe"],
+                    help="all (default): the config-1 headline line with the other configs "
+                         "nested (configs 0, 2, 3 and the HBM probe on one GPU; config 4's "
+                         "sequence split at every GPU count); cfg1: the headline alone; "
+                         "cfg0/cfg2/cfg3/cfg4/probe: that config's line alone")
+    ap.add_argument("--no-check", action="store_true",
+                    help="skip config 4's check of the merged output against the C oracle")
     return ap.parse_args()
 
 
@@ -205,9 +215,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         tq.sdpa_int4(Lr["q"], *c.tensors(), H // HKV, 1.0, window, s=s, n_tokens=n_ctx,
                      out=Lr["out"], ws=ws)
 
-    # eager warm-up (plans, occupancy, attributes), then CUDA graphs: one per
-    # layer (1 step) and one of CHUNK consecutive steps over the rotation, so
-    # host launch overhead is amortised over CHUNK steps.
+    # eager warm-up (plans, occupancy, attributes), then CUDA graphs: the
+    # warm-up steps and the timed steps are one graph each, of exactly
+    # `--warmup` and `--steps` steps over the layer rotation, so the timed
+    # region is one graph launch whatever the step count.
     with torch.cuda.stream(stream):
         for Lr in layers:
             step(Lr, stream)
@@ -222,21 +233,16 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         return g
 
     CHUNK = 8 * LAYERS
-    single = [capture([i]) for i in range(LAYERS)]
-    chunk = capture(range(CHUNK))
+    warm = capture(range(args.warmup)) if args.warmup > 0 else None
+    timed = capture(range(args.steps))
     kchunk = capture(range(CHUNK), with_append=False)
     torch.cuda.synchronize()
 
-    def run_steps(n):
-        with torch.cuda.stream(stream):
-            for _ in range(n // CHUNK):
-                chunk.replay()
-            for i in range(n % CHUNK):
-                single[i % LAYERS].replay()
-
     clocks = Clocks(local_rank)
     clocks.start()
-    run_steps(args.warmup)
+    if warm is not None:
+        with torch.cuda.stream(stream):
+            warm.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -244,7 +250,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    run_steps(args.steps)
+    with torch.cuda.stream(stream):
+        timed.replay()
     e1.record(stream)
     torch.cuda.synchronize()
     if world > 1:
@@ -339,7 +346,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     t_ms, e2e_ms, async_ms = float(tt[0]), float(tt[1]), float(tt[2])
 
     # release graphs before the process group goes away
-    del single, chunk, kchunk
+    del warm, timed, kchunk
     torch.cuda.synchronize()
     return dict(t_ms=t_ms, kern_us=kern_us, e2e_ms=e2e_ms, async_ms=async_ms, e2e_steps=e2e_steps,
                 clocks=clk, layer0=layers[0])
@@ -350,13 +357,31 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 C4_H, C4_HKV, C4_D, C4_N = 32, 8, 256, 262144
 
 
-def run_cfg4(args, rank: int, world: int, local_rank: int):
+def _graph_time(stream, graph, reps: int) -> float:
+    """Milliseconds of `reps` replays of `graph` on `stream` (CUDA events)."""
+    import torch
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    with torch.cuda.stream(stream):
+        for _ in range(reps):
+            graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, check: bool = True):
     """Config 4: one decode step of a 262144-token global-attention layer
-    (H=32, Hkv=8, D=256) whose int4 cache is split by sequence over the GPUs.
-    Step = append the new token on the last rank + partial decode on every
-    rank + exchange of the fp32 (o, m, l) states + LSE merge (one peer-memory
-    kernel, or NCCL all-gather + merge kernel with --exchange nccl), captured
-    in CUDA graphs. Layers rotate so every step streams its shard from HBM."""
+    (H=32, Hkv=8, D=256) whose int4 cache is split by sequence over the GPUs
+    (strong scaling). Step = append the new token on the last rank + partial
+    decode on every rank + exchange of the fp32 (o, m, l) states + LSE merge
+    (one peer-memory kernel, or NCCL all-gather + merge kernel with
+    --exchange nccl), captured in CUDA graphs; layers rotate so every step
+    streams its shard from HBM. Also timed on their own: the append + partial
+    decode, and the exchange + merge. `check`: rank 0 rebuilds layer 0's whole
+    cache on the host with the C oracle's quantizer and compares the merged
+    output with the oracle's dequantize + fp64 SDPA."""
     import math
 
     import torch
@@ -370,8 +395,13 @@ def run_cfg4(args, rank: int, world: int, local_rank: int):
     gen = torch.Generator(device=dev)
     gen.manual_seed(13)
     t0, t1 = seqsplit.shard_bounds(C4_N - 1, world, rank)
-    shard_bytes = (t1 - t0) * C4_HKV * 2 * (C4_D // 2 + 4 * (C4_D // 64))
+    per_tok = C4_HKV * 2 * (C4_D // 2 + 4 * (C4_D // 64))
+    shard_bytes = (t1 - t0) * per_tok
     layers_n = max(2, math.ceil(400e6 / max(shard_bytes, 1)))
+    host_cache = None
+    if check and rank == 0:
+        from oracle import oracle as O
+        host_cache = {"k": [], "v": []}  # per chunk: (codes, scales, biases)
 
     def rms_norm(x, w):
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True)) * w
@@ -379,7 +409,7 @@ def run_cfg4(args, rank: int, world: int, local_rank: int):
     wq = 1 + 0.1 * torch.randn(C4_D, device=dev, generator=gen)
     wk = 1 + 0.1 * torch.randn(C4_D, device=dev, generator=gen)
     layers = []
-    for _ in range(layers_n):
+    for li in range(layers_n):
         sc = seqsplit.SeqSplitCache(C4_N - 1, C4_HKV, C4_D, capacity_extra=4, device=dev)
         # every rank draws the same full-sequence chunks, quantizes its own slice
         step_tok = 16384
@@ -390,6 +420,9 @@ def run_cfg4(args, rank: int, world: int, local_rank: int):
             a, b = max(c0, sc.t0), min(c1, sc.t1)
             if b > a:
                 sc.cache.append(k[:, :, a - c0:b - c0], v[:, :, a - c0:b - c0], pos=a - sc.t0)
+            if host_cache is not None and li == 0:  # the oracle quantizes the same values itself
+                host_cache["k"].append(O.quantize(k.float().cpu().numpy()))
+                host_cache["v"].append(O.quantize(v.float().cpu().numpy()))
         q = rms_norm(torch.randn(1, C4_H, C4_D, device=dev, generator=gen), wq).half()
         kn = rms_norm(torch.randn(1, C4_HKV, 1, C4_D, device=dev, generator=gen), wk).half()
         vn = torch.randn(1, C4_HKV, 1, C4_D, device=dev, generator=gen).half()
@@ -404,94 +437,201 @@ def run_cfg4(args, rank: int, world: int, local_rank: int):
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(device=dev)
 
-    def step(Lr):
+    def partial(Lr):
         sc = Lr["sc"]
         if last:  # the appended token rewrites the same slot every rotation
             tq.quantize_append(Lr["kn"], Lr["vn"], *sc.cache.tensors(), pos=n_local, s=stream)
         nl = n_local + (1 if last else 0)
         tq.sdpa_int4_partial(Lr["q"], *sc.cache.tensors(), C4_H // C4_HKV, 1.0, 0, n_local=nl,
                              token_offset=sc.t0, n_total=C4_N, part_out=Lr["part"], ws=ws, s=stream)
+
+    def exchange(Lr):
         if peer is not None:
             peer.merge(Lr["part"], out=Lr["out"], s=stream)
             return
         if world > 1:
             dist.all_gather_into_tensor(Lr["parts"], Lr["part"])
-        else:
-            Lr["parts"][0].copy_(Lr["part"])
-        tq.lse_merge(Lr["parts"], C4_H, C4_D, out=Lr["out"], s=stream)
+            tq.lse_merge(Lr["parts"], C4_H, C4_D, out=Lr["out"], s=stream)
+        else:  # one GPU: the merge normalises the one state in place
+            tq.lse_merge(Lr["part"].view(1, 1, -1), C4_H, C4_D, out=Lr["out"], s=stream)
+
+    def step(Lr):
+        partial(Lr)
+        exchange(Lr)
 
     with torch.cuda.stream(stream):
         for Lr in layers:
             step(Lr)
     torch.cuda.synchronize()
     CH = 4 * layers_n
-    graph = None
-    try:
+
+    def capture(fn, n):
         g = torch.cuda.CUDAGraph()
         with torch.cuda.stream(stream):
             with torch.cuda.graph(g, stream=stream):
-                for i in range(CH):
-                    step(layers[i % layers_n])
-        graph = g
-    except Exception as e:  # NCCL capture not available: time the eager loop
-        print(f"[bench] CUDA graph capture failed ({e}); timing eagerly", file=sys.stderr)
-        torch.cuda.synchronize()
+                for i in range(n):
+                    fn(layers[i % layers_n])
+        return g
 
-    def run_steps(n):
-        with torch.cuda.stream(stream):
-            if graph is not None:
-                for _ in range(max(1, n // CH)):
-                    graph.replay()
-                return max(1, n // CH) * CH
-            for i in range(n):
-                step(layers[i % layers_n])
-            return n
-
+    graphs = {"step": capture(step, CH), "partial": capture(partial, CH),
+              "exchange": capture(exchange, CH)}
+    singles = [capture(step, 1) for _ in range(1)]  # the host-buffer leg re-targets layer 0 only
+    torch.cuda.synchronize()
+    reps = max(1, steps // CH)
     clocks = Clocks(local_rank)
     clocks.start()
-    run_steps(args.warmup)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    steps = run_steps(args.steps)
-    e1.record(stream)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
+    times = {}
+    for name in ("step", "partial", "exchange"):
+        with torch.cuda.stream(stream):
+            graphs[name].replay()  # warm-up
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        times[name] = _graph_time(stream, graphs[name], reps)
+        if world > 1:
+            dist.barrier()
     clk = clocks.stop()
-    t_ms = e0.elapsed_time(e1)
-    tt = torch.tensor([t_ms], device=dev, dtype=torch.float64)
+    n_timed = reps * CH
+
+    # end to end from host buffers on every rank: the step's q | k_new | v_new
+    # go up from pinned memory, the step graph runs, the merged output comes
+    # back and the host synchronises; host clock, max over ranks
+    L0 = layers[0]
+    nq, nkv = C4_H * C4_D, C4_HKV * C4_D
+    hin = torch.empty(nq + 2 * nkv, dtype=torch.float16, pin_memory=True)
+    hin[:nq].copy_(L0["q"].reshape(-1).cpu())
+    hin[nq:nq + nkv].copy_(L0["kn"].reshape(-1).cpu())
+    hin[nq + nkv:].copy_(L0["vn"].reshape(-1).cpu())
+    hout = torch.empty(1, C4_H, C4_D, dtype=torch.float16, pin_memory=True)
+    din = torch.empty(nq + 2 * nkv, dtype=torch.float16, device=dev)
+
+    def host_step():
+        with torch.cuda.stream(stream):
+            din.copy_(hin, non_blocking=True)
+            L0["q"].view(-1).copy_(din[:nq], non_blocking=True)
+            L0["kn"].view(-1).copy_(din[nq:nq + nkv], non_blocking=True)
+            L0["vn"].view(-1).copy_(din[nq + nkv:], non_blocking=True)
+            singles[0].replay()
+            hout.copy_(L0["out"], non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(4):
+        host_step()
+    e2e_steps = 64
+    if world > 1:
+        dist.barrier()
+    th0 = time.perf_counter()
+    for _ in range(e2e_steps):
+        host_step()
+    e2e_ms = (time.perf_counter() - th0) * 1000.0
+    assert tq.device_error() == 0, "a kernel reported a device error"
+
+    tt = torch.tensor([times["step"], times["partial"], times["exchange"], e2e_ms], device=dev,
+                      dtype=torch.float64)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-    t_ms = float(tt[0])
-    assert tq.device_error() == 0, "a kernel reported a device error"
-    del graph
+    t_step, t_part, t_exch, e2e_ms = (float(x) for x in tt)
+
+    acc = None
+    if host_cache is not None:
+        # the appended token sits at global position C4_N - 1 on the last rank
+        host_cache["k"].append(O.quantize(L0["kn"].float().cpu().numpy()))
+        host_cache["v"].append(O.quantize(L0["vn"].float().cpu().numpy()))
+        full = [np.concatenate([c[f] for c in host_cache[kv]], axis=2)
+                for kv in ("k", "v") for f in range(3)]
+        G = C4_H // C4_HKV
+        qh = L0["q"].float().cpu().numpy()
+        refs = []
+        for g0 in range(0, C4_HKV, 2):
+            sl = slice(g0, g0 + 2)
+            refs.append(O.sdpa_int4(qh[:, g0 * G:(g0 + 2) * G], *(a[:, sl] for a in full), f64=True))
+        ref = np.concatenate(refs, axis=1).astype(np.float64)
+        got = hout.float().numpy().astype(np.float64)
+        acc = {"max_abs": float(np.max(np.abs(got - ref))),
+               "cosine": float(got.ravel() @ ref.ravel() / (np.linalg.norm(got) * np.linalg.norm(ref))),
+               "oracle": "C oracle: quantize of the same values, dequantize + fp64 SDPA over all "
+                         "262144 tokens (layer 0, after the timed steps)"}
+        del full, host_cache
+    if world > 1:
+        dist.barrier()
+
+    cpu = None
+    if rank == 0 and world == 1 and check and not args.no_cpu_baseline:
+        cpu = cpu_reference_cfg4(L0)
+    del graphs, singles
     torch.cuda.synchronize()
     if peer is not None:
         peer.close()
-    value = steps / (t_ms / 1000.0)
-    total_bytes = C4_N * C4_HKV * 2 * (C4_D // 2 + 4 * (C4_D // 64))
-    line = {"metric": "int4-KV decode-attention tokens/s", "value": value, "unit": "tokens/s",
-            "n_gpus": world, "steps": steps, "warmup": args.warmup,
-            "ms_per_step": t_ms / steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded torch.randn, RMS-normalised Q/K as task configs[0])",
-            "config": {"workload": "cfg4 decode step: 262144-token global layer split by sequence, "
-                                   "append + partial decode + " +
-                                   ("peer-memory exchange + merge (one kernel)" if peer is not None
-                                    else "NCCL all-gather + LSE merge"),
-                       "batch": 1, "heads": C4_H, "kv_heads": C4_HKV, "head_dim": C4_D,
-                       "context": C4_N, "layers_rotated": layers_n,
-                       "l2": f"inputs larger than L2: {layers_n} rotating shards of {shard_bytes / 1e6:.0f} MB",
-                       "parallelism": f"sequence split over {world} GPU(s)"},
-            "hbm_gbs_per_gpu": shard_bytes / (t_ms / steps * 1e-3) / 1e9,
-            "hbm_gbs_total": total_bytes / (t_ms / steps * 1e-3) / 1e9,
-            "clocks": clk}
-    return line
+    us_step = t_step * 1000.0 / n_timed
+    us_part = t_part * 1000.0 / n_timed
+    us_exch = t_exch * 1000.0 / n_timed
+    total_bytes = C4_N * per_tok
+    peaks = measured_peaks()
+    # HBM roofline of the partial decode on the largest shard: algorithmic
+    # bytes of that shard (+ q and the fp32 state) over its time
+    shard_max = (seqsplit.shard_bounds(C4_N - 1, world, world - 1)[1]
+                 - seqsplit.shard_bounds(C4_N - 1, world, world - 1)[0] + 1)
+    part_bytes = shard_max * per_tok + C4_H * C4_D * 2 + C4_H * (C4_D + 2) * 4
+    ach = part_bytes / (us_part * 1e-6) / 1e9
+    return {
+        "workload": "cfg4 decode step: 262144-token global layer (H=32, Hkv=8, D=256) split by "
+                    "sequence, append + partial decode + " +
+                    ("peer-memory exchange + merge (one kernel)" if peer is not None else
+                     "NCCL all-gather + LSE merge"),
+        "metric": "int4-KV decode-attention tokens/s", "unit": "tokens/s", "scaling": "strong",
+        "n_gpus": world, "steps": n_timed,
+        "value": n_timed / (t_step / 1000.0), "ms_per_step": t_step / n_timed,
+        "time_split_us": {"step": us_step, "append_plus_partial_decode": us_part,
+                          "exchange_plus_merge": us_exch,
+                          "limiter": ("partial decode (HBM stream of the shard)"
+                                      if us_part >= 0.6 * us_step else "exchange + merge")},
+        "hbm_gbs_per_gpu": shard_bytes / (us_step * 1e-6) / 1e9,
+        "hbm_gbs_total": total_bytes / (us_step * 1e-6) / 1e9,
+        "roofline": {"bound": "hbm", "kernel": "tq::decode_mma_kernel<256,4,__half> (partial)",
+                     "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": ach / peaks["hbm_gbs"], "frac_of_8tbs_nominal": ach / 8000.0,
+                     "kernel_us": us_part, "algorithmic_bytes_per_launch": part_bytes,
+                     "traffic": None, "peak_source": peaks["source"]},
+        "accuracy_vs_oracle": acc,
+        "cpu_baseline": cpu,
+        "e2e": {"value": e2e_steps / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": (nq + 2 * nkv) * 2, "d2h_bytes_per_step": nq * 2,
+                "path": "pinned q|k_new|v_new -> device on every rank, step graph "
+                        "(append + tq_sdpa_int4_partial + tq_peer_merge), merged output -> pinned "
+                        "host, stream sync; host clock, max over ranks"},
+        "layers_rotated": layers_n,
+        "l2": f"inputs larger than L2: {layers_n} rotating shards of {shard_bytes / 1e6:.0f} MB",
+        "gpu_launches_per_step": ("quantize_rows_kernel (last rank), decode_mma_kernel (partial), " +
+                                  ("peer_merge_kernel" if peer is not None else
+                                   "lse_merge_kernel" + (" + NCCL all-gather" if world > 1 else ""))),
+        "clocks": clk,
+    }
+
+
+def cpu_reference_cfg4(L0) -> dict:
+    """The reference's algorithm for config 4 on the host (dequantize + fp32
+    SDPA, the C oracle with OpenMP over all host threads) on a bounded
+    sample: 2 of the 8 KV heads (8 of the 32 query heads) over all 262144
+    tokens, scaled to a whole step (x4)."""
+    from oracle import oracle as O
+    O.set_num_threads(os.cpu_count() or 1)
+    sc = L0["sc"]
+    n = sc.n_local
+    arrs = [t[:, 0:2, :n].cpu().numpy() for t in sc.cache.tensors()]
+    arrs = [a.view(np.uint32) if a.dtype == np.int32 else a for a in arrs]
+    q = L0["q"][:, 0:8].float().cpu().numpy()
+    base = O.Int4Baseline(q, *arrs)
+    base()
+    t0 = time.perf_counter()
+    reps = 0
+    while reps < 2 or time.perf_counter() - t0 < 4.0:
+        base()
+        reps += 1
+    dt = (time.perf_counter() - t0) / reps * 4.0
+    return {"value": 1.0 / dt, "unit": "tokens/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{reps} runs of 2 of 8 KV heads over {n} tokens (dequantize + fp32 SDPA, "
+                      f"the shard of this GPU), scaled x4 to the whole step"}
 
 
 # ----------------------------------------- config 2: tcgen05 multi-query --
@@ -766,6 +906,332 @@ def cfg2_line(args, world, res, cpu):
     return line
 
 
+# ------------------------------------------------- config 0: one layer --
+
+C0_N, C0_LAYERS, C0_STEPS = 1024, 128, 1024
+
+
+def run_cfg0(args, local_rank: int) -> dict:
+    """Config 0: one decode step of one attention layer over 1024 cached
+    tokens (H=32, Hkv=16, D=128, fp16 Q/out, scale 1.0), no append: the
+    reference test's single-layer case. 128 rotating layer caches (302 MB,
+    larger than L2); one graph of C0_STEPS steps. Latency-bound: 2.4 MB per
+    step."""
+    import torch
+
+    import gemma4metal_b200.turboquant as tq
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(0)
+
+    def rms_norm(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True)) * w
+
+    wq = 1 + 0.1 * torch.randn(D, device=dev, generator=gen)
+    wk = 1 + 0.1 * torch.randn(D, device=dev, generator=gen)
+    layers = []
+    for _ in range(C0_LAYERS):
+        cache = tq.KVCache(1, HKV, D, C0_N, device=dev)
+        cache.append(rms_norm(torch.randn(1, HKV, C0_N, D, device=dev, generator=gen), wk).half(),
+                     torch.randn(1, HKV, C0_N, D, device=dev, generator=gen).half(), pos=0)
+        q = rms_norm(torch.randn(1, H, D, device=dev, generator=gen), wq).half()
+        layers.append(dict(cache=cache, q=q, out=torch.empty(1, H, D, dtype=torch.float16, device=dev)))
+    ws = tq.workspace(dev, tq.sdpa_int4_workspace_size(1, H, HKV, D, C0_N, 0))
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(Lr):
+        tq.sdpa_int4(Lr["q"], *Lr["cache"].tensors(), H // HKV, 1.0, 0, s=stream, n_tokens=C0_N,
+                     out=Lr["out"], ws=ws)
+
+    with torch.cuda.stream(stream):
+        for Lr in layers:
+            step(Lr)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(C0_STEPS):
+                step(layers[i % C0_LAYERS])
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = 4
+    t_ms = _graph_time(stream, g, reps)
+    n = reps * C0_STEPS
+    us = t_ms * 1000.0 / n
+
+    # end to end: pinned q up, the decode, the output back, synchronise
+    Lr0 = layers[0]
+    hq = torch.empty(1, H, D, dtype=torch.float16, pin_memory=True)
+    hq.copy_(Lr0["q"].cpu())
+    ho = torch.empty(1, H, D, dtype=torch.float16, pin_memory=True)
+
+    def host_step():
+        with torch.cuda.stream(stream):
+            Lr0["q"].copy_(hq, non_blocking=True)
+            step(Lr0)
+            ho.copy_(Lr0["out"], non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(20):
+        host_step()
+    e2e_n = 500
+    th = time.perf_counter()
+    for _ in range(e2e_n):
+        host_step()
+    e2e_ms = (time.perf_counter() - th) * 1000.0
+    assert tq.device_error() == 0, "a kernel reported a device error"
+    del g
+    torch.cuda.synchronize()
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle as O
+        O.set_num_threads(os.cpu_count() or 1)
+        arrs = [t.cpu().numpy() for t in Lr0["cache"].tensors()]
+        arrs = [a.view(np.uint32) if a.dtype == np.int32 else a for a in arrs]
+        base = O.Int4Baseline(Lr0["q"].cpu().numpy(), *arrs)
+        base()
+        t0 = time.perf_counter()
+        k = 0
+        while k < 5 or time.perf_counter() - t0 < 2.0:
+            base()
+            k += 1
+        dt = (time.perf_counter() - t0) / k
+        cpu = {"value": 1.0 / dt, "unit": "tokens/s", "cores": O.num_threads(), "kind": "port",
+               "sample": f"{k} decode steps of the same layer (dequantize + fp32 SDPA, C oracle)"}
+    bytes_step = 2304 * C0_N + 2 * H * D * 2
+    peaks = measured_peaks()
+    ach = bytes_step / (us * 1e-6) / 1e9
+    return {"workload": "cfg0 decode step: one layer, 1024 tokens, no append (sdpa_int4)",
+            "metric": "int4-KV decode-attention tokens/s", "unit": "tokens/s", "steps": n,
+            "value": n / (t_ms / 1000.0), "ms_per_step": t_ms / n, "latency_us": us,
+            "roofline": {"bound": "hbm (latency in practice: 2.4 MB per launch)",
+                         "kernel": "tq::decode_mma_kernel<128,2,__half,false>", "achieved": ach,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
+                         "kernel_us": us, "algorithmic_bytes_per_launch": bytes_step,
+                         "traffic": None, "peak_source": peaks["source"]},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_n / (e2e_ms / 1000.0), "unit": "tokens/s",
+                    "h2d_bytes_per_step": H * D * 2, "d2h_bytes_per_step": H * D * 2,
+                    "path": "pinned q -> device, tq_sdpa_int4, output -> pinned host, stream sync "
+                            "(host clock)"},
+            "layers_rotated": C0_LAYERS, "l2": "inputs larger than L2: 128 rotating 2.4 MB layers",
+            "gpu_launches": n}
+
+
+# ------------------------------------- config 3: PolarQuant + QJL keys --
+
+C3_N, C3_BLOCK, C3_M, C3_LAYERS, C3_STEPS = 4096, 128, 256, 24, 192
+
+
+def run_cfg3(args, local_rank: int) -> dict:
+    """Config 3: compressed-key attention. Keys of 16 KV heads x 4096 tokens
+    (D=128) as PolarQuant (one 128-value block: 7 levels of 4-bit angles +
+    fp16 radius) + QJL (256 sign bits of the residual through a seeded
+    Gaussian 256x128 matrix + fp16 residual norm), int4 V; 32 query heads
+    (GQA 2), scale 1.0. A step is one compressed attention (scores with the
+    QJL correction, softmax, . int4 V) over one layer; 24 rotating layers
+    (270 MB). Encode throughput (polar_quantize + qjl_encode of all 65536
+    keys) is timed on its own."""
+    import torch
+
+    import gemma4metal_b200.turboquant as tq
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11)
+
+    def rms_norm(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True)) * w
+
+    levels = 7
+    cb = tq.uniform_codebooks(levels, device="cpu")
+    S = tq.qjl_matrix(C3_M, D, 11, device=dev)
+    wq = 1 + 0.1 * torch.randn(D, device=dev, generator=gen)
+    wk = 1 + 0.1 * torch.randn(D, device=dev, generator=gen)
+    layers = []
+    for _ in range(C3_LAYERS):
+        k = rms_norm(torch.randn(HKV, C3_N, D, device=dev, generator=gen), wk)
+        v = torch.randn(HKV, C3_N, D, device=dev, generator=gen)
+        _, pk, rad = tq.polar_quantize(k, C3_BLOCK, cb)
+        kh = tq.polar_dequantize(pk, rad, D, C3_BLOCK, cb)
+        sg, rn = tq.qjl_encode(k, kh, S)
+        vq, vs, vb = tq.quantize(v.half())
+        q = rms_norm(torch.randn(H, D, device=dev, generator=gen), wq).half()
+        layers.append(dict(k=k if not layers else None, pk=pk, rad=rad, sg=sg, rn=rn, vq=vq, vs=vs,
+                           vb=vb, q=q, out=torch.empty(H, D, dtype=torch.float16, device=dev)))
+        del kh, v
+    lib = tq.load_library()
+    ws = tq.workspace(dev, int(lib.tq_compressed_sdpa_workspace_size(H, HKV, D, C3_N)))
+    stream = torch.cuda.Stream(device=dev)
+
+    def step(Lr):
+        tq.compressed_sdpa(Lr["q"], Lr["pk"], Lr["rad"], cb, Lr["vq"], Lr["vs"], Lr["vb"], C3_BLOCK,
+                           1.0, Lr["sg"], Lr["rn"], S, out=Lr["out"], ws=ws, s=stream)
+
+    with torch.cuda.stream(stream):
+        for Lr in layers:
+            step(Lr)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(C3_STEPS):
+                step(layers[i % C3_LAYERS])
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = 8
+    t_ms = _graph_time(stream, g, reps)
+    n = reps * C3_STEPS
+    us = t_ms * 1000.0 / n
+
+    # encode of all keys of one layer (polar + its decode for the residual + QJL)
+    k0 = layers[0]["k"]
+    ek = 10
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        tq.polar_quantize(k0, C3_BLOCK, cb, s=stream)
+        e0.record(stream)
+        for _ in range(ek):
+            _, pk0, rad0 = tq.polar_quantize(k0, C3_BLOCK, cb, s=stream)
+            kh0 = tq.polar_dequantize(pk0, rad0, D, C3_BLOCK, cb, s=stream)
+            tq.qjl_encode(k0, kh0, S, s=stream)
+        e1.record(stream)
+    torch.cuda.synchronize()
+    enc_us = e0.elapsed_time(e1) * 1000.0 / ek
+
+    # end to end: pinned q up, the compressed attention, the output back, sync
+    Lr0 = layers[0]
+    hq = torch.empty(H, D, dtype=torch.float16, pin_memory=True)
+    hq.copy_(Lr0["q"].cpu())
+    ho = torch.empty(H, D, dtype=torch.float16, pin_memory=True)
+
+    def host_step():
+        with torch.cuda.stream(stream):
+            Lr0["q"].copy_(hq, non_blocking=True)
+            step(Lr0)
+            ho.copy_(Lr0["out"], non_blocking=True)
+        stream.synchronize()
+
+    for _ in range(10):
+        host_step()
+    e2e_n = 300
+    th = time.perf_counter()
+    for _ in range(e2e_n):
+        host_step()
+    e2e_ms = (time.perf_counter() - th) * 1000.0
+    assert tq.device_error() == 0, "a kernel reported a device error"
+    del g
+    torch.cuda.synchronize()
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        from oracle import oracle as O
+        O.set_num_threads(os.cpu_count() or 1)
+        hn = lambda t: t.cpu().numpy()
+        a = dict(q=hn(Lr0["q"]).astype(np.float32), pk=hn(Lr0["pk"]), rad=hn(Lr0["rad"]),
+                 sg=hn(Lr0["sg"]).view(np.uint32), rn=hn(Lr0["rn"]), vq=hn(Lr0["vq"]).view(np.uint32),
+                 vs=hn(Lr0["vs"]), vb=hn(Lr0["vb"]), S=hn(S), cb=cb.numpy())
+
+        def one():
+            return O.compressed_sdpa(a["q"], a["pk"], a["rad"], a["cb"], C3_BLOCK, a["vq"], a["vs"],
+                                     a["vb"], 1.0, a["sg"], a["rn"], a["S"])
+        ref = one()
+        err = float(np.max(np.abs(ho.float().numpy() - ref)))
+        t0 = time.perf_counter()
+        kk = 0
+        while kk < 3 or time.perf_counter() - t0 < 2.0:
+            one()
+            kk += 1
+        dt = (time.perf_counter() - t0) / kk
+        cpu = {"value": 1.0 / dt, "unit": "tokens/s", "cores": O.num_threads(), "kind": "port",
+               "sample": f"{kk} compressed attention steps of the same layer (C oracle: polar "
+                         f"decode + QJL correction + softmax . int4 V)",
+               "max_abs_vs_gpu_fp16_out": err}
+    per_key = D // 2 + 2 + C3_M // 8 + 2 + (D // 2 + 4 * (D // 64))
+    bytes_step = HKV * C3_N * per_key + 2 * H * D * 2
+    peaks = measured_peaks()
+    ach = bytes_step / (us * 1e-6) / 1e9
+    return {"workload": "cfg3 compressed-key attention: PolarQuant (7 levels x 4 bit + fp16 radius) "
+                        "+ QJL (256 bits + fp16 norm) keys, int4 V, 16 KV heads x 4096 keys",
+            "metric": "int4-KV decode-attention tokens/s", "unit": "tokens/s", "steps": n,
+            "value": n / (t_ms / 1000.0), "ms_per_step": t_ms / n,
+            "roofline": {"bound": "hbm (latency in practice: 11.3 MB per launch)",
+                         "kernel": "tq::compressed_attn_kernel", "achieved": ach,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": ach / peaks["hbm_gbs"],
+                         "kernel_us": us, "algorithmic_bytes_per_launch": bytes_step,
+                         "traffic": None, "peak_source": peaks["source"]},
+            "encode": {"keys": HKV * C3_N, "us": enc_us, "keys_per_s": HKV * C3_N / (enc_us * 1e-6),
+                       "kernels": "polar_encode_kernel + polar_decode_kernel (residual) + qjl_encode_kernel"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_n / (e2e_ms / 1000.0), "unit": "tokens/s",
+                    "h2d_bytes_per_step": H * D * 2, "d2h_bytes_per_step": H * D * 2,
+                    "path": "pinned q -> device, tq_compressed_sdpa, output -> pinned host, stream "
+                            "sync (host clock)"},
+            "layers_rotated": C3_LAYERS, "l2": "inputs larger than L2: 24 rotating 11.3 MB layers",
+            "gpu_launches": n}
+
+
+# ------------------------------------------------ read-only HBM probe --
+
+def run_probe(local_rank: int) -> dict:
+    """tq_read_probe: the read-only ceiling. (a) decode-shaped: one launch
+    reads one config-1 layer's cache bytes (75.5 MB) with the decode grid's
+    CTA count (432, 3 per SM) through bulk copies into shared memory, 8
+    rotating buffers; (b) a 2 GiB stream, bulk copies with 3 CTAs per SM;
+    (c) the same with 16-byte non-caching loads, 4 CTAs of 512 threads per SM."""
+    import torch
+
+    import gemma4metal_b200.turboquant as tq
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    lib = tq.load_library()
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    stream = torch.cuda.Stream(device=dev)
+    res = {}
+    layer = bytes_per_step(32768, 0)["attn"] - H * D * 4  # cache bytes of one layer
+    layer = layer // 16 * 16
+    cases = [("decode_shaped", layer, 8, 432, 0), ("stream_bulk", 2 << 30, 1, 3 * sms, 0),
+             ("stream_ldg", 2 << 30, 1, 4 * sms, 1)]
+    for name, nbytes, nbuf, ctas, mode in cases:
+        bufs = [torch.empty(nbytes, dtype=torch.uint8, device=dev).fill_(i + 1) for i in range(nbuf)]
+        sink = torch.zeros(ctas, dtype=torch.int32, device=dev)
+        launches = 64 if nbuf > 1 else 8
+
+        def go(n):
+            for i in range(n):
+                b = bufs[i % nbuf]
+                tq._check(lib.tq_read_probe(tq._ptr(b), nbytes, ctas, mode, tq._ptr(sink),
+                                            tq._stream(stream)))
+
+        go(nbuf)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                go(launches)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            g.replay()
+        torch.cuda.synchronize()
+        t_ms = _graph_time(stream, g, 4)
+        us = t_ms * 1000.0 / (4 * launches)
+        res[name] = {"bytes_per_launch": nbytes, "ctas": ctas, "us_per_launch": us,
+                     "gbs": nbytes / (us * 1e-6) / 1e9,
+                     "mode": "bulk copies into smem" if mode == 0 else "16-byte ld.global.nc"}
+        del g, bufs
+        torch.cuda.synchronize()
+    assert tq.device_error() == 0, "a kernel reported a device error"
+    torch.cuda.empty_cache()
+    return res
+
+
 # ----------------------------------------------------------- CPU reference --
 
 def cpu_reference(n_ctx: int, window: int, steps: int, warmup: int, seed: int = 5):
@@ -799,6 +1265,34 @@ def cpu_reference(n_ctx: int, window: int, steps: int, warmup: int, seed: int = 
 
 # --------------------------------------------------------------------- main --
 
+def reference_line(args, config: dict) -> dict:
+    """The reference arm: the reference's algorithm for config 1 on the host
+    cores (the oracle port: quantize the new token, concatenate it onto the
+    packed cache, dequantize, fp32 SDPA), OpenMP over every host thread --
+    set explicitly, since torch.distributed.run exports OMP_NUM_THREADS=1."""
+    from oracle import oracle as O
+    O.set_num_threads(os.cpu_count() or 1)
+    steps = max(1, min(args.steps, 20))
+    warm = max(0, min(args.warmup, 2))
+    value, cores, dt = cpu_reference(args.context, args.window, steps, warm)
+    return {"metric": "int4-KV decode-attention tokens/s", "value": value, "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": steps, "warmup": warm,
+            "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy)",
+            "config": config, "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port",
+                             "sample": f"{steps} full decode steps (quantize+concatenate "
+                                       f"append, dequantize, fp32 SDPA) of the same layer"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def _nested(line: dict) -> dict:
+    """A standalone line as a nested object of the headline line."""
+    drop = ("n_gpus", "warmup", "higher_is_better", "vs_baseline", "data")
+    return {k: v for k, v in line.items() if k not in drop}
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -818,6 +1312,8 @@ def main():
     if args.impl == "reference" and args.workload == "cfg2":
         if rank != 0:
             return
+        from oracle import oracle as O
+        O.set_num_threads(os.cpu_count() or 1)
         cpu = cpu_reference_cfg2()
         v = cpu["batched_tokens_s"]
         line = {"metric": "int4-KV decode-attention tokens/s", "value": v, "unit": "tokens/s",
@@ -835,21 +1331,7 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        steps = max(1, min(args.steps, 20))
-        warm = max(0, min(args.warmup, 2))
-        value, cores, dt = cpu_reference(n_ctx, window, steps, warm)
-        line = {"metric": "int4-KV decode-attention tokens/s", "value": value, "unit": "tokens/s",
-                "n_gpus": args.gpus, "steps": steps, "warmup": warm,
-                "ms_per_step": 1000.0 / value, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded numpy)",
-                "config": config, "impl": "reference",
-                "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores,
-                                 "kind": "port",
-                                 "sample": f"{steps} full decode steps (quantize+concatenate "
-                                           f"append, dequantize, fp32 SDPA) of the same layer"},
-                "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                        "d2h_bytes_per_step": 0}}
-        print(json.dumps(line), flush=True)
+        print(json.dumps(reference_line(args, config)), flush=True)
         return
 
     import torch
@@ -857,25 +1339,32 @@ def main():
     if world > 1:
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120))
-    if args.workload == "cfg4":
-        line = run_cfg4(args, rank, world, local_rank)
+
+    def finish(line):
         if rank == 0:
             print(json.dumps(line), flush=True)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
-        return
+
+    if args.workload == "cfg4":
+        line = run_cfg4(args, rank, world, local_rank, steps=max(64, args.steps),
+                        check=not args.no_check)
+        line.update({"n_gpus": world, "warmup": args.warmup, "higher_is_better": True,
+                     "vs_baseline": None, "dtype": "f32",
+                     "data": "synthetic (seeded torch.randn, RMS-normalised Q/K as task configs[0])"})
+        return finish(line)
     if args.workload == "cfg2":
         res = run_cfg2(args, rank, world, local_rank)
         cpu = None
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             cpu = cpu_reference_cfg2()
-        if rank == 0:
-            print(json.dumps(cfg2_line(args, world, res, cpu)), flush=True)
-        if world > 1:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
+        return finish(cfg2_line(args, world, res, cpu))
+    if args.workload in ("cfg0", "cfg3", "probe"):
+        fn = {"cfg0": lambda: run_cfg0(args, local_rank), "cfg3": lambda: run_cfg3(args, local_rank),
+              "probe": lambda: run_probe(local_rank)}[args.workload]
+        return finish(fn())
+
     res = run_ours(args, rank, world, local_rank)
     steps_total = args.steps * world
     value = steps_total / (res["t_ms"] / 1000.0)
@@ -891,6 +1380,8 @@ def main():
                 "frac_of_8tbs_nominal": achieved / 8000.0}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        O.set_num_threads(os.cpu_count() or 1)
         cv, cores, dt = cpu_reference(n_ctx, window, steps=10, warmup=1)
         cpu = {"value": cv, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"10 decode steps of one layer at ctx {n_ctx} ({dt:.1f} s): "
@@ -917,13 +1408,34 @@ def main():
             "gpu_launches": (2 if args.split_step else 1) * args.steps,
             "launches_per_step": ("2 (quantize_rows_kernel for K+V, decode_mma_kernel)" if args.split_step
                                   else "1 (decode_mma_kernel with the new token's quantize-on-append fused)"),
+            "timed_region": f"one CUDA graph of exactly {args.steps} steps",
             "clocks": res["clocks"],
             "hbm_gbs_step": bps["step"] * value / world / 1e9}
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    del res
+    torch.cuda.empty_cache()
+
+    if args.workload == "all":
+        # the other configs, nested; the sequence split (config 4) at every N,
+        # the single-GPU configs on one GPU only
+        nested = {}
+        if world == 1:
+            nested["cfg0"] = run_cfg0(args, local_rank)
+            torch.cuda.empty_cache()
+            r2 = run_cfg2(args, rank, world, local_rank)
+            cpu2 = None if args.no_cpu_baseline else cpu_reference_cfg2(budget_s=8.0)
+            nested["cfg2"] = _nested(cfg2_line(args, world, r2, cpu2))
+            torch.cuda.empty_cache()
+            nested["cfg3"] = run_cfg3(args, local_rank)
+            torch.cuda.empty_cache()
+            nested["hbm_probe"] = run_probe(local_rank)
+            if nested["hbm_probe"]:
+                best = max(v["gbs"] for v in nested["hbm_probe"].values())
+                line["roofline"]["frac_of_read_probe"] = achieved / best
+                line["roofline"]["read_probe_gbs"] = best
+        nested["cfg4"] = run_cfg4(args, rank, world, local_rank, steps=256, check=not args.no_check)
+        torch.cuda.empty_cache()
+        line["configs"] = nested
+    finish(line)
 
 
 if __name__ == "__main__":

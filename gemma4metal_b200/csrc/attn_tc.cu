@@ -706,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
     // split partials, column-major so a warp's 32 rows are one 128 B store:
     // ws[unit][split][d or m or l][row]
     float* wsr = p.ws + (unit * p.splits + split) * (kD + 2) * kRows + rl;
-    const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
+    const float inv = l_tot == 0.0f ? 0.0f : 1.0f / l_tot;
     const long long ob = (static_cast<long long>(qi) * p.H + h) * kD;
     const bool ovec = (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0;
 #pragma unroll 1
@@ -737,7 +737,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
       }
     }
     if (!direct && hf == 0) {
-      __stcg(wsr + kD * kRows, l_tot > 0.0f ? m_run : -INFINITY);
+      __stcg(wsr + kD * kRows, l_tot == 0.0f ? -INFINITY : m_run);
       __stcg(wsr + (kD + 1) * kRows, l_tot);
     }
   }
@@ -816,7 +816,7 @@ __global__ void __launch_bounds__(256) attn_tc_merge_kernel(const TCParams p, in
       for (int k = 0; k < 4; ++k) acc[k] = fmaf(e, v[k], acc[k]);
     }
   }
-  const float invL = L > 0.0f ? 1.0f / L : 0.0f;
+  const float invL = L == 0.0f ? 0.0f : 1.0f / L;
 #pragma unroll
   for (int k = 0; k < 4; ++k) tile[lane][4 * warp + k] = acc[k] * invL;
   __syncthreads();

@@ -29,7 +29,8 @@ __global__ void __launch_bounds__(kMergeThreads) lse_merge_kernel(const float* _
     for (int p = 0; p < P; ++p) {
       const float m = base[p * stride_p + static_cast<long long>(H) * D + 2 * h];
       const float l = base[p * stride_p + static_cast<long long>(H) * D + 2 * h + 1];
-      const float w = (M == -INFINITY || m == -INFINITY) ? 0.0f : __expf(m - M);
+      // an empty state (m = -inf) weighs 0; a NaN state makes the result NaN
+      const float w = m == -INFINITY ? 0.0f : __expf(m - M);
       e[p] = w;
       L += w * l;
     }
@@ -39,9 +40,10 @@ __global__ void __launch_bounds__(kMergeThreads) lse_merge_kernel(const float* _
   const float L = Ls;
   for (int d = threadIdx.x; d < D; d += kMergeThreads) {
     float acc = 0.0f;
-    for (int p = 0; p < P; ++p) acc += e[p] * base[p * stride_p + static_cast<long long>(h) * D + d];
+    for (int p = 0; p < P; ++p)  // an empty state's o is never read
+      if (e[p] != 0.0f) acc += e[p] * base[p * stride_p + static_cast<long long>(h) * D + d];
     store_from_float(out, (static_cast<long long>(b) * H + h) * D + d, out_dtype,
-                     L > 0.0f ? acc / L : 0.0f);
+                     L == 0.0f ? 0.0f : acc / L);
   }
 }
 

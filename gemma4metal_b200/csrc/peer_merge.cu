@@ -13,8 +13,13 @@
 // Flags only grow and the ranks advance in lockstep (a rank's step e + 1
 // needs every rank's push of e + 1, which follows that rank's merge of e), so
 // a rank is at most one step ahead and the parity slots never collide. Every
-// wait is bounded; on timeout the kernel records kErrPeerTimeout in the device
-// error word and returns.
+// wait is bounded. On timeout the kernel records kErrPeerTimeout in the device
+// error word, writes NaN to the outputs of the items whose states it could not
+// gather (never a merge of stale slots), marks the exchange failed in its own
+// header and leaves its step counter where it was; every later merge on a
+// failed exchange records the timeout again and writes NaN. A failed exchange
+// is out of step with the other ranks for good: the caller closes it and
+// builds a new one.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -29,6 +34,7 @@ namespace {
 
 constexpr int kHeaderWords = 32 * 66;  // step counter, 64 flags (128 B apart), grid counter
 constexpr int kGridCounter = 32 * 65;
+constexpr int kFailedWord = 32 * 65 + 16;  // nonzero once a wait of this rank timed out
 __device__ __forceinline__ int flag_word(int k) { return 32 * (1 + k); }
 constexpr int kMaxWorld = 64;
 constexpr int kPeerThreads = 256;
@@ -57,8 +63,12 @@ __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerPara
   __shared__ uint32_t s_step;
   __shared__ float s_w[kMaxWorld];
   __shared__ float s_L;
+  __shared__ int s_failed;
   uint32_t* own = static_cast<uint32_t*>(p.bufs[p.rank]);
-  if (threadIdx.x == 0) s_step = *reinterpret_cast<volatile uint32_t*>(own) + 1u;
+  if (threadIdx.x == 0) {
+    s_step = *reinterpret_cast<volatile uint32_t*>(own) + 1u;
+    s_failed = *reinterpret_cast<volatile uint32_t*>(own + kFailedWord) != 0u;
+  }
   __syncthreads();
   const uint32_t step = s_step;
   const long long blk = static_cast<long long>(p.B) * p.H * (p.D + 2);  // floats per state
@@ -80,18 +90,21 @@ __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerPara
     if (threadIdx.x == 0) st_release_sys(static_cast<uint32_t*>(p.bufs[j]) + flag_word(p.rank), step);
   }
 
-  // ---- wait for every rank's state of this step (bounded)
-  if (threadIdx.x < p.world) {
+  // ---- wait for every rank's state of this step (bounded; none on a failed exchange)
+  if (threadIdx.x < p.world && !s_failed) {
     const uint32_t* flag = own + flag_word(threadIdx.x);
     const long long t0 = clock64();
     while (static_cast<int>(ld_acquire_sys(flag) - step) < 0) {
       if (clock64() - t0 > p.budget) {
-        atomicOr(p.err, kErrPeerTimeout);
+        s_failed = 1;
+        atomicOr(own + kFailedWord, 1u);
         break;
       }
     }
   }
   __syncthreads();
+  const bool failed = s_failed != 0;
+  if (failed && threadIdx.x == 0) atomicOr(p.err, kErrPeerTimeout);
 
   // ---- merge: CTA c takes (sequence, head) items c, c + grid, ...
   const float* data = reinterpret_cast<const float*>(own + kHeaderWords) +
@@ -100,6 +113,11 @@ __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerPara
   for (int item = blockIdx.x; item < p.B * p.H; item += gridDim.x) {
     const int b = item / p.H, h = item % p.H;
     const float* base = data + static_cast<long long>(b) * p.H * (p.D + 2);
+    if (failed) {  // no complete set of states: NaN, never stale slots
+      for (int d = threadIdx.x; d < p.D; d += kPeerThreads)
+        store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * p.D + d, p.out_dtype, NAN);
+      continue;
+    }
     if (threadIdx.x == 0) {
       float M = -INFINITY;
       for (int k = 0; k < p.world; ++k) M = fmaxf(M, __ldcg(base + k * blk + hd + 2 * h));
@@ -107,7 +125,8 @@ __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerPara
       for (int k = 0; k < p.world; ++k) {
         const float m = __ldcg(base + k * blk + hd + 2 * h);
         const float l = __ldcg(base + k * blk + hd + 2 * h + 1);
-        const float w = (M == -INFINITY || m == -INFINITY) ? 0.0f : __expf(m - M);
+        // an empty state (m = -inf) weighs 0; a NaN state makes the result NaN
+      const float w = m == -INFINITY ? 0.0f : __expf(m - M);
         s_w[k] = w;
         L += w * l;
       }
@@ -117,9 +136,10 @@ __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerPara
     const float L = s_L;
     for (int d = threadIdx.x; d < p.D; d += kPeerThreads) {
       float acc = 0.0f;
-      for (int k = 0; k < p.world; ++k) acc += s_w[k] * __ldcg(base + k * blk + static_cast<long long>(h) * p.D + d);
+      for (int k = 0; k < p.world; ++k)  // an empty state's o is never read
+        if (s_w[k] != 0.0f) acc += s_w[k] * __ldcg(base + k * blk + static_cast<long long>(h) * p.D + d);
       store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * p.D + d, p.out_dtype,
-                       L > 0.0f ? acc / L : 0.0f);
+                       L == 0.0f ? 0.0f : acc / L);
     }
     __syncthreads();
   }
@@ -132,7 +152,9 @@ __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerPara
     const unsigned done = atomicAdd(own + kGridCounter, 1u);
     if (done == gridDim.x - 1) {
       own[kGridCounter] = 0u;
-      *reinterpret_cast<volatile uint32_t*>(own) = step;
+      // a failed exchange keeps its step: it is out of step with the others for good
+      if (*reinterpret_cast<volatile uint32_t*>(own + kFailedWord) == 0u)
+        *reinterpret_cast<volatile uint32_t*>(own) = step;
     }
   }
 }

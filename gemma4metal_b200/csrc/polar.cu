@@ -427,7 +427,7 @@ __global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p, c
       acc = fmaf(e, __ldcg(ps + d), acc);
     }
     store_from_float(p.out, static_cast<long long>(h0 + g) * D + d, p.out_dtype,
-                     L > 0.0f ? acc / L : 0.0f);
+                     L == 0.0f ? 0.0f : acc / L);
   }
   if (tid == 0) p.counters[kv] = 0u;
 }

@@ -440,18 +440,18 @@ __global__ void __launch_bounds__(kThreads, G >= 8 ? 2 : kMinBlocksPerSM) decode
         float* blk = p.part_out + static_cast<long long>(b) * p.H * (D + 2);
         blk[static_cast<long long>(h) * D + d] = acc;
         if (d == 0) {
-          blk[static_cast<long long>(p.H) * D + 2 * h] = lg > 0.0f ? mg * kLn2 : -INFINITY;
+          blk[static_cast<long long>(p.H) * D + 2 * h] = lg == 0.0f ? -INFINITY : mg * kLn2;
           blk[static_cast<long long>(p.H) * D + 2 * h + 1] = lg;
         }
       } else {
         store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * D + d, p.out_dtype,
-                         lg > 0.0f ? acc / lg : 0.0f);
+                         lg == 0.0f ? 0.0f : acc / lg);
       }
     } else {
       const long long base = (unit * p.splits + split) * G;
       p.ws_o[(base + g) * D + d] = acc;
       if (d == 0) {
-        p.ws_ml[(base + g) * 2] = lg > 0.0f ? mg : -INFINITY;
+        p.ws_ml[(base + g) * 2] = lg == 0.0f ? -INFINITY : mg;
         p.ws_ml[(base + g) * 2 + 1] = lg;
       }
     }
@@ -519,12 +519,12 @@ __global__ void __launch_bounds__(kThreads, G >= 8 ? 2 : kMinBlocksPerSM) decode
       float* blk = p.part_out + static_cast<long long>(b) * p.H * (D + 2);
       blk[static_cast<long long>(h) * D + d] = acc;
       if (d == 0) {
-        blk[static_cast<long long>(p.H) * D + 2 * h] = L > 0.0f ? Mv * kLn2 : -INFINITY;
+        blk[static_cast<long long>(p.H) * D + 2 * h] = L == 0.0f ? -INFINITY : Mv * kLn2;
         blk[static_cast<long long>(p.H) * D + 2 * h + 1] = L;
       }
     } else {
       store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * D + d, p.out_dtype,
-                       L > 0.0f ? acc / L : 0.0f);
+                       L == 0.0f ? 0.0f : acc / L);
     }
   }
   if (tid == 0) p.counters[unit] = 0u;  // ready for the next launch

@@ -699,8 +699,8 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
           w[g] = pr[bt][it] * sv[bt][f][g];
           float cb = pr[bt][it] * fmaf(-64.0f, sv[bt][f][g], bv[bt][f][g]);
           if constexpr (MASKED) {  // stale scales of masked tokens must not leak
-            w[g] = pr[bt][it] > 0.0f ? w[g] : 0.0f;
-            cb = pr[bt][it] > 0.0f ? cb : 0.0f;
+            w[g] = pr[bt][it] == 0.0f ? 0.0f : w[g];
+            cb = pr[bt][it] == 0.0f ? 0.0f : cb;
           }
           corr[e][g] += cb;
         }
@@ -920,18 +920,18 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
         float* blk = p.part_out + static_cast<long long>(b) * p.H * (D + 2);
         blk[static_cast<long long>(h) * D + d] = acc;
         if (d == 0) {
-          blk[static_cast<long long>(p.H) * D + 2 * h] = L > 0.0f ? M * kLn2 : -INFINITY;
+          blk[static_cast<long long>(p.H) * D + 2 * h] = L == 0.0f ? -INFINITY : M * kLn2;
           blk[static_cast<long long>(p.H) * D + 2 * h + 1] = L;
         }
       } else {
         store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * D + d, p.out_dtype,
-                         L > 0.0f ? acc / L : 0.0f);
+                         L == 0.0f ? 0.0f : acc / L);
       }
     } else {
       const long long base = (unit * p.splits + split) * G;
       p.ws_o[(base + g) * D + d] = acc;
       if (d == 0) {
-        p.ws_ml[(base + g) * 2] = L > 0.0f ? M : -INFINITY;
+        p.ws_ml[(base + g) * 2] = L == 0.0f ? -INFINITY : M;
         p.ws_ml[(base + g) * 2 + 1] = L;
       }
     }
@@ -1033,11 +1033,11 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
 #pragma unroll
       for (int j = 0; j < 4; ++j) blk[static_cast<long long>(h) * D + d + j] = av[j];
       if (d == 0) {
-        blk[static_cast<long long>(p.H) * D + 2 * h] = L > 0.0f ? M * kLn2 : -INFINITY;
+        blk[static_cast<long long>(p.H) * D + 2 * h] = L == 0.0f ? -INFINITY : M * kLn2;
         blk[static_cast<long long>(p.H) * D + 2 * h + 1] = L;
       }
     } else {
-      const float inv = L > 0.0f ? 1.0f / L : 0.0f;
+      const float inv = L == 0.0f ? 0.0f : 1.0f / L;
 #pragma unroll
       for (int j = 0; j < 4; ++j)
         store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * D + d + j, p.out_dtype,

@@ -93,6 +93,7 @@ class PeerExchange:
         self.world, self.rank = _world_rank(group)
         self.B, self.H, self.D = batch, num_heads, head_dim
         self.timeout_us = int(timeout_us)
+        self.failed = False
         self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         lib = tq.load_library()
         nbytes = int(lib.tq_peer_buffer_bytes(self.world, batch, num_heads, head_dim))
@@ -127,7 +128,11 @@ class PeerExchange:
     def merge(self, part: torch.Tensor, out: Optional[torch.Tensor] = None,
               out_dtype: torch.dtype = torch.float32, s=None) -> torch.Tensor:
         """Push this rank's state (B, H*(D+2)) fp32, wait for the others',
-        return the merged (B, H, D)."""
+        return the merged (B, H, D). Raises once `check` has seen a timeout:
+        the exchange is then out of step with the other ranks for good."""
+        if self.failed:
+            raise RuntimeError("PeerExchange: a merge timed out on this exchange; close it and "
+                               "build a new one on every rank")
         if out is None:
             out = torch.empty(self.B, self.H, self.D, dtype=out_dtype, device=self.device)
         pc = part.contiguous()
@@ -135,6 +140,17 @@ class PeerExchange:
             tq._ptr(pc), self.bufs.data_ptr(), self.world, self.rank, self.B, self.H, self.D,
             tq._ptr(out), tq._dt(out), self.timeout_us, tq._stream(s)))
         return out
+
+    def check(self, s=None) -> None:
+        """Read (and clear) the device error word after the merges enqueued so
+        far (synchronises the stream); raise if one of them timed out waiting
+        for a rank. After that every merge raises: a timed-out exchange is
+        marked failed on the device, writes NaN and never advances again."""
+        code = tq.device_error(s)
+        if code & 2:  # TQ_DEVICE_ERR_PEER_TIMEOUT
+            self.failed = True
+            raise RuntimeError("PeerExchange: a rank did not deliver its state within "
+                               f"{self.timeout_us} us (device error {code})")
 
     def close(self) -> None:
         lib = tq.load_library()
@@ -222,3 +238,116 @@ class SeqSplitCache:
         return seqsplit_decode(queries, self.cache.tensors(), self.n_local, self.t0, self.n_total,
                                gqa_factor, scale, sliding_window, group=self.group,
                                out_dtype=out_dtype, exchange=exchange)
+
+
+# ------------------------------------------------------------- failures --
+# A sequence split needs every rank at every step: one missing shard makes
+# every rank's merge wrong or stuck. Failures are caught on the host, between
+# steps (a rank leaves only between steps, with nothing of its own in flight):
+#   * StepGuard.begin(step): every rank posts a heartbeat for `step` to the
+#     process group's key-value store and waits, bounded, for the others'
+#     heartbeats of the same step before it launches anything; a rank that
+#     exited, crashed or hangs on the host is named in RankLost.
+#   * StepGuard.wait(event): the host waits, bounded, for an enqueued step to
+#     complete on the GPU; past the bound the communicator is aborted (NCCL:
+#     ncclCommAbort through the process group) and StepTimeout is raised, so
+#     no rank waits for good on a collective a lost rank will never join.
+#   * init_split_group(): NCCL communicators are created non-blocking
+#     (config.blocking = 0); the process group polls the communicator's
+#     asynchronous error state (ncclCommGetAsyncError) while it waits, so an
+#     init or a collective that fails is reported instead of hanging, within
+#     the group's timeout.
+# The peer-memory exchange has its own bound (PeerExchange: NaN outputs,
+# TQ_DEVICE_ERR_PEER_TIMEOUT, check()).
+
+
+class RankLost(RuntimeError):
+    """Ranks of the split that did not reach a step within the bound."""
+
+    def __init__(self, step: int, missing):
+        self.step, self.missing = step, sorted(missing)
+        super().__init__(f"sequence split: rank(s) {self.missing} did not reach step {step}")
+
+
+class StepTimeout(RuntimeError):
+    """An enqueued step did not complete within the host's bound."""
+
+
+def init_split_group(backend: str = "nccl", timeout_s: float = 60.0, device=None):
+    """init_process_group for a sequence split with a short timeout and, for
+    NCCL, non-blocking communicator creation."""
+    from datetime import timedelta
+    kw = {"timeout": timedelta(seconds=timeout_s)}
+    if backend == "nccl":
+        opts = dist.ProcessGroupNCCL.Options()
+        opts.config.blocking = 0
+        kw["pg_options"] = opts
+        if device is not None:
+            kw["device_id"] = torch.device(device)
+    dist.init_process_group(backend, **kw)
+
+
+def abort_group(group=None) -> None:
+    """Abort the group's communicators (pending collectives return with an
+    error on every rank that is still there)."""
+    from torch.distributed import distributed_c10d as c10d
+    if hasattr(c10d, "_abort_process_group"):
+        c10d._abort_process_group(group)
+        return
+    pg = group if group is not None else c10d._get_default_group()
+    pg.abort()
+
+
+class StepGuard:
+    """Host-side liveness checks of a sequence split between steps (see the
+    section comment above). `store` defaults to the default process group's
+    store; `timeout_s` bounds each wait; `abort` is what runs when a step
+    overruns (abort_group by default)."""
+
+    def __init__(self, world: int, rank: int, timeout_s: float = 10.0, store=None,
+                 prefix: str = "tq/split", abort: Optional[Callable] = None, group=None):
+        from torch.distributed import distributed_c10d as c10d
+        self.world, self.rank = world, rank
+        self.timeout_s = float(timeout_s)
+        self.store = store if store is not None else c10d._get_default_store()
+        self.prefix = prefix
+        self.group = group
+        self.abort = abort if abort is not None else (lambda: abort_group(group))
+
+    def _key(self, step: int, rank: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def begin(self, step: int) -> None:
+        """Post this rank's heartbeat for `step`, then wait (bounded) until
+        every rank has posted it; raise RankLost naming the missing ranks."""
+        import time
+        self.store.set(self._key(step, self.rank), "1")
+        if step >= 2:  # keys two steps back are read by nobody any more
+            try:
+                self.store.delete_key(self._key(step - 2, self.rank))
+            except Exception:
+                pass
+        deadline = time.monotonic() + self.timeout_s
+        missing = {r for r in range(self.world) if r != self.rank}
+        while True:
+            for r in sorted(missing):
+                if self.store.check([self._key(step, r)]):
+                    missing.discard(r)
+            if not missing:
+                return
+            if time.monotonic() >= deadline:
+                raise RankLost(step, missing)
+            time.sleep(0.0002)
+
+    def wait(self, event, what: str = "step") -> None:
+        """Wait (bounded) for `event` (anything with .query(), e.g. a
+        torch.cuda.Event recorded after the step); past the bound abort the
+        communicators and raise StepTimeout."""
+        import time
+        deadline = time.monotonic() + self.timeout_s
+        while not event.query():
+            if time.monotonic() > deadline:
+                self.abort()
+                raise StepTimeout(f"sequence split: {what} did not complete within "
+                                  f"{self.timeout_s} s; communicators aborted")
+            time.sleep(0.0005)

@@ -102,6 +102,8 @@ def _register_extra(L) -> None:
     L.tq_sdpa_int4_append_slots.argtypes = [P, I, P, P, I, P, P, P, P, P, P, I, I, F, I, I, I, I,
                                             I, I, P, P, P, I, P, SZ, P]
     L.tq_decode_step_destroy.argtypes = [P]
+    L.tq_read_probe.argtypes = [P, SZ, I, I, P, P]
+    L.tq_wait_selftest.argtypes = [I, P, P]
     L.tq_sdpa_int4_multi_workspace_size.restype = SZ
     L.tq_sdpa_int4_multi_workspace_size.argtypes = [I, I, I, I, I]
     L.tq_sdpa_int4_multi.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, I, I, P, I,

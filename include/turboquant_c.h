@@ -207,8 +207,11 @@ TQ_API int tq_sdpa_int4_partial(const void* queries, tq_dtype q_dtype, const uin
  * the world's buffer pointers (this rank's own at [rank]). Every rank calls it
  * once per step, in the same order; a rank that does not arrive within
  * timeout_us makes the others record TQ_DEVICE_ERR_PEER_TIMEOUT in the device
- * error word (tq_device_error) and return. No counterpart in the reference
- * (it is single-device). */
+ * error word (tq_device_error) and return with NaN in the outputs they could
+ * not merge. Such an exchange is marked failed in its own buffer and stays
+ * failed (later merges return NaN and record the timeout again, its step
+ * counter no longer moves): close it and allocate a new one. No counterpart
+ * in the reference (it is single-device). */
 #define TQ_IPC_HANDLE_BYTES 64
 #define TQ_DEVICE_ERR_BARRIER_TIMEOUT 1u
 #define TQ_DEVICE_ERR_PEER_TIMEOUT 2u
@@ -458,6 +461,15 @@ TQ_API int tq_decode_step_destroy(tq_decode_step* step);
  * write per read). No counterpart in the reference. */
 TQ_API int tq_read_probe(const void* src, size_t bytes, int ctas, int mode, uint32_t* sink,
                          void* stream);
+
+/* Failure-path self-test: one warp waits on a shared-memory barrier that
+ * never completes, with the bounded wait every pipeline here uses, given up
+ * after timeout_us (1 .. 10^7). Expected outcome: TQ_DEVICE_ERR_BARRIER_TIMEOUT
+ * in the device error word, *gave_up (device uint32, caller-zeroed)
+ * incremented by each of the 32 threads, and a usable context afterwards.
+ * (The pipelines' own bound is about 2 s of SM clock.) No counterpart in the
+ * reference. */
+TQ_API int tq_wait_selftest(int timeout_us, uint32_t* gave_up, void* stream);
 
 /* Read and clear the device error word that kernels set when a bounded wait
  * gives up (0 = no error). Synchronises `stream`. */

@@ -313,15 +313,19 @@ def lse_merge_np(parts: np.ndarray, H: int, D: int) -> np.ndarray:
     o = parts[:, : H * D].reshape(P, H, D).astype(np.float64)
     ml = parts[:, H * D:].reshape(P, H, 2).astype(np.float64)
     m, l = ml[..., 0], ml[..., 1]
+    bad = np.isnan(m).any(axis=0) | np.isnan(l).any(axis=0)  # a NaN state poisons its head
+    m = np.where(np.isnan(m), -np.inf, m)
     M = m.max(axis=0)
-    out = np.zeros((H, D), np.float32)
     ok = np.isfinite(M)
     e = np.where(ok[None], np.exp(m - np.where(ok, M, 0.0)[None]), 0.0)
     L = (e * l).sum(axis=0)
-    num = (e[..., None] * o).sum(axis=0)
-    good = L > 0
-    out[good] = (num[good] / L[good][:, None]).astype(np.float32)
-    return out
+    num = (np.where(e[..., None] == 0, 0.0, e[..., None] * o)).sum(axis=0)
+    L = np.where(bad, np.nan, L)
+    # the reference's rule: an empty softmax (sum 0) gives 0, a NaN sum stays
+    # NaN (lib/turboquant.metal:886)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        out = np.where((L == 0)[:, None], 0.0, num / np.where(L == 0, 1.0, L)[:, None])
+    return out.astype(np.float32)
 
 
 def lse_merge(parts: np.ndarray, H: int, D: int) -> np.ndarray:
@@ -460,8 +464,8 @@ def sdpa_multi_f64(q, k, v, scale=1.0, causal=False, pos0=0, window=0, n_tokens=
             m = s.max(axis=1, keepdims=True)
             p = np.where(vis, np.exp(s - np.where(np.isfinite(m), m, 0.0)), 0.0)
             l = p.sum(axis=1, keepdims=True)
-            o = (p @ vv) / np.where(l > 0, l, 1.0)
-            o = np.where(l > 0, o, 0.0)
+            o = (p @ vv) / np.where(l == 0, 1.0, l)
+            o = np.where(l == 0, 0.0, o)
             out[r0:r1, hk * G:(hk + 1) * G] = o.reshape(r1 - r0, G, D).astype(np.float32)
     return out
 
@@ -488,5 +492,5 @@ def sdpa_multi_np(q, k, v, scale=1.0, causal=False, pos0=0, window=0, n_tokens=N
     p = np.where(np.isfinite(s), np.exp(s - np.where(np.isfinite(m), m, 0)), 0.0)
     l = p.sum(axis=-1, keepdims=True)
     o = np.einsum("qhgt,htd->qhgd", p, v[:, :N].astype(np.float64))
-    out = np.where(l > 0, o / np.where(l > 0, l, 1), 0.0)
+    out = np.where(l == 0, 0.0, o / np.where(l == 0, 1, l))
     return out.reshape(nq, H, D).astype(np.float32)

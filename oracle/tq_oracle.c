@@ -199,7 +199,7 @@ void tqo_sdpa_dense(const float* q, const float* k, const float* v, int B, int H
           const float* vt = vb + (int64_t)(t0 + i) * D;
           for (int d = 0; d < D; ++d) acc[d] += p * (double)vt[d];
         }
-        for (int d = 0; d < D; ++d) oh[d] = l > 0.0 ? (float)(acc[d] / l) : 0.0f;
+        for (int d = 0; d < D; ++d) oh[d] = l == 0.0 ? 0.0f : (float)(acc[d] / l);
         free(sc);
         free(acc);
       } else {
@@ -221,7 +221,7 @@ void tqo_sdpa_dense(const float* q, const float* k, const float* v, int B, int H
           const float* vt = vb + (int64_t)(t0 + i) * D;
           for (int d = 0; d < D; ++d) acc[d] += p * vt[d];
         }
-        for (int d = 0; d < D; ++d) oh[d] = l > 0.0f ? acc[d] / l : 0.0f;
+        for (int d = 0; d < D; ++d) oh[d] = l == 0.0f ? 0.0f : acc[d] / l;
         free(sc);
         free(acc);
         free(qs);
@@ -375,16 +375,15 @@ void tqo_lse_merge(const float* parts, int P, int H, int D, float* out) {
     }
     double L = 0.0;
     double* acc = (double*)calloc(D, sizeof(double));
-    if (M != -INFINITY) {
-      for (int p = 0; p < P; ++p) {
-        const double m = parts[p * blk + (int64_t)H * D + 2 * h];
-        const double l = parts[p * blk + (int64_t)H * D + 2 * h + 1];
-        const double e = exp(m - M);
-        L += e * l;
-        for (int d = 0; d < D; ++d) acc[d] += e * parts[p * blk + (int64_t)h * D + d];
-      }
+    for (int p = 0; p < P; ++p) {
+      const double m = parts[p * blk + (int64_t)H * D + 2 * h];
+      const double l = parts[p * blk + (int64_t)H * D + 2 * h + 1];
+      if (m == -INFINITY) continue; /* an empty state (its o is never read) */
+      const double e = exp(m - M);  /* a NaN state makes L and the head NaN */
+      L += e * l;
+      for (int d = 0; d < D; ++d) acc[d] += e * parts[p * blk + (int64_t)h * D + d];
     }
-    for (int d = 0; d < D; ++d) out[h * D + d] = L > 0.0 ? (float)(acc[d] / L) : 0.0f;
+    for (int d = 0; d < D; ++d) out[h * D + d] = L == 0.0 ? 0.0f : (float)(acc[d] / L);
     free(acc);
   }
 }

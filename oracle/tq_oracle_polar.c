@@ -278,7 +278,7 @@ void tqo_compressed_sdpa(const void* q, int q_dtype, int H, int Hkv, int D, int 
         o[d] += p * (sc * c + bi);
       }
     }
-    for (int d = 0; d < D; ++d) out[(int64_t)h * D + d] = l > 0 ? (float)(o[d] / l) : 0.0f;
+    for (int d = 0; d < D; ++d) out[(int64_t)h * D + d] = l == 0 ? 0.0f : (float)(o[d] / l);
     free(s);
   }
 }

@@ -129,9 +129,25 @@ def _peer_worker(rank, world, port, q, mode):
         else:  # rank 1 misses one step: rank 0's merge must time out, record it, return
             part_q = q16
             if rank == 0:
-                sc.decode(part_q, H // Hkv, 1.0, 0, out_dtype=torch.float32, exchange=ex)
+                out = sc.decode(part_q, H // Hkv, 1.0, 0, out_dtype=torch.float32, exchange=ex)
                 torch.cuda.synchronize()
                 code = tq.device_error()
+                # never a merge of stale slots: the outputs are NaN
+                assert bool(torch.isnan(out).all()), "timed-out merge must write NaN"
+                # the exchange stays failed: the next merge gives up at once
+                out2 = sc.decode(part_q, H // Hkv, 1.0, 0, out_dtype=torch.float32, exchange=ex)
+                torch.cuda.synchronize()
+                assert bool(torch.isnan(out2).all())
+                try:
+                    ex.check()
+                    raise AssertionError("check() must raise after a timeout")
+                except RuntimeError:
+                    pass
+                try:
+                    ex.merge(torch.zeros(1, H * (D + 2), device="cuda"))
+                    raise AssertionError("merge() must raise on a failed exchange")
+                except RuntimeError:
+                    pass
             else:
                 code = -1
             dist.barrier()

@@ -119,6 +119,8 @@ def load_kv_cache(path: str, device=None, capacity: Optional[int] = None,
         _, hkv, T, w8 = arr[0].shape
         D = w8 * 8
         sdt = arr[1].dtype
+        if sdt == torch.bfloat16:  # an engine running in bf16; widened exactly (kernels: f16/f32)
+            sdt = torch.float32
         if windows and layer in windows:
             W = windows[layer]
             if T > W:

@@ -235,7 +235,10 @@ class RingKVCache(KVCache):
 
     def __init__(self, num_kv_heads: int, head_dim: int, window: int, device=None,
                  scales_dtype: torch.dtype = torch.float16):
-        super().__init__(1, num_kv_heads, head_dim, window, device=device, scales_dtype=scales_dtype)
+        # any window: the token axis is the window rounded up to 4 (16-byte
+        # aligned rows per KV head); slots past the window stay unused
+        super().__init__(1, num_kv_heads, head_dim, (window + 3) // 4 * 4, device=device,
+                         scales_dtype=scales_dtype)
         self.window = window
         self.total = 0  # tokens appended so far (the layer's position)
 

@@ -30,6 +30,7 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <map>
 #include <memory>
 #include <string>
 #include <vector>
@@ -104,12 +105,24 @@ TQ_CXX_API array dequantize(const array& w, const array& scales, const array& bi
 // queries (H, D); k_quant/v_quant (Hkv, N, D/8) uint32; scales/biases
 // (Hkv, N, D/64). Returns (H, D) in the query dtype. Query head h reads KV
 // head h / gqa_factor; sliding_window > 0 masks tokens t with
-// (N-1-t) >= sliding_window. A token count N that is not a multiple of 4 is
-// served through a padded copy of the cache (KVCache avoids it).
+// (N-1-t) >= sliding_window. The kernels need every KV head's rows 16-byte
+// aligned, i.e. a token axis that is a multiple of 4; a reference-shaped
+// cache with any other N (the reference's test uses N = 10) is served through
+// a copy into a capacity rounded up to 4 -- O(N) per call, as the engine's
+// concatenate is. Engine code avoids it with KVCache, RingKVCache (any
+// window) or sdpa_int4_tokens.
 TQ_CXX_API array sdpa_int4(const array& queries, const array& k_quant, const array& k_scales,
                 const array& k_biases, const array& v_quant, const array& v_scales,
                 const array& v_biases, int gqa_factor, float scale = 1.0f,
                 int sliding_window = 0, cudaStream_t s = nullptr);
+// The same over the first n_tokens rows of cache arrays whose token axis is a
+// capacity (a multiple of 4, >= n_tokens): any n_tokens, no copy.
+TQ_CXX_API array sdpa_int4_tokens(const array& queries, const array& k_quant,
+                                  const array& k_scales, const array& k_biases,
+                                  const array& v_quant, const array& v_scales,
+                                  const array& v_biases, int n_tokens, int gqa_factor,
+                                  float scale = 1.0f, int sliding_window = 0,
+                                  cudaStream_t s = nullptr);
 
 // No-op (lib/turboquant.h:209): kernels are linked into the library.
 TQ_CXX_API void set_metallib_path(const std::string& path);
@@ -146,6 +159,9 @@ class TQ_CXX_API KVCache {
   int length() const { return length_; }
   int capacity() const { return capacity_; }
   void reset() { length_ = 0; }
+  // Valid token count after the arrays were filled directly (e.g. by
+  // load_kv_cache); 0 <= n <= capacity.
+  void set_length(int n);
   array k_quant, k_scales, k_biases, v_quant, v_scales, v_biases;
 
  private:
@@ -196,6 +212,8 @@ class TQ_CXX_API HostDecodeStep {
 };
 
 // ---- sliding-window layer as a ring of `window` slots (batch 1) ---------------
+// Any window (the engine's 950-token cap included): the arrays' token axis is
+// the window rounded up to 4, slots past the window stay unused.
 // Token t lives in slot t % window, so the cache holds exactly the last
 // `window` tokens -- the set the window rule keeps -- with no copy (the
 // engine concatenates and trims the front, engine/gemma4_multilayer.cpp:228-249).
@@ -212,6 +230,10 @@ class TQ_CXX_API RingKVCache {
                     float scale = 1.0f, cudaStream_t s = nullptr);
   int n_valid() const { return total_ < window_ ? static_cast<int>(total_) : window_; }
   long long total() const { return total_; }
+  int window() const { return window_; }
+  // Tokens seen so far after the slots were filled directly (slot t % window
+  // holds token t); sets the cache's length to n_valid().
+  void set_total(long long total);
   KVCache cache;
 
  private:
@@ -287,6 +309,30 @@ TQ_CXX_API array compressed_score(const array& queries, const array& indices_l1,
                                   const array& cb_l2, const array& cb_l3, const array& cb_l4, int N,
                                   int block_size = 16, float scale = 0.0884f,
                                   cudaStream_t s = nullptr);
+
+// ---- the engine's on-disk int4 KV cache (kv_cache.safetensors) ---------------
+// Same file as the engine's save_kv_cache / load_kv_cache
+// (engine/gemma4_multilayer.cpp:113-144): one safetensors file holding
+// cache_offset (int32 [1]) and, per layer L with a cache, l{L}.kq/ks/kb/vq/vs/vb
+// = codes (1, Hkv, T, D/8) uint32 and scales/biases (1, Hkv, T, D/64), T
+// tokens oldest first (a sliding layer holds its last `window` tokens).
+struct TQ_CXX_API LoadedKVCache {
+  int cache_offset = 0;
+  std::map<int, std::unique_ptr<KVCache>> caches;     // layers not in `windows`
+  std::map<int, std::unique_ptr<RingKVCache>> rings;  // layers in `windows`
+};
+// Writes the valid tokens of every cache (batch 1), oldest first.
+TQ_CXX_API void save_kv_cache(const std::string& path, int cache_offset,
+                              const std::map<int, const KVCache*>& caches,
+                              const std::map<int, const RingKVCache*>& rings = {},
+                              cudaStream_t s = nullptr);
+// Layers listed in `windows` (layer -> window) load into a RingKVCache, the
+// others into a KVCache with room for max(capacity, T rounded up to 4)
+// tokens. fp16 and fp32 scales/biases load as stored; bf16 ones (an engine
+// running in bf16) are widened to fp32 exactly. Throws on a malformed file.
+TQ_CXX_API LoadedKVCache load_kv_cache(const std::string& path, int capacity = 0,
+                                       const std::map<int, int>& windows = {},
+                                       cudaStream_t s = nullptr);
 
 }  // namespace turboquant
 

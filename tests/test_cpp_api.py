@@ -53,3 +53,34 @@ def test_cpp_programs_pass(name):
     print(r.stdout)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "FAIL" not in r.stdout and r.stdout.strip().endswith("PASS")
+
+
+@pytest.mark.gpu
+def test_cpp_kv_cache_file_round_trip(tmp_path):
+    """The engine's kv_cache.safetensors written by the Python store (a
+    global layer of 1001 tokens and a sliding layer of window 950 that has
+    seen 1500 tokens) loads through turboquant::load_kv_cache, decodes, and
+    comes back out of turboquant::save_kv_cache as the same file, byte for
+    byte (engine/gemma4_multilayer.cpp:113-144)."""
+    import torch
+
+    import gemma4metal_b200.turboquant as tq
+    from gemma4metal_b200 import build as b
+    from gemma4metal_b200.kvstore import save_kv_cache
+    g = torch.Generator(device="cuda").manual_seed(5)
+    glob = tq.KVCache(1, 16, 128, 1004)
+    glob.append(torch.randn(1, 16, 1001, 128, device="cuda", generator=g).half(),
+                torch.randn(1, 16, 1001, 128, device="cuda", generator=g).half())
+    ring = tq.RingKVCache(16, 128, 950)
+    for _ in range(3):
+        ring.append(torch.randn(1, 16, 500, 128, device="cuda", generator=g).half(),
+                    torch.randn(1, 16, 500, 128, device="cuda", generator=g).half())
+    src, dst = tmp_path / "engine.safetensors", tmp_path / "cpp.safetensors"
+    save_kv_cache(str(src), {0: glob, 3: ring}, cache_offset=1501)
+    exe = b.cpp_test_binary("test_kvstore")
+    if not os.path.exists(exe):
+        b.build_cpp_tests()
+    r = subprocess.run([exe, str(src), str(dst)], capture_output=True, text=True, timeout=300)
+    print(r.stdout)
+    assert r.returncode == 0 and r.stdout.strip().endswith("PASS"), r.stdout + r.stderr
+    assert src.read_bytes() == dst.read_bytes()

@@ -78,9 +78,17 @@ __host__ __device__ constexpr int level_off(int block, int L) {
 // l + 2^(L-3) inside the block (lanes l with l % 2^(L-2) == 0 compute).
 __global__ void __launch_bounds__(128) polar_encode_kernel(const float* __restrict__ y,
                                                            long long groups, int block,
-                                                           PolarTables T, uint8_t* angles,
+                                                           const __grid_constant__ PolarTables T,
+                                                           uint8_t* angles,
                                                            uint8_t* packed, __half* radii) {
   __shared__ uint8_t s_idx[4][128];
+  // the codebooks from shared memory (a dynamically indexed kernel parameter
+  // would be copied to every thread's local memory)
+  __shared__ float s_cb[kMaxLevels][kCB];
+  __shared__ int s_n[kMaxLevels];
+  for (int i = threadIdx.x; i < kMaxLevels * kCB; i += blockDim.x) (&s_cb[0][0])[i] = (&T.cb[0][0])[i];
+  if (threadIdx.x < kMaxLevels) s_n[threadIdx.x] = T.n[threadIdx.x];
+  __syncthreads();
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int levels = 31 - __clz(block);
   const int lpb = block / 4;            // lanes per block
@@ -97,8 +105,8 @@ __global__ void __launch_bounds__(128) polar_encode_kernel(const float* __restri
       if (a0 < 0.0f) a0 = __fadd_rn(a0, 6.2831854820251465f);
       float a1 = polar_atan2(v.w, v.z);
       if (a1 < 0.0f) a1 = __fadd_rn(a1, 6.2831854820251465f);
-      si[2 * ll] = static_cast<uint8_t>(nearest(a0, T.cb[0], T.n[0]));
-      si[2 * ll + 1] = static_cast<uint8_t>(nearest(a1, T.cb[0], T.n[0]));
+      si[2 * ll] = static_cast<uint8_t>(nearest(a0, s_cb[0], s_n[0]));
+      si[2 * ll + 1] = static_cast<uint8_t>(nearest(a1, s_cb[0], s_n[0]));
       r1a = __fsqrt_rn(fmaf(v.x, v.x, __fmul_rn(v.y, v.y)));
       r1b = __fsqrt_rn(fmaf(v.z, v.z, __fmul_rn(v.w, v.w)));
     }
@@ -106,7 +114,7 @@ __global__ void __launch_bounds__(128) polar_encode_kernel(const float* __restri
     float r = r1a;
     if (levels >= 2) {
       const float a = polar_atan2(r1b, r1a);
-      si[level_off(block, 2) + ll] = static_cast<uint8_t>(nearest(a, T.cb[1], T.n[1]));
+      si[level_off(block, 2) + ll] = static_cast<uint8_t>(nearest(a, s_cb[1], s_n[1]));
       r = __fsqrt_rn(fmaf(r1a, r1a, __fmul_rn(r1b, r1b)));
     }
     for (int L = 3; L <= levels; ++L) {
@@ -115,7 +123,7 @@ __global__ void __launch_bounds__(128) polar_encode_kernel(const float* __restri
       if ((ll & ((step << 1) - 1)) == 0) {
         const float a = polar_atan2(other, r);
         si[level_off(block, L) + (ll >> (L - 2))] =
-            static_cast<uint8_t>(nearest(a, T.cb[L - 1], T.n[L - 1]));
+            static_cast<uint8_t>(nearest(a, s_cb[L - 1], s_n[L - 1]));
         r = __fsqrt_rn(fmaf(r, r, __fmul_rn(other, other)));
       }
     }
@@ -172,7 +180,9 @@ __device__ __forceinline__ float4 decode4(IdxFn idx, float radius, int block, in
 __global__ void __launch_bounds__(128) polar_decode_kernel(const uint8_t* angles,
                                                            const uint8_t* packed,
                                                            const __half* radii, long long groups,
-                                                           int block, PolarTables T, float* y) {
+                                                           int block,
+                                                           const __grid_constant__ PolarTables T,
+                                                           float* y) {
   __shared__ float s_cs[kMaxLevels][kCB][2];
   for (int i = threadIdx.x; i < kMaxLevels * kCB * 2; i += blockDim.x)
     (&s_cs[0][0][0])[i] = (&T.cs[0][0][0])[i];
@@ -196,34 +206,78 @@ __global__ void __launch_bounds__(128) polar_decode_kernel(const uint8_t* angles
 }
 
 // ---- QJL: r = y - yhat, signs of S r (m rows), |r| -------------------------------
-// One CTA per key row; thread i computes (S r)_i as a sequential fmaf sum over
-// j = 0..D-1 (the oracle's order), warp ballots pack the sign bits.
-__global__ void __launch_bounds__(256) qjl_encode_kernel(const float* __restrict__ y,
-                                                         const float* __restrict__ yhat,
-                                                         long long rows, int D,
-                                                         const float* __restrict__ S, int m,
-                                                         uint32_t* signs, __half* rnorm) {
-  extern __shared__ float s_r[];
-  for (long long n = blockIdx.x; n < rows; n += gridDim.x) {
-    for (int j = threadIdx.x; j < D; j += blockDim.x)
-      s_r[j] = __fsub_rn(y[n * D + j], yhat[n * D + j]);
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float nn = 0.0f;
-      for (int j = 0; j < D; ++j) nn = fmaf(s_r[j], s_r[j], nn);
-      rnorm[n] = __float2half_rn(__fsqrt_rn(nn));
+// A CTA takes kQjlKeys keys at a time: their residuals go to shared memory
+// dim-major, S streams through shared memory in chunks of kQjlDims dims
+// (transposed, one padded row per dim), and thread i accumulates (S r)_i for
+// all the keys with a sequential fmaf sum over j = 0..D-1 -- the oracle's
+// order, so the sign bits are bit-identical. Warp ballots pack the bits; the
+// norms |r| are sequential fmaf sums too (lanes of warp 0, one key each).
+constexpr int kQjlKeys = 16;
+constexpr int kQjlDims = 32;
+constexpr int kQjlThreads = 256;
+
+size_t qjl_smem_bytes(int D, int m) {
+  return (static_cast<size_t>(D) * kQjlKeys + static_cast<size_t>(kQjlDims) * (m + 1)) * sizeof(float);
+}
+
+__global__ void __launch_bounds__(kQjlThreads) qjl_encode_kernel(const float* __restrict__ y,
+                                                                 const float* __restrict__ yhat,
+                                                                 long long rows, int D,
+                                                                 const float* __restrict__ S, int m,
+                                                                 uint32_t* signs, __half* rnorm) {
+  extern __shared__ float smq[];
+  float* s_r = smq;                                  // [D][kQjlKeys]
+  float* s_S = smq + static_cast<size_t>(D) * kQjlKeys;  // [kQjlDims][m + 1]
+  const int tid = threadIdx.x;
+  const long long batches = (rows + kQjlKeys - 1) / kQjlKeys;
+  for (long long bt = blockIdx.x; bt < batches; bt += gridDim.x) {
+    const long long n0 = bt * kQjlKeys;
+    const int nk = static_cast<int>(min(static_cast<long long>(kQjlKeys), rows - n0));
+    for (int idx = tid; idx < D * kQjlKeys; idx += kQjlThreads) {
+      const int k = idx / D, j = idx % D;
+      s_r[j * kQjlKeys + k] =
+          k < nk ? __fsub_rn(y[(n0 + k) * D + j], yhat[(n0 + k) * D + j]) : 0.0f;
     }
-    for (int i0 = 0; i0 < m; i0 += blockDim.x) {
-      const int i = i0 + threadIdx.x;
-      float acc = 0.0f;
-      if (i < m) {
-        const float* Si = S + static_cast<long long>(i) * D;
-        for (int j = 0; j < D; ++j) acc = fmaf(Si[j], s_r[j], acc);
+    float acc[kQjlKeys];
+#pragma unroll
+    for (int k = 0; k < kQjlKeys; ++k) acc[k] = 0.0f;
+    for (int j0 = 0; j0 < D; j0 += kQjlDims) {
+      const int nj = min(kQjlDims, D - j0);
+      __syncthreads();  // residuals written / previous chunk consumed
+      for (int idx = tid; idx < m * kQjlDims; idx += kQjlThreads) {
+        const int i = idx / kQjlDims, jj = idx % kQjlDims;
+        if (jj < nj) s_S[jj * (m + 1) + i] = S[static_cast<long long>(i) * D + j0 + jj];
       }
-      const unsigned bits = __ballot_sync(0xffffffffu, i < m && acc >= 0.0f);
-      if ((threadIdx.x & 31) == 0 && i < m) signs[n * (m / 32) + i / 32] = bits;
+      __syncthreads();
+      if (tid < m) {
+        for (int jj = 0; jj < nj; ++jj) {
+          const float sv = s_S[jj * (m + 1) + tid];
+          const float4* r4 = reinterpret_cast<const float4*>(s_r + (j0 + jj) * kQjlKeys);
+#pragma unroll
+          for (int q = 0; q < kQjlKeys / 4; ++q) {
+            const float4 r = r4[q];
+            acc[4 * q] = fmaf(sv, r.x, acc[4 * q]);
+            acc[4 * q + 1] = fmaf(sv, r.y, acc[4 * q + 1]);
+            acc[4 * q + 2] = fmaf(sv, r.z, acc[4 * q + 2]);
+            acc[4 * q + 3] = fmaf(sv, r.w, acc[4 * q + 3]);
+          }
+        }
+      }
     }
-    __syncthreads();
+    // signs: warp w holds rows 32w .. 32w + 31 of S r for every key
+    for (int k = 0; k < nk; ++k) {
+      const unsigned bits = __ballot_sync(0xffffffffu, tid < m && acc[k] >= 0.0f);
+      if ((tid & 31) == 0 && tid < m) signs[(n0 + k) * (m / 32) + tid / 32] = bits;
+    }
+    if (tid < nk) {
+      float nn = 0.0f;
+      for (int j = 0; j < D; ++j) {
+        const float r = s_r[j * kQjlKeys + tid];
+        nn = fmaf(r, r, nn);
+      }
+      rnorm[n0 + tid] = __float2half_rn(__fsqrt_rn(nn));
+    }
+    __syncthreads();  // s_r is rewritten by the next batch
   }
 }
 
@@ -261,7 +315,8 @@ struct CParams {
 };
 
 template <int D, int G>
-__global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p, const PolarTables T) {
+__global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p,
+                                                              const __grid_constant__ PolarTables T) {
   constexpr int DPL = D / 128;      // 128-value groups per key
   __shared__ float s_cs[kMaxLevels][kCB][2];
   __shared__ float s_sq[G][256];    // S q per head (m <= 256)
@@ -276,13 +331,30 @@ __global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p, c
   for (int i = tid; i < G * D; i += 128) s_q[i / D][i % D] = load_as_float(p.q, static_cast<long long>(h0) * D + i, p.q_dtype);
   __syncthreads();
   const bool qjl = p.signs != nullptr;
-  if (qjl)
-    for (int i = tid; i < G * p.m; i += 128) {
-      const int g = i / p.m, r = i % p.m;
-      float a = 0.0f;
-      for (int j = 0; j < D; ++j) a = fmaf(p.S[static_cast<long long>(r) * D + j], s_q[g][j], a);
-      s_sq[g][r] = a;
+  if (qjl) {
+    // S q for the CTA's G heads: a warp per row of S, lanes over 4 consecutive
+    // dims each (coalesced 512-byte row reads), summed by shuffles
+    for (int r = w; r < p.m; r += 4) {
+      float a[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) a[g] = 0.0f;
+#pragma unroll
+      for (int c = 0; c < D / 128; ++c) {
+        const float4 s4 = reinterpret_cast<const float4*>(p.S + static_cast<long long>(r) * D + c * 128)[lane];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float* qq = &s_q[g][c * 128 + 4 * lane];
+          a[g] = fmaf(s4.x, qq[0], fmaf(s4.y, qq[1], fmaf(s4.z, qq[2], fmaf(s4.w, qq[3], a[g]))));
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) a[g] += __shfl_xor_sync(0xffffffffu, a[g], off);
+        if (lane == 0) s_sq[g][r] = a[g];
+      }
     }
+  }
   __syncthreads();
   const float qjl_c = 1.2533141373155003f / static_cast<float>(p.m > 0 ? p.m : 1);  // sqrt(pi/2)/m
 
@@ -612,8 +684,15 @@ TQ_API int tq_qjl_encode(const float* y, const float* y_hat, int64_t rows, int h
       m < 32 || m % 32 != 0 || m > 256)
     return err(TQ_ERR_INVALID, "tq_qjl_encode: bad arguments (m a multiple of 32 in [32, 256])");
   if (rows == 0) return TQ_OK;
-  const int grid = static_cast<int>(rows < 8192 ? rows : 8192);
-  qjl_encode_kernel<<<grid, 256, head_dim * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
+  const size_t smem = qjl_smem_bytes(head_dim, m);
+  cudaFuncSetAttribute(qjl_encode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(smem));
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long long batches = (rows + kQjlKeys - 1) / kQjlKeys;
+  const long long cap = 2LL * device_sm_count(dev);
+  const int grid = static_cast<int>(batches < cap ? batches : cap);
+  qjl_encode_kernel<<<grid, kQjlThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       y, y_hat, rows, head_dim, S, m, signs, static_cast<__half*>(rnorm));
   const cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? TQ_OK : cuda_err(e, "tq_qjl_encode");

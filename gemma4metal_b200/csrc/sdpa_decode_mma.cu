@@ -61,6 +61,18 @@ namespace tq {
 namespace {
 
 constexpr int kChunk = 64;  // tokens per TMA box; splits are whole chunks
+#ifndef TQ_DECODE_MINB_128
+#define TQ_DECODE_MINB_128 3
+#endif
+#ifndef TQ_DECODE_STAGES_128
+#define TQ_DECODE_STAGES_128 3
+#endif
+#ifndef TQ_DECODE_PREFETCH_TILES
+#define TQ_DECODE_PREFETCH_TILES 2
+#endif
+// Tiles of its range a CTA warms L2 with before it waits for the preceding
+// kernel (a hint: nothing is read into the kernel before the wait).
+constexpr int kPrefetchTiles = TQ_DECODE_PREFETCH_TILES;
 
 // Per head_dim: W consumer warps (+ one TMA producer warp), each taking TB
 // independent 16-token blocks of every tile (two interleaved dependency
@@ -73,9 +85,9 @@ struct MCfg {
   static constexpr int THREADS = (W + 1) * 32;
   static constexpr int TILE = 16 * W * TB;
   static constexpr int CPT = TILE / kChunk;  // chunks per tile
-  static constexpr int MINB = D == 128 ? 3 : 2;  // CTAs per SM with f16 queries; f32/bf16
-                                                 // queries (hi+lo split) run 1 per SM
-  static constexpr int STAGES = D == 128 ? 3 : 5;
+  static constexpr int MINB = D == 128 ? TQ_DECODE_MINB_128 : 2;  // CTAs per SM with f16
+                                                 // queries; f32/bf16 queries (hi+lo split) run 1 per SM
+  static constexpr int STAGES = D == 128 ? TQ_DECODE_STAGES_128 : 5;
 };
 
 template <int D, int G, typename SB>
@@ -326,17 +338,22 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     mbar_init(nbar, D / 128);  // one arrival per writer warp of a fused append
     fence_barrier_init();
   }
-  if (tid == W * 32) {
-    prefetch_tensormap(&tmk);
-    prefetch_tensormap(&tmv);
-    const int qel = p.q_dtype == kF32 ? 4 : 2;
-    prefetch_l2(static_cast<const unsigned char*>(p.q) + (static_cast<long long>(b) * p.H + h0) * D * qel,
-                static_cast<uint32_t>(G * D * qel));
+  if (warp == W) {
+    if (lane == 0) {
+      prefetch_tensormap(&tmk);
+      prefetch_tensormap(&tmv);
+      const int qel = p.q_dtype == kF32 ? 4 : 2;
+      prefetch_l2(static_cast<const unsigned char*>(p.q) + (static_cast<long long>(b) * p.H + h0) * D * qel,
+                  static_cast<uint32_t>(G * D * qel));
+    }
     const int n_pf = max(0, min(p.n_tokens, p.capacity));
     const int n_pf4 = (n_pf + 3) & ~3;  // <= capacity: rows past it are never touched
     int lo, c0, c1;
     range(n_pf, lo, c0, c1);
-    for (int c = c0; c < min(c1, c0 + 2 * CPT); c += CPT) {
+    // the producer warp's lanes prefetch kPrefetchTiles tiles each (one tile
+    // per lane); kPrefetchTiles < 0: the CTA's whole range
+    const int pf_end = kPrefetchTiles < 0 ? c1 : min(c1, c0 + kPrefetchTiles * CPT);
+    for (int c = c0 + lane * CPT; c < pf_end; c += 32 * CPT) {
       const int rows = min(min(CPT, c1 - c) * kChunk, n_pf4 - c * kChunk);
       const long long t0 = tok_base + static_cast<long long>(c) * kChunk;
       const uint32_t cbytes = static_cast<uint32_t>(rows * (D / 2));

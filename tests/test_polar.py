@@ -74,6 +74,20 @@ def test_encoder_matches_float64_restatement(block):
     assert np.array_equal(nib, got)
 
 
+def test_config3_indices_agree_with_float64_atan2():
+    """Config 3 at full size (16 KV heads x 4096 keys x 127 angles = 8.3M
+    indices): the encoder's fp32 polynomial atan2 picks the same codebook
+    entry as a float64 arctan2 restatement for all but a handful of angles
+    that sit within rounding of a bin boundary (1 of 8.3M with seed 11)."""
+    k = keys(11, 16, 4096, 128).reshape(-1, 128)
+    cb = codebooks(7)
+    ang, _, rad = O.polar_encode(k, 128, cb)
+    ref_idx, ref_rad = np_encode(k, 128, cb)
+    rate = float(np.mean(ang.reshape(-1, 127) != ref_idx))
+    assert rate <= 1e-6, rate
+    np.testing.assert_allclose(rad.reshape(-1).astype(np.float64), ref_rad, rtol=1e-3)
+
+
 @pytest.mark.parametrize("block", [16, 128])
 def test_decode_preserves_norm_and_bounds_error(block):
     y = keys(12, 2, 64, 256).reshape(-1, 256)
@@ -245,8 +259,24 @@ def test_gpu_compressed_score(Hkv, H, D, N, block, qjl, qdt):
     ref = O.compressed_score(qref, c["pk"], c["rad"], c["cb"], block, 1.0, c["signs"], c["rn"], c["S"])
     got = tq.compressed_score(qg, _dev(c["pk"]), _dev(c["rad"]), torch.from_numpy(c["cb"]), block, 1.0,
                               _dev(c["signs"]), _dev(c["rn"]), _dev(c["S"])).cpu().numpy()
-    tol = 1e-3 * (np.abs(ref) + np.sqrt(np.mean(ref ** 2)))
-    assert np.all(np.abs(got - ref) <= tol), float(np.max(np.abs(got - ref) / tol))
+    # 1e-3 relative per score, except where the score cancels: there the
+    # bound is the fp32 forward error of the dot products themselves,
+    # 1e-5 * sum |q_d k_d| (plus the QJL term's sum of magnitudes) -- an
+    # element-wise relative error has no meaning at a score near zero
+    G = H // Hkv
+    kh = O.polar_decode(c["pk"], c["rad"], D, block, c["cb"]).reshape(Hkv, N, D).astype(np.float64)
+    mag = np.einsum("hgd,hnd->hgn", np.abs(qref.astype(np.float64)).reshape(Hkv, G, D),
+                    np.abs(kh)).reshape(H, N)
+    if qjl:
+        sq = np.abs(qref.astype(np.float64) @ c["S"].astype(np.float64).T)  # (H, m)
+        rn = c["rn"].reshape(Hkv, N).astype(np.float64)
+        mag += (np.sqrt(np.pi / 2) / c["S"].shape[0] * rn[np.arange(H) // G] * sq.sum(1)[:, None])
+    tol = 1e-3 * np.abs(ref) + 1e-5 * mag
+    bad = np.abs(got - ref) > tol
+    assert not bad.any(), float(np.max((np.abs(got - ref) / tol)))
+    # how often the floor is what admits an element (reported, not asserted)
+    print(f"compressed scores: {np.mean(np.abs(got - ref) > 1e-3 * np.abs(ref)):.2e} of "
+          f"{ref.size} rely on the cancellation floor")
 
 
 @pytest.mark.gpu

@@ -401,6 +401,7 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
     host_cache = None
     if check and rank == 0:
         from oracle import oracle as O
+        O.set_num_threads(os.cpu_count() or 1)
         host_cache = {"k": [], "v": []}  # per chunk: (codes, scales, biases)
 
     def rms_norm(x, w):
@@ -477,6 +478,8 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
               "exchange": capture(exchange, CH)}
     singles = [capture(step, 1) for _ in range(1)]  # the host-buffer leg re-targets layer 0 only
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()  # every rank has its graphs before any rank's first peer merge
     reps = max(1, steps // CH)
     clocks = Clocks(local_rank)
     clocks.start()
@@ -535,6 +538,7 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
 
     acc = None
     if host_cache is not None:
+        O.set_num_threads(os.cpu_count() or 1)  # torch.distributed.run exports OMP_NUM_THREADS=1
         # the appended token sits at global position C4_N - 1 on the last rank
         host_cache["k"].append(O.quantize(L0["kn"].float().cpu().numpy()))
         host_cache["v"].append(O.quantize(L0["vn"].float().cpu().numpy()))

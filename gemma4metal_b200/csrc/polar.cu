@@ -309,10 +309,26 @@ struct CParams {
   float* scores;          // (H, N) when scores-only
   void* out;              // (H, D)
   int out_dtype;
-  float* ws;              // split partials: (Hkv, splits, 4 warps, G, D + 2)
+  float* ws;              // split partials: (Hkv, splits, G, D + 2)
   unsigned* counters;     // Hkv tickets
   int splits;
 };
+
+constexpr int kCKeys = 64;  // keys per shared-memory chunk of compressed attention
+
+// Dynamic shared memory of compressed attention: one staged chunk of keys,
+// reused at the end for the 4 warps' (o, m, l) states.
+constexpr size_t cattn_smem_bytes(int D, int G) {
+  const size_t chunk = static_cast<size_t>(kCKeys) * (D / 8 + 8 + D / 8 + 2 * (D / 64) + 16 + 1) * 4;
+  const size_t states = static_cast<size_t>(4) * G * (D + 2) * 4;
+  return chunk > states ? chunk : states;
+}
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
 template <int D, int G>
 __global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p,
@@ -333,25 +349,37 @@ __global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p,
   const bool qjl = p.signs != nullptr;
   if (qjl) {
     // S q for the CTA's G heads: a warp per row of S, lanes over 4 consecutive
-    // dims each (coalesced 512-byte row reads), summed by shuffles
-    for (int r = w; r < p.m; r += 4) {
-      float a[G];
+    // dims each (coalesced 512-byte row reads, RB rows' loads in flight),
+    // summed by shuffles
+    constexpr int RB = D == 128 ? 16 : 8;
+    for (int r0 = w; r0 < p.m; r0 += 4 * RB) {
+      float4 s4[RB][D / 128];
 #pragma unroll
-      for (int g = 0; g < G; ++g) a[g] = 0.0f;
+      for (int j = 0; j < RB; ++j) {
+        const int r = r0 + 4 * j;
 #pragma unroll
-      for (int c = 0; c < D / 128; ++c) {
-        const float4 s4 = reinterpret_cast<const float4*>(p.S + static_cast<long long>(r) * D + c * 128)[lane];
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float* qq = &s_q[g][c * 128 + 4 * lane];
-          a[g] = fmaf(s4.x, qq[0], fmaf(s4.y, qq[1], fmaf(s4.z, qq[2], fmaf(s4.w, qq[3], a[g]))));
-        }
+        for (int c = 0; c < D / 128; ++c)
+          s4[j][c] = r < p.m ? reinterpret_cast<const float4*>(p.S + static_cast<long long>(r) * D + c * 128)[lane]
+                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
       }
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
+      for (int j = 0; j < RB; ++j) {
+        const int r = r0 + 4 * j;
+        float a[G];
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) a[g] += __shfl_xor_sync(0xffffffffu, a[g], off);
-        if (lane == 0) s_sq[g][r] = a[g];
+        for (int g = 0; g < G; ++g) {
+          a[g] = 0.0f;
+#pragma unroll
+          for (int c = 0; c < D / 128; ++c) {
+            const float* qq = &s_q[g][c * 128 + 4 * lane];
+            a[g] = fmaf(s4[j][c].x, qq[0], fmaf(s4[j][c].y, qq[1], fmaf(s4[j][c].z, qq[2], fmaf(s4[j][c].w, qq[3], a[g]))));
+          }
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) a[g] += __shfl_xor_sync(0xffffffffu, a[g], off);
+        }
+        if (lane == 0 && r < p.m)
+#pragma unroll
+          for (int g = 0; g < G; ++g) s_sq[g][r] = a[g];
       }
     }
   }
@@ -382,99 +410,180 @@ __global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p,
 
   const int t_begin = split * p.keys_per_split;
   const int t_end = min(p.N, t_begin + p.keys_per_split);
-  for (int t = t_begin + w; t < t_end; t += 4) {
-    const long long row = static_cast<long long>(kv) * p.N + t;
-    float part[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) part[g] = 0.0f;
-#pragma unroll
-    for (int c = 0; c < DPL; ++c) {
-      const long long b = row * nbk + c * (128 / block) + kb;
-      const uint8_t* pk = p.packed + b * (block / 2);
-      const float4 kv4 = decode4([&](int i) { return packed_idx(pk, i); },
-                                 __half2float(p.radii[b]), block, ll, s_cs);
-#pragma unroll
-      for (int g = 0; g < G; ++g)
-        part[g] += qv[g][c][0] * kv4.x + qv[g][c][1] * kv4.y + qv[g][c][2] * kv4.z +
-                   qv[g][c][3] * kv4.w;
+  // The split's keys go through shared memory kCKeys at a time: every array
+  // of a chunk (angle nibbles, radii, QJL bits and norms, int4 V and its
+  // scales) is one contiguous range, copied by all threads with asynchronous
+  // 4-byte copies (2-byte loads for the fp16 radii and norms), so a key's
+  // data costs the warps no dependent global round trips.
+  extern __shared__ __align__(16) unsigned char dsm[];
+  constexpr int PKW = D / 8;                    // 32-bit words of angle nibbles per key
+  const int mw = p.m / 32;                      // QJL sign words per key
+  uint32_t* s_pk = reinterpret_cast<uint32_t*>(dsm);                // [kCKeys][PKW]
+  uint32_t* s_sg = s_pk + kCKeys * PKW;                             // [kCKeys][mw <= 8]
+  uint32_t* s_vq = s_sg + kCKeys * 8;                               // [kCKeys][D/8]
+  float* s_vs = reinterpret_cast<float*>(s_vq + kCKeys * (D / 8));  // [kCKeys][D/64]
+  float* s_vb = s_vs + kCKeys * (D / 64);
+  float* s_rad = s_vb + kCKeys * (D / 64);                          // [kCKeys][nbk <= 16]
+  float* s_rn = s_rad + kCKeys * 16;                                // [kCKeys]
+  const bool stage_v = p.attend && !p.vdense;
+  for (int c0 = t_begin; c0 < t_end; c0 += kCKeys) {
+    const int nk = min(kCKeys, t_end - c0);
+    const long long row0 = static_cast<long long>(kv) * p.N + c0;
+    __syncthreads();  // the previous chunk is consumed
+    {
+      const uint32_t* src = reinterpret_cast<const uint32_t*>(p.packed) + row0 * PKW;
+      for (int i = tid; i < nk * PKW; i += 128) cp_async4(s_pk + i, src + i);
     }
     if (qjl) {
-      // lane l owns sign bits [l*m/32, (l+1)*m/32)
-      const int per = p.m / 32;
-      const uint32_t* sg = p.signs + row * (p.m / 32);
-      const float rn = __half2float(p.rnorm[row]) * qjl_c;
-      for (int i = lane * per; i < (lane + 1) * per; ++i) {
-        const bool bit = (sg[i >> 5] >> (i & 31)) & 1u;
-#pragma unroll
-        for (int g = 0; g < G; ++g) part[g] += rn * (bit ? s_sq[g][i] : -s_sq[g][i]);
+      const uint32_t* src = p.signs + row0 * mw;
+      for (int i = tid; i < nk * mw; i += 128) cp_async4(s_sg + (i / mw) * 8 + i % mw, src + i);
+    }
+    if (stage_v) {
+      const uint32_t* src = p.vq + row0 * (D / 8);
+      for (int i = tid; i < nk * (D / 8); i += 128) cp_async4(s_vq + i, src + i);
+      if (p.sb_f32) {
+        const float* vs = reinterpret_cast<const float*>(p.vs) + row0 * (D / 64);
+        const float* vb = reinterpret_cast<const float*>(p.vb) + row0 * (D / 64);
+        for (int i = tid; i < nk * (D / 64); i += 128) {
+          cp_async4(s_vs + i, vs + i);
+          cp_async4(s_vb + i, vb + i);
+        }
       }
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
-      part[g] *= p.scale;
-    }
-    if (!p.attend) {  // scores only
-      if (lane < G) {
-        float v = part[0];
-#pragma unroll
-        for (int g = 1; g < G; ++g) v = (lane == g) ? part[g] : v;
-        p.scores[static_cast<long long>(h0 + lane) * p.N + t] = v;
+    cp_async_commit();
+    // the fp16 arrays with plain loads (no 4-byte alignment), converted
+    for (int i = tid; i < nk * nbk; i += 128)
+      s_rad[(i / nbk) * 16 + i % nbk] = __half2float(p.radii[row0 * nbk + i]);
+    if (qjl)
+      for (int i = tid; i < nk; i += 128) s_rn[i] = __half2float(p.rnorm[row0 + i]);
+    if (stage_v && !p.sb_f32) {
+      const __half* vs = reinterpret_cast<const __half*>(p.vs) + row0 * (D / 64);
+      const __half* vb = reinterpret_cast<const __half*>(p.vb) + row0 * (D / 64);
+      for (int i = tid; i < nk * (D / 64); i += 128) {
+        s_vs[i] = __half2float(vs[i]);
+        s_vb[i] = __half2float(vb[i]);
       }
-      continue;
     }
-    // online softmax (natural log) and V accumulation
+    cp_async_wait_all();
+    __syncthreads();
+
+    for (int tl = w; tl < nk; tl += 4) {
+      const int t = c0 + tl;
+      const long long row = row0 + tl;
+      const unsigned char* pkb = reinterpret_cast<const unsigned char*>(s_pk + tl * PKW);
+      float part[G];
 #pragma unroll
-    for (int c = 0; c < DPL; ++c) {
-      const int d0 = c * 128 + 4 * lane;
-      float vv[4];
-      if (p.vdense) {
+      for (int g = 0; g < G; ++g) part[g] = 0.0f;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) vv[e] = load_as_float(p.vdense, row * D + d0 + e, p.vdense_dtype);
-      } else {
-        const uint32_t word = p.vq[row * (D / 8) + d0 / 8];
-        const int sh = 4 * (d0 % 8);
-        const long long gi = row * (D / 64) + d0 / 64;
-        const float sc = p.sb_f32 ? reinterpret_cast<const float*>(p.vs)[gi]
-                                  : __half2float(reinterpret_cast<const __half*>(p.vs)[gi]);
-        const float bi = p.sb_f32 ? reinterpret_cast<const float*>(p.vb)[gi]
-                                  : __half2float(reinterpret_cast<const __half*>(p.vb)[gi]);
+      for (int c = 0; c < DPL; ++c) {
+        const int bi = c * (128 / block) + kb;
+        const unsigned char* pk = pkb + bi * (block / 2);
+        const float4 kv4 = decode4([&](int i) { return packed_idx(pk, i); },
+                                   s_rad[tl * 16 + bi], block, ll, s_cs);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) vv[e] = fmaf(sc, static_cast<float>((word >> (sh + 4 * e)) & 15u), bi);
+        for (int g = 0; g < G; ++g)
+          part[g] += qv[g][c][0] * kv4.x + qv[g][c][1] * kv4.y + qv[g][c][2] * kv4.z +
+                     qv[g][c][3] * kv4.w;
+      }
+      if (qjl) {
+        // lane l owns sign bits [l*m/32, (l+1)*m/32)
+        const int per = p.m / 32;
+        const float rn = s_rn[tl] * qjl_c;
+        for (int i = lane * per; i < (lane + 1) * per; ++i) {
+          const bool bit = (s_sg[tl * 8 + (i >> 5)] >> (i & 31)) & 1u;
+#pragma unroll
+          for (int g = 0; g < G; ++g) part[g] += rn * (bit ? s_sq[g][i] : -s_sq[g][i]);
+        }
       }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        if (c == 0) {
-          const float mn = fmaxf(m_run[g], part[g]);
-          const float a = (m_run[g] == -INFINITY) ? 0.0f : __expf(m_run[g] - mn);
-          const float pe = __expf(part[g] - mn);
-          l_run[g] = l_run[g] * a + pe;
-          m_run[g] = mn;
 #pragma unroll
-          for (int cc = 0; cc < DPL; ++cc)
+        for (int off = 16; off > 0; off >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
+        part[g] *= p.scale;
+      }
+      if (!p.attend) {  // scores only
+        if (lane < G) {
+          float v = part[0];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) o[g][cc][e] *= a;
-          part[g] = pe;  // reuse as this key's weight
+          for (int g = 1; g < G; ++g) v = (lane == g) ? part[g] : v;
+          p.scores[static_cast<long long>(h0 + lane) * p.N + t] = v;
+        }
+        continue;
+      }
+      // online softmax (natural log) and V accumulation
+#pragma unroll
+      for (int c = 0; c < DPL; ++c) {
+        const int d0 = c * 128 + 4 * lane;
+        float vv[4];
+        if (p.vdense) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) vv[e] = load_as_float(p.vdense, row * D + d0 + e, p.vdense_dtype);
+        } else {
+          const uint32_t word = s_vq[tl * (D / 8) + d0 / 8];
+          const int sh = 4 * (d0 % 8);
+          const float sc = s_vs[tl * (D / 64) + d0 / 64];
+          const float bi = s_vb[tl * (D / 64) + d0 / 64];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) vv[e] = fmaf(sc, static_cast<float>((word >> (sh + 4 * e)) & 15u), bi);
         }
 #pragma unroll
-        for (int e = 0; e < 4; ++e) o[g][c][e] = fmaf(part[g], vv[e], o[g][c][e]);
+        for (int g = 0; g < G; ++g) {
+          if (c == 0) {
+            const float mn = fmaxf(m_run[g], part[g]);
+            const float a = (m_run[g] == -INFINITY) ? 0.0f : __expf(m_run[g] - mn);
+            const float pe = __expf(part[g] - mn);
+            l_run[g] = l_run[g] * a + pe;
+            m_run[g] = mn;
+#pragma unroll
+            for (int cc = 0; cc < DPL; ++cc)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) o[g][cc][e] *= a;
+            part[g] = pe;  // reuse as this key's weight
+          }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) o[g][c][e] = fmaf(part[g], vv[e], o[g][c][e]);
+        }
       }
     }
   }
   if (!p.attend) return;
 
-  // ---- per-warp partial (m, l, o) -> workspace; last CTA of the KV head merges
-  float* wsp = p.ws + ((static_cast<long long>(kv) * p.splits + split) * 4 + w) * G * (D + 2);
+  // ---- the 4 warps' states combined in shared memory (the chunk buffer is
+  // free now), one partial per CTA to the workspace; the last CTA of the KV
+  // head merges the splits' partials, 16 splits' loads in flight per thread
+  __syncthreads();
+  float* wst = reinterpret_cast<float*>(dsm);  // [4 warps][G][D + 2]
 #pragma unroll
   for (int g = 0; g < G; ++g) {
+    float* ws_g = wst + (w * G + g) * (D + 2);
 #pragma unroll
     for (int c = 0; c < DPL; ++c)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) wsp[g * (D + 2) + c * 128 + 4 * lane + e] = o[g][c][e];
+      for (int e = 0; e < 4; ++e) ws_g[c * 128 + 4 * lane + e] = o[g][c][e];
     if (lane == 0) {
-      wsp[g * (D + 2) + D] = m_run[g];
-      wsp[g * (D + 2) + D + 1] = l_run[g];
+      ws_g[D] = m_run[g];
+      ws_g[D + 1] = l_run[g];
+    }
+  }
+  __syncthreads();
+  float* wsp = p.ws + (static_cast<long long>(kv) * p.splits + split) * G * (D + 2);
+  for (int i = tid; i < G * D; i += 128) {
+    const int g = i / D, d = i % D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int ww = 0; ww < 4; ++ww) M = fmaxf(M, wst[(ww * G + g) * (D + 2) + D]);
+    float L = 0.0f, acc = 0.0f;
+#pragma unroll
+    for (int ww = 0; ww < 4; ++ww) {
+      const float* st = wst + (ww * G + g) * (D + 2);
+      const float e = st[D] == -INFINITY ? 0.0f : __expf(st[D] - M);
+      L = fmaf(e, st[D + 1], L);
+      if (e != 0.0f) acc = fmaf(e, st[d], acc);
+    }
+    wsp[g * (D + 2) + d] = acc;
+    if (d == 0) {
+      wsp[g * (D + 2) + D] = M;
+      wsp[g * (D + 2) + D + 1] = L;
     }
   }
   __syncthreads();
@@ -484,19 +593,35 @@ __global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p,
   }
   __syncthreads();
   if (!s_last) return;
-  const int parts = p.splits * 4;
-  const float* base = p.ws + static_cast<long long>(kv) * parts * G * (D + 2);
+  const int S_ = p.splits;
+  const float* base = p.ws + static_cast<long long>(kv) * S_ * G * (D + 2);
   for (int i = tid; i < G * D; i += 128) {
     const int g = i / D, d = i % D;
-    float M = -INFINITY;
-    for (int s = 0; s < parts; ++s) M = fmaxf(M, __ldcg(base + (s * G + g) * (D + 2) + D));
-    float L = 0.0f, acc = 0.0f;
-    for (int s = 0; s < parts; ++s) {
-      const float* ps = base + (s * G + g) * (D + 2);
-      const float ms = __ldcg(ps + D);
-      const float e = (ms == -INFINITY) ? 0.0f : __expf(ms - M);
-      L = fmaf(e, __ldcg(ps + D + 1), L);
-      acc = fmaf(e, __ldcg(ps + d), acc);
+    float M = -INFINITY, L = 0.0f, acc = 0.0f;
+    for (int s0 = 0; s0 < S_; s0 += 16) {
+      float ms[16], ls[16], os[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const int sp = s0 + j;
+        const float* ps = base + (static_cast<long long>(sp) * G + g) * (D + 2);
+        ms[j] = sp < S_ ? __ldcg(ps + D) : -INFINITY;
+        ls[j] = sp < S_ ? __ldcg(ps + D + 1) : 0.0f;
+        os[j] = sp < S_ ? __ldcg(ps + d) : 0.0f;
+      }
+      float mb = M;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) mb = fmaxf(mb, ms[j]);
+      const float a = M == -INFINITY ? 0.0f : __expf(M - mb);
+      L *= a;
+      acc *= a;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        // an empty state (m = -inf) weighs 0; a NaN state makes the head NaN
+        const float e = ms[j] == -INFINITY ? 0.0f : __expf(ms[j] - mb);
+        L = fmaf(e, ls[j], L);
+        if (e != 0.0f) acc = fmaf(e, os[j], acc);
+      }
+      M = mb;
     }
     store_from_float(p.out, static_cast<long long>(h0 + g) * D + d, p.out_dtype,
                      L == 0.0f ? 0.0f : acc / L);
@@ -706,7 +831,7 @@ TQ_API size_t tq_compressed_sdpa_workspace_size(int num_heads, int num_kv_heads,
   // merge counters in the counter region every workspace of this library
   // starts with (so decode and compressed calls can share one workspace)
   return kCounterRegionBytes +
-         static_cast<size_t>(num_kv_heads) * s * 4 * G * (head_dim + 2) * sizeof(float);
+         static_cast<size_t>(num_kv_heads) * s * G * (head_dim + 2) * sizeof(float);
 }
 
 static int compressed_common(const void* q, tq_dtype q_dtype, const uint8_t* packed,
@@ -773,8 +898,11 @@ static int compressed_common(const void* q, tq_dtype q_dtype, const uint8_t* pac
       return err(TQ_ERR_UNSUPPORTED, "compressed attention: too many KV heads");
   }
   void* fn_ptr = head_dim == 128 ? pick_cattn<128>(G) : pick_cattn<256>(G);
+  const size_t dsmem = cattn_smem_bytes(head_dim, G);
+  cudaFuncSetAttribute(fn_ptr, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dsmem));
   void* args[] = {&p, &T};
-  const cudaError_t e = cudaLaunchKernel(fn_ptr, dim3(p.splits, num_kv_heads), dim3(128), args, 0,
+  const cudaError_t e = cudaLaunchKernel(fn_ptr, dim3(p.splits, num_kv_heads), dim3(128), args,
+                                         dsmem,
                                          static_cast<cudaStream_t>(stream));
   return e == cudaSuccess ? TQ_OK : cuda_err(e, fn);
 }

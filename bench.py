@@ -60,9 +60,11 @@ def parse():
     ap.add_argument("--context", type=int, default=32768)
     ap.add_argument("--window", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+    ap.add_argument("--exchange", default="peer", choices=["peer", "published", "nccl"],
                     help="cfg4 with N>1: partial states exchanged and merged by one kernel over "
-                         "NVLink peer memory (peer) or NCCL all-gather + merge kernel (nccl)")
+                         "NVLink peer memory (peer), stored into the peers' buffers by the "
+                         "decode kernel itself and merged by a merge-only kernel (published), "
+                         "or NCCL all-gather + merge kernel (nccl)")
     ap.add_argument("--split-step", action="store_true",
                     help="cfg1: run the step as two launches (quantize_append, then sdpa_int4) "
                          "instead of the fused sdpa_int4_append")
@@ -240,9 +242,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     clocks = Clocks(local_rank)
     clocks.start()
-    if warm is not None:
-        with torch.cuda.stream(stream):
+    with torch.cuda.stream(stream):
+        if warm is not None:
             warm.replay()
+        timed.replay()  # a graph's first launch uploads it: kept out of the timed region
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -434,7 +437,9 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
     n_local = layers[0]["sc"].n_local
     last = rank == world - 1
     ws = tq.workspace(dev, tq.sdpa_int4_workspace_size(1, C4_H, C4_HKV, C4_D, n_local + 1, 0))
-    peer = seqsplit.PeerExchange(1, C4_H, C4_D, device=dev) if world > 1 and args.exchange == "peer" else None
+    peer = (seqsplit.PeerExchange(1, C4_H, C4_D, device=dev)
+            if world > 1 and args.exchange in ("peer", "published") else None)
+    published = peer is not None and args.exchange == "published"
     torch.cuda.synchronize()
     stream = torch.cuda.Stream(device=dev)
 
@@ -457,6 +462,13 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
             tq.lse_merge(Lr["part"].view(1, 1, -1), C4_H, C4_D, out=Lr["out"], s=stream)
 
     def step(Lr):
+        if published:  # the decode kernel stores the states; a merge-only launch follows
+            sc = Lr["sc"]
+            if last:
+                tq.quantize_append(Lr["kn"], Lr["vn"], *sc.cache.tensors(), pos=n_local, s=stream)
+            peer.decode(Lr["q"], sc.cache.tensors(), n_local + (1 if last else 0), sc.t0, C4_N,
+                        C4_H // C4_HKV, 1.0, 0, out=Lr["out"], ws=ws, s=stream)
+            return
         partial(Lr)
         exchange(Lr)
 
@@ -474,8 +486,11 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
                     fn(layers[i % layers_n])
         return g
 
-    graphs = {"step": capture(step, CH), "partial": capture(partial, CH),
-              "exchange": capture(exchange, CH)}
+    # (published: a merge-only graph would wait for states nobody publishes;
+    # its time is the step's minus the plain partial decode's)
+    graphs = {"step": capture(step, CH), "partial": capture(partial, CH)}
+    if not published:
+        graphs["exchange"] = capture(exchange, CH)
     singles = [capture(step, 1) for _ in range(1)]  # the host-buffer leg re-targets layer 0 only
     torch.cuda.synchronize()
     if world > 1:
@@ -484,7 +499,7 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
     clocks = Clocks(local_rank)
     clocks.start()
     times = {}
-    for name in ("step", "partial", "exchange"):
+    for name in graphs:
         with torch.cuda.stream(stream):
             graphs[name].replay()  # warm-up
         torch.cuda.synchronize()
@@ -530,6 +545,8 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
     e2e_ms = (time.perf_counter() - th0) * 1000.0
     assert tq.device_error() == 0, "a kernel reported a device error"
 
+    if published:
+        times["exchange"] = times["step"] - times["partial"]
     tt = torch.tensor([times["step"], times["partial"], times["exchange"], e2e_ms], device=dev,
                       dtype=torch.float64)
     if world > 1:
@@ -581,7 +598,9 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
     return {
         "workload": "cfg4 decode step: 262144-token global layer (H=32, Hkv=8, D=256) split by "
                     "sequence, append + partial decode + " +
-                    ("peer-memory exchange + merge (one kernel)" if peer is not None else
+                    ("decode kernel stores its states into the peers' buffers + merge-only "
+                     "kernel" if published else
+                     "peer-memory exchange + merge (one kernel)" if peer is not None else
                      "NCCL all-gather + LSE merge"),
         "metric": "int4-KV decode-attention tokens/s", "unit": "tokens/s", "scaling": "strong",
         "n_gpus": world, "steps": n_timed,

@@ -10,6 +10,7 @@
 #include "../../include/turboquant_c.h"
 #include "tq_common.cuh"
 #include "tq_internal.h"
+#include "peer_layout.cuh"
 
 namespace {
 
@@ -70,6 +71,9 @@ struct DecodeCommon {
   int new_dtype = 0;
   int new_slot = -1;
   const int32_t* new_slots = nullptr;  // device, one slot per sequence (overrides new_slot)
+  // partial state published into every rank's exchange buffer (nullable)
+  void* const* peer_bufs = nullptr;
+  int peer_world = 0, peer_rank = 0;
 };
 
 int validate_decode(const DecodeCommon& c, const char* fn) {
@@ -265,6 +269,15 @@ static int decode_common(const DecodeCommon& c, const char* fn, const int32_t* s
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
   a.err = device_error_ptr();
+  if (c.peer_bufs) {
+    // one unit (flag) per (sequence, KV head): the tensor-core kernel with
+    // all of a KV head's query heads in one CTA
+    if (pl.variant != tq::kDecodeMma || pl.nsub != 1)
+      return fail(TQ_ERR_UNSUPPORTED, "%s: publishing needs the tensor-core decode kernel", fn);
+    a.peer_bufs = c.peer_bufs;
+    a.peer_world = c.peer_world;
+    a.peer_rank = c.peer_rank;
+  }
   if (c.k_new) {
     // the mma kernel quantizes the new token in the same launch; the CUDA-core
     // kernel gets it from a quantize-on-append launch just before
@@ -399,6 +412,31 @@ int tq_sdpa_int4_partial(const void* queries, tq_dtype q_dtype, const uint32_t* 
                  capacity, scale};
   return decode_common(c, "tq_sdpa_int4_partial", nullptr, token_offset, n_total, 1, nullptr,
                        TQ_F32, part_out, workspace, workspace_bytes, stream);
+}
+
+int tq_sdpa_int4_partial_publish(const void* queries, tq_dtype q_dtype, const uint32_t* k_quant,
+                                 const void* k_scales, const void* k_biases,
+                                 const uint32_t* v_quant, const void* v_scales,
+                                 const void* v_biases, tq_dtype sb_dtype, int gqa_factor,
+                                 float scale, int sliding_window, int batch, int num_kv_heads,
+                                 int head_dim, int n_local, int capacity, int token_offset,
+                                 int n_total, void* const* peer_bufs, int world, int rank,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  t_err.clear();
+  if (!peer_bufs) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_partial_publish: null peer_bufs");
+  if (world < 1 || world > tq::kPeerMaxWorld || rank < 0 || rank >= world)
+    return fail(TQ_ERR_INVALID, "tq_sdpa_int4_partial_publish: bad world/rank");
+  if (token_offset < 0 || n_total < token_offset + n_local)
+    return fail(TQ_ERR_INVALID, "tq_sdpa_int4_partial_publish: need 0 <= token_offset and "
+                "token_offset + n_local <= n_total");
+  DecodeCommon c{queries, q_dtype, k_quant, v_quant, k_scales, k_biases, v_scales, v_biases,
+                 sb_dtype, gqa_factor, sliding_window, batch, num_kv_heads, head_dim, n_local,
+                 capacity, scale};
+  c.peer_bufs = peer_bufs;
+  c.peer_world = world;
+  c.peer_rank = rank;
+  return decode_common(c, "tq_sdpa_int4_partial_publish", nullptr, token_offset, n_total, 1,
+                       nullptr, TQ_F32, nullptr, workspace, workspace_bytes, stream);
 }
 
 int tq_lse_merge(const float* parts, int n_parts, int batch, int num_heads, int head_dim,

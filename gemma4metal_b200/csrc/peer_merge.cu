@@ -28,25 +28,25 @@
 #include "../../include/turboquant_c.h"
 #include "tq_common.cuh"
 #include "tq_internal.h"
+#include "peer_layout.cuh"
 
 namespace tq {
 namespace {
 
-constexpr int kHeaderWords = 32 * 66;  // step counter, 64 flags (128 B apart), grid counter
-constexpr int kGridCounter = 32 * 65;
-constexpr int kFailedWord = 32 * 65 + 16;  // nonzero once a wait of this rank timed out
-__device__ __forceinline__ int flag_word(int k) { return 32 * (1 + k); }
-constexpr int kMaxWorld = 64;
+constexpr int kGridCounter = kPeerGridCounter;
+constexpr int kFailedWord = kPeerFailedWord;
+constexpr int kMaxWorld = kPeerMaxWorld;
 constexpr int kPeerThreads = 256;
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
+__device__ __forceinline__ int flag_word(int k) { return peer_flag_word(k); }
+#ifndef TQ_PEER_MERGE_PDL
+#define TQ_PEER_MERGE_PDL 1
+#endif
+constexpr bool kPublishedMergePdl = TQ_PEER_MERGE_PDL != 0;
+// back-off between flag polls: a waiting CTA shares its SM with decode CTAs
+#ifndef TQ_PEER_POLL_NS
+#define TQ_PEER_POLL_NS 0
+#endif
+constexpr unsigned kPollSleepNs = TQ_PEER_POLL_NS;
 
 struct PeerParams {
   const float* part;      // this rank's partial state (B, H*(D+2))
@@ -57,6 +57,7 @@ struct PeerParams {
   int out_dtype;
   long long budget;       // SM clocks a wait may take
   uint32_t* err;
+  int units;              // > 0: the decode kernel published the states per unit (no push here)
 };
 
 __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerParams p) {
@@ -74,9 +75,10 @@ __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerPara
   const long long blk = static_cast<long long>(p.B) * p.H * (p.D + 2);  // floats per state
   const int par = static_cast<int>(step & 1u);
 
-  // ---- push: CTA j copies the state into rank j's slot [par][rank]
-  for (int j = blockIdx.x; j < p.world; j += gridDim.x) {
-    float* dst = reinterpret_cast<float*>(static_cast<uint32_t*>(p.bufs[j]) + kHeaderWords) +
+  // ---- push: CTA j copies the state into rank j's slot [par][rank] (when the
+  // decode kernel did not publish it per unit already)
+  for (int j = blockIdx.x; j < p.world && p.units == 0; j += gridDim.x) {
+    float* dst = reinterpret_cast<float*>(static_cast<uint32_t*>(p.bufs[j]) + peer_data_word(p.B, p.H)) +
                  (static_cast<long long>(par) * p.world + p.rank) * blk;
     if ((blk & 3) == 0) {
       const float4* s4 = reinterpret_cast<const float4*>(p.part);
@@ -90,30 +92,39 @@ __global__ void __launch_bounds__(kPeerThreads) peer_merge_kernel(const PeerPara
     if (threadIdx.x == 0) st_release_sys(static_cast<uint32_t*>(p.bufs[j]) + flag_word(p.rank), step);
   }
 
-  // ---- wait for every rank's state of this step (bounded; none on a failed exchange)
-  if (threadIdx.x < p.world && !s_failed) {
-    const uint32_t* flag = own + flag_word(threadIdx.x);
-    const long long t0 = clock64();
-    while (static_cast<int>(ld_acquire_sys(flag) - step) < 0) {
-      if (clock64() - t0 > p.budget) {
-        s_failed = 1;
-        atomicOr(own + kFailedWord, 1u);
-        break;
+  // ---- wait (bounded; none on a failed exchange) for the states of this step:
+  // whole states, every rank's flag before any item; published states, the
+  // flags of an item's (sequence, KV head) unit before that item, so items
+  // merge while other units are still being published
+  auto wait_flags = [&](int n, int unit) {
+    for (int k = threadIdx.x; k < n && !s_failed; k += kPeerThreads) {
+      const uint32_t* flag =
+          unit >= 0 ? own + peer_unit_flag_word(k, unit, p.B, p.H) : own + flag_word(k);
+      const long long t0 = clock64();
+      while (static_cast<int>(ld_acquire_sys(flag) - step) < 0) {
+        if (kPollSleepNs > 0) __nanosleep(kPollSleepNs);
+        if (clock64() - t0 > p.budget) {
+          s_failed = 1;
+          atomicOr(own + kFailedWord, 1u);
+          atomicOr(p.err, kErrPeerTimeout);
+          break;
+        }
       }
     }
-  }
-  __syncthreads();
-  const bool failed = s_failed != 0;
-  if (failed && threadIdx.x == 0) atomicOr(p.err, kErrPeerTimeout);
+    __syncthreads();
+  };
+  if (p.units == 0) wait_flags(p.world, -1);
+  if (s_failed && threadIdx.x == 0) atomicOr(p.err, kErrPeerTimeout);  // (again, on a failed exchange)
 
   // ---- merge: CTA c takes (sequence, head) items c, c + grid, ...
-  const float* data = reinterpret_cast<const float*>(own + kHeaderWords) +
+  const float* data = reinterpret_cast<const float*>(own + peer_data_word(p.B, p.H)) +
                       static_cast<long long>(par) * p.world * blk;
   const long long hd = static_cast<long long>(p.H) * p.D;
   for (int item = blockIdx.x; item < p.B * p.H; item += gridDim.x) {
     const int b = item / p.H, h = item % p.H;
     const float* base = data + static_cast<long long>(b) * p.H * (p.D + 2);
-    if (failed) {  // no complete set of states: NaN, never stale slots
+    if (p.units > 0) wait_flags(p.world, b * (p.units / p.B) + h / (p.H / (p.units / p.B)));
+    if (s_failed) {  // no complete set of states: NaN, never stale slots
       for (int d = threadIdx.x; d < p.D; d += kPeerThreads)
         store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * p.D + d, p.out_dtype, NAN);
       continue;
@@ -172,7 +183,8 @@ extern "C" {
 
 TQ_API size_t tq_peer_buffer_bytes(int world, int batch, int num_heads, int head_dim) {
   if (world < 1 || world > kMaxWorld || batch < 1 || num_heads < 1 || head_dim < 1) return 0;
-  return kHeaderWords * sizeof(uint32_t) + state_floats(world, batch, num_heads, head_dim) * sizeof(float);
+  return static_cast<size_t>(peer_data_word(batch, num_heads)) * sizeof(uint32_t) +
+         state_floats(world, batch, num_heads, head_dim) * sizeof(float);
 }
 
 TQ_API int tq_peer_buffer_alloc(size_t bytes, void** buf) {
@@ -238,10 +250,36 @@ TQ_API int tq_ipc_close(void* peer_buf) {
   return TQ_OK;
 }
 
+static int peer_merge_common(const float* part, void* const* peer_bufs, int world, int rank,
+                             int batch, int num_heads, int head_dim, int units, void* out,
+                             tq_dtype out_dtype, int timeout_us, void* stream);
+
 TQ_API int tq_peer_merge(const float* part, void* const* peer_bufs, int world, int rank,
                          int batch, int num_heads, int head_dim, void* out, tq_dtype out_dtype,
                          int timeout_us, void* stream) {
-  if (!part || !peer_bufs || !out) {
+  if (!part) {
+    set_last_error("tq_peer_merge: null pointer");
+    return TQ_ERR_INVALID;
+  }
+  return peer_merge_common(part, peer_bufs, world, rank, batch, num_heads, head_dim, 0, out,
+                           out_dtype, timeout_us, stream);
+}
+
+TQ_API int tq_peer_merge_published(void* const* peer_bufs, int world, int rank, int batch,
+                                   int num_heads, int num_kv_heads, int head_dim, void* out,
+                                   tq_dtype out_dtype, int timeout_us, void* stream) {
+  if (num_kv_heads < 1 || num_heads % num_kv_heads != 0 || batch < 1) {
+    set_last_error("tq_peer_merge_published: bad sizes");
+    return TQ_ERR_INVALID;
+  }
+  return peer_merge_common(nullptr, peer_bufs, world, rank, batch, num_heads, head_dim,
+                           batch * num_kv_heads, out, out_dtype, timeout_us, stream);
+}
+
+static int peer_merge_common(const float* part, void* const* peer_bufs, int world, int rank,
+                             int batch, int num_heads, int head_dim, int units, void* out,
+                             tq_dtype out_dtype, int timeout_us, void* stream) {
+  if (!peer_bufs || !out) {
     set_last_error("tq_peer_merge: null pointer");
     return TQ_ERR_INVALID;
   }
@@ -250,7 +288,7 @@ TQ_API int tq_peer_merge(const float* part, void* const* peer_bufs, int world, i
     set_last_error("tq_peer_merge: bad sizes");
     return TQ_ERR_INVALID;
   }
-  if (reinterpret_cast<uintptr_t>(part) & 15u) {
+  if (part && (reinterpret_cast<uintptr_t>(part) & 15u)) {
     set_last_error("tq_peer_merge: part must be 16-byte aligned");
     return TQ_ERR_INVALID;
   }
@@ -269,11 +307,21 @@ TQ_API int tq_peer_merge(const float* part, void* const* peer_bufs, int world, i
   p.out_dtype = out_dtype;
   p.budget = static_cast<long long>(timeout_us) * (khz > 0 ? khz : 2000000) / 1000;
   p.err = device_error_word();
+  p.units = units;
   int grid = batch * num_heads;
   if (grid < world) grid = world;
   if (grid > 148) grid = 148;
-  peer_merge_kernel<<<grid, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
-  const cudaError_t e = cudaGetLastError();
+  cudaError_t e;
+  if (units > 0 && kPublishedMergePdl) {
+    // published states: nothing of the preceding decode kernel is read
+    // without a flag, so the merge may start once that kernel's CTAs have all
+    // started and merge each unit as soon as its flags are up
+    e = launch_pdl(peer_merge_kernel, dim3(grid), dim3(kPeerThreads), 0,
+                   static_cast<cudaStream_t>(stream), p);
+  } else {
+    peer_merge_kernel<<<grid, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) {
     set_last_error("tq_peer_merge: %s", cudaGetErrorString(e));
     return TQ_ERR_CUDA;

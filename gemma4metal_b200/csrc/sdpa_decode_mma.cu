@@ -55,6 +55,7 @@
 
 #include "tq_common.cuh"
 #include "tq_internal.h"
+#include "peer_layout.cuh"
 
 namespace tq {
 
@@ -125,7 +126,7 @@ struct MParams {
   const void* vb;
   const int32_t* seq_lens;
   int n_tokens;
-  int H, Hkv, Gtot, nsub;
+  int B, H, Hkv, Gtot, nsub;
   int capacity;
   long long bstride_tok;
   float qscale;  // scale * log2(e)
@@ -148,6 +149,11 @@ struct MParams {
   float* ws_ml;
   unsigned* counters;
   uint32_t* err;
+  // partial == 1 with peer_bufs: the state goes straight into slot
+  // [step parity][peer_rank] of every rank's exchange buffer, then the
+  // unit's flag is raised in each (peer_layout.cuh); part_out is unused
+  void* const* peer_bufs;
+  int peer_world, peer_rank;
 };
 
 // ---- PTX wrappers -------------------------------------------------------------
@@ -915,6 +921,35 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
 
   const bool direct = p.splits == 1;
   const long long unit = static_cast<long long>(b) * gridDim.y + hg;
+  // a value of this sequence's partial state: to part_out, or (published)
+  // into slot [parity][peer_rank] of every rank's exchange buffer
+  const long long sblk = static_cast<long long>(b) * p.H * (D + 2);
+  const uint32_t pstep =
+      p.peer_bufs ? *reinterpret_cast<volatile const uint32_t*>(p.peer_bufs[p.peer_rank]) + 1u : 0u;
+  auto put_state = [&](long long off, float v) {
+    if (!p.peer_bufs) {
+      p.part_out[sblk + off] = v;
+      return;
+    }
+    const long long slot = (static_cast<long long>(pstep & 1u) * p.peer_world + p.peer_rank) *
+                           p.B * p.H * (D + 2);
+    for (int k = 0; k < p.peer_world; ++k)
+      (reinterpret_cast<float*>(static_cast<uint32_t*>(p.peer_bufs[k]) + peer_data_word(p.B, p.H)) +
+       slot + sblk)[off] = v;
+  };
+  // after every thread's put_state: raise this unit's flag in every buffer
+  // (the barrier orders the stores before thread 0's system-scope fence)
+  auto publish_flags = [&]() {
+    if (!p.peer_bufs || !p.partial) return;
+    consumers_sync<W>();
+    if (tid == 0) {
+      __threadfence_system();
+      for (int k = 0; k < p.peer_world; ++k)
+        st_release_sys(static_cast<uint32_t*>(p.peer_bufs[k]) +
+                           peer_unit_flag_word(p.peer_rank, static_cast<int>(unit), p.B, p.H),
+                       pstep);
+    }
+  };
   const float* wall = reinterpret_cast<const float*>(smem);
   constexpr int NTH = W * 32;
   for (int it = tid; it < G * D; it += NTH) {
@@ -934,11 +969,10 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     const int h = h0 + g;
     if (direct) {
       if (p.partial) {
-        float* blk = p.part_out + static_cast<long long>(b) * p.H * (D + 2);
-        blk[static_cast<long long>(h) * D + d] = acc;
+        put_state(static_cast<long long>(h) * D + d, acc);
         if (d == 0) {
-          blk[static_cast<long long>(p.H) * D + 2 * h] = L == 0.0f ? -INFINITY : M * kLn2;
-          blk[static_cast<long long>(p.H) * D + 2 * h + 1] = L;
+          put_state(static_cast<long long>(p.H) * D + 2 * h, L == 0.0f ? -INFINITY : M * kLn2);
+          put_state(static_cast<long long>(p.H) * D + 2 * h + 1, L);
         }
       } else {
         store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * D + d, p.out_dtype,
@@ -953,7 +987,10 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
       }
     }
   }
-  if (direct) return;
+  if (direct) {
+    publish_flags();
+    return;
+  }
 
   // ---- last CTA of this (b, head group) merges the splits -------------------
   // Release: the CTA barrier orders every thread's partial stores before
@@ -1046,12 +1083,11 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     const int h = h0 + g;
     const float av[4] = {a.x, a.y, a.z, a.w};
     if (p.partial) {
-      float* blk = p.part_out + static_cast<long long>(b) * p.H * (D + 2);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) blk[static_cast<long long>(h) * D + d + j] = av[j];
+      for (int j = 0; j < 4; ++j) put_state(static_cast<long long>(h) * D + d + j, av[j]);
       if (d == 0) {
-        blk[static_cast<long long>(p.H) * D + 2 * h] = L == 0.0f ? -INFINITY : M * kLn2;
-        blk[static_cast<long long>(p.H) * D + 2 * h + 1] = L;
+        put_state(static_cast<long long>(p.H) * D + 2 * h, L == 0.0f ? -INFINITY : M * kLn2);
+        put_state(static_cast<long long>(p.H) * D + 2 * h + 1, L);
       }
     } else {
       const float inv = L == 0.0f ? 0.0f : 1.0f / L;
@@ -1062,6 +1098,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     }
   }
   if (tid == 0) p.counters[unit] = 0u;
+  publish_flags();
 }
 
 // ---- host side ----------------------------------------------------------------
@@ -1216,6 +1253,10 @@ cudaError_t launch_decode_mma(const DecodeArgs& a, const DecodePlan& pl, cudaStr
     p.counters = reinterpret_cast<unsigned*>(ws + pl.ws_cnt_off);
   }
   p.err = a.err;
+  p.peer_bufs = a.peer_bufs;
+  p.peer_world = a.peer_world;
+  p.peer_rank = a.peer_rank;
+  p.B = a.B;
   dim3 grid(pl.splits, a.Hkv * pl.nsub, a.B);
   return launch_pdl(k.fn, grid, dim3(k.threads), static_cast<size_t>(k.smem), stream, tmk, tmv, p);
 }

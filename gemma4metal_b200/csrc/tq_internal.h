@@ -55,6 +55,11 @@ struct DecodeArgs {
   int new_dtype = 0;
   int new_slot = -1;  // < 0: n_local - 1
   const int32_t* new_slots = nullptr;  // device, one slot per sequence (overrides new_slot)
+  // partial == 1, tensor-core kernel: publish the state into every rank's
+  // exchange buffer (peer_layout.cuh) instead of part_out
+  void* const* peer_bufs = nullptr;
+  int peer_world = 0;
+  int peer_rank = 0;
 };
 
 // Decode kernel variants: the CUDA-core kernel (sdpa_decode.cu) and the

@@ -141,6 +141,35 @@ class PeerExchange:
             tq._ptr(out), tq._dt(out), self.timeout_us, tq._stream(s)))
         return out
 
+    def decode(self, queries: torch.Tensor, cache, n_local: int, token_offset: int, n_total: int,
+               gqa_factor: int, scale: float = 1.0, sliding_window: int = 0,
+               out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+               ws: Optional[torch.Tensor] = None, s=None) -> torch.Tensor:
+        """One sequence-split decode step with the exchange inside the decode
+        kernel: each (sequence, KV head) unit's partial state is stored into
+        every rank's buffer as soon as it is complete
+        (`tq_sdpa_int4_partial_publish`), then a merge-only launch
+        (`tq_peer_merge_published`) waits for the units' flags and merges.
+        Same lockstep and failure rules as `merge`; use one exchange with
+        either `merge` or `decode`."""
+        if self.failed:
+            raise RuntimeError("PeerExchange: a merge timed out on this exchange; close it and "
+                               "build a new one on every rank")
+        B, H, D = queries.shape
+        if (B, H, D) != (self.B, self.H, self.D):
+            raise ValueError(f"queries {tuple(queries.shape)} do not match the exchange "
+                             f"({self.B}, {self.H}, {self.D})")
+        Hkv = H // int(gqa_factor)
+        if out is None:
+            out = torch.empty(B, H, D, dtype=out_dtype or queries.dtype, device=self.device)
+        tq.sdpa_int4_partial_publish(queries, cache, gqa_factor, scale, sliding_window, self.bufs,
+                                     self.world, self.rank, n_local=n_local,
+                                     token_offset=token_offset, n_total=n_total, ws=ws, s=s)
+        tq._check(tq.load_library().tq_peer_merge_published(
+            self.bufs.data_ptr(), self.world, self.rank, B, H, Hkv, D, tq._ptr(out), tq._dt(out),
+            self.timeout_us, tq._stream(s)))
+        return out
+
     def check(self, s=None) -> None:
         """Read (and clear) the device error word after the merges enqueued so
         far (synchronises the stream); raise if one of them timed out waiting
@@ -179,7 +208,8 @@ def seqsplit_decode(queries: torch.Tensor, cache, n_local: int, token_offset: in
                     group=None, out_dtype: Optional[torch.dtype] = None,
                     partial_fn: Optional[Callable] = None,
                     merge_fn: Optional[Callable] = None,
-                    exchange: Optional[PeerExchange] = None) -> torch.Tensor:
+                    exchange: Optional[PeerExchange] = None,
+                    published: bool = False) -> torch.Tensor:
     """Decode attention of a sequence split across the ranks of `group`.
 
     queries (B, H, D) (the same on every rank); cache = this rank's shard
@@ -188,9 +218,16 @@ def seqsplit_decode(queries: torch.Tensor, cache, n_local: int, token_offset: in
     Returns (B, H, D) on every rank. partial_fn / merge_fn default to the CUDA
     kernels; tests substitute CPU implementations to check the host logic.
     With `exchange` the states move over peer memory and the merge happens in
-    the same kernel (`PeerExchange.merge`) instead of all-gather + merge."""
+    the same kernel (`PeerExchange.merge`) instead of all-gather + merge; with
+    `published` as well, the decode kernel stores each unit's state into the
+    buffers itself and a merge-only launch follows (`PeerExchange.decode`)."""
     world, _ = _world_rank(group)
     B, H, D = queries.shape
+    if exchange is not None and published:
+        if partial_fn is not None:
+            raise ValueError("published states come from the CUDA decode kernel")
+        return exchange.decode(queries, cache, n_local, token_offset, n_total, gqa_factor, scale,
+                               sliding_window, out_dtype=out_dtype or queries.dtype)
     part = (partial_fn or _cuda_partial)(queries, cache, n_local, token_offset, n_total,
                                          gqa_factor, scale, sliding_window)
     part = part.reshape(B, H * (D + 2))
@@ -234,10 +271,10 @@ class SeqSplitCache:
 
     def decode(self, queries: torch.Tensor, gqa_factor: int, scale: float = 1.0,
                sliding_window: int = 0, out_dtype: Optional[torch.dtype] = None,
-               exchange: Optional[PeerExchange] = None) -> torch.Tensor:
+               exchange: Optional[PeerExchange] = None, published: bool = False) -> torch.Tensor:
         return seqsplit_decode(queries, self.cache.tensors(), self.n_local, self.t0, self.n_total,
                                gqa_factor, scale, sliding_window, group=self.group,
-                               out_dtype=out_dtype, exchange=exchange)
+                               out_dtype=out_dtype, exchange=exchange, published=published)
 
 
 # ------------------------------------------------------------- failures --

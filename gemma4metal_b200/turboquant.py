@@ -72,6 +72,9 @@ def load_library() -> ctypes.CDLL:
                                       P, P, I, P, SZ, P]
     L.tq_sdpa_int4_partial.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, I, I, P,
                                        P, SZ, P]
+    L.tq_sdpa_int4_partial_publish.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I,
+                                               I, I, P, I, I, P, SZ, P]
+    L.tq_peer_merge_published.argtypes = [P, I, I, I, I, I, I, P, I, I, P]
     L.tq_lse_merge.argtypes = [P, I, I, I, I, P, I, P]
     L.tq_device_error.argtypes = [P, ctypes.POINTER(ctypes.c_uint32)]
     _register_extra(L)
@@ -558,6 +561,20 @@ class HostDecodeStep:
             pass
 
 
+def _shard_args(queries, cache, n_local, token_offset, n_total, sliding_window, ws, s):
+    q = queries.unsqueeze(0) if queries.dim() == 2 else queries
+    cache = list(cache)
+    if cache[0].dim() == 3:
+        cache = [c.unsqueeze(0) for c in cache]
+    B, H, D = q.shape
+    _, Hkv, cap, _ = cache[0].shape
+    nl = cap if n_local is None else int(n_local)
+    nt = token_offset + nl if n_total is None else int(n_total)
+    if ws is None:
+        ws = workspace(q.device, sdpa_int4_workspace_size(B, H, Hkv, D, nl, sliding_window), s)
+    return q, q.contiguous(), cache, B, H, D, Hkv, cap, nl, nt, ws
+
+
 def sdpa_int4_partial(queries: torch.Tensor, k_quant, k_scales, k_biases, v_quant, v_scales,
                       v_biases, gqa_factor: int, scale: float = 1.0, sliding_window: int = 0,
                       *, n_local: Optional[int] = None, token_offset: int = 0,
@@ -565,25 +582,33 @@ def sdpa_int4_partial(queries: torch.Tensor, k_quant, k_scales, k_biases, v_quan
                       ws: Optional[torch.Tensor] = None, s=None) -> torch.Tensor:
     """Partial softmax state of a sequence shard, returned as (B, H*(D+2))
     fp32 in the tq_lse_merge layout."""
-    q = queries.unsqueeze(0) if queries.dim() == 2 else queries
-    cache = [k_quant, k_scales, k_biases, v_quant, v_scales, v_biases]
-    if k_quant.dim() == 3:
-        cache = [c.unsqueeze(0) for c in cache]
-    B, H, D = q.shape
-    _, Hkv, cap, _ = cache[0].shape
-    nl = cap if n_local is None else int(n_local)
-    nt = token_offset + nl if n_total is None else int(n_total)
+    q, qc, cache, B, H, D, Hkv, cap, nl, nt, ws = _shard_args(
+        queries, (k_quant, k_scales, k_biases, v_quant, v_scales, v_biases), n_local,
+        token_offset, n_total, sliding_window, ws, s)
     if part_out is None:
         part_out = torch.empty(B, H * (D + 2), dtype=torch.float32, device=q.device)
-    nbytes = sdpa_int4_workspace_size(B, H, Hkv, D, nl, sliding_window)
-    if ws is None:
-        ws = workspace(q.device, nbytes, s)
-    qc = q.contiguous()
     _check(load_library().tq_sdpa_int4_partial(
         _ptr(qc), _dt(q), *[_ptr(c) for c in cache], _dt(cache[1]), int(gqa_factor),
         float(scale), int(sliding_window), B, Hkv, D, nl, cap, int(token_offset), nt,
         _ptr(part_out), _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
     return part_out
+
+
+def sdpa_int4_partial_publish(queries: torch.Tensor, cache, gqa_factor: int, scale: float,
+                              sliding_window: int, peer_bufs: torch.Tensor, world: int,
+                              rank: int, *, n_local: Optional[int] = None, token_offset: int = 0,
+                              n_total: Optional[int] = None, ws: Optional[torch.Tensor] = None,
+                              s=None) -> None:
+    """The shard's partial state, stored by the decode kernel straight into
+    every rank's exchange buffer (peer_bufs: device int64 array of the
+    world's buffer pointers); tq_peer_merge_published merges it."""
+    q, qc, cache, B, H, D, Hkv, cap, nl, nt, ws = _shard_args(
+        queries, cache, n_local, token_offset, n_total, sliding_window, ws, s)
+    _check(load_library().tq_sdpa_int4_partial_publish(
+        _ptr(qc), _dt(q), *[_ptr(c) for c in cache], _dt(cache[1]), int(gqa_factor),
+        float(scale), int(sliding_window), B, Hkv, D, nl, cap, int(token_offset), nt,
+        peer_bufs.data_ptr(), int(world), int(rank), _ptr(ws), 0 if ws is None else ws.numel(),
+        _stream(s)))
 
 
 def lse_merge(parts: torch.Tensor, num_heads: int, head_dim: int,

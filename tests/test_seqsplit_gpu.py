@@ -101,9 +101,13 @@ def _peer_worker(rank, world, port, q, mode):
         # peer step within the wait bound
         sc.decode(q16, H // Hkv, 1.0, 0, out_dtype=torch.float32)
         torch.cuda.synchronize()
+        pub = mode.endswith("published")
         ex = seqsplit.PeerExchange(1, H, D, device=f"cuda:{rank}",
                                    timeout_us=5_000_000 if mode == "parity" else 200_000)
         if mode == "parity":
+            # a second exchange for the published path (decode kernel stores
+            # the states, merge-only launch)
+            ex_pub = seqsplit.PeerExchange(1, H, D, device=f"cuda:{rank}")
             res, codes = [], []
             # several steps: the exchange alternates its two slots and step flags
             for step in range(5):
@@ -111,10 +115,13 @@ def _peer_worker(rank, world, port, q, mode):
                 vn = torch.from_numpy(L["v_new"]).cuda() * (1 - 0.1 * step)
                 sc.append(kn, vn)
                 peer = sc.decode(q16, H // Hkv, 1.0, 0, out_dtype=torch.float32, exchange=ex)
+                publ = sc.decode(q16, H // Hkv, 1.0, 0, out_dtype=torch.float32, exchange=ex_pub,
+                                 published=True)
                 nccl = sc.decode(q16, H // Hkv, 1.0, 0, out_dtype=torch.float32)
                 torch.cuda.synchronize()
-                res.append(float((peer - nccl).abs().max()))
+                res.append(max(float((peer - nccl).abs().max()), float((publ - nccl).abs().max())))
                 codes.append(tq.device_error())
+            ex_pub.close()
             assert codes == [0] * 5, codes
             # the last step against the oracle's unsplit dequantize + SDPA
             ks = [L["k"]] + [L["k_new"] * (1 + 0.1 * s) for s in range(5)]
@@ -129,13 +136,15 @@ def _peer_worker(rank, world, port, q, mode):
         else:  # rank 1 misses one step: rank 0's merge must time out, record it, return
             part_q = q16
             if rank == 0:
-                out = sc.decode(part_q, H // Hkv, 1.0, 0, out_dtype=torch.float32, exchange=ex)
+                out = sc.decode(part_q, H // Hkv, 1.0, 0, out_dtype=torch.float32, exchange=ex,
+                                published=pub)
                 torch.cuda.synchronize()
                 code = tq.device_error()
                 # never a merge of stale slots: the outputs are NaN
                 assert bool(torch.isnan(out).all()), "timed-out merge must write NaN"
                 # the exchange stays failed: the next merge gives up at once
-                out2 = sc.decode(part_q, H // Hkv, 1.0, 0, out_dtype=torch.float32, exchange=ex)
+                out2 = sc.decode(part_q, H // Hkv, 1.0, 0, out_dtype=torch.float32, exchange=ex,
+                                 published=pub)
                 torch.cuda.synchronize()
                 assert bool(torch.isnan(out2).all())
                 try:
@@ -181,13 +190,15 @@ def test_peer_exchange_two_gpus():
         assert err <= 2e-3 and cos >= 0.99999, (rank, err, cos)
 
 
-def test_peer_exchange_missing_rank_times_out():
+@pytest.mark.parametrize("mode", ["timeout", "timeout_published"])
+def test_peer_exchange_missing_rank_times_out(mode):
     """A rank that skips a step (host-side failure, no GPU fault): the other
     rank's merge gives up after its bound and reports the peer timeout in the
-    device error word instead of hanging."""
+    device error word instead of hanging -- with whole states pushed by the
+    merge kernel, and with states published per unit by the decode kernel."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    res = _run_two("timeout")
+    res = _run_two(mode)
     assert res[0] == 2  # TQ_DEVICE_ERR_PEER_TIMEOUT
 
 
@@ -208,5 +219,35 @@ def test_peer_exchange_single_gpu_equals_merge():
         torch.cuda.synchronize()
         assert tq.device_error() == 0
         assert torch.allclose(got, ref, rtol=1e-6, atol=1e-6)
+    finally:
+        ex.close()
+
+
+@pytest.mark.parametrize("H,Hkv,D,N,win", [(16, 8, 128, 2049, 0), (32, 8, 256, 3001, 700),
+                                           (8, 8, 128, 100, 0)])
+def test_published_single_gpu_equals_partial_merge(H, Hkv, D, N, win):
+    """World of one: the decode kernel stores its state into its own exchange
+    buffer (split-KV merge path and, at N = 100, the one-split direct path),
+    the merge-only launch merges it -- the same as lse_merge of
+    tq_sdpa_int4_partial's state, over several steps."""
+    import gemma4metal_b200.turboquant as tq
+    from gemma4metal_b200 import seqsplit
+    from oracle import inputs
+    B = 2
+    L = inputs.make_layer(23, H, Hkv, D, N, batch=B)
+    cache = tq.KVCache(B, Hkv, D, (N + 3) // 4 * 4)
+    cache.append(torch.from_numpy(L["k"]).cuda(), torch.from_numpy(L["v"]).cuda())
+    q = torch.from_numpy(L["q"]).half().cuda()
+    ex = seqsplit.PeerExchange(B, H, D)
+    try:
+        for step in range(3):  # slot parity and step counter
+            qs = q * (1 + 0.25 * step)
+            got = ex.decode(qs, cache.tensors(), N, 0, N, H // Hkv, 0.125, win,
+                            out_dtype=torch.float32)
+            part = tq.sdpa_int4_partial(qs, *cache.tensors(), H // Hkv, 0.125, win, n_local=N)
+            ref = tq.lse_merge(part[None], H, D)
+            torch.cuda.synchronize()
+            assert tq.device_error() == 0
+            assert torch.allclose(got, ref, rtol=1e-6, atol=1e-6), float((got - ref).abs().max())
     finally:
         ex.close()

@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload all|cfg0|cfg1|cfg2|cfg3|cfg4|probe]
-                    [--context 32768] [--window 0] [--exchange peer|nccl]
+                    [--context 32768] [--window 0] [--exchange published|peer|nccl]
 
 Headline (top-level keys): config 1 at 32K tokens. One step = one decode step
 of one attention layer: quantize-on-append of the new token's K/V into the
@@ -21,7 +21,9 @@ Nested under "configs" (default `--workload all`): config 0 (one layer, 1024
 tokens), config 2 (tcgen05: 64 x 1 batched decode over a shared 8K cache and
 the 512-query prefill chunk), config 3 (PolarQuant + QJL compressed keys) and
 a read-only HBM probe on one GPU; config 4 (one 262144-token sequence split
-over all N GPUs, peer-memory exchange + merge, strong scaling) at every N,
+over all N GPUs, the decode kernel storing its partial state into every
+rank's exchange buffer over NVLink + a merge-only kernel, strong scaling) at
+every N,
 with its time split and its merged output checked against the C oracle.
 
 `--impl reference` times the reference's algorithm on the host CPU instead
@@ -60,11 +62,11 @@ def parse():
     ap.add_argument("--context", type=int, default=32768)
     ap.add_argument("--window", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "published", "nccl"],
-                    help="cfg4 with N>1: partial states exchanged and merged by one kernel over "
-                         "NVLink peer memory (peer), stored into the peers' buffers by the "
-                         "decode kernel itself and merged by a merge-only kernel (published), "
-                         "or NCCL all-gather + merge kernel (nccl)")
+    ap.add_argument("--exchange", default="published", choices=["published", "peer", "nccl"],
+                    help="cfg4 with N>1: partial states stored into every rank's buffer by the "
+                         "decode kernel itself as {value, step} pairs and merged by a merge-only "
+                         "kernel (published), exchanged and merged by one kernel over NVLink "
+                         "peer memory (peer), or NCCL all-gather + merge kernel (nccl)")
     ap.add_argument("--split-step", action="store_true",
                     help="cfg1: run the step as two launches (quantize_append, then sdpa_int4) "
                          "instead of the fused sdpa_int4_append")
@@ -379,10 +381,13 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
     (H=32, Hkv=8, D=256) whose int4 cache is split by sequence over the GPUs
     (strong scaling). Step = append the new token on the last rank + partial
     decode on every rank + exchange of the fp32 (o, m, l) states + LSE merge
-    (one peer-memory kernel, or NCCL all-gather + merge kernel with
-    --exchange nccl), captured in CUDA graphs; layers rotate so every step
-    streams its shard from HBM. Also timed on their own: the append + partial
-    decode, and the exchange + merge. `check`: rank 0 rebuilds layer 0's whole
+    (by default the decode kernel stores its state into every rank's buffer
+    and a merge-only kernel follows; --exchange peer: one peer-memory
+    exchange + merge kernel; --exchange nccl: NCCL all-gather + merge kernel),
+    captured in CUDA graphs; layers rotate so every step streams its shard
+    from HBM. Also timed on their own: the append + partial decode, and the
+    exchange + merge (for the default exchange: the step's time less that of
+    the plain partial decode). `check`: rank 0 rebuilds layer 0's whole
     cache on the host with the C oracle's quantizer and compares the merged
     output with the oracle's dequantize + fp64 SDPA."""
     import math

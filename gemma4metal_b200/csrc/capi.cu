@@ -270,9 +270,7 @@ static int decode_common(const DecodeCommon& c, const char* fn, const int32_t* s
   a.workspace_bytes = workspace_bytes;
   a.err = device_error_ptr();
   if (c.peer_bufs) {
-    // one unit (flag) per (sequence, KV head): the tensor-core kernel with
-    // all of a KV head's query heads in one CTA
-    if (pl.variant != tq::kDecodeMma || pl.nsub != 1)
+    if (pl.variant != tq::kDecodeMma)
       return fail(TQ_ERR_UNSUPPORTED, "%s: publishing needs the tensor-core decode kernel", fn);
     a.peer_bufs = c.peer_bufs;
     a.peer_world = c.peer_world;

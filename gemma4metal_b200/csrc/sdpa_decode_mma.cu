@@ -921,34 +921,37 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
 
   const bool direct = p.splits == 1;
   const long long unit = static_cast<long long>(b) * gridDim.y + hg;
-  // a value of this sequence's partial state: to part_out, or (published)
-  // into slot [parity][peer_rank] of every rank's exchange buffer
+  // a value of this sequence's partial state: to part_out, or (published) as a
+  // {value, step} pair into slot [step parity][peer_rank] of every rank's
+  // exchange buffer (peer_layout.cuh), which needs no fence or flag: the
+  // reader takes a value once its pair carries the step
   const long long sblk = static_cast<long long>(b) * p.H * (D + 2);
-  const uint32_t pstep =
-      p.peer_bufs ? *reinterpret_cast<volatile const uint32_t*>(p.peer_bufs[p.peer_rank]) + 1u : 0u;
+  uint32_t pstep = 0;
+  long long pub_off = 0;  // this sequence's block in the slot, in pairs from the data start
+  if (p.peer_bufs) {
+    pstep = *reinterpret_cast<volatile const uint32_t*>(p.peer_bufs[p.peer_rank]) + 1u;
+    pub_off = (static_cast<long long>(pstep & 1u) * p.peer_world + p.peer_rank) *
+                  p.B * p.H * (D + 2) + sblk;
+  }
+  auto pub_ptr = [&](int k, long long off) {
+    return reinterpret_cast<uint2*>(static_cast<uint32_t*>(p.peer_bufs[k]) + peer_data_word()) +
+           pub_off + off;
+  };
   auto put_state = [&](long long off, float v) {
     if (!p.peer_bufs) {
       p.part_out[sblk + off] = v;
       return;
     }
-    const long long slot = (static_cast<long long>(pstep & 1u) * p.peer_world + p.peer_rank) *
-                           p.B * p.H * (D + 2);
-    for (int k = 0; k < p.peer_world; ++k)
-      (reinterpret_cast<float*>(static_cast<uint32_t*>(p.peer_bufs[k]) + peer_data_word(p.B, p.H)) +
-       slot + sblk)[off] = v;
+    for (int k = 0; k < p.peer_world; ++k) st_pair(pub_ptr(k, off), v, pstep);
   };
-  // after every thread's put_state: raise this unit's flag in every buffer
-  // (the barrier orders the stores before thread 0's system-scope fence)
-  auto publish_flags = [&]() {
-    if (!p.peer_bufs || !p.partial) return;
-    consumers_sync<W>();
-    if (tid == 0) {
-      __threadfence_system();
-      for (int k = 0; k < p.peer_world; ++k)
-        st_release_sys(static_cast<uint32_t*>(p.peer_bufs[k]) +
-                           peer_unit_flag_word(p.peer_rank, static_cast<int>(unit), p.B, p.H),
-                       pstep);
+  // two adjacent values, off even (one 16-byte store per rank when published)
+  auto put_state2 = [&](long long off, float v0, float v1) {
+    if (!p.peer_bufs) {
+      p.part_out[sblk + off] = v0;
+      p.part_out[sblk + off + 1] = v1;
+      return;
     }
+    for (int k = 0; k < p.peer_world; ++k) st_pair2(pub_ptr(k, off), v0, v1, pstep);
   };
   const float* wall = reinterpret_cast<const float*>(smem);
   constexpr int NTH = W * 32;
@@ -970,10 +973,8 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     if (direct) {
       if (p.partial) {
         put_state(static_cast<long long>(h) * D + d, acc);
-        if (d == 0) {
-          put_state(static_cast<long long>(p.H) * D + 2 * h, L == 0.0f ? -INFINITY : M * kLn2);
-          put_state(static_cast<long long>(p.H) * D + 2 * h + 1, L);
-        }
+        if (d == 0)
+          put_state2(static_cast<long long>(p.H) * D + 2 * h, L == 0.0f ? -INFINITY : M * kLn2, L);
       } else {
         store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * D + d, p.out_dtype,
                          L == 0.0f ? 0.0f : acc / L);
@@ -987,10 +988,7 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
       }
     }
   }
-  if (direct) {
-    publish_flags();
-    return;
-  }
+  if (direct) return;
 
   // ---- last CTA of this (b, head group) merges the splits -------------------
   // Release: the CTA barrier orders every thread's partial stores before
@@ -1083,12 +1081,10 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     const int h = h0 + g;
     const float av[4] = {a.x, a.y, a.z, a.w};
     if (p.partial) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) put_state(static_cast<long long>(h) * D + d + j, av[j]);
-      if (d == 0) {
-        put_state(static_cast<long long>(p.H) * D + 2 * h, L == 0.0f ? -INFINITY : M * kLn2);
-        put_state(static_cast<long long>(p.H) * D + 2 * h + 1, L);
-      }
+      put_state2(static_cast<long long>(h) * D + d, av[0], av[1]);
+      put_state2(static_cast<long long>(h) * D + d + 2, av[2], av[3]);
+      if (d == 0)
+        put_state2(static_cast<long long>(p.H) * D + 2 * h, L == 0.0f ? -INFINITY : M * kLn2, L);
     } else {
       const float inv = L == 0.0f ? 0.0f : 1.0f / L;
 #pragma unroll
@@ -1098,7 +1094,6 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
     }
   }
   if (tid == 0) p.counters[unit] = 0u;
-  publish_flags();
 }
 
 // ---- host side ----------------------------------------------------------------

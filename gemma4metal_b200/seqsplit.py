@@ -146,12 +146,12 @@ class PeerExchange:
                out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
                ws: Optional[torch.Tensor] = None, s=None) -> torch.Tensor:
         """One sequence-split decode step with the exchange inside the decode
-        kernel: each (sequence, KV head) unit's partial state is stored into
-        every rank's buffer as soon as it is complete
-        (`tq_sdpa_int4_partial_publish`), then a merge-only launch
-        (`tq_peer_merge_published`) waits for the units' flags and merges.
-        Same lockstep and failure rules as `merge`; use one exchange with
-        either `merge` or `decode`."""
+        kernel: each (sequence, KV head) slice of the partial state is stored
+        into every rank's buffer as {value, step} pairs as soon as it is
+        complete (`tq_sdpa_int4_partial_publish`), then a merge-only launch
+        (`tq_peer_merge_published`) waits for the pairs of the step and
+        merges. Same lockstep and failure rules as `merge`; use one exchange
+        with either `merge` or `decode`."""
         if self.failed:
             raise RuntimeError("PeerExchange: a merge timed out on this exchange; close it and "
                                "build a new one on every rank")
@@ -159,14 +159,13 @@ class PeerExchange:
         if (B, H, D) != (self.B, self.H, self.D):
             raise ValueError(f"queries {tuple(queries.shape)} do not match the exchange "
                              f"({self.B}, {self.H}, {self.D})")
-        Hkv = H // int(gqa_factor)
         if out is None:
             out = torch.empty(B, H, D, dtype=out_dtype or queries.dtype, device=self.device)
         tq.sdpa_int4_partial_publish(queries, cache, gqa_factor, scale, sliding_window, self.bufs,
                                      self.world, self.rank, n_local=n_local,
                                      token_offset=token_offset, n_total=n_total, ws=ws, s=s)
         tq._check(tq.load_library().tq_peer_merge_published(
-            self.bufs.data_ptr(), self.world, self.rank, B, H, Hkv, D, tq._ptr(out), tq._dt(out),
+            self.bufs.data_ptr(), self.world, self.rank, B, H, D, tq._ptr(out), tq._dt(out),
             self.timeout_us, tq._stream(s)))
         return out
 

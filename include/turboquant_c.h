@@ -226,19 +226,21 @@ TQ_API int tq_peer_merge(const float* part, void* const* peer_bufs, int world, i
                          int timeout_us, void* stream);
 
 /* The same exchange with the push moved into the decode kernel: the CTA that
- * finishes a (sequence, KV head) unit's partial state stores it straight
- * into slot [step parity][rank] of every rank's exchange buffer and raises
- * that unit's flag there (step = this rank's step counter + 1), so the
- * states cross NVLink while the other units are still being computed.
- * tq_sdpa_int4_partial_publish takes the arguments of tq_sdpa_int4_partial
- * with (peer_bufs, world, rank) in place of part_out; it runs on the
- * tensor-core decode kernel only (head_dim 128 or 256 with f16 or f32
- * scales; else TQ_ERR_UNSUPPORTED). tq_peer_merge_published, called next on
- * the same stream, waits for each unit's flags of the step from every rank,
- * merges and advances the step counter; its timeout, NaN and failed-exchange
- * rules are tq_peer_merge's. Use one exchange either with tq_peer_merge or
- * with this pair, not both. No counterpart in the reference (it is
- * single-device). */
+ * finishes a (sequence, KV head) slice of the partial state stores it straight
+ * into slot [step parity][rank] of every rank's exchange buffer as
+ * {fp32 value, step} pairs, one store per pair (step = this rank's step
+ * counter + 1), so the state crosses NVLink while the rest is still being
+ * computed and no fence or flag is needed: the merge takes a value once its
+ * pair carries the step. tq_sdpa_int4_partial_publish takes the arguments of
+ * tq_sdpa_int4_partial with (peer_bufs, world, rank) in place of part_out; the
+ * buffers must come from tq_peer_buffer_bytes with the same world, batch,
+ * num_heads and head_dim. It runs on the tensor-core decode kernel only
+ * (head_dim 128 or 256; else TQ_ERR_UNSUPPORTED). tq_peer_merge_published,
+ * called next on the same stream, may start before the decode kernel ends,
+ * waits for the pairs of the step from every rank, merges and advances the
+ * step counter; its timeout, NaN and failed-exchange rules are tq_peer_merge's.
+ * Use one exchange either with tq_peer_merge or with this pair, not both. No
+ * counterpart in the reference (it is single-device). */
 TQ_API int tq_sdpa_int4_partial_publish(const void* queries, tq_dtype q_dtype,
                                         const uint32_t* k_quant, const void* k_scales,
                                         const void* k_biases, const uint32_t* v_quant,
@@ -249,8 +251,8 @@ TQ_API int tq_sdpa_int4_partial_publish(const void* queries, tq_dtype q_dtype,
                                         int n_total, void* const* peer_bufs, int world, int rank,
                                         void* workspace, size_t workspace_bytes, void* stream);
 TQ_API int tq_peer_merge_published(void* const* peer_bufs, int world, int rank, int batch,
-                                   int num_heads, int num_kv_heads, int head_dim, void* out,
-                                   tq_dtype out_dtype, int timeout_us, void* stream);
+                                   int num_heads, int head_dim, void* out, tq_dtype out_dtype,
+                                   int timeout_us, void* stream);
 
 /* Log-sum-exp merge of n_parts partial states (e.g. one per GPU after an
  * all-gather). parts: n_parts blocks of (H*(D+2)) floats per batch entry,

@@ -625,13 +625,17 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_steps / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": (nq + 2 * nkv) * 2, "d2h_bytes_per_step": nq * 2,
-                "path": "pinned q|k_new|v_new -> device on every rank, step graph "
-                        "(append + tq_sdpa_int4_partial + tq_peer_merge), merged output -> pinned "
-                        "host, stream sync; host clock, max over ranks"},
+                "path": "pinned q|k_new|v_new -> device on every rank, step graph (append + " +
+                        ("tq_sdpa_int4_partial_publish + tq_peer_merge_published" if published else
+                         "tq_sdpa_int4_partial + tq_peer_merge" if peer is not None else
+                         "tq_sdpa_int4_partial + " + ("NCCL all-gather + " if world > 1 else "") +
+                         "tq_lse_merge") +
+                        "), merged output -> pinned host, stream sync; host clock, max over ranks"},
         "layers_rotated": layers_n,
         "l2": f"inputs larger than L2: {layers_n} rotating shards of {shard_bytes / 1e6:.0f} MB",
         "gpu_launches_per_step": ("quantize_rows_kernel (last rank), decode_mma_kernel (partial), " +
-                                  ("peer_merge_kernel" if peer is not None else
+                                  ("peer_merge_published_kernel" if published else
+                                   "peer_merge_kernel" if peer is not None else
                                    "lse_merge_kernel" + (" + NCCL all-gather" if world > 1 else ""))),
         "clocks": clk,
     }

@@ -282,11 +282,24 @@ __global__ void __launch_bounds__(kQjlThreads) qjl_encode_kernel(const float* __
 }
 
 // ---- compressed-key attention ----------------------------------------------------
-// grid = (splits, Hkv); 4 warps. Each warp takes keys of its split's range in
-// turn; lane l decodes values 4l..4l+3 of each 128-value group (DPL = D/128
-// groups), forms the partial dot products with the G query heads plus its 8
-// QJL sign terms, a warp sum gives the scores; softmax . int4 V (lane l owns
-// dims 4l..4l+3 of every group) or the scores themselves are the output.
+// grid = (splits, Hkv), 128 threads; a split's keys go through shared memory
+// 128 at a time (kCChunk). Per chunk:
+//  * scores, one thread per key: the PolarQuant part is q . k without
+//    rebuilding k -- the angle tree evaluated bottom-up, a level-1 node
+//    (values 2j, 2j+1) giving q_2j cos + q_2j+1 sin of its angle and a node
+//    at level L giving cos(theta) u_left + sin(theta) u_right of its
+//    children (the decode's products, lib/turboquant.metal:100-224,
+//    reassociated), times the block's radius; the QJL part sums a table of
+//    the signed S q sums of every 4-bit sign pattern (one lookup per 4 sign
+//    bits) times |r| sqrt(pi/2) / m;
+//  * the chunk's max and sum per head over the CTA, then softmax . int4 V
+//    with each thread on 8 consecutive dimensions (one V word) of every
+//    KV_SUB-th key: exact fp32 codes times (p * scale), the bias term summed
+//    once per key and group;
+// then the per-thread states are summed, one partial per CTA goes to the
+// workspace and the last CTA of the KV head merges the splits.
+// S q (the QJL projection of the queries) comes from cattn_sq_kernel when the
+// caller gives a workspace, else every CTA computes it.
 struct CParams {
   const void* q;
   int q_dtype;
@@ -295,6 +308,7 @@ struct CParams {
   const uint32_t* signs;  // (Hkv, N, m/32) or null
   const __half* rnorm;    // (Hkv, N)
   const float* S;         // (m, D)
+  const float* sq;        // (H, m) precomputed S q, or null
   int m;
   const uint32_t* vq;     // (Hkv, N, D/8) int4 V, or null when vdense is used
   const void* vdense;     // (Hkv, N, D) dense V in vdense_dtype (the reference's fp32 values)
@@ -314,276 +328,476 @@ struct CParams {
   int splits;
 };
 
-constexpr int kCKeys = 64;  // keys per shared-memory chunk of compressed attention
+constexpr int kCChunk = 128;  // keys per chunk: one per thread while scoring
+#ifndef TQ_CATTN_SQ_KERNEL
+#define TQ_CATTN_SQ_KERNEL 1
+#endif
+constexpr bool kCattnSqKernel = TQ_CATTN_SQ_KERNEL != 0;  // S q in its own kernel
 
-// Dynamic shared memory of compressed attention: one staged chunk of keys,
-// reused at the end for the 4 warps' (o, m, l) states.
-constexpr size_t cattn_smem_bytes(int D, int G) {
-  const size_t chunk = static_cast<size_t>(kCKeys) * (D / 8 + 8 + D / 8 + 2 * (D / 64) + 16 + 1) * 4;
-  const size_t states = static_cast<size_t>(4) * G * (D + 2) * 4;
-  return chunk > states ? chunk : states;
+// Shared-memory layout of compressed attention (32-bit words; rows padded so
+// that 16-byte loads of consecutive keys' rows hit distinct banks).
+template <int D, int G, int BLOCK>
+struct CLay {
+  static constexpr int PKW = D / 8;        // angle-nibble words per key
+  static constexpr int PKS = PKW + 4;      // padded row
+  static constexpr int SGS = 12;           // sign words per key (<= 8 used)
+  static constexpr int VQW = D / 8;        // int4 V words per key
+  static constexpr int NG = D / 64;        // V groups per key
+  static constexpr int NBK = D / BLOCK;    // radii per key
+  static constexpr int KSUB = 128 / (D / 8);  // keys in flight in the V phase
+  static constexpr int PK = 0;
+  static constexpr int SG = PK + kCChunk * PKS;
+  static constexpr int VQ = SG + kCChunk * SGS;
+  static constexpr int VSB = VQ + kCChunk * VQW;      // (scale, bias) pairs
+  static constexpr int RAD = VSB + kCChunk * NG * 2;  // [kCChunk][NBK]
+  static constexpr int RN = RAD + kCChunk * NBK;
+  static constexpr int P = RN + kCChunk;              // [kCChunk][G] softmax weights
+  static constexpr int QT = P + kCChunk * G;          // [64][16][G] QJL nibble table
+  static constexpr int Q2 = QT + 64 * 16 * G;         // [D/2][G] float2 query pairs
+  static constexpr int SQ = Q2 + D * G;               // [G][256] S q
+  // level-1 table [D/2][16][G]: q_2j cos + q_2j+1 sin of every codebook
+  // angle, when it fits in 16 KB
+  static constexpr bool U1 = (D / 2) * 16 * G <= 4096;
+  static constexpr int U1T = SQ + G * 256;
+  static constexpr int WORDS = U1T + (U1 ? (D / 2) * 16 * G : 0);
+  // reused after the last chunk: [KSUB][G][D] per-thread output sums
+  static_assert(KSUB * G * D <= WORDS, "output sums must fit in the chunk buffers");
+};
+
+template <int D, int G, int BLOCK>
+constexpr size_t cattn_smem_bytes() {
+  return static_cast<size_t>(CLay<D, G, BLOCK>::WORDS) * 4;
+}
+
+constexpr int ilog2c(int x) { return x <= 1 ? 0 : 1 + ilog2c(x / 2); }
+
+template <int I, int W>
+__device__ __forceinline__ int nib(const uint32_t (&w)[W]) {
+  return static_cast<int>((w[I >> 3] >> (4 * (I & 7))) & 15u);
+}
+
+// Angle I's entry of a 16-entry float2 table: its byte offset (index * 8)
+// taken from the nibble with one shift and one mask.
+template <int I, int W>
+__device__ __forceinline__ const float2& cs_entry(const float2* row, const uint32_t (&w)[W]) {
+  constexpr int sh = 4 * (I & 7);
+  const uint32_t off = sh >= 3 ? (w[I >> 3] >> (sh - 3)) & 0x78u : (w[I >> 3] << (3 - sh)) & 0x78u;
+  return *reinterpret_cast<const float2*>(reinterpret_cast<const char*>(row) + off);
+}
+
+// q . (unit vector of node N at level L of a BLOCK-value angle tree), for G
+// query heads; q2 = this block's query pairs [BLOCK/2][G], u1 (when U1) =
+// this block's level-1 table [BLOCK/2][16][G].
+template <int BLOCK, int L, int N, int G, bool U1>
+__device__ __forceinline__ void polar_node(const uint32_t (&pkw)[BLOCK / 8],
+                                           const float2* __restrict__ q2,
+                                           const float* __restrict__ u1,
+                                           const float2 (*cs)[kCB], float (&out)[G]) {
+  if constexpr (L == 1) {
+    if constexpr (U1) {
+      const float* t = u1 + (N * 16 + nib<N>(pkw)) * G;
+      if constexpr (G == 1) {
+        out[0] = t[0];
+      } else if constexpr (G == 2) {
+        const float2 v = *reinterpret_cast<const float2*>(t);
+        out[0] = v.x;
+        out[1] = v.y;
+      } else {
+#pragma unroll
+        for (int g0 = 0; g0 < G; g0 += 4) {
+          const float4 v = *reinterpret_cast<const float4*>(t + g0);
+          out[g0] = v.x;
+          out[g0 + 1] = v.y;
+          out[g0 + 2] = v.z;
+          out[g0 + 3] = v.w;
+        }
+      }
+    } else {
+      const float2 c = cs_entry<N>(cs[0], pkw);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float2 qq = q2[N * G + g];
+        out[g] = fmaf(qq.x, c.x, qq.y * c.y);
+      }
+    }
+  } else {
+    float a[G], b[G];
+    polar_node<BLOCK, L - 1, 2 * N, G, U1>(pkw, q2, u1, cs, a);
+    polar_node<BLOCK, L - 1, 2 * N + 1, G, U1>(pkw, q2, u1, cs, b);
+    const float2 c = cs_entry<level_off(BLOCK, L) + N>(cs[L - 1], pkw);
+#pragma unroll
+    for (int g = 0; g < G; ++g) out[g] = fmaf(c.x, a[g], c.y * b[g]);
+  }
 }
 
 __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-template <int D, int G>
+// nrows rows of rw 32-bit words from contiguous global memory into shared
+// rows of stride ds words: 16-byte copies when rows and source allow.
+__device__ __forceinline__ void stage_rows(uint32_t* dst, int ds, const uint32_t* src, int rw,
+                                           int nrows, int tid) {
+  if ((rw & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+    const int r4 = rw / 4;
+    for (int i = tid; i < nrows * r4; i += 128)
+      cp_async16(dst + (i / r4) * ds + 4 * (i % r4), src + 4 * i);
+  } else {
+    for (int i = tid; i < nrows * rw; i += 128) cp_async4(dst + (i / rw) * ds + i % rw, src + i);
+  }
+}
+
+// S q for H heads: CTA (rb, hb) takes rows 8 rb .. 8 rb + 7 of S (a warp per
+// row, lanes over the dimensions) and heads 8 hb .. 8 hb + 7 (queries staged
+// in shared memory); shuffles sum each (row, head) dot product.
+constexpr int kSqRows = 8, kSqHeads = 8;
+template <int D>
+__global__ void __launch_bounds__(256) cattn_sq_kernel(const void* q, int q_dtype, const float* S,
+                                                       int m, int H, float* sq) {
+  __shared__ __align__(16) float sQ[kSqHeads][D];
+  pdl_wait();
+  pdl_trigger();
+  const int hq0 = blockIdx.y * kSqHeads;
+  for (int i = threadIdx.x; i < kSqHeads * D; i += 256) {
+    const int h = i / D, d = i % D;
+    sQ[h][d] = hq0 + h < H ? load_as_float(q, static_cast<long long>(hq0 + h) * D + d, q_dtype) : 0.0f;
+  }
+  const int lane = threadIdx.x & 31, r = blockIdx.x * kSqRows + (threadIdx.x >> 5);
+  float4 s4[D / 128];
+#pragma unroll
+  for (int c = 0; c < D / 128; ++c)
+    s4[c] = r < m ? reinterpret_cast<const float4*>(S + static_cast<long long>(r) * D + c * 128)[lane]
+                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  __syncthreads();
+  float a[kSqHeads];
+#pragma unroll
+  for (int h = 0; h < kSqHeads; ++h) {
+    a[h] = 0.0f;
+#pragma unroll
+    for (int c = 0; c < D / 128; ++c) {
+      const float4 q4 = reinterpret_cast<const float4*>(&sQ[h][c * 128])[lane];
+      a[h] = fmaf(s4[c].x, q4.x, fmaf(s4[c].y, q4.y, fmaf(s4[c].z, q4.z, fmaf(s4[c].w, q4.w, a[h]))));
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+    for (int h = 0; h < kSqHeads; ++h) a[h] += __shfl_xor_sync(0xffffffffu, a[h], off);
+  if (lane < kSqHeads && r < m && hq0 + lane < H) {
+    float v = a[0];
+#pragma unroll
+    for (int h = 1; h < kSqHeads; ++h) v = lane == h ? a[h] : v;
+    sq[static_cast<long long>(hq0 + lane) * m + r] = v;
+  }
+}
+
+template <int D, int G, int BLOCK>
 __global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p,
                                                               const __grid_constant__ PolarTables T) {
-  constexpr int DPL = D / 128;      // 128-value groups per key
-  __shared__ float s_cs[kMaxLevels][kCB][2];
-  __shared__ float s_sq[G][256];    // S q per head (m <= 256)
-  __shared__ float s_q[G][D];
+  using Ly = CLay<D, G, BLOCK>;
+  constexpr int LV = ilog2c(BLOCK);
+  constexpr int NBK = D / BLOCK;
+  constexpr int OCT = D / 8;  // V words per key
+  __shared__ float2 s_cs[kMaxLevels][kCB];
+  __shared__ float s_red[2][4][G];
+  __shared__ float s_m[G], s_l[G], s_a[G];
   __shared__ int s_last;
+  extern __shared__ __align__(16) uint32_t dsw[];
+  uint32_t* s_pk = dsw + Ly::PK;
+  uint32_t* s_sg = dsw + Ly::SG;
+  uint32_t* s_vq = dsw + Ly::VQ;
+  float2* s_vsb = reinterpret_cast<float2*>(dsw + Ly::VSB);
+  float* s_rad = reinterpret_cast<float*>(dsw + Ly::RAD);
+  float* s_rn = reinterpret_cast<float*>(dsw + Ly::RN);
+  float* s_p = reinterpret_cast<float*>(dsw + Ly::P);
+  float* s_qt = reinterpret_cast<float*>(dsw + Ly::QT);
+  float2* s_q2 = reinterpret_cast<float2*>(dsw + Ly::Q2);
+  float* s_sq = reinterpret_cast<float*>(dsw + Ly::SQ);
+  float* s_u1 = reinterpret_cast<float*>(dsw + Ly::U1T);
+
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int split = blockIdx.x, kv = blockIdx.y;
   const int h0 = kv * G;
-  pdl_wait();
-  pdl_trigger();
-  for (int i = tid; i < kMaxLevels * kCB * 2; i += 128) (&s_cs[0][0][0])[i] = (&T.cs[0][0][0])[i];
-  for (int i = tid; i < G * D; i += 128) s_q[i / D][i % D] = load_as_float(p.q, static_cast<long long>(h0) * D + i, p.q_dtype);
-  __syncthreads();
   const bool qjl = p.signs != nullptr;
-  if (qjl) {
-    // S q for the CTA's G heads: a warp per row of S, lanes over 4 consecutive
-    // dims each (coalesced 512-byte row reads, RB rows' loads in flight),
-    // summed by shuffles
-    constexpr int RB = D == 128 ? 16 : 8;
-    for (int r0 = w; r0 < p.m; r0 += 4 * RB) {
-      float4 s4[RB][D / 128];
-#pragma unroll
-      for (int j = 0; j < RB; ++j) {
-        const int r = r0 + 4 * j;
-#pragma unroll
-        for (int c = 0; c < D / 128; ++c)
-          s4[j][c] = r < p.m ? reinterpret_cast<const float4*>(p.S + static_cast<long long>(r) * D + c * 128)[lane]
-                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  const int mw = p.m / 32;  // sign words per key
+  const int t_begin = split * p.keys_per_split;
+  const int t_end = min(p.N, t_begin + p.keys_per_split);
+  const bool stage_v = p.attend && !p.vdense;
+  // a chunk of keys into shared memory: the word arrays by asynchronous
+  // copies (waited for by the caller), the fp16 arrays by plain loads
+  auto stage = [&](int c0) {
+    const int nk = min(kCChunk, t_end - c0);
+    const long long row0 = static_cast<long long>(kv) * p.N + c0;
+    stage_rows(s_pk, Ly::PKS, reinterpret_cast<const uint32_t*>(p.packed) + row0 * Ly::PKW, Ly::PKW, nk, tid);
+    if (qjl) stage_rows(s_sg, Ly::SGS, p.signs + row0 * mw, mw, nk, tid);
+    if (stage_v) stage_rows(s_vq, Ly::VQW, p.vq + row0 * Ly::VQW, Ly::VQW, nk, tid);
+    cp_async_commit();
+    for (int i = tid; i < nk * NBK; i += 128) s_rad[i] = __half2float(p.radii[row0 * NBK + i]);
+    if (qjl)
+      for (int i = tid; i < nk; i += 128) s_rn[i] = __half2float(p.rnorm[row0 + i]);
+    if (stage_v) {
+      for (int i = tid; i < nk * Ly::NG; i += 128) {
+        const long long gi = row0 * Ly::NG + i;
+        s_vsb[i] = p.sb_f32 ? make_float2(reinterpret_cast<const float*>(p.vs)[gi],
+                                          reinterpret_cast<const float*>(p.vb)[gi])
+                            : make_float2(__half2float(reinterpret_cast<const __half*>(p.vs)[gi]),
+                                          __half2float(reinterpret_cast<const __half*>(p.vb)[gi]));
       }
-#pragma unroll
-      for (int j = 0; j < RB; ++j) {
-        const int r = r0 + 4 * j;
+    }
+  };
+  // Dependencies: with p.sq the preceding kernel is cattn_sq_kernel, which
+  // signals its dependents only after its own wait for the kernels before
+  // it, so the keys, values and queries those wrote are visible here already
+  // and the first chunk and the query set-up go ahead of this kernel's wait,
+  // which then covers S q alone. Without it, everything waits.
+  if (!p.sq) pdl_wait();
+  pdl_trigger();
+  if (t_begin < t_end) stage(t_begin);  // the first chunk's loads go out before the set-up's
+  for (int i = tid; i < kMaxLevels * kCB; i += 128)
+    s_cs[i / kCB][i % kCB] = make_float2(T.cs[i / kCB][i % kCB][0], T.cs[i / kCB][i % kCB][1]);
+  for (int i = tid; i < G * D / 2; i += 128) {
+    const int g = i / (D / 2), j = i % (D / 2);
+    const long long qi = static_cast<long long>(h0 + g) * D + 2 * j;
+    s_q2[j * G + g] = make_float2(load_as_float(p.q, qi, p.q_dtype), load_as_float(p.q, qi + 1, p.q_dtype));
+  }
+  if (tid < G) {
+    s_m[tid] = -INFINITY;
+    s_l[tid] = 0.0f;
+  }
+  __syncthreads();
+  if constexpr (Ly::U1) {
+    // level-1 table: entry (pair j, angle v, head g)
+    for (int i = tid; i < (D / 2) * 16 * G; i += 128) {
+      const int g = i % G, v = (i / G) % 16, j = i / (16 * G);
+      const float2 qq = s_q2[j * G + g], c = s_cs[0][v];
+      s_u1[i] = fmaf(qq.x, c.x, qq.y * c.y);
+    }
+  }
+
+  if (qjl) {
+    if (p.sq) {
+      pdl_wait();  // S q
+      for (int i = tid; i < G * p.m; i += 128)
+        s_sq[(i / p.m) * 256 + i % p.m] = __ldcg(p.sq + static_cast<long long>(h0 + i / p.m) * p.m + i % p.m);
+    } else {
+      // a warp per row of S, lanes over 4 consecutive dims each, summed by shuffles
+      for (int r = w; r < p.m; r += 4) {
         float a[G];
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          a[g] = 0.0f;
+        for (int g = 0; g < G; ++g) a[g] = 0.0f;
 #pragma unroll
-          for (int c = 0; c < D / 128; ++c) {
-            const float* qq = &s_q[g][c * 128 + 4 * lane];
-            a[g] = fmaf(s4[j][c].x, qq[0], fmaf(s4[j][c].y, qq[1], fmaf(s4[j][c].z, qq[2], fmaf(s4[j][c].w, qq[3], a[g]))));
+        for (int c = 0; c < D / 128; ++c) {
+          const float4 s4 = reinterpret_cast<const float4*>(p.S + static_cast<long long>(r) * D + c * 128)[lane];
+          const int j = c * 64 + 2 * lane;
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float2 q0 = s_q2[j * G + g], q1 = s_q2[(j + 1) * G + g];
+            a[g] = fmaf(s4.x, q0.x, fmaf(s4.y, q0.y, fmaf(s4.z, q1.x, fmaf(s4.w, q1.y, a[g]))));
           }
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
 #pragma unroll
           for (int off = 16; off > 0; off >>= 1) a[g] += __shfl_xor_sync(0xffffffffu, a[g], off);
         }
-        if (lane == 0 && r < p.m)
+        if (lane == 0)
 #pragma unroll
-          for (int g = 0; g < G; ++g) s_sq[g][r] = a[g];
+          for (int g = 0; g < G; ++g) s_sq[g * 256 + r] = a[g];
       }
     }
+    __syncthreads();
+    // table [pos][pattern][g]: sum over the 4 bits of pattern of +-(S q)_(4 pos + b)
+    for (int i = tid; i < (p.m / 4) * 16 * G; i += 128) {
+      const int g = i % G, v = (i / G) % 16, pos = i / (16 * G);
+      float t = 0.0f;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const float x = s_sq[g * 256 + 4 * pos + b];
+        t += ((v >> b) & 1) ? x : -x;
+      }
+      s_qt[i] = t;
+    }
   }
-  __syncthreads();
   const float qjl_c = 1.2533141373155003f / static_cast<float>(p.m > 0 ? p.m : 1);  // sqrt(pi/2)/m
 
-  // this lane's query values and QJL terms
-  float qv[G][DPL][4];
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int c = 0; c < DPL; ++c)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) qv[g][c][e] = s_q[g][c * 128 + 4 * lane + e];
-  const int block = p.block, lpb = block / 4, ll = lane % lpb, kb = lane / lpb;
-  const int nbk = D / block;  // blocks per key
-
-  float m_run[G], l_run[G], o[G][DPL][4];
+  // V-phase thread roles: 8 dimensions (one V word) of every KSUB-th key
+  const int oct = tid % OCT, ksub = tid / OCT;
+  float acc[G][8], bsum[G];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    m_run[g] = -INFINITY;
-    l_run[g] = 0.0f;
+    bsum[g] = 0.0f;
 #pragma unroll
-    for (int c = 0; c < DPL; ++c)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) o[g][c][e] = 0.0f;
+    for (int e = 0; e < 8; ++e) acc[g][e] = 0.0f;
   }
 
-  const int t_begin = split * p.keys_per_split;
-  const int t_end = min(p.N, t_begin + p.keys_per_split);
-  // The split's keys go through shared memory kCKeys at a time: every array
-  // of a chunk (angle nibbles, radii, QJL bits and norms, int4 V and its
-  // scales) is one contiguous range, copied by all threads with asynchronous
-  // 4-byte copies (2-byte loads for the fp16 radii and norms), so a key's
-  // data costs the warps no dependent global round trips.
-  extern __shared__ __align__(16) unsigned char dsm[];
-  constexpr int PKW = D / 8;                    // 32-bit words of angle nibbles per key
-  const int mw = p.m / 32;                      // QJL sign words per key
-  uint32_t* s_pk = reinterpret_cast<uint32_t*>(dsm);                // [kCKeys][PKW]
-  uint32_t* s_sg = s_pk + kCKeys * PKW;                             // [kCKeys][mw <= 8]
-  uint32_t* s_vq = s_sg + kCKeys * 8;                               // [kCKeys][D/8]
-  float* s_vs = reinterpret_cast<float*>(s_vq + kCKeys * (D / 8));  // [kCKeys][D/64]
-  float* s_vb = s_vs + kCKeys * (D / 64);
-  float* s_rad = s_vb + kCKeys * (D / 64);                          // [kCKeys][nbk <= 16]
-  float* s_rn = s_rad + kCKeys * 16;                                // [kCKeys]
-  const bool stage_v = p.attend && !p.vdense;
-  for (int c0 = t_begin; c0 < t_end; c0 += kCKeys) {
-    const int nk = min(kCKeys, t_end - c0);
+  for (int c0 = t_begin; c0 < t_end; c0 += kCChunk) {
+    const int nk = min(kCChunk, t_end - c0);
     const long long row0 = static_cast<long long>(kv) * p.N + c0;
-    __syncthreads();  // the previous chunk is consumed
-    {
-      const uint32_t* src = reinterpret_cast<const uint32_t*>(p.packed) + row0 * PKW;
-      for (int i = tid; i < nk * PKW; i += 128) cp_async4(s_pk + i, src + i);
-    }
-    if (qjl) {
-      const uint32_t* src = p.signs + row0 * mw;
-      for (int i = tid; i < nk * mw; i += 128) cp_async4(s_sg + (i / mw) * 8 + i % mw, src + i);
-    }
-    if (stage_v) {
-      const uint32_t* src = p.vq + row0 * (D / 8);
-      for (int i = tid; i < nk * (D / 8); i += 128) cp_async4(s_vq + i, src + i);
-      if (p.sb_f32) {
-        const float* vs = reinterpret_cast<const float*>(p.vs) + row0 * (D / 64);
-        const float* vb = reinterpret_cast<const float*>(p.vb) + row0 * (D / 64);
-        for (int i = tid; i < nk * (D / 64); i += 128) {
-          cp_async4(s_vs + i, vs + i);
-          cp_async4(s_vb + i, vb + i);
-        }
-      }
-    }
-    cp_async_commit();
-    // the fp16 arrays with plain loads (no 4-byte alignment), converted
-    for (int i = tid; i < nk * nbk; i += 128)
-      s_rad[(i / nbk) * 16 + i % nbk] = __half2float(p.radii[row0 * nbk + i]);
-    if (qjl)
-      for (int i = tid; i < nk; i += 128) s_rn[i] = __half2float(p.rnorm[row0 + i]);
-    if (stage_v && !p.sb_f32) {
-      const __half* vs = reinterpret_cast<const __half*>(p.vs) + row0 * (D / 64);
-      const __half* vb = reinterpret_cast<const __half*>(p.vb) + row0 * (D / 64);
-      for (int i = tid; i < nk * (D / 64); i += 128) {
-        s_vs[i] = __half2float(vs[i]);
-        s_vb[i] = __half2float(vb[i]);
-      }
+    if (c0 != t_begin) {
+      __syncthreads();  // the previous chunk is consumed
+      stage(c0);
     }
     cp_async_wait_all();
     __syncthreads();
 
-    for (int tl = w; tl < nk; tl += 4) {
-      const int t = c0 + tl;
-      const long long row = row0 + tl;
-      const unsigned char* pkb = reinterpret_cast<const unsigned char*>(s_pk + tl * PKW);
-      float part[G];
+    // ---- scores: thread tid scores key c0 + tid for the G heads
+    float s[G];
+    if (tid < nk) {
+      float sc[G];
 #pragma unroll
-      for (int g = 0; g < G; ++g) part[g] = 0.0f;
+      for (int g = 0; g < G; ++g) sc[g] = 0.0f;
 #pragma unroll
-      for (int c = 0; c < DPL; ++c) {
-        const int bi = c * (128 / block) + kb;
-        const unsigned char* pk = pkb + bi * (block / 2);
-        const float4 kv4 = decode4([&](int i) { return packed_idx(pk, i); },
-                                   s_rad[tl * 16 + bi], block, ll, s_cs);
+      for (int bk = 0; bk < NBK; ++bk) {
+        uint32_t pkw[BLOCK / 8];
+        const uint32_t* src = s_pk + tid * Ly::PKS + bk * (BLOCK / 8);
+        if constexpr (BLOCK / 8 >= 4) {
 #pragma unroll
-        for (int g = 0; g < G; ++g)
-          part[g] += qv[g][c][0] * kv4.x + qv[g][c][1] * kv4.y + qv[g][c][2] * kv4.z +
-                     qv[g][c][3] * kv4.w;
+          for (int i = 0; i < BLOCK / 32; ++i) {
+            const uint4 v4 = reinterpret_cast<const uint4*>(src)[i];
+            pkw[4 * i] = v4.x;
+            pkw[4 * i + 1] = v4.y;
+            pkw[4 * i + 2] = v4.z;
+            pkw[4 * i + 3] = v4.w;
+          }
+        } else {
+          const uint2 v2 = *reinterpret_cast<const uint2*>(src);
+          pkw[0] = v2.x;
+          pkw[1] = v2.y;
+        }
+        float u[G];
+        polar_node<BLOCK, LV, 0, G, Ly::U1>(pkw, s_q2 + bk * (BLOCK / 2) * G,
+                                            s_u1 + bk * (BLOCK / 2) * 16 * G, s_cs, u);
+        const float r = s_rad[tid * NBK + bk];
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[g] = fmaf(r, u[g], sc[g]);
       }
       if (qjl) {
-        // lane l owns sign bits [l*m/32, (l+1)*m/32)
-        const int per = p.m / 32;
-        const float rn = s_rn[tl] * qjl_c;
-        for (int i = lane * per; i < (lane + 1) * per; ++i) {
-          const bool bit = (s_sg[tl * 8 + (i >> 5)] >> (i & 31)) & 1u;
+        float qs[G];
 #pragma unroll
-          for (int g = 0; g < G; ++g) part[g] += rn * (bit ? s_sq[g][i] : -s_sq[g][i]);
+        for (int g = 0; g < G; ++g) qs[g] = 0.0f;
+        const uint32_t* sgr = s_sg + tid * Ly::SGS;
+#pragma unroll
+        for (int wd = 0; wd < 8; ++wd) {
+          if (wd < mw) {
+            const uint32_t word = sgr[wd];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const float* tq = s_qt + ((wd * 8 + k) * 16 + ((word >> (4 * k)) & 15u)) * G;
+#pragma unroll
+              for (int g = 0; g < G; ++g) qs[g] += tq[g];
+            }
+          }
         }
+        const float rn = s_rn[tid] * qjl_c;
+#pragma unroll
+        for (int g = 0; g < G; ++g) sc[g] = fmaf(rn, qs[g], sc[g]);
       }
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
+      for (int g = 0; g < G; ++g) s[g] = sc[g] * p.scale;
+      if (!p.attend) {
 #pragma unroll
-        for (int off = 16; off > 0; off >>= 1) part[g] += __shfl_xor_sync(0xffffffffu, part[g], off);
-        part[g] *= p.scale;
+        for (int g = 0; g < G; ++g) p.scores[static_cast<long long>(h0 + g) * p.N + c0 + tid] = s[g];
       }
-      if (!p.attend) {  // scores only
-        if (lane < G) {
-          float v = part[0];
+    } else {
 #pragma unroll
-          for (int g = 1; g < G; ++g) v = (lane == g) ? part[g] : v;
-          p.scores[static_cast<long long>(h0 + lane) * p.N + t] = v;
-        }
-        continue;
-      }
-      // online softmax (natural log) and V accumulation
+      for (int g = 0; g < G; ++g) s[g] = -INFINITY;
+    }
+    if (!p.attend) continue;
+
+    // ---- the chunk's max per head, the running max, the weights and their sum
 #pragma unroll
-      for (int c = 0; c < DPL; ++c) {
-        const int d0 = c * 128 + 4 * lane;
-        float vv[4];
-        if (p.vdense) {
+    for (int g = 0; g < G; ++g) {
+      float mx = s[g];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) vv[e] = load_as_float(p.vdense, row * D + d0 + e, p.vdense_dtype);
-        } else {
-          const uint32_t word = s_vq[tl * (D / 8) + d0 / 8];
-          const int sh = 4 * (d0 % 8);
-          const float sc = s_vs[tl * (D / 64) + d0 / 64];
-          const float bi = s_vb[tl * (D / 64) + d0 / 64];
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      if (lane == 0) s_red[0][w][g] = mx;
+    }
+    __syncthreads();
+    if (tid < G) {
+      const float cm = fmaxf(fmaxf(s_red[0][0][tid], s_red[0][1][tid]), fmaxf(s_red[0][2][tid], s_red[0][3][tid]));
+      const float mo = s_m[tid], mn = fmaxf(mo, cm);
+      s_a[tid] = mo == -INFINITY ? 0.0f : __expf(mo - mn);
+      s_m[tid] = mn;
+    }
+    __syncthreads();
 #pragma unroll
-          for (int e = 0; e < 4; ++e) vv[e] = fmaf(sc, static_cast<float>((word >> (sh + 4 * e)) & 15u), bi);
-        }
+    for (int g = 0; g < G; ++g) {
+      const float pe = s[g] == -INFINITY ? 0.0f : __expf(s[g] - s_m[g]);
+      s_p[tid * G + g] = pe;
+      float sm = pe;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) sm += __shfl_xor_sync(0xffffffffu, sm, off);
+      if (lane == 0) s_red[1][w][g] = sm;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float a = s_a[g];
+      bsum[g] *= a;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[g][e] *= a;
+    }
+    __syncthreads();
+    if (tid < G)
+      s_l[tid] = fmaf(s_l[tid], s_a[tid], (s_red[1][0][tid] + s_red[1][1][tid]) + (s_red[1][2][tid] + s_red[1][3][tid]));
+
+    // ---- softmax . V: this thread's 8 dimensions of keys ksub, ksub + KSUB, ...
+    for (int tk = ksub; tk < nk; tk += Ly::KSUB) {
+      float pw[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) pw[g] = s_p[tk * G + g];
+      if (stage_v) {
+        const uint32_t word = s_vq[tk * Ly::VQW + oct];
+        const float2 sb = s_vsb[tk * Ly::NG + oct / 8];
+        float ps[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
-          if (c == 0) {
-            const float mn = fmaxf(m_run[g], part[g]);
-            const float a = (m_run[g] == -INFINITY) ? 0.0f : __expf(m_run[g] - mn);
-            const float pe = __expf(part[g] - mn);
-            l_run[g] = l_run[g] * a + pe;
-            m_run[g] = mn;
+          ps[g] = pw[g] * sb.x;
+          bsum[g] = fmaf(pw[g], sb.y, bsum[g]);
+        }
 #pragma unroll
-            for (int cc = 0; cc < DPL; ++cc)
+        for (int e = 0; e < 8; ++e) {
+          // the code as an exact fp32: 2^23 + c read from its bits, minus 2^23
+          const float c = __uint_as_float(0x4B000000u | ((word >> (4 * e)) & 15u)) - 8388608.0f;
 #pragma unroll
-              for (int e = 0; e < 4; ++e) o[g][cc][e] *= a;
-            part[g] = pe;  // reuse as this key's weight
-          }
+          for (int g = 0; g < G; ++g) acc[g][e] = fmaf(ps[g], c, acc[g][e]);
+        }
+      } else {
+        const long long vi = (row0 + tk) * D + 8 * oct;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) o[g][c][e] = fmaf(part[g], vv[e], o[g][c][e]);
+        for (int e = 0; e < 8; ++e) {
+          const float v = load_as_float(p.vdense, vi + e, p.vdense_dtype);
+#pragma unroll
+          for (int g = 0; g < G; ++g) acc[g][e] = fmaf(pw[g], v, acc[g][e]);
         }
       }
     }
   }
   if (!p.attend) return;
 
-  // ---- the 4 warps' states combined in shared memory (the chunk buffer is
-  // free now), one partial per CTA to the workspace; the last CTA of the KV
-  // head merges the splits' partials, 16 splits' loads in flight per thread
-  __syncthreads();
-  float* wst = reinterpret_cast<float*>(dsm);  // [4 warps][G][D + 2]
+  // ---- this CTA's partial: the threads' sums over their key subsets, then
+  // (o, m, l) to the workspace; the last CTA of the KV head merges the splits
+  __syncthreads();  // the chunk buffers are free
+  float* s_o = reinterpret_cast<float*>(dsw);  // [KSUB][G][D]
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float* ws_g = wst + (w * G + g) * (D + 2);
+  for (int g = 0; g < G; ++g)
 #pragma unroll
-    for (int c = 0; c < DPL; ++c)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) ws_g[c * 128 + 4 * lane + e] = o[g][c][e];
-    if (lane == 0) {
-      ws_g[D] = m_run[g];
-      ws_g[D + 1] = l_run[g];
-    }
-  }
+    for (int e = 0; e < 8; ++e) s_o[(ksub * G + g) * D + 8 * oct + e] = acc[g][e] + bsum[g];
   __syncthreads();
   float* wsp = p.ws + (static_cast<long long>(kv) * p.splits + split) * G * (D + 2);
   for (int i = tid; i < G * D; i += 128) {
     const int g = i / D, d = i % D;
-    float M = -INFINITY;
+    float o = 0.0f;
 #pragma unroll
-    for (int ww = 0; ww < 4; ++ww) M = fmaxf(M, wst[(ww * G + g) * (D + 2) + D]);
-    float L = 0.0f, acc = 0.0f;
-#pragma unroll
-    for (int ww = 0; ww < 4; ++ww) {
-      const float* st = wst + (ww * G + g) * (D + 2);
-      const float e = st[D] == -INFINITY ? 0.0f : __expf(st[D] - M);
-      L = fmaf(e, st[D + 1], L);
-      if (e != 0.0f) acc = fmaf(e, st[d], acc);
-    }
-    wsp[g * (D + 2) + d] = acc;
+    for (int k = 0; k < Ly::KSUB; ++k) o += s_o[(k * G + g) * D + d];
+    wsp[g * (D + 2) + d] = o;
     if (d == 0) {
-      wsp[g * (D + 2) + D] = M;
-      wsp[g * (D + 2) + D + 1] = L;
+      wsp[g * (D + 2) + D] = s_m[g];
+      wsp[g * (D + 2) + D + 1] = s_l[g];
     }
   }
   __syncthreads();
@@ -597,7 +811,7 @@ __global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p,
   const float* base = p.ws + static_cast<long long>(kv) * S_ * G * (D + 2);
   for (int i = tid; i < G * D; i += 128) {
     const int g = i / D, d = i % D;
-    float M = -INFINITY, L = 0.0f, acc = 0.0f;
+    float M = -INFINITY, L = 0.0f, o = 0.0f;
     for (int s0 = 0; s0 < S_; s0 += 16) {
       float ms[16], ls[16], os[16];
 #pragma unroll
@@ -613,29 +827,40 @@ __global__ void __launch_bounds__(128) compressed_attn_kernel(const CParams p,
       for (int j = 0; j < 16; ++j) mb = fmaxf(mb, ms[j]);
       const float a = M == -INFINITY ? 0.0f : __expf(M - mb);
       L *= a;
-      acc *= a;
+      o *= a;
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         // an empty state (m = -inf) weighs 0; a NaN state makes the head NaN
         const float e = ms[j] == -INFINITY ? 0.0f : __expf(ms[j] - mb);
         L = fmaf(e, ls[j], L);
-        if (e != 0.0f) acc = fmaf(e, os[j], acc);
+        if (e != 0.0f) o = fmaf(e, os[j], o);
       }
       M = mb;
     }
     store_from_float(p.out, static_cast<long long>(h0 + g) * D + d, p.out_dtype,
-                     L == 0.0f ? 0.0f : acc / L);
+                     L == 0.0f ? 0.0f : o / L);
   }
   if (tid == 0) p.counters[kv] = 0u;
 }
 
+template <int D, int G>
+void* pick_cattn_g(int block, size_t* smem) {
+  switch (block) {
+    case 16: *smem = cattn_smem_bytes<D, G, 16>(); return reinterpret_cast<void*>(compressed_attn_kernel<D, G, 16>);
+    case 32: *smem = cattn_smem_bytes<D, G, 32>(); return reinterpret_cast<void*>(compressed_attn_kernel<D, G, 32>);
+    case 64: *smem = cattn_smem_bytes<D, G, 64>(); return reinterpret_cast<void*>(compressed_attn_kernel<D, G, 64>);
+    case 128: *smem = cattn_smem_bytes<D, G, 128>(); return reinterpret_cast<void*>(compressed_attn_kernel<D, G, 128>);
+  }
+  return nullptr;
+}
+
 template <int D>
-void* pick_cattn(int G) {
+void* pick_cattn(int G, int block, size_t* smem) {
   switch (G) {
-    case 1: return reinterpret_cast<void*>(compressed_attn_kernel<D, 1>);
-    case 2: return reinterpret_cast<void*>(compressed_attn_kernel<D, 2>);
-    case 4: return reinterpret_cast<void*>(compressed_attn_kernel<D, 4>);
-    case 8: return reinterpret_cast<void*>(compressed_attn_kernel<D, 8>);
+    case 1: return pick_cattn_g<D, 1>(block, smem);
+    case 2: return pick_cattn_g<D, 2>(block, smem);
+    case 4: return pick_cattn_g<D, 4>(block, smem);
+    case 8: return pick_cattn_g<D, 8>(block, smem);
   }
   return nullptr;
 }
@@ -691,6 +916,10 @@ int csplits(int Hkv, int N) {
   s = s < 1 ? 1 : (s > kCSplitsMax ? kCSplitsMax : s);
   const int per = (N + s - 1) / (s > 0 ? s : 1);
   return per > 0 ? (N + per - 1) / per : 1;
+}
+
+size_t cattn_partials_bytes(int H, int Hkv, int D, int splits) {
+  return static_cast<size_t>(Hkv) * splits * (H / Hkv) * (D + 2) * sizeof(float);
 }
 
 // ---- the reference's packed format for 16-value blocks (lib/turboquant.metal:501-600)
@@ -826,12 +1055,12 @@ TQ_API int tq_qjl_encode(const float* y, const float* y_hat, int64_t rows, int h
 TQ_API size_t tq_compressed_sdpa_workspace_size(int num_heads, int num_kv_heads, int head_dim,
                                                 int n_keys) {
   if (num_kv_heads < 1 || num_heads < num_kv_heads || n_keys < 0) return 0;
-  const int G = num_heads / num_kv_heads;
   const int s = csplits(num_kv_heads, n_keys);
   // merge counters in the counter region every workspace of this library
-  // starts with (so decode and compressed calls can share one workspace)
-  return kCounterRegionBytes +
-         static_cast<size_t>(num_kv_heads) * s * G * (head_dim + 2) * sizeof(float);
+  // starts with (so decode and compressed calls can share one workspace),
+  // the split partials, then S q for every query head (m <= 256)
+  return kCounterRegionBytes + cattn_partials_bytes(num_heads, num_kv_heads, head_dim, s) +
+         static_cast<size_t>(num_heads) * 256 * sizeof(float);
 }
 
 static int compressed_common(const void* q, tq_dtype q_dtype, const uint8_t* packed,
@@ -897,13 +1126,37 @@ static int compressed_common(const void* q, tq_dtype q_dtype, const uint8_t* pac
     if (num_kv_heads * sizeof(unsigned) > kCounterRegionBytes)
       return err(TQ_ERR_UNSUPPORTED, "compressed attention: too many KV heads");
   }
-  void* fn_ptr = head_dim == 128 ? pick_cattn<128>(G) : pick_cattn<256>(G);
-  const size_t dsmem = cattn_smem_bytes(head_dim, G);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (attend && signs && n_keys > 0 && kCattnSqKernel) {
+    // S q once per query head into the workspace (after the split partials)
+    float* sq = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kCounterRegionBytes +
+                                         cattn_partials_bytes(num_heads, num_kv_heads, head_dim,
+                                                              p.splits));
+    const dim3 sgrid((m + kSqRows - 1) / kSqRows, (num_heads + kSqHeads - 1) / kSqHeads);
+    const cudaError_t e =
+        head_dim == 128
+            ? launch_pdl(cattn_sq_kernel<128>, sgrid, dim3(256), 0, st, q, static_cast<int>(q_dtype), S, m,
+                         num_heads, sq)
+            : launch_pdl(cattn_sq_kernel<256>, sgrid, dim3(256), 0, st, q, static_cast<int>(q_dtype), S, m,
+                         num_heads, sq);
+    if (e != cudaSuccess) return cuda_err(e, fn);
+    p.sq = sq;
+  }
+  size_t dsmem = 0;
+  void* fn_ptr = head_dim == 128 ? pick_cattn<128>(G, block, &dsmem) : pick_cattn<256>(G, block, &dsmem);
   cudaFuncSetAttribute(fn_ptr, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dsmem));
   void* args[] = {&p, &T};
-  const cudaError_t e = cudaLaunchKernel(fn_ptr, dim3(p.splits, num_kv_heads), dim3(128), args,
-                                         dsmem,
-                                         static_cast<cudaStream_t>(stream));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits, num_kv_heads);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = dsmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_launches() ? 1 : 0;
+  const cudaError_t e = cudaLaunchKernelExC(&cfg, fn_ptr, args);
   return e == cudaSuccess ? TQ_OK : cuda_err(e, fn);
 }
 

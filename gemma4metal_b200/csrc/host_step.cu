@@ -6,8 +6,9 @@
 // kernel). Here the step is a CUDA graph of two kernels captured once per
 // decode plan:
 //
-//   gather: one CTA reads [queries | k_new | v_new | seq_lens | slots] from
-//           mapped pinned host memory into a device buffer
+//   gather: one thread per 16 bytes reads [queries | k_new | v_new |
+//           seq_lens | slots] from mapped pinned host memory into a device
+//           buffer
 //   -> tq_sdpa_int4_append (quantize-on-append fused into the decode kernel),
 //      a programmatic dependent launch: its prologue (barrier init, L2
 //      prefetch of its first tiles) overlaps the gather; it writes the output
@@ -64,14 +65,17 @@ namespace {
 constexpr int kGatherThreads = 256;
 
 // Copy n16 16-byte words of the step's inputs from mapped host memory into
-// device memory. The dependent decode kernel may start at once: it reads the
-// copy only after its griddepcontrol.wait, which returns once this grid has
-// completed and its writes are visible. Loads bypass the caches (.cv): the
-// host rewrites the staging buffer between steps.
-__global__ void __launch_bounds__(kGatherThreads) step_gather_kernel(const uint4* src, uint4* dst,
-                                                                     int n16) {
+// device memory, one word per thread over as many CTAs as that takes, so all
+// the reads cross PCIe at once (one round trip). The dependent decode kernel
+// may start at once: it reads the copy only after its griddepcontrol.wait,
+// which returns once this grid has completed and its writes are visible.
+// Loads bypass the caches (.cv): the host rewrites the staging buffer between
+// steps.
+__global__ void __launch_bounds__(kGatherThreads) step_gather_kernel(const uint4* __restrict__ src,
+                                                                     uint4* __restrict__ dst, int n16) {
   tq::pdl_trigger();
-  for (int i = threadIdx.x; i < n16; i += kGatherThreads) dst[i] = __ldcv(src + i);
+  const int i = blockIdx.x * kGatherThreads + threadIdx.x;
+  if (i < n16) dst[i] = __ldcv(src + i);
 }
 
 size_t dtype_bytes(tq_dtype d) { return d == TQ_F32 ? 4 : 2; }
@@ -117,8 +121,9 @@ int capture(tq_decode_step* s, int n, const tq::DecodePlan& pl) {
   const int32_t* seq = reinterpret_cast<const int32_t*>(s->d_in + s->q_bytes + 2 * s->kv_bytes);
   const int32_t* slots = reinterpret_cast<const int32_t*>(s->d_in + s->q_bytes + 2 * s->kv_bytes +
                                                           s->len_bytes);
-  step_gather_kernel<<<1, kGatherThreads, 0, s->stream>>>(
-      s->h_in_dev, reinterpret_cast<uint4*>(s->d_in), static_cast<int>(s->in_bytes / 16));
+  const int n16 = static_cast<int>(s->in_bytes / 16);
+  step_gather_kernel<<<(n16 + kGatherThreads - 1) / kGatherThreads, kGatherThreads, 0, s->stream>>>(
+      s->h_in_dev, reinterpret_cast<uint4*>(s->d_in), n16);
   e = cudaGetLastError();
   int rc = TQ_OK;
   if (e == cudaSuccess)

@@ -280,6 +280,35 @@ __device__ __forceinline__ void store8(void* p, long long i, int dtype, bool vec
   }
 }
 
+// Paired fp32 arithmetic (fma/mul/add .rn.f32x2: two IEEE fp32 operations per
+// instruction, each rounded exactly as the scalar one): the softmax works on
+// two tokens at a time.
+__device__ __forceinline__ unsigned long long pk2(float2 v) {
+  unsigned long long r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(v.x), "f"(v.y));
+  return r;
+}
+__device__ __forceinline__ float2 upk2(unsigned long long r) {
+  float2 v;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(v.x), "=f"(v.y) : "l"(r));
+  return v;
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)), "l"(pk2(c)));
+  return upk2(d);
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)));
+  return upk2(d);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(pk2(a)), "l"(pk2(b)));
+  return upk2(d);
+}
+
 // shared-memory float4 load kept in program order with the tcgen05 loads (a
 // plain load may be hoisted above them, which costs registers)
 __device__ __forceinline__ float4 lds4(const float4* p) {
@@ -288,6 +317,19 @@ __device__ __forceinline__ float4 lds4(const float4* p) {
                : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
                : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
   return v;
+}
+
+// Per-token terms {x, y, z, w} of a tile stored pair-interleaved: tokens 2u
+// and 2u + 1 share 8 floats {x_2u, x_2u+1, y_2u, y_2u+1, z.., z.., w.., w..},
+// so one 16-byte load gives two tokens' (x, y) or (z, w) as register pairs.
+// Lanes 2u and 2u + 1 (tokens t, t ^ 1 of one warp) swap halves by shuffles
+// and each writes one float4.
+__device__ __forceinline__ void store_term_pair(unsigned char* base, int tok, int lane, float4 v) {
+  const bool odd = (lane & 1) != 0;
+  const float r0 = __shfl_xor_sync(0xffffffffu, odd ? v.x : v.z, 1);
+  const float r1 = __shfl_xor_sync(0xffffffffu, odd ? v.y : v.w, 1);
+  float4* dst = reinterpret_cast<float4*>(base) + 2 * (tok >> 1) + (odd ? 1 : 0);
+  *dst = odd ? make_float4(r0, v.z, r1, v.w) : make_float4(v.x, r0, v.y, r1);
 }
 
 template <bool kQLo>
@@ -538,10 +580,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
         unpack_codes(c0, c1, stage + TLayout::K, false);
         unpack_codes(c2, c3, stage + TLayout::K + kTok * 128, false);
         const float qs = p.qscale;
-        float4* ts = reinterpret_cast<float4*>(smem + TLayout::TS + b * kTok * 16);
-        ts[ptok] = tv ? make_float4(64.0f * sc2.x * qs, 64.0f * sc2.y * qs, (bc2.x - 64.0f * sc2.x) * qs,
-                                    (bc2.y - 64.0f * sc2.y) * qs)
-                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const float4 t4 = tv ? make_float4(64.0f * sc2.x * qs, 64.0f * sc2.y * qs,
+                                           (bc2.x - 64.0f * sc2.x) * qs, (bc2.y - 64.0f * sc2.y) * qs)
+                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        store_term_pair(smem + TLayout::TS + b * kTok * 16, ptok, lane, t4);
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&k_full[b]);
@@ -551,9 +593,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
         if (i + 1 < n_tiles) prefetch(t0 + kTok);
         unpack_codes(c0, c1, stage + TLayout::V, true);
         unpack_codes(c2, c3, stage + TLayout::V + kTok * 128, true);
-        float4* tvv = reinterpret_cast<float4*>(smem + TLayout::TV + b * kTok * 16);
-        tvv[ptok] = tv ? make_float4(sc2.x, sc2.y, fmaf(8.0f, sc2.x, bc2.x), fmaf(8.0f, sc2.y, bc2.y))
-                       : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const float4 t4 = tv ? make_float4(sc2.x, sc2.y, fmaf(8.0f, sc2.x, bc2.x), fmaf(8.0f, sc2.y, bc2.y))
+                             : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        store_term_pair(smem + TLayout::TV + b * kTok * 16, ptok, lane, t4);
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&v_full[b]);
@@ -564,10 +606,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
   // ======================= softmax warps ========================================
   if (is_softmax) {
     const float qsum0 = s_mx[rl], qsum1 = s_mx[rl + kRows];
+    const float2 qs0p = make_float2(qsum0, qsum0), qs1p = make_float2(qsum1, qsum1);
     const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
     // the two threads of a row meet on named barrier 1 + warp % 4 (64 threads)
     auto pair_sync = [&]() { asm volatile("bar.sync %0, 64;" ::"r"(1 + (warp & 3)) : "memory"); };
-    float m_run = -INFINITY, l_run = 0.0f, corr0 = 0.0f, corr1 = 0.0f;
+    float m_run = -INFINITY, l_run = 0.0f;
+    // bias-term sums per scale group, as (even tokens, odd tokens) pairs
+    float2 corr0 = make_float2(0.0f, 0.0f), corr1 = make_float2(0.0f, 0.0f);
     pair_sync();  // both halves have read the q sums before s_mx is reused
     for (int i = 0; i < n_tiles; ++i) {
       const int b = i & 1;
@@ -593,11 +638,19 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&s_free[b]);  // S[b] may take tile i + 2
+        const float2 nm = make_float2(-mref, -mref);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float4 a = lds4(&s_ts[32 * hf + j]);
-          sc[j] = fmaf(a.x, __uint_as_float(r0[j]),
-                       fmaf(a.y, __uint_as_float(r1[j]), fmaf(a.z, qsum0, fmaf(a.w, qsum1, -mref))));
+        for (int j = 0; j < 32; j += 2) {
+          const float4 a = lds4(&s_ts[2 * (16 * hf + j / 2)]);      // (A0, A0', A1, A1')
+          const float4 bz = lds4(&s_ts[2 * (16 * hf + j / 2) + 1]); // (B0, B0', B1, B1')
+          const float2 s2 = fma2(make_float2(a.x, a.y),
+                                 make_float2(__uint_as_float(r0[j]), __uint_as_float(r0[j + 1])),
+                                 fma2(make_float2(a.z, a.w),
+                                      make_float2(__uint_as_float(r1[j]), __uint_as_float(r1[j + 1])),
+                                      fma2(make_float2(bz.x, bz.y), qs0p,
+                                           fma2(make_float2(bz.z, bz.w), qs1p, nm))));
+          sc[j] = s2.x;
+          sc[j + 1] = s2.y;
         }
       }
       const bool full = t0 + kTok <= t_end && (!p.causal || t0 + kTok - 1 <= qpos_lo) &&
@@ -631,8 +684,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
         for (int j = 0; j < 32; ++j) sc[j] -= delta;
         m_run = m_new;
         l_run *= alpha;
-        corr0 *= alpha;
-        corr1 *= alpha;
+        corr0 = mul2(corr0, make_float2(alpha, alpha));
+        corr1 = mul2(corr1, make_float2(alpha, alpha));
       }
       // O_hf *= alpha once PV(i-1) is done; tcgen05.ld/st are warp-wide, so the
       // whole warp takes the branch with alpha = 1 on the other rows
@@ -654,7 +707,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
       // P[b] is free once PV(i-2) is done; the value terms of tile i are in
       if (i >= 2) mbar_wait_bounded(&pv_done[b], (use - 1) & 1u, p.err, kWaitBudget);
       mbar_wait_bounded(&v_full[b], use & 1u, p.err, kWaitBudget);
-      float lsum = 0.0f;  // masked scores give exp2(-inf) = 0
+      float2 lsum = make_float2(0.0f, 0.0f);  // masked scores give exp2(-inf) = 0
       unsigned char* prow = smem + TLayout::P + b * TLayout::PB;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
@@ -663,13 +716,16 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int j = 8 * cc + 2 * e;
-          const float pa = fast_exp2(sc[j]), pb2 = fast_exp2(sc[j + 1]);
-          lsum += pa + pb2;
-          const float4 va = lds4(&s_tv[32 * hf + j]), vb = lds4(&s_tv[32 * hf + j + 1]);
-          const __half2 h0 = __floats2half2_rn(pa * va.x, pb2 * vb.x);
-          const __half2 h1 = __floats2half2_rn(pa * va.y, pb2 * vb.y);
-          corr0 = fmaf(pa, va.z, fmaf(pb2, vb.z, corr0));
-          corr1 = fmaf(pa, va.w, fmaf(pb2, vb.w, corr1));
+          const float2 pp = make_float2(fast_exp2(sc[j]), fast_exp2(sc[j + 1]));
+          lsum = add2(lsum, pp);
+          const float4 vs = lds4(&s_tv[2 * (16 * hf + j / 2)]);      // (vs0, vs0', vs1, vs1')
+          const float4 vc = lds4(&s_tv[2 * (16 * hf + j / 2) + 1]);  // (c0, c0', c1, c1')
+          const float2 p0 = mul2(pp, make_float2(vs.x, vs.y));
+          const float2 p1 = mul2(pp, make_float2(vs.z, vs.w));
+          const __half2 h0 = __floats2half2_rn(p0.x, p0.y);
+          const __half2 h1 = __floats2half2_rn(p1.x, p1.y);
+          corr0 = fma2(pp, make_float2(vc.x, vc.y), corr0);
+          corr1 = fma2(pp, make_float2(vc.z, vc.w), corr1);
           w0[e] = *reinterpret_cast<const uint32_t*>(&h0);
           w1[e] = *reinterpret_cast<const uint32_t*>(&h1);
         }
@@ -677,7 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
         *reinterpret_cast<uint4*>(prow + kRows * 128 + sw128(rl, ch)) =
             make_uint4(w1[0], w1[1], w1[2], w1[3]);
       }
-      l_run += lsum;
+      l_run += lsum.x + lsum.y;
       fence_async_smem();
       tc_fence_before();
       __syncwarp();
@@ -695,12 +751,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const TCParams p) 
     }
     float* s_red = reinterpret_cast<float*>(smem + TLayout::RED);  // [3][256]
     s_red[xs] = l_run;
-    s_red[kSoftmaxThreads + xs] = corr0;
-    s_red[2 * kSoftmaxThreads + xs] = corr1;
+    const float corr0s = corr0.x + corr0.y, corr1s = corr1.x + corr1.y;
+    s_red[kSoftmaxThreads + xs] = corr0s;
+    s_red[2 * kSoftmaxThreads + xs] = corr1s;
     pair_sync();
     const int pt = xs ^ kRows;  // partner's slot
     const float l_tot = l_run + s_red[pt];
-    const float corr = (hf ? corr1 : corr0) + s_red[(hf ? 2 : 1) * kSoftmaxThreads + pt];
+    const float corr = (hf ? corr1s : corr0s) + s_red[(hf ? 2 : 1) * kSoftmaxThreads + pt];
     const bool direct = p.splits == 1;
     const long long unit = static_cast<long long>(kv) * gridDim.y + mt;
     // split partials, column-major so a warp's 32 rows are one 128 B store:

@@ -606,7 +606,8 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
                     ("decode kernel stores its states into the peers' buffers + merge-only "
                      "kernel" if published else
                      "peer-memory exchange + merge (one kernel)" if peer is not None else
-                     "NCCL all-gather + LSE merge"),
+                     "NCCL all-gather + LSE merge" if world > 1 else
+                     "LSE normalisation of the one state (no exchange on one GPU)"),
         "metric": "int4-KV decode-attention tokens/s", "unit": "tokens/s", "scaling": "strong",
         "n_gpus": world, "steps": n_timed,
         "value": n_timed / (t_step / 1000.0), "ms_per_step": t_step / n_timed,

@@ -60,8 +60,12 @@ struct PeerParams {
   uint32_t* err;
 };
 
-// Reads this rank's step counter and failed word; returns the step.
+// Reads this rank's step counter and failed word; returns the step. Lets the
+// next kernel of the stream launch now (its griddepcontrol.wait still waits
+// for this grid to complete): a decode kernel after the merge runs its
+// prologue while the merge waits for the other ranks.
 __device__ __forceinline__ uint32_t begin_step(uint32_t* own, uint32_t* s_step, int* s_failed) {
+  pdl_trigger();
   if (threadIdx.x == 0) {
     *s_step = *reinterpret_cast<volatile uint32_t*>(own) + 1u;
     *s_failed = *reinterpret_cast<volatile uint32_t*>(own + kFailedWord) != 0u;

@@ -23,7 +23,8 @@ the 512-query prefill chunk), config 3 (PolarQuant + QJL compressed keys) and
 a read-only HBM probe on one GPU; config 4 (one 262144-token sequence split
 over all N GPUs, the decode kernel storing its partial state into every
 rank's exchange buffer over NVLink + a merge-only kernel, strong scaling) at
-every N,
+every N, and at N > 1 the same layer split by KV heads (append + decode of a
+rank's heads, NCCL all-gather of the outputs),
 with its time split and its merged output checked against the C oracle.
 
 `--impl reference` times the reference's algorithm on the host CPU instead
@@ -71,11 +72,12 @@ def parse():
                     help="cfg1: run the step as two launches (quantize_append, then sdpa_int4) "
                          "instead of the fused sdpa_int4_append")
     ap.add_argument("--workload", default="all",
-                    choices=["all", "cfg0", "cfg1", "cfg2", "cfg3", "cfg4", "probe"],
+                    choices=["all", "cfg0", "cfg1", "cfg2", "cfg3", "cfg4", "cfg4_heads", "probe"],
                     help="all (default): the config-1 headline line with the other configs "
                          "nested (configs 0, 2, 3 and the HBM probe on one GPU; config 4's "
-                         "sequence split at every GPU count); cfg1: the headline alone; "
-                         "cfg0/cfg2/cfg3/cfg4/probe: that config's line alone")
+                         "sequence split at every GPU count, and its KV-head split at N > 1); "
+                         "cfg1: the headline alone; cfg0/cfg2/cfg3/cfg4/cfg4_heads/probe: that "
+                         "config's line alone")
     ap.add_argument("--no-check", action="store_true",
                     help="skip config 4's check of the merged output against the C oracle")
     return ap.parse_args()
@@ -639,6 +641,163 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
                                    "peer_merge_kernel" if peer is not None else
                                    "lse_merge_kernel" + (" + NCCL all-gather" if world > 1 else ""))),
         "clocks": clk,
+    }
+
+
+def run_cfg4_heads(args, rank: int, world: int, local_rank: int, steps: int = 256,
+                   check: bool = True):
+    """Config 4 split by KV heads (N > 1, Hkv % N == 0): rank r holds the
+    whole 262144-token int4 cache of KV heads seqsplit.head_bounds(8, N, r)
+    and their query heads; one step = quantize-on-append of the new token +
+    decode of those heads in one launch (tq_sdpa_int4_append), then an NCCL
+    all-gather of the (H/N, D) outputs so every rank holds the full (H, D)
+    output -- the exchange of the head-parallel form. Captured in CUDA graphs
+    over rotating layers (inputs larger than L2); max over ranks. `check`:
+    rank 0 compares its heads' output with the C oracle's dequantize + fp64
+    SDPA over all tokens (the oracle quantizes the same values itself)."""
+    import math
+
+    import torch
+    import torch.distributed as dist
+
+    import gemma4metal_b200.turboquant as tq
+    from gemma4metal_b200 import seqsplit
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    h0, h1 = seqsplit.head_bounds(C4_HKV, world, rank)
+    hk = h1 - h0
+    G = C4_H // C4_HKV
+    hq = hk * G
+    n_ctx = C4_N  # the new token is the last of the 262144
+    per_tok = hk * 2 * (C4_D // 2 + 4 * (C4_D // 64))
+    shard_bytes = (n_ctx - 1) * per_tok
+    layers_n = max(2, math.ceil(400e6 / max(shard_bytes, 1)))
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(13)
+    host = None
+    if check and rank == 0:
+        from oracle import oracle as O
+        O.set_num_threads(os.cpu_count() or 1)
+        host = {"k": [], "v": []}
+
+    def rms_norm(x, w):
+        return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True)) * w
+
+    wq = 1 + 0.1 * torch.randn(C4_D, device=dev, generator=gen)
+    wk = 1 + 0.1 * torch.randn(C4_D, device=dev, generator=gen)
+    cap = (n_ctx + 3) // 4 * 4
+    layers = []
+    for li in range(layers_n):
+        cache = tq.KVCache(1, hk, C4_D, cap, device=dev)
+        step_tok = 16384
+        for c0 in range(0, n_ctx - 1, step_tok):
+            c1 = min(n_ctx - 1, c0 + step_tok)
+            # every rank draws the same full chunk and keeps its heads
+            k = rms_norm(torch.randn(1, C4_HKV, c1 - c0, C4_D, device=dev, generator=gen), wk).half()
+            v = torch.randn(1, C4_HKV, c1 - c0, C4_D, device=dev, generator=gen).half()
+            cache.append(k[:, h0:h1].contiguous(), v[:, h0:h1].contiguous(), pos=c0)
+            if host is not None and li == 0:
+                host["k"].append(O.quantize(k[:, h0:h1].float().cpu().numpy()))
+                host["v"].append(O.quantize(v[:, h0:h1].float().cpu().numpy()))
+            del k, v
+        q = rms_norm(torch.randn(1, C4_H, C4_D, device=dev, generator=gen), wq).half()
+        kn = rms_norm(torch.randn(1, C4_HKV, 1, C4_D, device=dev, generator=gen), wk).half()
+        vn = torch.randn(1, C4_HKV, 1, C4_D, device=dev, generator=gen).half()
+        layers.append(dict(cache=cache, q=q[:, h0 * G:h1 * G].contiguous(),
+                           kn=kn[:, h0:h1, 0].contiguous(), vn=vn[:, h0:h1, 0].contiguous(),
+                           kn_full=kn, vn_full=vn,
+                           out=torch.empty(1, hq, C4_D, dtype=torch.float16, device=dev),
+                           full=torch.empty(world, 1, hq, C4_D, dtype=torch.float16, device=dev)))
+    ws = tq.workspace(dev, tq.sdpa_int4_workspace_size(1, hq, hk, C4_D, n_ctx, 0))
+    stream = torch.cuda.Stream(device=dev)
+
+    def decode(Lr):
+        tq.sdpa_int4_append(Lr["q"], Lr["kn"], Lr["vn"], *Lr["cache"].tensors(), G, 1.0, 0, stream,
+                            n_tokens=n_ctx, out=Lr["out"], ws=ws)
+
+    def step(Lr):
+        decode(Lr)
+        dist.all_gather_into_tensor(Lr["full"], Lr["out"])
+
+    with torch.cuda.stream(stream):
+        for Lr in layers:
+            step(Lr)
+    torch.cuda.synchronize()
+    CH = 4 * layers_n
+
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(CH):
+                    fn(layers[i % layers_n])
+        return g
+
+    graphs = {"step": capture(step), "decode": capture(decode)}
+    torch.cuda.synchronize()
+    dist.barrier()
+    reps = max(1, steps // CH)
+    times = {}
+    for name, g in graphs.items():
+        with torch.cuda.stream(stream):
+            g.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        times[name] = _graph_time(stream, g, reps)
+        dist.barrier()
+    n_timed = reps * CH
+    tt = torch.tensor([times["step"], times["decode"]], device=dev, dtype=torch.float64)
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    t_step, t_dec = (float(x) for x in tt)
+    assert tq.device_error() == 0, "a kernel reported a device error"
+
+    acc = None
+    if host is not None:
+        L0 = layers[0]
+        O.set_num_threads(os.cpu_count() or 1)
+        host["k"].append(O.quantize(L0["kn"][:, :, None].float().cpu().numpy()))
+        host["v"].append(O.quantize(L0["vn"][:, :, None].float().cpu().numpy()))
+        full = [np.concatenate([c[f] for c in host[kv]], axis=2) for kv in ("k", "v") for f in range(3)]
+        qh = L0["q"].float().cpu().numpy()
+        refs = []
+        for g0 in range(0, hk, 2):
+            sl = slice(g0, min(hk, g0 + 2))
+            refs.append(O.sdpa_int4(qh[:, g0 * G:min(hk, g0 + 2) * G], *(a[:, sl] for a in full), f64=True))
+        ref = np.concatenate(refs, axis=1).astype(np.float64)
+        # the gathered output: rank 0's block holds its heads
+        got = L0["full"][0].float().cpu().numpy().astype(np.float64)
+        acc = {"max_abs": float(np.max(np.abs(got - ref))),
+               "cosine": float(got.ravel() @ ref.ravel() / (np.linalg.norm(got) * np.linalg.norm(ref))),
+               "oracle": f"C oracle: quantize of the same values, dequantize + fp64 SDPA over all "
+                         f"{n_ctx} tokens of rank 0's {hk} KV heads (layer 0, after the timed steps)"}
+        del full, host
+    dist.barrier()
+    del graphs
+    torch.cuda.synchronize()
+    us_step = t_step * 1000.0 / n_timed
+    us_dec = t_dec * 1000.0 / n_timed
+    dec_bytes = n_ctx * per_tok + hq * C4_D * 4
+    peaks = measured_peaks()
+    ach = dec_bytes / (us_dec * 1e-6) / 1e9
+    return {
+        "workload": f"cfg4 decode step: 262144-token global layer (H=32, Hkv=8, D=256) split by KV "
+                    f"heads ({hk} per GPU): append + decode of the rank's heads in one launch, "
+                    f"NCCL all-gather of the outputs",
+        "metric": "int4-KV decode-attention tokens/s", "unit": "tokens/s", "scaling": "strong",
+        "n_gpus": world, "steps": n_timed,
+        "value": n_timed / (t_step / 1000.0), "ms_per_step": t_step / n_timed,
+        "time_split_us": {"step": us_step, "append_plus_decode": us_dec,
+                          "all_gather": us_step - us_dec},
+        "roofline": {"bound": "hbm", "kernel": f"tq::decode_mma_kernel<256,4,__half> ({hk} KV heads)",
+                     "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": ach / peaks["hbm_gbs"], "kernel_us": us_dec,
+                     "algorithmic_bytes_per_launch": dec_bytes, "traffic": None,
+                     "peak_source": peaks["source"]},
+        "accuracy_vs_oracle": acc,
+        "layers_rotated": layers_n,
+        "l2": f"inputs larger than L2: {layers_n} rotating caches of {shard_bytes / 1e6:.0f} MB",
+        "gpu_launches_per_step": "decode_mma_kernel (append fused) + NCCL all-gather",
     }
 
 
@@ -1380,9 +1539,11 @@ def main():
             dist.barrier()
             dist.destroy_process_group()
 
-    if args.workload == "cfg4":
-        line = run_cfg4(args, rank, world, local_rank, steps=max(64, args.steps),
-                        check=not args.no_check)
+    if args.workload in ("cfg4", "cfg4_heads"):
+        if args.workload == "cfg4_heads" and (world < 2 or C4_HKV % world):
+            raise SystemExit("cfg4_heads needs 2, 4 or 8 GPUs (8 KV heads split evenly)")
+        fn = run_cfg4 if args.workload == "cfg4" else run_cfg4_heads
+        line = fn(args, rank, world, local_rank, steps=max(64, args.steps), check=not args.no_check)
         line.update({"n_gpus": world, "warmup": args.warmup, "higher_is_better": True,
                      "vs_baseline": None, "dtype": "f32",
                      "data": "synthetic (seeded torch.randn, RMS-normalised Q/K as task configs[0])"})
@@ -1467,6 +1628,11 @@ def main():
                 line["roofline"]["read_probe_gbs"] = best
         nested["cfg4"] = run_cfg4(args, rank, world, local_rank, steps=256, check=not args.no_check)
         torch.cuda.empty_cache()
+        if world > 1 and C4_HKV % world == 0:
+            # the same layer split by KV heads instead of by sequence
+            nested["cfg4_heads"] = run_cfg4_heads(args, rank, world, local_rank, steps=256,
+                                                  check=not args.no_check)
+            torch.cuda.empty_cache()
         line["configs"] = nested
     finish(line)
 

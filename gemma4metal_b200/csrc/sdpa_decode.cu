@@ -668,7 +668,11 @@ DecodePlan plan_decode(int device, int B, int H, int Hkv, int D, int n_visible_m
     pl.ws_o_off = kCounterRegionBytes;
     pl.ws_ml_off = pl.ws_o_off + align256(n_part * D * sizeof(float));
     pl.ws_bytes = pl.ws_ml_off + align256(n_part * 2 * sizeof(float));
-    if (units * sizeof(unsigned) > kCounterRegionBytes) pl.ws_bytes = 0, pl.splits = -1;
+    // the tensor-core kernel merges more than 64 splits in two levels, with
+    // one more counter per group of 32 splits of a unit
+    const long long groups = pl.splits > 64 ? (pl.splits + 31) / 32 : 0;
+    if (static_cast<size_t>(units * (1 + groups)) * sizeof(unsigned) > kCounterRegionBytes)
+      pl.ws_bytes = 0, pl.splits = -1;
   }
   return pl;
 }

@@ -62,6 +62,7 @@ namespace tq {
 namespace {
 
 constexpr int kChunk = 64;  // tokens per TMA box; splits are whole chunks
+constexpr int kMergeGroup = 32;  // splits per first-level group of a two-level merge
 #ifndef TQ_DECODE_MINB_128
 #define TQ_DECODE_MINB_128 3
 #endif
@@ -994,104 +995,141 @@ __global__ void __launch_bounds__(MCfg<D>::THREADS, QSPLIT ? 1 : MCfg<D>::MINB)
   // Release: the CTA barrier orders every thread's partial stores before
   // thread 0's acquire-release ticket; the CTA that draws the last ticket has
   // acquired every other CTA's partials, and its barrier passes that on.
-  consumers_sync<W>();
-  if (tid == 0) {
-    const unsigned prev = atomic_add_acq_rel(&p.counters[unit], 1u);
-    s_flag[0] = (prev == static_cast<unsigned>(p.splits - 1)) ? 1 : 0;
-  }
-  consumers_sync<W>();
-  if (s_flag[0] == 0) return;
-
-  // float4 items (head, 4 dims); the splits of an item are spread over R
-  // thread subsets, each running an online log-sum-exp merge with kML splits'
-  // (m, l, o) loads in flight per step (16 at G <= 2: one round of L2 loads
-  // for up to 32 splits; 8 above, where 16 would spill), then the R states
-  // are combined.
+  // Up to 2 * kMergeGroup splits one CTA merges them all. Beyond that (few
+  // (sequence, KV head) units over a long context, so one wave holds
+  // hundreds of splits per unit) the merge has two levels: the last CTA of
+  // each group of kMergeGroup consecutive splits merges its group into the
+  // group's first slot, then the last of those merges the groups -- a
+  // single CTA streaming hundreds of partials from L2 took longer than the
+  // attention itself.
   const int S_ = p.splits;
   const long long base = unit * S_ * G;
+  auto ticket = [&](unsigned* counter, int expected) {
+    consumers_sync<W>();
+    if (tid == 0) {
+      const unsigned prev = atomic_add_acq_rel(counter, 1u);
+      s_flag[0] = (prev == static_cast<unsigned>(expected - 1)) ? 1 : 0;
+    }
+    consumers_sync<W>();
+    return s_flag[0] != 0;
+  };
+
+  // float4 items (head, 4 dims); the slots first, first + stride, ... (count
+  // of them) of an item are spread over R thread subsets, each running an
+  // online log-sum-exp merge with kML slots' (m, l, o) loads in flight per
+  // step (16 at G <= 2: one round of L2 loads for up to 32 slots; 8 above,
+  // where 16 would spill), then the R states are combined: into the outputs
+  // (to_out) or, as a partial state, into slot `first`.
   constexpr int NI = G * D / 4;
   constexpr int R = NI >= NTH ? 1 : NTH / NI;
   constexpr int kML = G <= 2 ? 16 : 8;
   float2* mst = reinterpret_cast<float2*>(smem);           // [R][NI] (M, L)
   float4* ost = reinterpret_cast<float4*>(smem + R * NI * 8);  // [R][NI] o
-  for (int it = tid; it < NI * R; it += NTH) {
-    const int item = it % NI, sub = it / NI;
-    const int g = item / (D / 4);
-    const float* ow = p.ws_o + (base + g) * D + 4 * (item % (D / 4));
-    const float* mw = p.ws_ml + (base + g) * 2;
-    float M = -INFINITY, L = 0.0f;
-    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    for (int s0 = sub; s0 < S_; s0 += kML * R) {
-      float2 ml[kML];
-      float4 v[kML];
+  auto merge = [&](int first, int count, int stride, bool to_out) {
+    for (int it = tid; it < NI * R; it += NTH) {
+      const int item = it % NI, sub = it / NI;
+      const int g = item / (D / 4);
+      const float* ow = p.ws_o + (base + g) * D + 4 * (item % (D / 4));
+      const float* mw = p.ws_ml + (base + g) * 2;
+      float M = -INFINITY, L = 0.0f;
+      float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      for (int j0 = sub; j0 < count; j0 += kML * R) {
+        float2 ml[kML];
+        float4 v[kML];
 #pragma unroll
-      for (int j = 0; j < kML; ++j) {
-        const int s = s0 + j * R;
-        if (s < S_) {
-          ml[j] = __ldcg(reinterpret_cast<const float2*>(mw + static_cast<long long>(s) * G * 2));
-          v[j] = __ldcg(reinterpret_cast<const float4*>(ow + static_cast<long long>(s) * G * D));
-        } else {
-          ml[j] = make_float2(-INFINITY, 0.0f);
-          v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int j = 0; j < kML; ++j) {
+          const int jj = j0 + j * R;
+          const long long sl = first + static_cast<long long>(jj) * stride;
+          if (jj < count) {
+            ml[j] = __ldcg(reinterpret_cast<const float2*>(mw + sl * G * 2));
+            v[j] = __ldcg(reinterpret_cast<const float4*>(ow + sl * G * D));
+          } else {
+            ml[j] = make_float2(-INFINITY, 0.0f);
+            v[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          }
         }
+        float mb = M;
+#pragma unroll
+        for (int j = 0; j < kML; ++j) mb = fmaxf(mb, ml[j].x);
+        const float sc = M == -INFINITY ? 0.0f : fast_exp2(M - mb);
+        L *= sc;
+        a.x *= sc;
+        a.y *= sc;
+        a.z *= sc;
+        a.w *= sc;
+#pragma unroll
+        for (int j = 0; j < kML; ++j) {
+          const float e = ml[j].x == -INFINITY ? 0.0f : fast_exp2(ml[j].x - mb);
+          L = fmaf(e, ml[j].y, L);
+          a.x = fmaf(e, v[j].x, a.x);
+          a.y = fmaf(e, v[j].y, a.y);
+          a.z = fmaf(e, v[j].z, a.z);
+          a.w = fmaf(e, v[j].w, a.w);
+        }
+        M = mb;
       }
-      float mb = M;
+      mst[sub * NI + item] = make_float2(M, L);
+      ost[sub * NI + item] = a;
+    }
+    consumers_sync<W>();  // (every slot is read before slot `first` is rewritten)
+    for (int item = tid; item < NI; item += NTH) {
+      float M = -INFINITY;
 #pragma unroll
-      for (int j = 0; j < kML; ++j) mb = fmaxf(mb, ml[j].x);
-      const float sc = M == -INFINITY ? 0.0f : fast_exp2(M - mb);
-      L *= sc;
-      a.x *= sc;
-      a.y *= sc;
-      a.z *= sc;
-      a.w *= sc;
+      for (int sub = 0; sub < R; ++sub) M = fmaxf(M, mst[sub * NI + item].x);
+      float L = 0.0f;
+      float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
 #pragma unroll
-      for (int j = 0; j < kML; ++j) {
-        const float e = ml[j].x == -INFINITY ? 0.0f : fast_exp2(ml[j].x - mb);
-        L = fmaf(e, ml[j].y, L);
-        a.x = fmaf(e, v[j].x, a.x);
-        a.y = fmaf(e, v[j].y, a.y);
-        a.z = fmaf(e, v[j].z, a.z);
-        a.w = fmaf(e, v[j].w, a.w);
+      for (int sub = 0; sub < R; ++sub) {
+        const float2 ml = mst[sub * NI + item];
+        const float4 v = ost[sub * NI + item];
+        const float e = ml.x == -INFINITY ? 0.0f : fast_exp2(ml.x - M);
+        L = fmaf(e, ml.y, L);
+        a.x = fmaf(e, v.x, a.x);
+        a.y = fmaf(e, v.y, a.y);
+        a.z = fmaf(e, v.z, a.z);
+        a.w = fmaf(e, v.w, a.w);
       }
-      M = mb;
-    }
-    mst[sub * NI + item] = make_float2(M, L);
-    ost[sub * NI + item] = a;
-  }
-  consumers_sync<W>();
-  for (int item = tid; item < NI; item += NTH) {
-    float M = -INFINITY;
+      const int g = item / (D / 4);
+      const int d = 4 * (item % (D / 4));
+      const int h = h0 + g;
+      const float av[4] = {a.x, a.y, a.z, a.w};
+      if (!to_out) {  // the group's state, in the layout of a split's partial
+        const long long sb = base + static_cast<long long>(first) * G + g;
+        *reinterpret_cast<float4*>(p.ws_o + sb * D + d) = a;
+        if (d == 0) {
+          p.ws_ml[sb * 2] = L == 0.0f ? -INFINITY : M;
+          p.ws_ml[sb * 2 + 1] = L;
+        }
+      } else if (p.partial) {
+        put_state2(static_cast<long long>(h) * D + d, av[0], av[1]);
+        put_state2(static_cast<long long>(h) * D + d + 2, av[2], av[3]);
+        if (d == 0)
+          put_state2(static_cast<long long>(p.H) * D + 2 * h, L == 0.0f ? -INFINITY : M * kLn2, L);
+      } else {
+        const float inv = L == 0.0f ? 0.0f : 1.0f / L;
 #pragma unroll
-    for (int sub = 0; sub < R; ++sub) M = fmaxf(M, mst[sub * NI + item].x);
-    float L = 0.0f;
-    float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-#pragma unroll
-    for (int sub = 0; sub < R; ++sub) {
-      const float2 ml = mst[sub * NI + item];
-      const float4 v = ost[sub * NI + item];
-      const float e = ml.x == -INFINITY ? 0.0f : fast_exp2(ml.x - M);
-      L = fmaf(e, ml.y, L);
-      a.x = fmaf(e, v.x, a.x);
-      a.y = fmaf(e, v.y, a.y);
-      a.z = fmaf(e, v.z, a.z);
-      a.w = fmaf(e, v.w, a.w);
+        for (int j = 0; j < 4; ++j)
+          store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * D + d + j, p.out_dtype,
+                           av[j] * inv);
+      }
     }
-    const int g = item / (D / 4);
-    const int d = 4 * (item % (D / 4));
-    const int h = h0 + g;
-    const float av[4] = {a.x, a.y, a.z, a.w};
-    if (p.partial) {
-      put_state2(static_cast<long long>(h) * D + d, av[0], av[1]);
-      put_state2(static_cast<long long>(h) * D + d + 2, av[2], av[3]);
-      if (d == 0)
-        put_state2(static_cast<long long>(p.H) * D + 2 * h, L == 0.0f ? -INFINITY : M * kLn2, L);
-    } else {
-      const float inv = L == 0.0f ? 0.0f : 1.0f / L;
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        store_from_float(p.out, (static_cast<long long>(b) * p.H + h) * D + d + j, p.out_dtype,
-                         av[j] * inv);
-    }
+  };
+
+  if (S_ <= 2 * kMergeGroup) {
+    if (!ticket(&p.counters[unit], S_)) return;
+    merge(0, S_, 1, true);
+  } else {
+    const int ng = (S_ + kMergeGroup - 1) / kMergeGroup;
+    const int grp = split / kMergeGroup;
+    const int gsz = min(kMergeGroup, S_ - grp * kMergeGroup);
+    // group counters follow the units' counters: [units][ng]
+    const long long units = static_cast<long long>(gridDim.z) * gridDim.y;
+    unsigned* gc = p.counters + units + unit * ng + grp;
+    if (!ticket(gc, gsz)) return;
+    merge(grp * kMergeGroup, gsz, 1, false);
+    if (tid == 0) *gc = 0u;
+    if (!ticket(&p.counters[unit], ng)) return;
+    merge(0, ng, kMergeGroup, true);
   }
   if (tid == 0) p.counters[unit] = 0u;
 }

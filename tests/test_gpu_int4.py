@@ -237,6 +237,38 @@ def test_scale_parameter(variant):
     parity(out, ref)
 
 
+@pytest.mark.parametrize("H,Hkv,D,N,window,batch,seq_lens", [
+    (4, 1, 128, 65536, 0, 1, None),          # one unit: ~444 splits, 14 groups
+    (4, 1, 256, 40000, 0, 1, None),          # D = 256, ~296 splits
+    (8, 2, 128, 50000, 30000, 1, None),      # window inside a long context
+    (4, 1, 128, 60000, 0, 2, [60000, 13]),   # the short sequence's splits are empty
+])
+def test_many_splits_two_level_merge(H, Hkv, D, N, window, batch, seq_lens, variant):
+    """Few (sequence, KV head) units over a long context: one wave holds
+    hundreds of splits per unit, which the tensor-core kernel merges in two
+    levels (groups of 32 splits, then the groups)."""
+    out, ref = run_decode(H, Hkv, D, N, seed=N % 89, window=window, batch=batch, seq_lens=seq_lens)
+    parity(out, ref)
+
+
+def test_many_splits_partial_state():
+    """The partial state of a one-unit shard with hundreds of splits (two-level
+    merge into the tq_lse_merge layout) normalises to the full decode."""
+    H, Hkv, D, N = 4, 1, 128, 65536
+    L = inputs.make_layer(31, H, Hkv, D, N)
+    c = [*O.quantize(L["k"]), *O.quantize(L["v"])]
+    dc = [dev(a) for a in c]
+    q = torch.from_numpy(L["q"]).half().cuda()
+    part = tq.sdpa_int4_partial(q, *dc, H // Hkv, 1.0, 0, n_local=N, token_offset=0, n_total=N)
+    merged = tq.lse_merge(part[None], H, D)
+    full = tq.sdpa_int4(q, *dc, H // Hkv, 1.0, 0, n_tokens=N, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert tq.device_error() == 0
+    np.testing.assert_allclose(host(merged), host(full), rtol=0, atol=2e-5)
+    ref = O.sdpa_int4(L["q"].astype(np.float16), *c, n_tokens=[N], f64=True)
+    parity(host(merged), ref)
+
+
 def test_partial_shards_merge_to_full(variant):
     """Sequence split: 3 shards -> partial states -> LSE merge == unsplit."""
     H, Hkv, D, N = 16, 4, 256, 5003

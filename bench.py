@@ -471,10 +471,11 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
     def step(Lr):
         if published:  # the decode kernel stores the states; a merge-only launch follows
             sc = Lr["sc"]
-            if last:
-                tq.quantize_append(Lr["kn"], Lr["vn"], *sc.cache.tensors(), pos=n_local, s=stream)
+            # the last rank's decode launch quantizes the new token in as well
+            kn = Lr["kn"].reshape(1, C4_HKV, C4_D) if last else None
+            vn = Lr["vn"].reshape(1, C4_HKV, C4_D) if last else None
             peer.decode(Lr["q"], sc.cache.tensors(), n_local + (1 if last else 0), sc.t0, C4_N,
-                        C4_H // C4_HKV, 1.0, 0, out=Lr["out"], ws=ws, s=stream)
+                        C4_H // C4_HKV, 1.0, 0, out=Lr["out"], ws=ws, k_new=kn, v_new=vn, s=stream)
             return
         partial(Lr)
         exchange(Lr)
@@ -636,7 +637,9 @@ def run_cfg4(args, rank: int, world: int, local_rank: int, steps: int = 256, che
                         "), merged output -> pinned host, stream sync; host clock, max over ranks"},
         "layers_rotated": layers_n,
         "l2": f"inputs larger than L2: {layers_n} rotating shards of {shard_bytes / 1e6:.0f} MB",
-        "gpu_launches_per_step": ("quantize_rows_kernel (last rank), decode_mma_kernel (partial), " +
+        "gpu_launches_per_step": ("decode_mma_kernel (partial; the new token's append fused on the "
+                                  "last rank), " if published else
+                                  "quantize_rows_kernel (last rank), decode_mma_kernel (partial), ") + (
                                   ("peer_merge_published_kernel" if published else
                                    "peer_merge_kernel" if peer is not None else
                                    "lse_merge_kernel" + (" + NCCL all-gather" if world > 1 else ""))),

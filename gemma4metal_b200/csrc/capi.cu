@@ -418,10 +418,16 @@ int tq_sdpa_int4_partial_publish(const void* queries, tq_dtype q_dtype, const ui
                                  const void* v_biases, tq_dtype sb_dtype, int gqa_factor,
                                  float scale, int sliding_window, int batch, int num_kv_heads,
                                  int head_dim, int n_local, int capacity, int token_offset,
-                                 int n_total, void* const* peer_bufs, int world, int rank,
+                                 int n_total, const void* k_new, const void* v_new,
+                                 tq_dtype new_dtype, void* const* peer_bufs, int world, int rank,
                                  void* workspace, size_t workspace_bytes, void* stream) {
   t_err.clear();
   if (!peer_bufs) return fail(TQ_ERR_INVALID, "tq_sdpa_int4_partial_publish: null peer_bufs");
+  if (!k_new != !v_new)
+    return fail(TQ_ERR_INVALID, "tq_sdpa_int4_partial_publish: give both k_new and v_new or neither");
+  if (k_new && (!valid_dtype(new_dtype) || !aligned16(k_new) || !aligned16(v_new) || n_local < 1))
+    return fail(TQ_ERR_INVALID, "tq_sdpa_int4_partial_publish: k_new/v_new need a valid dtype, "
+                "16-byte alignment and n_local >= 1 (the new token's slot is n_local - 1)");
   if (world < 1 || world > tq::kPeerMaxWorld || rank < 0 || rank >= world)
     return fail(TQ_ERR_INVALID, "tq_sdpa_int4_partial_publish: bad world/rank");
   if (token_offset < 0 || n_total < token_offset + n_local)
@@ -433,6 +439,9 @@ int tq_sdpa_int4_partial_publish(const void* queries, tq_dtype q_dtype, const ui
   c.peer_bufs = peer_bufs;
   c.peer_world = world;
   c.peer_rank = rank;
+  c.k_new = k_new;  // quantize-on-append of the new token in the same launch (nullable)
+  c.v_new = v_new;
+  c.new_dtype = new_dtype;
   return decode_common(c, "tq_sdpa_int4_partial_publish", nullptr, token_offset, n_total, 1,
                        nullptr, TQ_F32, nullptr, workspace, workspace_bytes, stream);
 }

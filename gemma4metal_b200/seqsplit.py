@@ -144,14 +144,17 @@ class PeerExchange:
     def decode(self, queries: torch.Tensor, cache, n_local: int, token_offset: int, n_total: int,
                gqa_factor: int, scale: float = 1.0, sliding_window: int = 0,
                out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
-               ws: Optional[torch.Tensor] = None, s=None) -> torch.Tensor:
+               ws: Optional[torch.Tensor] = None, k_new: Optional[torch.Tensor] = None,
+               v_new: Optional[torch.Tensor] = None, s=None) -> torch.Tensor:
         """One sequence-split decode step with the exchange inside the decode
         kernel: each (sequence, KV head) slice of the partial state is stored
         into every rank's buffer as {value, step} pairs as soon as it is
         complete (`tq_sdpa_int4_partial_publish`), then a merge-only launch
         (`tq_peer_merge_published`) waits for the pairs of the step and
         merges. Same lockstep and failure rules as `merge`; use one exchange
-        with either `merge` or `decode`."""
+        with either `merge` or `decode`. k_new / v_new ((B, Hkv, D), on the
+        rank holding the sequence's end): the new token is quantized into
+        slot n_local - 1 in the same launch."""
         if self.failed:
             raise RuntimeError("PeerExchange: a merge timed out on this exchange; close it and "
                                "build a new one on every rank")
@@ -163,7 +166,8 @@ class PeerExchange:
             out = torch.empty(B, H, D, dtype=out_dtype or queries.dtype, device=self.device)
         tq.sdpa_int4_partial_publish(queries, cache, gqa_factor, scale, sliding_window, self.bufs,
                                      self.world, self.rank, n_local=n_local,
-                                     token_offset=token_offset, n_total=n_total, ws=ws, s=s)
+                                     token_offset=token_offset, n_total=n_total, ws=ws,
+                                     k_new=k_new, v_new=v_new, s=s)
         tq._check(tq.load_library().tq_peer_merge_published(
             self.bufs.data_ptr(), self.world, self.rank, B, H, D, tq._ptr(out), tq._dt(out),
             self.timeout_us, tq._stream(s)))

@@ -73,7 +73,7 @@ def load_library() -> ctypes.CDLL:
     L.tq_sdpa_int4_partial.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I, I, I, P,
                                        P, SZ, P]
     L.tq_sdpa_int4_partial_publish.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I,
-                                               I, I, P, I, I, P, SZ, P]
+                                               I, I, P, P, I, P, I, I, P, SZ, P]
     L.tq_peer_merge_published.argtypes = [P, I, I, I, I, I, P, I, I, P]
     L.tq_lse_merge.argtypes = [P, I, I, I, I, P, I, P]
     L.tq_device_error.argtypes = [P, ctypes.POINTER(ctypes.c_uint32)]
@@ -598,17 +598,22 @@ def sdpa_int4_partial_publish(queries: torch.Tensor, cache, gqa_factor: int, sca
                               sliding_window: int, peer_bufs: torch.Tensor, world: int,
                               rank: int, *, n_local: Optional[int] = None, token_offset: int = 0,
                               n_total: Optional[int] = None, ws: Optional[torch.Tensor] = None,
-                              s=None) -> None:
+                              k_new: Optional[torch.Tensor] = None,
+                              v_new: Optional[torch.Tensor] = None, s=None) -> None:
     """The shard's partial state, stored by the decode kernel straight into
     every rank's exchange buffer (peer_bufs: device int64 array of the
-    world's buffer pointers); tq_peer_merge_published merges it."""
+    world's buffer pointers); tq_peer_merge_published merges it. k_new and
+    v_new ((B, Hkv, D), optional) are quantized into slot n_local - 1 in the
+    same launch (the rank that holds the sequence's end)."""
     q, qc, cache, B, H, D, Hkv, cap, nl, nt, ws = _shard_args(
         queries, cache, n_local, token_offset, n_total, sliding_window, ws, s)
+    kn = None if k_new is None else k_new.contiguous()
+    vn = None if v_new is None else v_new.contiguous()
     _check(load_library().tq_sdpa_int4_partial_publish(
         _ptr(qc), _dt(q), *[_ptr(c) for c in cache], _dt(cache[1]), int(gqa_factor),
         float(scale), int(sliding_window), B, Hkv, D, nl, cap, int(token_offset), nt,
-        peer_bufs.data_ptr(), int(world), int(rank), _ptr(ws), 0 if ws is None else ws.numel(),
-        _stream(s)))
+        _ptr(kn), _ptr(vn), 0 if kn is None else _dt(kn), peer_bufs.data_ptr(), int(world),
+        int(rank), _ptr(ws), 0 if ws is None else ws.numel(), _stream(s)))
 
 
 def lse_merge(parts: torch.Tensor, num_heads: int, head_dim: int,

@@ -232,7 +232,10 @@ TQ_API int tq_peer_merge(const float* part, void* const* peer_bufs, int world, i
  * counter + 1), so the state crosses NVLink while the rest is still being
  * computed and no fence or flag is needed: the merge takes a value once its
  * pair carries the step. tq_sdpa_int4_partial_publish takes the arguments of
- * tq_sdpa_int4_partial with (peer_bufs, world, rank) in place of part_out; the
+ * tq_sdpa_int4_partial with (peer_bufs, world, rank) in place of part_out, and
+ * optionally the new token's K/V rows (k_new, v_new: (B, Hkv, D) in new_dtype,
+ * NULL for none), quantized into slot n_local - 1 of this shard in the same
+ * launch, as tq_sdpa_int4_append does (the rank holding the sequence's end); the
  * buffers must come from tq_peer_buffer_bytes with the same world, batch,
  * num_heads and head_dim. It runs on the tensor-core decode kernel only
  * (head_dim 128 or 256; else TQ_ERR_UNSUPPORTED). tq_peer_merge_published,
@@ -248,8 +251,10 @@ TQ_API int tq_sdpa_int4_partial_publish(const void* queries, tq_dtype q_dtype,
                                         tq_dtype sb_dtype, int gqa_factor, float scale,
                                         int sliding_window, int batch, int num_kv_heads,
                                         int head_dim, int n_local, int capacity, int token_offset,
-                                        int n_total, void* const* peer_bufs, int world, int rank,
-                                        void* workspace, size_t workspace_bytes, void* stream);
+                                        int n_total, const void* k_new, const void* v_new,
+                                        tq_dtype new_dtype, void* const* peer_bufs, int world,
+                                        int rank, void* workspace, size_t workspace_bytes,
+                                        void* stream);
 TQ_API int tq_peer_merge_published(void* const* peer_bufs, int world, int rank, int batch,
                                    int num_heads, int head_dim, void* out, tq_dtype out_dtype,
                                    int timeout_us, void* stream);

@@ -251,3 +251,37 @@ def test_published_single_gpu_equals_partial_merge(H, Hkv, D, N, win):
             assert torch.allclose(got, ref, rtol=1e-6, atol=1e-6), float((got - ref).abs().max())
     finally:
         ex.close()
+
+
+def test_published_fused_append_single_gpu():
+    """World of one: the publishing decode launch also quantizes the new
+    token into slot n_local - 1 (the rank holding the sequence's end) -- the
+    cache bytes equal quantize_append's and the merged output equals
+    quantize_append + partial + lse_merge."""
+    import gemma4metal_b200.turboquant as tq
+    from gemma4metal_b200 import seqsplit
+    from oracle import inputs
+    H, Hkv, D, N = 32, 8, 256, 3000
+    L = inputs.make_layer(29, H, Hkv, D, N)
+    a = tq.KVCache(1, Hkv, D, N)
+    b = tq.KVCache(1, Hkv, D, N)
+    for c in (a, b):
+        c.append(torch.from_numpy(L["k"][:, :, :N - 1]).cuda().half(),
+                 torch.from_numpy(L["v"][:, :, :N - 1]).cuda().half())
+    kn = torch.from_numpy(L["k"][:, :, N - 1]).cuda().half()  # (1, Hkv, D)
+    vn = torch.from_numpy(L["v"][:, :, N - 1]).cuda().half()
+    q = torch.from_numpy(L["q"]).half().cuda()
+    ex = seqsplit.PeerExchange(1, H, D)
+    try:
+        got = ex.decode(q, a.tensors(), N, 0, N, H // Hkv, 0.0625, 0, out_dtype=torch.float32,
+                        k_new=kn, v_new=vn)
+        tq.quantize_append(kn[:, :, None], vn[:, :, None], *b.tensors(), pos=N - 1)
+        part = tq.sdpa_int4_partial(q, *b.tensors(), H // Hkv, 0.0625, 0, n_local=N)
+        ref = tq.lse_merge(part[None], H, D)
+        torch.cuda.synchronize()
+        assert tq.device_error() == 0
+        for x, y in zip(a.tensors(), b.tensors()):
+            assert torch.equal(x, y)
+        assert torch.allclose(got, ref, rtol=1e-6, atol=1e-6), float((got - ref).abs().max())
+    finally:
+        ex.close()

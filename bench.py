@@ -68,6 +68,10 @@ def parse():
                          "decode kernel itself as {value, step} pairs and merged by a merge-only "
                          "kernel (published), exchanged and merged by one kernel over NVLink "
                          "peer memory (peer), or NCCL all-gather + merge kernel (nccl)")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="cfg4_heads (config 4 split by KV heads): the outputs gathered over "
+                         "NVLink peer memory by the publishing decode + a gather kernel (peer) "
+                         "or by an NCCL all-gather (nccl)")
     ap.add_argument("--split-step", action="store_true",
                     help="cfg1: run the step as two launches (quantize_append, then sdpa_int4) "
                          "instead of the fused sdpa_int4_append")
@@ -714,12 +718,20 @@ def run_cfg4_heads(args, rank: int, world: int, local_rank: int, steps: int = 25
                            full=torch.empty(world, 1, hq, C4_D, dtype=torch.float16, device=dev)))
     ws = tq.workspace(dev, tq.sdpa_int4_workspace_size(1, hq, hk, C4_D, n_ctx, 0))
     stream = torch.cuda.Stream(device=dev)
+    peer = args.gather == "peer"
+    ex = seqsplit.PeerExchange(1, hq, C4_D, device=dev) if peer else None
+    for Lr in layers:
+        Lr["gathered"] = torch.empty(1, C4_H, C4_D, dtype=torch.float16, device=dev)
 
     def decode(Lr):
         tq.sdpa_int4_append(Lr["q"], Lr["kn"], Lr["vn"], *Lr["cache"].tensors(), G, 1.0, 0, stream,
                             n_tokens=n_ctx, out=Lr["out"], ws=ws)
 
     def step(Lr):
+        if peer:  # the decode publishes its heads' state; a gather kernel assembles the output
+            ex.decode_heads(Lr["q"], Lr["cache"].tensors(), n_ctx, G, 1.0, 0, out=Lr["gathered"],
+                            ws=ws, k_new=Lr["kn"], v_new=Lr["vn"], s=stream)
+            return
         decode(Lr)
         dist.all_gather_into_tensor(Lr["full"], Lr["out"])
 
@@ -769,7 +781,7 @@ def run_cfg4_heads(args, rank: int, world: int, local_rank: int, steps: int = 25
             refs.append(O.sdpa_int4(qh[:, g0 * G:min(hk, g0 + 2) * G], *(a[:, sl] for a in full), f64=True))
         ref = np.concatenate(refs, axis=1).astype(np.float64)
         # the gathered output: rank 0's block holds its heads
-        got = L0["full"][0].float().cpu().numpy().astype(np.float64)
+        got = (L0["gathered"][:, :hq] if peer else L0["full"][0]).float().cpu().numpy().astype(np.float64)
         acc = {"max_abs": float(np.max(np.abs(got - ref))),
                "cosine": float(got.ravel() @ ref.ravel() / (np.linalg.norm(got) * np.linalg.norm(ref))),
                "oracle": f"C oracle: quantize of the same values, dequantize + fp64 SDPA over all "
@@ -778,6 +790,8 @@ def run_cfg4_heads(args, rank: int, world: int, local_rank: int, steps: int = 25
     dist.barrier()
     del graphs
     torch.cuda.synchronize()
+    if ex is not None:
+        ex.close()
     us_step = t_step * 1000.0 / n_timed
     us_dec = t_dec * 1000.0 / n_timed
     dec_bytes = n_ctx * per_tok + hq * C4_D * 4
@@ -785,13 +799,14 @@ def run_cfg4_heads(args, rank: int, world: int, local_rank: int, steps: int = 25
     ach = dec_bytes / (us_dec * 1e-6) / 1e9
     return {
         "workload": f"cfg4 decode step: 262144-token global layer (H=32, Hkv=8, D=256) split by KV "
-                    f"heads ({hk} per GPU): append + decode of the rank's heads in one launch, "
-                    f"NCCL all-gather of the outputs",
+                    f"heads ({hk} per GPU): append + decode of the rank's heads in one launch, " +
+                    ("its state stored into every rank's buffer over NVLink + a gather kernel"
+                     if peer else "NCCL all-gather of the outputs"),
         "metric": "int4-KV decode-attention tokens/s", "unit": "tokens/s", "scaling": "strong",
         "n_gpus": world, "steps": n_timed,
         "value": n_timed / (t_step / 1000.0), "ms_per_step": t_step / n_timed,
         "time_split_us": {"step": us_step, "append_plus_decode": us_dec,
-                          "all_gather": us_step - us_dec},
+                          "gather": us_step - us_dec},
         "roofline": {"bound": "hbm", "kernel": f"tq::decode_mma_kernel<256,4,__half> ({hk} KV heads)",
                      "achieved": ach, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": ach / peaks["hbm_gbs"], "kernel_us": us_dec,
@@ -800,7 +815,9 @@ def run_cfg4_heads(args, rank: int, world: int, local_rank: int, steps: int = 25
         "accuracy_vs_oracle": acc,
         "layers_rotated": layers_n,
         "l2": f"inputs larger than L2: {layers_n} rotating caches of {shard_bytes / 1e6:.0f} MB",
-        "gpu_launches_per_step": "decode_mma_kernel (append fused) + NCCL all-gather",
+        "gpu_launches_per_step": ("decode_mma_kernel (append fused, state published) + "
+                                  "peer_gather_published_kernel" if peer else
+                                  "decode_mma_kernel (append fused) + NCCL all-gather"),
     }
 
 

@@ -262,6 +262,69 @@ __global__ void __launch_bounds__(kPeerThreads) peer_merge_published_kernel(cons
   end_step(own, step);
 }
 
+// Gather of states the decode kernel published as {value, step} pairs when
+// the ranks split the heads rather than the sequence: rank k's slot holds
+// the complete state of its p.H heads, so each (sequence, rank, head) item is
+// normalised on its own (o / l) into head k * p.H + j of the (B, world * p.H,
+// D) output -- no merge across ranks. Waits, bound, NaN and failed-exchange
+// rules as for the merge.
+__global__ void __launch_bounds__(kPeerThreads) peer_gather_published_kernel(const PeerParams p) {
+  __shared__ uint32_t s_step;
+  __shared__ float s_l;
+  __shared__ int s_failed;
+  uint32_t* own = static_cast<uint32_t*>(p.bufs[p.rank]);
+  const uint32_t step = begin_step(own, &s_step, &s_failed);
+  if (s_failed && threadIdx.x == 0) atomicOr(p.err, kErrPeerTimeout);  // (again, on a failed exchange)
+  const long long blk = static_cast<long long>(p.B) * p.H * (p.D + 2);  // pairs per state
+  const uint2* data = reinterpret_cast<const uint2*>(own + peer_data_word()) +
+                      static_cast<long long>(step & 1u) * p.world * blk;
+  const long long hd = static_cast<long long>(p.H) * p.D;
+  const int Hout = p.world * p.H;
+  const long long t0 = clock64();
+  for (int item = blockIdx.x; item < p.B * Hout; item += gridDim.x) {
+    const int b = item / Hout, k = (item % Hout) / p.H, j = item % p.H;
+    const uint2* base = data + k * blk + static_cast<long long>(b) * p.H * (p.D + 2);
+    const long long ob = (static_cast<long long>(b) * Hout + k * p.H + j) * p.D;
+    if (threadIdx.x == 0 && !s_failed) {
+      const uint2* q = base + hd + 2 * j + 1;  // l
+      uint2 v = ld_pair(q);
+      while (v.y != step) {
+        if (clock64() - t0 > p.budget) {
+          record_timeout(own, p, &s_failed);
+          break;
+        }
+        __nanosleep(64);
+        v = ld_pair(q);
+      }
+      s_l = __uint_as_float(v.x);
+    }
+    __syncthreads();
+    if (s_failed) {  // no complete state: NaN, never stale pairs
+      for (int d = threadIdx.x; d < p.D; d += kPeerThreads)
+        store_from_float(p.out, ob + d, p.out_dtype, NAN);
+      continue;
+    }
+    const float L = s_l;
+    for (int d = threadIdx.x; d < p.D; d += kPeerThreads) {
+      const uint2* q = base + static_cast<long long>(j) * p.D + d;
+      uint2 v = ld_pair(q);
+      bool ok = true;
+      while (v.y != step) {
+        if (clock64() - t0 > p.budget) {
+          record_timeout(own, p, &s_failed);
+          ok = false;
+          break;
+        }
+        v = ld_pair(q);
+      }
+      store_from_float(p.out, ob + d, p.out_dtype,
+                       !ok ? NAN : L == 0.0f ? 0.0f : __uint_as_float(v.x) / L);
+    }
+    __syncthreads();
+  }
+  end_step(own, step);
+}
+
 size_t state_floats(int world, int B, int H, int D) {
   return 2ull * world * B * H * (D + 2);
 }
@@ -363,6 +426,43 @@ TQ_API int tq_peer_merge_published(void* const* peer_bufs, int world, int rank, 
                                    int timeout_us, void* stream) {
   return peer_merge_common(nullptr, peer_bufs, world, rank, batch, num_heads, head_dim, true, out,
                            out_dtype, timeout_us, stream);
+}
+
+TQ_API int tq_peer_gather_published(void* const* peer_bufs, int world, int rank, int batch,
+                                    int num_heads, int head_dim, void* out, tq_dtype out_dtype,
+                                    int timeout_us, void* stream) {
+  if (!peer_bufs || !out) {
+    set_last_error("tq_peer_gather_published: null pointer");
+    return TQ_ERR_INVALID;
+  }
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || batch < 1 || num_heads < 1 ||
+      head_dim < 1 || timeout_us < 1) {
+    set_last_error("tq_peer_gather_published: bad sizes");
+    return TQ_ERR_INVALID;
+  }
+  int dev = 0, khz = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&khz, cudaDevAttrClockRate, dev);
+  PeerParams p{};
+  p.bufs = peer_bufs;
+  p.world = world;
+  p.rank = rank;
+  p.B = batch;
+  p.H = num_heads;
+  p.D = head_dim;
+  p.out = out;
+  p.out_dtype = out_dtype;
+  p.budget = static_cast<long long>(timeout_us) * (khz > 0 ? khz : 2000000) / 1000;
+  p.err = device_error_word();
+  int grid = batch * num_heads * world;
+  if (grid > 148) grid = 148;
+  const cudaError_t e = launch_pdl(peer_gather_published_kernel, dim3(grid), dim3(kPeerThreads), 0,
+                                   static_cast<cudaStream_t>(stream), p);
+  if (e != cudaSuccess) {
+    set_last_error("tq_peer_gather_published: %s", cudaGetErrorString(e));
+    return TQ_ERR_CUDA;
+  }
+  return TQ_OK;
 }
 
 static int peer_merge_common(const float* part, void* const* peer_bufs, int world, int rank,

@@ -173,6 +173,36 @@ class PeerExchange:
             self.timeout_us, tq._stream(s)))
         return out
 
+    def decode_heads(self, queries: torch.Tensor, cache, n_tokens: int, gqa_factor: int,
+                     scale: float = 1.0, sliding_window: int = 0,
+                     out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                     ws: Optional[torch.Tensor] = None, k_new: Optional[torch.Tensor] = None,
+                     v_new: Optional[torch.Tensor] = None, s=None) -> torch.Tensor:
+        """One decode step of a head split: this rank's queries (B, H/world, D)
+        against its KV heads' cache over the whole sequence (n_tokens), the
+        state published into every rank's buffer, then every rank's heads
+        gathered into the full output (B, H, D) (`tq_peer_gather_published`),
+        rank k's heads at k * H/world. k_new / v_new: the new token of this
+        rank's KV heads, appended in the same launch. The exchange is built
+        with num_heads = H/world."""
+        if self.failed:
+            raise RuntimeError("PeerExchange: a merge timed out on this exchange; close it and "
+                               "build a new one on every rank")
+        B, Hl, D = queries.shape
+        if (B, Hl, D) != (self.B, self.H, self.D):
+            raise ValueError(f"queries {tuple(queries.shape)} do not match the exchange "
+                             f"({self.B}, {self.H}, {self.D})")
+        if out is None:
+            out = torch.empty(B, Hl * self.world, D, dtype=out_dtype or queries.dtype,
+                              device=self.device)
+        tq.sdpa_int4_partial_publish(queries, cache, gqa_factor, scale, sliding_window, self.bufs,
+                                     self.world, self.rank, n_local=n_tokens, token_offset=0,
+                                     n_total=n_tokens, ws=ws, k_new=k_new, v_new=v_new, s=s)
+        tq._check(tq.load_library().tq_peer_gather_published(
+            self.bufs.data_ptr(), self.world, self.rank, B, Hl, D, tq._ptr(out), tq._dt(out),
+            self.timeout_us, tq._stream(s)))
+        return out
+
     def check(self, s=None) -> None:
         """Read (and clear) the device error word after the merges enqueued so
         far (synchronises the stream); raise if one of them timed out waiting

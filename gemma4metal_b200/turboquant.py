@@ -75,6 +75,7 @@ def load_library() -> ctypes.CDLL:
     L.tq_sdpa_int4_partial_publish.argtypes = [P, I, P, P, P, P, P, P, I, I, F, I, I, I, I, I, I,
                                                I, I, P, P, I, P, I, I, P, SZ, P]
     L.tq_peer_merge_published.argtypes = [P, I, I, I, I, I, P, I, I, P]
+    L.tq_peer_gather_published.argtypes = [P, I, I, I, I, I, P, I, I, P]
     L.tq_lse_merge.argtypes = [P, I, I, I, I, P, I, P]
     L.tq_device_error.argtypes = [P, ctypes.POINTER(ctypes.c_uint32)]
     _register_extra(L)

@@ -258,6 +258,17 @@ TQ_API int tq_sdpa_int4_partial_publish(const void* queries, tq_dtype q_dtype,
 TQ_API int tq_peer_merge_published(void* const* peer_bufs, int world, int rank, int batch,
                                    int num_heads, int head_dim, void* out, tq_dtype out_dtype,
                                    int timeout_us, void* stream);
+/* Head split over the same exchange: every rank decodes its own num_heads
+ * query heads over the whole sequence and publishes their state with
+ * tq_sdpa_int4_partial_publish (token_offset 0, n_total = n_local);
+ * tq_peer_gather_published then writes each rank's heads, normalised, into
+ * the full output (batch, world * num_heads, head_dim): rank k's heads at
+ * k * num_heads.. -- a gather, not a merge. Same waits, timeout, NaN and
+ * failed-exchange rules as tq_peer_merge; use one exchange for one of the
+ * three forms. No counterpart in the reference (it is single-device). */
+TQ_API int tq_peer_gather_published(void* const* peer_bufs, int world, int rank, int batch,
+                                    int num_heads, int head_dim, void* out, tq_dtype out_dtype,
+                                    int timeout_us, void* stream);
 
 /* Log-sum-exp merge of n_parts partial states (e.g. one per GPU after an
  * all-gather). parts: n_parts blocks of (H*(D+2)) floats per batch entry,

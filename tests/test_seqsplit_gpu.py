@@ -285,3 +285,105 @@ def test_published_fused_append_single_gpu():
         assert torch.allclose(got, ref, rtol=1e-6, atol=1e-6), float((got - ref).abs().max())
     finally:
         ex.close()
+
+
+def test_head_split_gather_single_gpu():
+    """World of one: decode_heads (publishing decode with the append fused +
+    gather kernel) equals the fused append + decode of the same cache, over
+    several steps (slot parity, step counter)."""
+    import gemma4metal_b200.turboquant as tq
+    from gemma4metal_b200 import seqsplit
+    from oracle import inputs
+    H, Hkv, D, N = 16, 4, 256, 5000
+    L = inputs.make_layer(37, H, Hkv, D, N)
+    a = tq.KVCache(1, Hkv, D, N)
+    b = tq.KVCache(1, Hkv, D, N)
+    for c in (a, b):
+        c.append(torch.from_numpy(L["k"][:, :, :N - 1]).cuda().half(),
+                 torch.from_numpy(L["v"][:, :, :N - 1]).cuda().half())
+    kn = torch.from_numpy(L["k"][:, :, N - 1]).cuda().half()
+    vn = torch.from_numpy(L["v"][:, :, N - 1]).cuda().half()
+    q = torch.from_numpy(L["q"]).half().cuda()
+    ex = seqsplit.PeerExchange(1, H, D)
+    try:
+        for step in range(3):
+            qs = q * (1 + 0.25 * step)
+            got = ex.decode_heads(qs, a.tensors(), N, H // Hkv, 0.0625, 0, out_dtype=torch.float32,
+                                  k_new=kn, v_new=vn)
+            ref = tq.sdpa_int4_append(qs, kn, vn, *b.tensors(), H // Hkv, 0.0625, 0, n_tokens=N,
+                                      out_dtype=torch.float32)
+            torch.cuda.synchronize()
+            assert tq.device_error() == 0
+            assert torch.allclose(got, ref, rtol=1e-5, atol=1e-5), float((got - ref).abs().max())
+        for x, y in zip(a.tensors(), b.tensors()):
+            assert torch.equal(x, y)
+    finally:
+        ex.close()
+
+
+def _heads_worker(rank, world, port, q):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    import gemma4metal_b200.turboquant as tq
+    from gemma4metal_b200 import seqsplit
+    from oracle import inputs, oracle as O
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ex = None
+    try:
+        H, Hkv, D, N = 32, 8, 256, 3001
+        G = H // Hkv
+        L = inputs.make_layer(41, H, Hkv, D, N)
+        h0, h1 = seqsplit.head_bounds(Hkv, world, rank)
+        cap = (N + 3) // 4 * 4
+        c = tq.KVCache(1, h1 - h0, D, cap)
+        c.append(torch.from_numpy(L["k"][:, h0:h1, :N - 1]).cuda().half(),
+                 torch.from_numpy(L["v"][:, h0:h1, :N - 1]).cuda().half())
+        kn = torch.from_numpy(L["k"][:, h0:h1, N - 1]).cuda().half()
+        vn = torch.from_numpy(L["v"][:, h0:h1, N - 1]).cuda().half()
+        qh = torch.from_numpy(L["q"][:, h0 * G:h1 * G]).half().cuda()
+        ex = seqsplit.PeerExchange(1, (h1 - h0) * G, D, device=f"cuda:{rank}")
+        dist.barrier()
+        for _ in range(3):  # several steps: slot parity and step counter
+            out = ex.decode_heads(qh, c.tensors(), N, G, 1.0, 0, out_dtype=torch.float32,
+                                  k_new=kn, v_new=vn)
+        torch.cuda.synchronize()
+        code = tq.device_error()
+        kq, ks, kb = O.quantize(L["k"])
+        vq, vs, vb = O.quantize(L["v"])
+        ref = O.sdpa_int4(L["q"].astype(np.float16), kq, ks, kb, vq, vs, vb, f64=True)
+        got = out.cpu().numpy()
+        err = float(np.max(np.abs(got - ref)))
+        cos = float(got.ravel() @ ref.ravel() / (np.linalg.norm(got) * np.linalg.norm(ref)))
+        q.put((rank, (code, err, cos)))
+    finally:
+        if ex is not None:
+            ex.close()
+        dist.destroy_process_group()
+
+
+def test_head_split_gather_two_gpus():
+    """Head split over 2 GPUs: each rank decodes its KV heads over the whole
+    sequence (new token appended in the same launch) and the peer gather
+    assembles every head's output on every rank -- equal to the oracle's
+    unsplit dequantize + SDPA."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_heads_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+        assert p.exitcode == 0
+    for rank, (code, err, cos) in dict(q.get(timeout=10) for _ in range(2)).items():
+        assert code == 0, (rank, code)
+        assert err <= 2e-3 and cos >= 0.99999, (rank, err, cos)

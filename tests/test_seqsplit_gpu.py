@@ -343,11 +343,12 @@ def _heads_worker(rank, world, port, q):
         h0, h1 = seqsplit.head_bounds(Hkv, world, rank)
         cap = (N + 3) // 4 * 4
         c = tq.KVCache(1, h1 - h0, D, cap)
-        c.append(torch.from_numpy(L["k"][:, h0:h1, :N - 1]).cuda().half(),
-                 torch.from_numpy(L["v"][:, h0:h1, :N - 1]).cuda().half())
-        kn = torch.from_numpy(L["k"][:, h0:h1, N - 1]).cuda().half()
-        vn = torch.from_numpy(L["v"][:, h0:h1, N - 1]).cuda().half()
-        qh = torch.from_numpy(L["q"][:, h0 * G:h1 * G]).half().cuda()
+        # fp32 K/V on both sides: the oracle quantizes the same values
+        c.append(torch.from_numpy(np.ascontiguousarray(L["k"][:, h0:h1, :N - 1])).cuda(),
+                 torch.from_numpy(np.ascontiguousarray(L["v"][:, h0:h1, :N - 1])).cuda())
+        kn = torch.from_numpy(np.ascontiguousarray(L["k"][:, h0:h1, N - 1])).cuda()
+        vn = torch.from_numpy(np.ascontiguousarray(L["v"][:, h0:h1, N - 1])).cuda()
+        qh = torch.from_numpy(np.ascontiguousarray(L["q"][:, h0 * G:h1 * G])).half().cuda()
         ex = seqsplit.PeerExchange(1, (h1 - h0) * G, D, device=f"cuda:{rank}")
         dist.barrier()
         for _ in range(3):  # several steps: slot parity and step counter
